@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-KV hot path on B200: BASELINE config 3.
+
+One step = one decode step of a Qwen2.5-0.5B-shaped attention stack over 24
+layers for B = 256 sequences per GPU (contexts lognormal, median 1024, sigma
+0.5, clipped to [16, 8192]; fp16 KV; 16-token blocks scattered over a pool of
+1.1x the blocks needed; one pool per layer).  Per layer: one
+reshape_and_cache launch (append the new token) and one paged decode
+attention launch.  Inputs are synthetic (seeded), weights are not involved.
+
+Multi-GPU: one process per GPU (torchrun), sequences dealt round-robin, each
+GPU owns its own pools; per-GPU work is fixed as N grows ("weak"; --strong
+keeps 256 sequences in total).  The timed region is bracketed by a barrier and
+a device synchronisation; the time is the max over ranks.
+
+Prints ONE JSON line (rank 0).  --impl reference times the reference
+algorithm's CPU port (the oracle, oracle/pagedkv_oracle.c) on the host cores
+instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-inference-scheduler_b200"))
+
+METRIC = "paged decode attn KV GB/s (% of HBM peak) and decode tok/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+WORKLOAD = ("config3: paged decode step, 24 layers x (append + decode attention), "
+            "B=256 seqs/GPU, ctx lognormal(median 1024, sigma 0.5) in [16,8192], 14q/2kv, d64, fp16 KV")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
+    ap.add_argument("--strong", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="only run this many steps after warm-up (for ncu launch lists); no timing")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_from_profiles():
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "paged_decode_config3.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":")[1].strip().split()[0])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+# --------------------------------------------------------------- clock sampling
+
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.proc = None
+        self.lines = []
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", ",".join(str(i) for i in gpu_indices)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self, t0: float, t1: float):
+        import datetime
+
+        rows = []
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[2]), float(f[3]), f[6], f[7], f[8], f[9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05] or rows
+        reasons = set()
+        for r in inside:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                "sw_power_cap"), r[3:]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[1] for r in inside),
+                "sm_max_mhz": max(r[2] for r in inside), "reasons": sorted(reasons),
+                "samples": len(inside)}
+
+
+# --------------------------------------------------------------- CPU baseline (oracle port)
+
+def cpu_sample(seconds: float, n_seqs_subset: int | None = None, max_reps: int | None = None):
+    """Time the oracle (CPU port of the reference's append + gather + _attention)
+    on config-3 layers of rank 0's shard.  Returns (GB/s, cores, sample text)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from pagedkv import workloads as W
+
+    ctx = W.shard_contexts(256, 0, 1)
+    if n_seqs_subset is not None:
+        ctx = ctx[:: max(1, len(ctx) // n_seqs_subset)][:n_seqs_subset]
+    nb = int(math.ceil(1.1 * ((ctx + 15) // 16).sum()))
+    tabs = W.make_tables(ctx, nb, seed=100)
+    rng = np.random.default_rng(0)
+    kp = rng.standard_normal((nb, 16, 2, 64), dtype=np.float32).astype(np.float16)
+    vp = rng.standard_normal((nb, 16, 2, 64), dtype=np.float32).astype(np.float16)
+    B = len(ctx)
+    q = rng.standard_normal((B, 14, 64), dtype=np.float32).astype(np.float16)
+    kn = rng.standard_normal((B, 2, 64), dtype=np.float32).astype(np.float16)
+    vn = rng.standard_normal((B, 2, 64), dtype=np.float32).astype(np.float16)
+    pos = ctx - 1
+    slots = tabs[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16
+    qsl = np.arange(B + 1, dtype=np.int32)
+    prior = (ctx - 1).astype(np.int32)
+    bytes_per = W.decode_bytes(ctx) + W.append_bytes(B)
+    threads = oracle.num_threads()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.reshape_and_cache(kp, vp, kn, vn, slots, "f16")
+        oracle.paged_attention(q, kp, vp, tabs, qsl, prior, "f16", threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_reps is not None and reps >= max_reps):
+            break
+    gbs = bytes_per * reps / el / 1e9
+    sample = (f"oracle port (C, OpenMP) of the reference's append + gather + _attention; "
+              f"{reps} x one config-3 layer of {B} seqs (sum ctx {int(ctx.sum())}), {el:.1f} s")
+    return gbs, threads, sample, el, reps
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    # each step: one layer of a 32-sequence subset of config 3 (bounded sample)
+    n_sub = 32
+    total = args.warmup + args.steps
+    gbs_w, cores, sample, el, reps = cpu_sample(1e9, n_seqs_subset=n_sub, max_reps=max(1, args.warmup))
+    gbs, cores, sample, el, reps = cpu_sample(1e9, n_seqs_subset=n_sub, max_reps=max(1, args.steps))
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * el / reps, 4), "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "reference_step": f"1 layer, {n_sub}-sequence subset, CPU"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from pagedkv import BlockManager, PagedKVCache, ops
+    from pagedkv import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    L, scale, dt = args.layers, 0.125, torch.float16
+    ctx = W.shard_contexts(args.batch, rank, world, strong=args.strong)
+    B = len(ctx)
+    nblk = (ctx + 15) // 16
+    nb = int(math.ceil(1.1 * nblk.sum()))
+    tabs_np = W.make_tables(ctx, nb, seed=100 + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=dt)
+    for layer in range(L):
+        mgr.k_pool[layer].normal_(generator=g)
+        mgr.v_pool[layer].normal_(generator=g)
+    q = torch.randn((L, B, 14, 64), generator=g, device=dev, dtype=dt)
+    kn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+    vn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+    out = torch.empty_like(q)
+    pos = ctx - 1
+    slots = torch.from_numpy(tabs_np[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16).to(dev)
+    tabs = torch.from_numpy(tabs_np).to(dev)
+    ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    ws = ops.new_decode_workspace(B, 14, 64, dev)
+    err = ops.new_error_flags(dev)
+
+    appends = [ops.bind_reshape_and_cache(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], slots, err)
+               for l in range(L)]
+    decodes = [ops.bind_paged_decode_attention(q[l], mgr.k_pool[l], mgr.v_pool[l], tabs, ctx_d, scale,
+                                               ws, out[l], err) for l in range(L)]
+
+    dec_bytes = W.decode_bytes(ctx)
+    app_bytes = W.append_bytes(B)
+    step_bytes = L * (dec_bytes + app_bytes)
+
+    def step(ev=None):
+        for layer in range(L):
+            appends[layer]()
+            if ev is not None:
+                ev[layer][0].record()
+            decodes[layer]()
+            if ev is not None:
+                ev[layer][1].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_flags(err, "bench warm-up")
+
+    if args.profile_steps:
+        for _ in range(args.profile_steps):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # per-launch events on every 10th timed step (decode kernel roofline)
+    every = 10
+    ev_steps = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(L)] for _ in range((args.steps + every - 1) // every)]
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    start.record()
+    for i in range(args.steps):
+        step(ev_steps[i // every] if i % every == 0 else None)
+    end.record()
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    barrier()
+    if sampler:
+        sampler.stop()
+    ops.check_flags(err, "bench timed region")
+    ms_local = start.elapsed_time(end) / args.steps
+    dec_ms_samples = [a.elapsed_time(b) for evs in ev_steps for (a, b) in evs]
+    dec_ms_local = sum(dec_ms_samples) / len(dec_ms_samples)
+    ms = W.max_over_ranks(ms_local)
+    dec_ms = W.max_over_ranks(dec_ms_local)
+    total_bytes = W.sum_over_ranks(step_bytes)
+    total_seqs = W.sum_over_ranks(B)
+
+    # ---- end to end through the public API: pinned host inputs in, outputs back
+    kv = PagedKVCache(mgr)
+    for i in range(B):
+        kv.add_sequence(i, tabs_np[i, :nblk[i]].tolist(), int(ctx[i]) - 1)
+    hq = torch.empty_like(q, device="cpu").pin_memory()
+    hk = torch.empty_like(kn, device="cpu").pin_memory()
+    hv = torch.empty_like(vn, device="cpu").pin_memory()
+    hq.copy_(q)
+    hk.copy_(kn)
+    hv.copy_(vn)
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+    def e2e_step():
+        meta = kv.prepare_step([(i, 1) for i in range(B)])
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        for layer in range(L):
+            kv.forward_layer(layer, dq[layer], dk[layer], dv[layer], meta, scale, out=out[layer],
+                             advance=False)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ops.check_flags(err, "bench e2e")
+    e2e_ms = W.max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
+    d2h = hout.numel() * 2
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = peaks()
+    achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+    clocks = sampler.summary(t_wall0, t_wall1) if sampler else None
+    line = {
+        "metric": METRIC,
+        "value": round(total_bytes / (ms * 1e-3) / 1e9, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded normal K/V/Q; lognormal contexts); no weights involved",
+        "config": {"workload": WORKLOAD, "global_batch": int(total_seqs), "layers": L,
+                   "sum_ctx_rank0": int(ctx.sum()), "pool_blocks_rank0": nb,
+                   "parallelism": f"sequence-sharded x{world}, no collective on the data path",
+                   "l2": "inputs larger than L2: ~155 MB of KV per layer, 24 distinct layer pools per step"},
+        "decode_tok_s": round(total_seqs / (ms * 1e-3), 1),
+        "hbm_frac_step": round(total_bytes / world / (ms * 1e-3) / 1e9 / peak, 4),
+        "roofline": {"kernel": "paged_decode_kernel<half>", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic_from_profiles(), "bytes_per_launch": dec_bytes,
+                     "avg_launch_ms": round(dec_ms, 5)},
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "ms_per_step": round(e2e_ms, 4), "api": "PagedKVCache.prepare_step + forward_layer"},
+        "gpu_launches": 2 * L * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        gbs, cores, sample, _, _ = cpu_sample(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": cores,
+                                "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

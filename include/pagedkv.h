@@ -1,0 +1,154 @@
+/*
+ * pagedkv.h -- C ABI of libpagedkv.so, the B200 (sm_100a) paged-KV-cache hot
+ * path for mini_engine (kjoshiDTX/llm-inference-scheduler).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as an opaque pointer so this header needs no CUDA include), is
+ * asynchronous with respect to the host, allocates nothing, and returns an
+ * int status: 0 = ok, < 0 = an argument error detected on the host before
+ * anything was launched (see PKV_ERR_*), > 0 = the cudaError_t reported by
+ * the launch.  Kernels never trap: an out-of-range block id, slot or context
+ * length found on the device is skipped or clamped and recorded with atomicOr
+ * into *err_flags (PKV_FLAG_*), when err_flags is not NULL.
+ *
+ * Layouts (the reference's, block_manager.py:10-13,37):
+ *   pool      [num_blocks][block_size][n_kv_heads][head_dim], one per layer
+ *   q, out    [n_tokens][n_q_heads][head_dim] with a row stride in elements
+ *   k, v new  [n_tokens][n_kv_heads][head_dim] with a row stride in elements
+ *   slot      block * block_size + offset (int64), -1 = padding, skipped
+ *   tables    [n_seqs][block_table_stride] int32 physical block ids
+ *
+ * Threading: calls may come from any host thread; the library keeps only a
+ * mutex-protected cache of TMA descriptors.  One call = one or two kernel
+ * launches on `stream`.
+ */
+#ifndef PAGEDKV_H
+#define PAGEDKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PKV_ABI_VERSION 1
+
+/* element types of q / k / v / pools / out */
+#define PKV_DTYPE_F32 0
+#define PKV_DTYPE_F16 1
+#define PKV_DTYPE_BF16 2
+
+/* host-side status codes */
+#define PKV_OK 0
+#define PKV_ERR_NULL_POINTER (-1)
+#define PKV_ERR_BAD_SHAPE (-2)
+#define PKV_ERR_BAD_DTYPE (-3)
+#define PKV_ERR_WORKSPACE_TOO_SMALL (-4)
+#define PKV_ERR_MISALIGNED (-5)
+#define PKV_ERR_UNSUPPORTED (-6)
+#define PKV_ERR_DRIVER (-7)
+
+/* device-side error flag bits (atomicOr into *err_flags) */
+#define PKV_FLAG_SLOT_OUT_OF_RANGE 1
+#define PKV_FLAG_BLOCK_OUT_OF_RANGE 2
+#define PKV_FLAG_CONTEXT_EXCEEDS_TABLE 4
+#define PKV_FLAG_PIPELINE_TIMEOUT 8
+#define PKV_FLAG_BAD_QUERY_LAYOUT 16
+
+/* decode-attention kernel choice (pkv_set_decode_impl) */
+#define PKV_DECODE_AUTO 0
+#define PKV_DECODE_GENERIC 1
+
+typedef void* pkv_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* ABI version of the loaded library (PKV_ABI_VERSION it was built with). */
+int pkv_abi_version(void);
+
+/* Static description of a status code or error-flag word; never NULL. */
+const char* pkv_status_string(int status);
+
+/*
+ * KV append.  Replaces the scatter loop of PagedKVCache.append_and_fetch
+ * (mini_engine/paged/block_manager.py:121-131): token t's K and V rows are
+ * written to pool row slot_mapping[t]; slot -1 is skipped (padding).  One
+ * launch per layer covers every sequence of the step.  Bit-exact copy.
+ * A slot >= num_blocks * block_size sets PKV_FLAG_SLOT_OUT_OF_RANGE and is
+ * skipped.
+ */
+int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride,
+                          int64_t v_row_stride, void* k_pool, void* v_pool,
+                          const int64_t* slot_mapping, int n_tokens, int num_blocks,
+                          int block_size, int n_kv_heads, int head_dim, int dtype,
+                          int* err_flags, pkv_stream_t stream);
+
+/*
+ * Copy-on-write / fork block copies.  Replaces BlockManager.copy_block's
+ * per-layer loop (mini_engine/paged/block_manager.py:65-71), batched: for each
+ * (src, dst) pair in block_pairs [n_pairs][2] and each of n_layers layers,
+ * the K and V block dst becomes a copy of block src.  Layer l's pool starts
+ * at k_pools + l * layer_stride_bytes (same for v_pools).  dst blocks must
+ * be distinct and must not appear as a src in the same call.  An id outside
+ * [0, num_blocks) sets PKV_FLAG_BLOCK_OUT_OF_RANGE and the pair is skipped.
+ */
+int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
+                    const int32_t* block_pairs, int n_pairs, int num_blocks,
+                    int64_t block_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
+ * Bytes of device workspace pkv_paged_decode_attention needs for n_seqs
+ * sequences (split-K partials and per-sequence arrival counters).
+ */
+size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim);
+
+/*
+ * Paged decode attention (one new query token per sequence).  Replaces the
+ * gather of PagedKVCache.append_and_fetch (block_manager.py:136-141) plus
+ * Qwen2Model._attention with num_new == 1 (mini_engine/model/qwen2.py:98-128):
+ *   out[s, h, :] = softmax_j(scale * q[s, h, :] . K_s[j, h / G, :]) V_s[j, h / G, :]
+ * over the context_lens[s] tokens of sequence s, read in place through
+ * block_tables[s] (G = n_q_heads / n_kv_heads).  The new token must already
+ * have been written (pkv_reshape_and_cache).  context_lens[s] == 0 gives a
+ * zero row.  `workspace` must be zero-filled before its first use; every
+ * launch leaves its counters at zero again (re-zero it after an error flag).
+ */
+int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
+                               int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                               int num_blocks, const int32_t* block_tables,
+                               int64_t block_table_stride, int max_blocks_per_seq,
+                               const int32_t* context_lens, int n_seqs, int n_q_heads,
+                               int n_kv_heads, int head_dim, int block_size, float scale,
+                               int dtype, void* workspace, size_t workspace_bytes,
+                               int* err_flags, pkv_stream_t stream);
+
+/*
+ * Paged chunked-prefill attention.  Replaces the per-sequence gather +
+ * Qwen2Model._attention with num_new > 1 (qwen2.py:98-128): sequence s owns
+ * query rows [query_start_loc[s], query_start_loc[s+1]) and its new token i
+ * attends to keys 0 .. num_prior[s] + i of the sequence (causal with the
+ * reference's num_prior offset; the chunk's own K/V must already be in the
+ * pool).  Shared radix-prefix blocks are read in place.  max_query_len bounds
+ * query_start_loc[s+1] - query_start_loc[s]; n_tokens = query_start_loc[n_seqs].
+ */
+int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q,
+                                int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                int num_blocks, const int32_t* block_tables,
+                                int64_t block_table_stride, int max_blocks_per_seq,
+                                const int32_t* query_start_loc, const int32_t* num_prior,
+                                int n_seqs, int n_tokens, int max_query_len, int n_q_heads,
+                                int n_kv_heads, int head_dim, int block_size, float scale,
+                                int dtype, int* err_flags, pkv_stream_t stream);
+
+/*
+ * Select the decode kernel for later calls in this process: PKV_DECODE_AUTO
+ * (the TMA/tensor-core kernel where the shape allows it) or
+ * PKV_DECODE_GENERIC (the portable CUDA-core kernel).  Used by tests that
+ * cross-check the two kernels.  No counterpart in the reference.
+ */
+int pkv_set_decode_impl(int impl);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDKV_H */

@@ -1,0 +1,279 @@
+// pkv_abi.cu -- the extern "C" entry points of libpagedkv.so (include/pagedkv.h).
+//
+// Each entry point validates its arguments on the host (returning a negative
+// PKV_ERR_* code before anything is launched), picks a kernel, and launches
+// it on the caller's stream.  Nothing here allocates device memory or
+// synchronises.  TMA descriptors for pool tensors are encoded through the
+// driver entry point cuTensorMapEncodeTiled and cached per pool pointer.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "pkv_common.cuh"
+#include "pkv_internal.h"
+
+namespace pkv {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+struct MapKey {
+  const void* ptr;
+  int num_blocks, block_size, n_kv_heads, head_dim, dtype;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && num_blocks == o.num_blocks && block_size == o.block_size &&
+           n_kv_heads == o.n_kv_heads && head_dim == o.head_dim && dtype == o.dtype;
+  }
+};
+struct MapHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = reinterpret_cast<size_t>(k.ptr);
+    h ^= (static_cast<size_t>(k.num_blocks) << 20) ^ (static_cast<size_t>(k.dtype) << 60) ^
+         (static_cast<size_t>(k.n_kv_heads) << 52) ^ (static_cast<size_t>(k.head_dim) << 44);
+    return h * 0x9E3779B97F4A7C15ull;
+  }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapHash> g_maps;
+constexpr size_t kMaxCachedMaps = 4096;
+
+int cached_pool_map(CUtensorMap* out, const void* pool, int num_blocks, int block_size,
+                    int n_kv_heads, int head_dim, int dtype) {
+  const MapKey key{pool, num_blocks, block_size, n_kv_heads, head_dim, dtype};
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return 0;
+  }
+  CUtensorMap m;
+  const int rc = encode_pool_tensormap(&m, pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+  if (rc != 0) return rc;
+  if (g_maps.size() >= kMaxCachedMaps) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return 0;
+}
+
+std::atomic<int> g_decode_impl{PKV_DECODE_AUTO};
+
+inline bool valid_dtype(int dt) { return dt == PKV_DTYPE_F32 || dt == PKV_DTYPE_F16 || dt == PKV_DTYPE_BF16; }
+inline int esize_of(int dt) { return dt == PKV_DTYPE_F32 ? 4 : 2; }
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? PKV_OK : static_cast<int>(e); }
+
+// shared shape checks of the two attention entry points
+int check_attn(const void* out, int64_t out_stride, const void* q, int64_t q_stride,
+               const void* k_pool, const void* v_pool, int num_blocks, const int32_t* tables,
+               int64_t bt_stride, int max_blocks, int n_q_heads, int n_kv_heads, int head_dim,
+               int block_size, int dtype) {
+  if (!out || !q || !k_pool || !v_pool || !tables) return PKV_ERR_NULL_POINTER;
+  if (!valid_dtype(dtype)) return PKV_ERR_BAD_DTYPE;
+  if (n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0) return PKV_ERR_BAD_SHAPE;
+  if (head_dim <= 0 || head_dim > 256 || block_size <= 0 || num_blocks <= 0 || max_blocks <= 0)
+    return PKV_ERR_BAD_SHAPE;
+  if (bt_stride < max_blocks) return PKV_ERR_BAD_SHAPE;
+  const int64_t row = static_cast<int64_t>(n_q_heads) * head_dim;
+  if (q_stride < row || out_stride < row) return PKV_ERR_BAD_SHAPE;
+  if (static_cast<int64_t>(max_blocks) * block_size > 0x7fffffff) return PKV_ERR_BAD_SHAPE;
+  if (static_cast<int64_t>(num_blocks) * block_size > 0x7fffffff) return PKV_ERR_BAD_SHAPE;
+  return PKV_OK;
+}
+
+}  // namespace
+
+int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, int block_size,
+                          int n_kv_heads, int head_dim, int dtype) {
+  auto enc = encoder();
+  if (enc == nullptr) return PKV_ERR_DRIVER;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(n_kv_heads),
+                              static_cast<cuuint64_t>(num_blocks) * block_size};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2,
+                                 static_cast<cuuint64_t>(n_kv_heads) * head_dim * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), 1u, static_cast<cuuint32_t>(block_size)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUresult r = enc(map, dt, 3, const_cast<void*>(pool), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : PKV_ERR_DRIVER;
+}
+
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" {
+
+int pkv_abi_version(void) { return PKV_ABI_VERSION; }
+
+const char* pkv_status_string(int status) {
+  switch (status) {
+    case PKV_OK: return "ok";
+    case PKV_ERR_NULL_POINTER: return "a required pointer argument is NULL";
+    case PKV_ERR_BAD_SHAPE: return "inconsistent or out-of-range shape argument";
+    case PKV_ERR_BAD_DTYPE: return "dtype must be PKV_DTYPE_F32, PKV_DTYPE_F16 or PKV_DTYPE_BF16";
+    case PKV_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than pkv_decode_workspace_bytes()";
+    case PKV_ERR_MISALIGNED: return "pointer or stride misaligned for this kernel";
+    case PKV_ERR_UNSUPPORTED: return "combination of arguments not supported";
+    case PKV_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or failed";
+    default: break;
+  }
+  if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
+  return "unknown pagedkv status";
+}
+
+int pkv_set_decode_impl(int impl) {
+  if (impl != PKV_DECODE_AUTO && impl != PKV_DECODE_GENERIC) return PKV_ERR_UNSUPPORTED;
+  g_decode_impl.store(impl);
+  return PKV_OK;
+}
+
+int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
+                          void* k_pool, void* v_pool, const int64_t* slot_mapping, int n_tokens,
+                          int num_blocks, int block_size, int n_kv_heads, int head_dim, int dtype,
+                          int* err_flags, pkv_stream_t stream) {
+  if (n_tokens < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_tokens == 0) return PKV_OK;
+  if (!k || !v || !k_pool || !v_pool || !slot_mapping) return PKV_ERR_NULL_POINTER;
+  if (!valid_dtype(dtype)) return PKV_ERR_BAD_DTYPE;
+  if (num_blocks <= 0 || block_size <= 0 || n_kv_heads <= 0 || head_dim <= 0) return PKV_ERR_BAD_SHAPE;
+  const int64_t row = static_cast<int64_t>(n_kv_heads) * head_dim;
+  if (k_row_stride < row || v_row_stride < row) return PKV_ERR_BAD_SHAPE;
+  return status_of(launch_reshape_and_cache(k, v, k_row_stride, v_row_stride, k_pool, v_pool,
+                                            slot_mapping, n_tokens, num_blocks, block_size,
+                                            n_kv_heads, head_dim, esize_of(dtype), err_flags,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
+                    const int32_t* block_pairs, int n_pairs, int num_blocks, int64_t block_bytes,
+                    int* err_flags, pkv_stream_t stream) {
+  if (n_pairs < 0 || n_layers < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_pairs == 0 || n_layers == 0) return PKV_OK;
+  if (!k_pools || !v_pools || !block_pairs) return PKV_ERR_NULL_POINTER;
+  if (num_blocks <= 0 || block_bytes <= 0) return PKV_ERR_BAD_SHAPE;
+  if (n_layers > 65535) return PKV_ERR_UNSUPPORTED;
+  if (n_layers > 1 && layer_stride_bytes < static_cast<int64_t>(num_blocks) * block_bytes)
+    return PKV_ERR_BAD_SHAPE;
+  return status_of(launch_copy_blocks(k_pools, v_pools, layer_stride_bytes, n_layers, block_pairs,
+                                      n_pairs, num_blocks, block_bytes, err_flags,
+                                      static_cast<cudaStream_t>(stream)));
+}
+
+size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
+  if (n_seqs < 0 || n_q_heads <= 0 || head_dim <= 0) return 0;
+  return decode_workspace_bytes(n_seqs, n_q_heads, head_dim);
+}
+
+int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                               const void* k_pool, const void* v_pool, int num_blocks,
+                               const int32_t* block_tables, int64_t block_table_stride,
+                               int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+                               int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                               float scale, int dtype, void* workspace, size_t workspace_bytes,
+                               int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!context_lens) return PKV_ERR_NULL_POINTER;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.context_lens = context_lens;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_seqs;
+  a.max_query_len = 1;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a)) {
+    if (!workspace) return PKV_ERR_NULL_POINTER;
+    if (workspace_bytes < decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
+      return PKV_ERR_WORKSPACE_TOO_SMALL;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return PKV_ERR_MISALIGNED;
+    CUtensorMap km, vm;
+    rc = cached_pool_map(&km, k_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+    if (rc != 0) return rc;
+    rc = cached_pool_map(&vm, v_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+    if (rc != 0) return rc;
+    return status_of(launch_decode_fast(a, &km, &vm, workspace, st));
+  }
+  return status_of(launch_generic_attention(a, st));
+}
+
+int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                const void* k_pool, const void* v_pool, int num_blocks,
+                                const int32_t* block_tables, int64_t block_table_stride,
+                                int max_blocks_per_seq, const int32_t* query_start_loc,
+                                const int32_t* num_prior, int n_seqs, int n_tokens, int max_query_len,
+                                int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                                float scale, int dtype, int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0 || n_tokens < 0 || max_query_len < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0 || n_tokens == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!query_start_loc || !num_prior) return PKV_ERR_NULL_POINTER;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.query_start_loc = query_start_loc;
+  a.num_prior = num_prior;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_tokens;
+  a.max_query_len = max_query_len;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  return status_of(launch_generic_attention(a, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

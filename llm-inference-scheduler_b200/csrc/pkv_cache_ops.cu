@@ -1,0 +1,162 @@
+// pkv_cache_ops.cu -- KV append (reshape_and_cache) and block copy (copy_blocks).
+//
+// Both are byte movers bound by HBM bandwidth: rows of n_kv_heads*head_dim
+// elements (256 B for the reference's 2 x 64 fp16) move with 16-byte vector
+// loads/stores, one warp per token (append) or one CTA per (pair, layer)
+// (copy).  Results are bit-exact copies.
+#include "pkv_common.cuh"
+#include "pkv_internal.h"
+
+namespace pkv {
+
+// Append: warp w handles token w.  Lanes cover the K row then the V row in
+// 16-byte vectors (row_vecs per row); for 256-byte rows that is exactly one
+// vector per lane.  Reference: PagedKVCache.append_and_fetch scatter,
+// mini_engine/paged/block_manager.py:121-131.
+__global__ void __launch_bounds__(256) reshape_and_cache_vec16(
+    const char* __restrict__ k, const char* __restrict__ v, int64_t k_stride_b,
+    int64_t v_stride_b, char* __restrict__ k_pool, char* __restrict__ v_pool,
+    const int64_t* __restrict__ slots, int n_tokens, int64_t n_slots, int row_bytes, int* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_tokens) return;
+  const int64_t slot = __ldg(slots + warp);
+  if (slot < 0) return;  // padding token
+  if (slot >= n_slots) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
+    return;
+  }
+  const int row_vecs = row_bytes >> 4;
+  for (int i = lane; i < 2 * row_vecs; i += 32) {
+    const bool is_v = i >= row_vecs;
+    const int vi = is_v ? i - row_vecs : i;
+    const char* src = (is_v ? v + warp * v_stride_b : k + warp * k_stride_b) + vi * 16;
+    char* dst = (is_v ? v_pool : k_pool) + slot * row_bytes + vi * 16;
+    const int4 val = __ldg(reinterpret_cast<const int4*>(src));
+    __stcs(reinterpret_cast<int4*>(dst), val);
+  }
+}
+
+// Unaligned fallback: element-sized copies (esize 2 or 4 bytes).
+template <typename E>
+__global__ void __launch_bounds__(256) reshape_and_cache_elem(
+    const E* __restrict__ k, const E* __restrict__ v, int64_t k_stride, int64_t v_stride,
+    E* __restrict__ k_pool, E* __restrict__ v_pool, const int64_t* __restrict__ slots,
+    int n_tokens, int64_t n_slots, int row_elems, int* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_tokens) return;
+  const int64_t slot = slots[warp];
+  if (slot < 0) return;
+  if (slot >= n_slots) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
+    return;
+  }
+  for (int i = lane; i < row_elems; i += 32) {
+    k_pool[slot * row_elems + i] = k[warp * k_stride + i];
+    v_pool[slot * row_elems + i] = v[warp * v_stride + i];
+  }
+}
+
+cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_stride,
+                                     int64_t v_stride, void* k_pool, void* v_pool,
+                                     const int64_t* slots, int n_tokens, int num_blocks,
+                                     int block_size, int n_kv_heads, int head_dim, int esize,
+                                     int* err, cudaStream_t stream) {
+  if (n_tokens == 0) return cudaSuccess;
+  const int row_elems = n_kv_heads * head_dim;
+  const int row_bytes = row_elems * esize;
+  const int64_t n_slots = static_cast<int64_t>(num_blocks) * block_size;
+  const int threads = 256;
+  const int grid = (n_tokens + 7) / 8;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = (row_bytes % 16 == 0) && ((k_stride * esize) % 16 == 0) &&
+                   ((v_stride * esize) % 16 == 0) && al16(k) && al16(v) && al16(k_pool) &&
+                   al16(v_pool);
+  if (vec) {
+    reshape_and_cache_vec16<<<grid, threads, 0, stream>>>(
+        static_cast<const char*>(k), static_cast<const char*>(v), k_stride * esize,
+        v_stride * esize, static_cast<char*>(k_pool), static_cast<char*>(v_pool), slots,
+        n_tokens, n_slots, row_bytes, err);
+  } else if (esize == 4) {
+    reshape_and_cache_elem<uint32_t><<<grid, threads, 0, stream>>>(
+        static_cast<const uint32_t*>(k), static_cast<const uint32_t*>(v), k_stride, v_stride,
+        static_cast<uint32_t*>(k_pool), static_cast<uint32_t*>(v_pool), slots, n_tokens, n_slots,
+        row_elems, err);
+  } else {
+    reshape_and_cache_elem<uint16_t><<<grid, threads, 0, stream>>>(
+        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), k_stride, v_stride,
+        static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool), slots, n_tokens, n_slots,
+        row_elems, err);
+  }
+  return cudaGetLastError();
+}
+
+// Copy: CTA (pair p, layer l) copies K block then V block of that layer.
+// Reference: BlockManager.copy_block, mini_engine/paged/block_manager.py:65-71.
+__global__ void __launch_bounds__(256) copy_blocks_vec16(char* __restrict__ k_pools,
+                                                         char* __restrict__ v_pools,
+                                                         int64_t layer_stride,
+                                                         const int32_t* __restrict__ pairs,
+                                                         int num_blocks, int64_t block_bytes,
+                                                         int* err) {
+  const int p = blockIdx.x;
+  const int layer = blockIdx.y;
+  const int src = __ldg(pairs + 2 * p), dst = __ldg(pairs + 2 * p + 1);
+  if (src < 0 || dst < 0 || src >= num_blocks || dst >= num_blocks) {
+    if (threadIdx.x == 0 && layer == 0) raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t nvec = block_bytes >> 4;
+  const int64_t base = layer * layer_stride;
+  const int4* ks = reinterpret_cast<const int4*>(k_pools + base + src * block_bytes);
+  const int4* vs = reinterpret_cast<const int4*>(v_pools + base + src * block_bytes);
+  int4* kd = reinterpret_cast<int4*>(k_pools + base + dst * block_bytes);
+  int4* vd = reinterpret_cast<int4*>(v_pools + base + dst * block_bytes);
+  for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) {
+    const int4 a = ks[i];
+    const int4 b = vs[i];
+    kd[i] = a;
+    vd[i] = b;
+  }
+}
+
+__global__ void __launch_bounds__(256) copy_blocks_bytes(char* __restrict__ k_pools,
+                                                         char* __restrict__ v_pools,
+                                                         int64_t layer_stride,
+                                                         const int32_t* __restrict__ pairs,
+                                                         int num_blocks, int64_t block_bytes,
+                                                         int* err) {
+  const int p = blockIdx.x;
+  const int layer = blockIdx.y;
+  const int src = pairs[2 * p], dst = pairs[2 * p + 1];
+  if (src < 0 || dst < 0 || src >= num_blocks || dst >= num_blocks) {
+    if (threadIdx.x == 0 && layer == 0) raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t base = layer * layer_stride;
+  for (int64_t i = threadIdx.x; i < block_bytes; i += blockDim.x) {
+    k_pools[base + dst * block_bytes + i] = k_pools[base + src * block_bytes + i];
+    v_pools[base + dst * block_bytes + i] = v_pools[base + src * block_bytes + i];
+  }
+}
+
+cudaError_t launch_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride, int n_layers,
+                               const int32_t* pairs, int n_pairs, int num_blocks,
+                               int64_t block_bytes, int* err, cudaStream_t stream) {
+  if (n_pairs == 0 || n_layers == 0) return cudaSuccess;
+  dim3 grid(n_pairs, n_layers);
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (block_bytes % 16 == 0 && layer_stride % 16 == 0 && al16(k_pools) && al16(v_pools)) {
+    copy_blocks_vec16<<<grid, 256, 0, stream>>>(static_cast<char*>(k_pools),
+                                                static_cast<char*>(v_pools), layer_stride, pairs,
+                                                num_blocks, block_bytes, err);
+  } else {
+    copy_blocks_bytes<<<grid, 256, 0, stream>>>(static_cast<char*>(k_pools),
+                                                static_cast<char*>(v_pools), layer_stride, pairs,
+                                                num_blocks, block_bytes, err);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace pkv

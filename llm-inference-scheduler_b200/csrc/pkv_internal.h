@@ -1,0 +1,68 @@
+// pkv_internal.h -- host-side launchers shared between the kernel files and
+// the C ABI (pkv_abi.cu).  Argument validation happens in pkv_abi.cu; these
+// functions assume valid shapes and only launch.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pkv {
+
+struct AttnArgs {
+  void* out;
+  int64_t out_stride;  // elements between token rows of out
+  const void* q;
+  int64_t q_stride;    // elements between token rows of q
+  const void* k_pool;
+  const void* v_pool;
+  int num_blocks;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int max_blocks;
+  // decode: context_lens != nullptr, one query row per sequence
+  const int32_t* context_lens;
+  // prefill: query_start_loc / num_prior
+  const int32_t* query_start_loc;
+  const int32_t* num_prior;
+  int n_seqs;
+  int n_tokens;
+  int max_query_len;
+  int n_q_heads;
+  int n_kv_heads;
+  int head_dim;
+  int block_size;
+  float scale;
+  int dtype;
+  int* err;
+};
+
+cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_stride,
+                                     int64_t v_stride, void* k_pool, void* v_pool,
+                                     const int64_t* slots, int n_tokens, int num_blocks,
+                                     int block_size, int n_kv_heads, int head_dim, int esize,
+                                     int* err, cudaStream_t stream);
+
+cudaError_t launch_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride, int n_layers,
+                               const int32_t* pairs, int n_pairs, int num_blocks,
+                               int64_t block_bytes, int* err, cudaStream_t stream);
+
+// CUDA-core attention for any dtype / head_dim <= 256 / block_size; decode
+// (context_lens set) or chunked prefill (query_start_loc + num_prior set).
+cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
+
+// Decode fast path: TMA + mbarrier pipeline, tensor-core math, stream-K
+// split with fused combine.  Requires fp16/bf16, head_dim 64, block 16,
+// n_kv_heads in {1,2,4}, q heads per kv head <= 8.
+bool decode_fast_supported(const AttnArgs& a);
+size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim);
+cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
+                               void* workspace, cudaStream_t stream);
+
+// TMA descriptor for a pool [num_blocks*block_size][n_kv_heads][head_dim]
+// with one (head_dim x 1 head x block_size tokens) box, 128-byte swizzle.
+// Returns 0 or a CUresult.
+int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, int block_size,
+                          int n_kv_heads, int head_dim, int dtype);
+
+}  // namespace pkv

@@ -1,0 +1,229 @@
+"""Torch-facing wrappers of the paged-KV kernels (one C-ABI call each).
+
+All tensors must live on a CUDA device: there is no CPU implementation.  The
+kernels run asynchronously on the current torch stream of that device.
+Device-side bounds problems (bad slot, block id, context length) never fault:
+they are recorded in an optional int32 `err` tensor of one element (see
+pagedkv._lib.FLAG_*), which callers check with `check_flags` after a sync.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"unsupported KV dtype {dt}; use float32, float16 or bfloat16") from None
+
+
+def _cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"pagedkv: `{name}` must be a CUDA tensor (no CPU path exists)")
+    return t
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _row_stride(t: torch.Tensor, name: str) -> int:
+    """Token-row stride of a [T, H, D] tensor whose inner [H, D] is dense."""
+    if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError(f"pagedkv: `{name}` must be [tokens, heads, head_dim] with dense heads")
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1] * t.shape[2]
+
+
+def new_error_flags(device) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_flags(err: torch.Tensor, where: str = "pagedkv") -> None:
+    """Raise if a kernel recorded a device-side error (synchronises)."""
+    v = int(err.item())
+    if v:
+        raise _lib.PagedKVError(v, where + " (device error flags)")
+
+
+def _reshape_and_cache_args(k, v, k_pool, v_pool, slot_mapping, err):
+    for t, n in ((k, "k"), (v, "v"), (k_pool, "k_pool"), (v_pool, "v_pool"), (slot_mapping, "slot_mapping")):
+        _cuda(t, n)
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise TypeError("pagedkv: slot_mapping must be a contiguous int64 tensor")
+    if k_pool.dtype != k.dtype or v_pool.dtype != v.dtype or k.dtype != v.dtype:
+        raise TypeError("pagedkv: k, v and the pools must share one dtype")
+    if not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+        raise ValueError("pagedkv: pools must be contiguous")
+    nb, bs, hkv, d = k_pool.shape
+    T = slot_mapping.shape[0]
+    if k.shape[0] != T or v.shape[0] != T or tuple(k.shape[1:]) != (hkv, d) or tuple(v.shape[1:]) != (hkv, d):
+        raise ValueError("pagedkv: k/v shape does not match the pool and slot_mapping")
+    return (k.data_ptr(), v.data_ptr(), _row_stride(k, "k"), _row_stride(v, "v"), k_pool.data_ptr(),
+            v_pool.data_ptr(), slot_mapping.data_ptr(), T, nb, bs, hkv, d, dtype_code(k.dtype),
+            _ptr(err), _stream(k))
+
+
+def reshape_and_cache(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                      slot_mapping: torch.Tensor, err: torch.Tensor | None = None) -> None:
+    """k_pool.view(-1, Hkv, D)[slot_mapping[t]] = k[t] (same for v); slot -1 skipped.
+
+    k, v: [T, Hkv, D]; pools: [num_blocks, block_size, Hkv, D] (one layer);
+    slot_mapping: int64 [T].  Reference: block_manager.py:121-131.
+    """
+    args = _reshape_and_cache_args(k, v, k_pool, v_pool, slot_mapping, err)
+    if args[7] == 0:
+        return
+    _lib.check(_lib.load().pkv_reshape_and_cache(*args), "pkv_reshape_and_cache")
+
+
+def copy_blocks(k_cache: torch.Tensor, v_cache: torch.Tensor, pairs: torch.Tensor,
+                err: torch.Tensor | None = None) -> None:
+    """For every (src, dst) row of `pairs` (int32 [N, 2]) and every layer:
+    k_cache[l, dst] = k_cache[l, src] (same for v).  Reference: block_manager.py:65-71.
+
+    k_cache, v_cache: [L, num_blocks, block_size, Hkv, D] contiguous.
+    """
+    _cuda(k_cache, "k_cache"), _cuda(v_cache, "v_cache"), _cuda(pairs, "pairs")
+    if pairs.dtype != torch.int32 or not pairs.is_contiguous() or pairs.dim() != 2 or pairs.shape[1] != 2:
+        raise TypeError("pagedkv: pairs must be a contiguous int32 [N, 2] tensor")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()) or k_cache.shape != v_cache.shape:
+        raise ValueError("pagedkv: k_cache / v_cache must be contiguous and equally shaped")
+    L, nb = k_cache.shape[:2]
+    block_bytes = k_cache[0, 0].numel() * k_cache.element_size()
+    if pairs.shape[0] == 0:
+        return
+    rc = _lib.load().pkv_copy_blocks(
+        k_cache.data_ptr(), v_cache.data_ptr(), nb * block_bytes, L, pairs.data_ptr(),
+        pairs.shape[0], nb, block_bytes, _ptr(err), _stream(k_cache))
+    _lib.check(rc, "pkv_copy_blocks")
+
+
+def decode_workspace_bytes(n_seqs: int, n_q_heads: int, head_dim: int) -> int:
+    return int(_lib.load().pkv_decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
+
+
+def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device) -> torch.Tensor:
+    """Zero-filled workspace; the decode kernel keeps its counters at zero."""
+    return torch.zeros(decode_workspace_bytes(n_seqs, n_q_heads, head_dim), dtype=torch.uint8,
+                       device=device)
+
+
+def _check_tables(block_tables: torch.Tensor) -> None:
+    _cuda(block_tables, "block_tables")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise TypeError("pagedkv: block_tables must be int32 [n_seqs, max_blocks] with unit inner stride")
+
+
+def _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err):
+    for t, n in ((q, "q"), (k_pool, "k_pool"), (v_pool, "v_pool"), (context_lens, "context_lens")):
+        _cuda(t, n)
+    _check_tables(block_tables)
+    if context_lens.dtype != torch.int32 or not context_lens.is_contiguous():
+        raise TypeError("pagedkv: context_lens must be a contiguous int32 tensor")
+    if q.dtype != k_pool.dtype or k_pool.dtype != v_pool.dtype:
+        raise TypeError("pagedkv: q and the pools must share one dtype")
+    nb, bs, hkv, d = k_pool.shape
+    B, hq, dq = q.shape
+    if dq != d or block_tables.shape[0] < B or context_lens.shape[0] < B:
+        raise ValueError("pagedkv: q / block_tables / context_lens shapes disagree")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if workspace is None:
+        workspace = new_decode_workspace(B, hq, d, q.device)
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), nb, block_tables.data_ptr(), block_tables.stride(0),
+            block_tables.shape[1], context_lens.data_ptr(), B, hq, hkv, d, bs, float(scale),
+            dtype_code(q.dtype), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+            _ptr(err), _stream(q))
+    return args, out
+
+
+def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                           block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
+                           workspace: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                           err: torch.Tensor | None = None) -> torch.Tensor:
+    """out[s] = softmax(scale * q[s] K_s^T) V_s over context_lens[s] tokens of
+    sequence s, read in place through block_tables[s] (GQA: q head h uses kv
+    head h // (Hq // Hkv)).  q: [B, Hq, D]; returns [B, Hq, D].
+    Reference: block_manager.py:136-141 + qwen2.py:98-128 (num_new == 1).
+    """
+    args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err)
+    _lib.check(_lib.load().pkv_paged_decode_attention(*args), "pkv_paged_decode_attention")
+    return out
+
+
+class BoundLaunch:
+    """A validated launch with its C-ABI arguments fixed (pointers, sizes and
+    the stream that was current when it was bound).  Calling it re-issues the
+    kernel with no Python-side checks: for loops that replay one step, where
+    per-call validation would dominate the launch cost.  The tensors it was
+    bound to must stay alive and unchanged in shape."""
+
+    def __init__(self, fn, args, name, keep):
+        self._fn, self._args, self._name, self._keep = fn, args, name, keep
+
+    def __call__(self) -> None:
+        rc = self._fn(*self._args)
+        if rc:
+            _lib.check(rc, self._name)
+
+
+def bind_reshape_and_cache(k, v, k_pool, v_pool, slot_mapping, err=None) -> BoundLaunch:
+    args = _reshape_and_cache_args(k, v, k_pool, v_pool, slot_mapping, err)
+    return BoundLaunch(_lib.load().pkv_reshape_and_cache, args, "pkv_reshape_and_cache",
+                       (k, v, k_pool, v_pool, slot_mapping, err))
+
+
+def bind_paged_decode_attention(q, k_pool, v_pool, block_tables, context_lens, scale, workspace,
+                                out, err=None) -> BoundLaunch:
+    args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err)
+    return BoundLaunch(_lib.load().pkv_paged_decode_attention, args, "pkv_paged_decode_attention",
+                       (q, k_pool, v_pool, block_tables, context_lens, workspace, out, err))
+
+
+def paged_prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                            block_tables: torch.Tensor, query_start_loc: torch.Tensor,
+                            num_prior: torch.Tensor, max_query_len: int, scale: float,
+                            out: torch.Tensor | None = None,
+                            err: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked prefill: sequence s owns q rows [qsl[s], qsl[s+1]); its new token
+    i attends to keys 0 .. num_prior[s] + i through block_tables[s].
+    Reference: qwen2.py:98-128 causal mask with the num_prior offset.
+    """
+    for t, n in ((q, "q"), (k_pool, "k_pool"), (v_pool, "v_pool"),
+                 (query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
+        _cuda(t, n)
+    _check_tables(block_tables)
+    for t, n in ((query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise TypeError(f"pagedkv: {n} must be a contiguous int32 tensor")
+    if q.dtype != k_pool.dtype or k_pool.dtype != v_pool.dtype:
+        raise TypeError("pagedkv: q and the pools must share one dtype")
+    nb, bs, hkv, d = k_pool.shape
+    T, hq, dq = q.shape
+    B = num_prior.shape[0]
+    if dq != d or query_start_loc.shape[0] != B + 1 or block_tables.shape[0] < B:
+        raise ValueError("pagedkv: q / query_start_loc / num_prior / block_tables shapes disagree")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    rc = _lib.load().pkv_paged_prefill_attention(
+        out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
+        v_pool.data_ptr(), nb, block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+        query_start_loc.data_ptr(), num_prior.data_ptr(), B, T, int(max_query_len), hq, hkv, d, bs,
+        float(scale), dtype_code(q.dtype), _ptr(err), _stream(q))
+    _lib.check(rc, "pkv_paged_prefill_attention")
+    return out
+
+
+def set_decode_impl(impl: int) -> None:
+    _lib.check(_lib.load().pkv_set_decode_impl(int(impl)), "pkv_set_decode_impl")

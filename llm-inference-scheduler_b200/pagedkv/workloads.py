@@ -1,0 +1,106 @@
+"""Synthetic workloads of the BASELINE configurations and their per-GPU
+sharding (host-side helpers used by bench.py and the multi-rank tests).
+
+Work is partitioned by sequence: every GPU owns an independent block pool and
+a disjoint set of sequences, so no collective touches the data path.  The
+only cross-rank operations are a barrier and a max-reduction of timings.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+BLOCK_SIZE = 16
+N_Q_HEADS, N_KV_HEADS, HEAD_DIM, N_LAYERS = 14, 2, 64, 24  # Qwen2.5-0.5B (config.py:13-23)
+
+
+def config3_contexts(n_seqs: int, seed: int = 3, median: float = 1024.0, sigma: float = 0.5,
+                     lo: int = 16, hi: int = 8192) -> np.ndarray:
+    """Config 3 context lengths: clip(round(exp(N(ln median, sigma^2))), lo, hi).
+
+    The first draw of the seeded PCG64 stream, so the first 256 values are
+    the same for any n_seqs >= 256.
+    """
+    rng = np.random.default_rng(seed)
+    z = rng.standard_normal(n_seqs)
+    return np.clip(np.round(np.exp(np.log(median) + sigma * z)), lo, hi).astype(np.int64)
+
+
+def deal(n_total: int, rank: int, world: int) -> np.ndarray:
+    """Round-robin dealing of sequence indices to ranks (sequence -> GPU)."""
+    return np.arange(rank, n_total, world, dtype=np.int64)
+
+
+def shard_contexts(per_gpu_batch: int, rank: int, world: int, strong: bool = False,
+                   seed: int = 3) -> np.ndarray:
+    """Contexts of this rank's sequences.
+
+    weak (default): the job is per_gpu_batch * world sequences, each GPU gets
+    per_gpu_batch of them (per-GPU work fixed as N grows; N=1 is config 3).
+    strong: the job is per_gpu_batch sequences dealt over the world.
+    """
+    total = per_gpu_batch if strong else per_gpu_batch * world
+    ctx = config3_contexts(total, seed=seed)
+    return ctx[deal(total, rank, world)]
+
+
+def decode_bytes(ctx: np.ndarray, n_q_heads: int = N_Q_HEADS, n_kv_heads: int = N_KV_HEADS,
+                 head_dim: int = HEAD_DIM, esize: int = 2, block_size: int = BLOCK_SIZE) -> int:
+    """Algorithmic bytes of one paged-decode launch: every context token's K
+    and V rows once, q read + out written once, the used block-table entries
+    and the context lengths.  Split-K partials are not counted."""
+    ctx = np.asarray(ctx, dtype=np.int64)
+    kv = int(ctx.sum()) * n_kv_heads * head_dim * 2 * esize
+    qo = len(ctx) * n_q_heads * head_dim * esize * 2
+    tables = int(((ctx + block_size - 1) // block_size).sum()) * 4
+    return kv + qo + tables + len(ctx) * 4
+
+
+def append_bytes(n_tokens: int, n_kv_heads: int = N_KV_HEADS, head_dim: int = HEAD_DIM,
+                 esize: int = 2) -> int:
+    """Algorithmic bytes of one reshape_and_cache launch: K and V rows read and
+    written once, plus the int64 slot of each token."""
+    return n_tokens * (n_kv_heads * head_dim * esize * 2 * 2 + 8)
+
+
+def make_tables(ctx: np.ndarray, num_blocks: int, seed: int, block_size: int = BLOCK_SIZE):
+    """Scattered, disjoint block tables: consecutive slices of a seeded
+    permutation of the pool (config 3: "block tables scattered randomly")."""
+    rng = np.random.default_rng(seed)
+    nblk = (np.asarray(ctx) + block_size - 1) // block_size
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    width = int(nblk.max()) if len(nblk) else 1
+    tab = np.zeros((len(ctx), max(1, width)), dtype=np.int32)
+    o = 0
+    for i, n in enumerate(nblk):
+        tab[i, :n] = perm[o:o + n]
+        o += n
+    return tab
+
+
+def max_over_ranks(value: float, group=None) -> float:
+    """Max of a float over all ranks of the default process group (identity
+    when torch.distributed is not initialised)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return float(value)
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, group=None) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return float(value)
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return float(t.item())

@@ -1,0 +1,131 @@
+"""The C ABI surface of libpagedkv.so, checked without a GPU.
+
+* the library loads and exports every function include/pagedkv.h declares;
+* host-side argument validation answers with the documented negative codes
+  before anything is launched (so these calls never reach the device);
+* constants in the header agree with the Python binding.
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from pagedkv import _lib
+
+HEADER = os.path.join(ROOT, "include", "pagedkv.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    return re.findall(r"^\s*(?:int|size_t|const char\s*\*)\s+(pkv_\w+)\s*\(", src, re.M)
+
+
+def header_defines():
+    src = open(HEADER).read()
+    return {k: int(v) for k, v in re.findall(r"#define\s+(PKV_\w+)\s+\(?(-?\d+)\)?", src)}
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    names = header_functions()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in pagedkv.h but not exported"
+    assert sorted(names) == sorted(_lib.SIGNATURES), "binding and header disagree"
+
+
+def test_header_constants_match_binding():
+    d = header_defines()
+    assert d["PKV_ABI_VERSION"] == _lib.load().pkv_abi_version()
+    for name in ("F32", "F16", "BF16"):
+        assert d[f"PKV_DTYPE_{name}"] == getattr(_lib, name)
+    for name in ("NULL_POINTER", "BAD_SHAPE", "BAD_DTYPE", "WORKSPACE_TOO_SMALL", "MISALIGNED",
+                 "UNSUPPORTED", "DRIVER"):
+        assert d[f"PKV_ERR_{name}"] == getattr(_lib, f"ERR_{name}")
+    for name in ("SLOT_OUT_OF_RANGE", "BLOCK_OUT_OF_RANGE", "CONTEXT_EXCEEDS_TABLE",
+                 "PIPELINE_TIMEOUT", "BAD_QUERY_LAYOUT"):
+        assert d[f"PKV_FLAG_{name}"] == getattr(_lib, f"FLAG_{name}")
+
+
+def test_status_strings():
+    for code in (0, -1, -2, -3, -4, -5, -6, -7):
+        s = _lib.status_string(code)
+        assert s and "unknown" not in s
+    assert "unknown" in _lib.status_string(-99)
+
+
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+
+
+def test_reshape_and_cache_validation():
+    L = _lib.load()
+    f = L.pkv_reshape_and_cache
+    assert f(None, None, 128, 128, None, None, None, 0, 8, 16, 2, 64, 1, None, None) == 0  # no tokens
+    assert f(None, FAKE, 128, 128, FAKE, FAKE, FAKE, 4, 8, 16, 2, 64, 1, None, None) == _lib.ERR_NULL_POINTER
+    assert f(FAKE, FAKE, 128, 128, FAKE, FAKE, FAKE, 4, 8, 16, 2, 64, 7, None, None) == _lib.ERR_BAD_DTYPE
+    assert f(FAKE, FAKE, 64, 128, FAKE, FAKE, FAKE, 4, 8, 16, 2, 64, 1, None, None) == _lib.ERR_BAD_SHAPE
+    assert f(FAKE, FAKE, 128, 128, FAKE, FAKE, FAKE, -1, 8, 16, 2, 64, 1, None, None) == _lib.ERR_BAD_SHAPE
+
+
+def test_copy_blocks_validation():
+    L = _lib.load()
+    f = L.pkv_copy_blocks
+    assert f(None, None, 0, 24, None, 0, 8, 4096, None, None) == 0
+    assert f(FAKE, None, 8 * 4096, 24, FAKE, 3, 8, 4096, None, None) == _lib.ERR_NULL_POINTER
+    assert f(FAKE, FAKE, 100, 24, FAKE, 3, 8, 4096, None, None) == _lib.ERR_BAD_SHAPE
+    assert f(FAKE, FAKE, 8 * 4096, 70000, FAKE, 3, 8, 4096, None, None) == _lib.ERR_UNSUPPORTED
+
+
+def _decode(**kw):
+    a = dict(out=FAKE, out_stride=896, q=FAKE, q_stride=896, k_pool=FAKE, v_pool=FAKE,
+             num_blocks=64, tables=FAKE, bt_stride=8, max_blocks=8, ctx=FAKE, n_seqs=4, hq=14,
+             hkv=2, d=64, bs=16, scale=0.125, dtype=1, ws=FAKE, ws_bytes=1 << 30, err=None,
+             stream=None)
+    a.update(kw)
+    return _lib.load().pkv_paged_decode_attention(*a.values())
+
+
+def test_decode_validation():
+    assert _decode(n_seqs=0) == 0
+    assert _decode(q=None) == _lib.ERR_NULL_POINTER
+    assert _decode(ctx=None) == _lib.ERR_NULL_POINTER
+    assert _decode(dtype=3) == _lib.ERR_BAD_DTYPE
+    assert _decode(hkv=3) == _lib.ERR_BAD_SHAPE          # 14 % 3 != 0
+    assert _decode(d=512, q_stride=14 * 512, out_stride=14 * 512) == _lib.ERR_BAD_SHAPE
+    assert _decode(bt_stride=4) == _lib.ERR_BAD_SHAPE     # stride < max_blocks
+    assert _decode(q_stride=100) == _lib.ERR_BAD_SHAPE
+    assert _decode(ws_bytes=16) == _lib.ERR_WORKSPACE_TOO_SMALL
+    assert _decode(ws=None) == _lib.ERR_NULL_POINTER
+    assert _decode(ws=ctypes.c_void_p(0x1010)) == _lib.ERR_MISALIGNED
+
+
+def test_prefill_validation():
+    f = _lib.load().pkv_paged_prefill_attention
+    args = [FAKE, 896, FAKE, 896, FAKE, FAKE, 64, FAKE, 8, 8, FAKE, FAKE, 2, 10, 8, 14, 2, 64, 16,
+            0.125, 1, None, None]
+    bad = list(args)
+    bad[10] = None  # query_start_loc
+    assert f(*bad) == _lib.ERR_NULL_POINTER
+    bad = list(args)
+    bad[13] = -1  # n_tokens
+    assert f(*bad) == _lib.ERR_BAD_SHAPE
+    bad = list(args)
+    bad[13] = 0
+    assert f(*bad) == 0
+
+
+def test_workspace_bytes():
+    L = _lib.load()
+    a = L.pkv_decode_workspace_bytes(256, 14, 64)
+    b = L.pkv_decode_workspace_bytes(512, 14, 64)
+    assert a > 0 and b >= a and a % 256 == 0
+    assert L.pkv_decode_workspace_bytes(-1, 14, 64) == 0
+
+
+def test_set_decode_impl_validation():
+    L = _lib.load()
+    assert L.pkv_set_decode_impl(5) == _lib.ERR_UNSUPPORTED
+    assert L.pkv_set_decode_impl(_lib.DECODE_AUTO) == 0

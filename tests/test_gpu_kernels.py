@@ -1,0 +1,376 @@
+"""Parity of the CUDA kernels (through the C ABI) with the CPU oracle and the
+reference's golden vectors.  Marked gpu: run with `pytest -m gpu` on a B200.
+
+Bars (written here, as the north star states them):
+* append / copy: bit-exact (pool SHA-256 equal to the reference's);
+* attention: max |cuda - oracle| <= 1e-5 (fp32), 2e-3 (fp16), 1.6e-2 (bf16),
+  and the same bound against the reference's golden outputs.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from conftest import GOLDEN, PRODUCT_ATOL, golden, max_abs_diff
+from pagedkv import BlockManager, PagedKVCache, _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+DTS = ("f32", "f16", "bf16")
+
+
+def dev(a: np.ndarray, dt: str | None = None) -> torch.Tensor:
+    a = np.ascontiguousarray(a)
+    if dt == "bf16":
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+    return torch.from_numpy(a).cuda()
+
+
+def host(t: torch.Tensor, dt: str) -> np.ndarray:
+    t = t.contiguous().cpu()
+    if dt == "bf16":
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+@pytest.fixture(params=["auto", "generic"])
+def decode_impl(request):
+    ops.set_decode_impl(_lib.DECODE_AUTO if request.param == "auto" else _lib.DECODE_GENERIC)
+    yield request.param
+    ops.set_decode_impl(_lib.DECODE_AUTO)
+
+
+def run_decode_gpu(c, err=None, scale=0.125):
+    """Append the new token (reshape_and_cache) then decode-attend."""
+    dt = c["dt"]
+    kp, vp = dev(c["k_pool"], dt), dev(c["v_pool"], dt)
+    slots = torch.from_numpy(C.decode_slots(c)).cuda()
+    err = ops.new_error_flags("cuda") if err is None else err
+    ops.reshape_and_cache(dev(c["k_new"], dt), dev(c["v_new"], dt), kp, vp, slots, err)
+    tabs = dev(C.pad_tables(c["tables"]))
+    ctx = dev(c["ctx"].astype(np.int32))
+    out = ops.paged_decode_attention(dev(c["q"], dt), kp, vp, tabs, ctx, scale, err=err)
+    torch.cuda.synchronize()
+    return host(out, dt), kp, vp, int(err.item())
+
+
+def run_prefill_gpu(c, scale=0.125):
+    dt = c["dt"]
+    kp, vp = dev(c["k_pool"], dt), dev(c["v_pool"], dt)
+    err = ops.new_error_flags("cuda")
+    ops.reshape_and_cache(dev(c["k_new"], dt), dev(c["v_new"], dt), kp, vp,
+                          torch.from_numpy(C.prefill_slots(c)).cuda(), err)
+    out = ops.paged_prefill_attention(dev(c["q"], dt), kp, vp, dev(C.pad_tables(c["tables"])),
+                                      dev(c["qsl"]), dev(c["prior"].astype(np.int32)),
+                                      int(c["chunk"].max()), scale, err=err)
+    torch.cuda.synchronize()
+    return host(out, dt), int(err.item())
+
+
+# ---------------------------------------------------------------- append / copy
+
+def test_append_and_cow_config2_bit_exact():
+    """Config 2 through the product path: reshape_and_cache per layer, then the
+    BlockManager's batched copy_blocks; pool digests equal the reference's."""
+    c = C.make_append_cow_case()
+    with open(f"{GOLDEN}/append_cow_c2_f16.json") as f:
+        g = json.load(f)
+    L, dt = c["n_layers"], "f16"
+    m = BlockManager(c["num_blocks"], C.BS, L, C.HKV, C.D, device="cuda", dtype=torch.float16)
+    m.k_cache.copy_(dev(c["k_pools"], dt))
+    m.v_cache.copy_(dev(c["v_pools"], dt))
+    m.free_list = list(c["free_list"])
+    kv = PagedKVCache(m)
+    n = len(c["ctx"])
+    for s in range(n):
+        ctx = int(c["ctx"][s])
+        kv.add_sequence(s, [m.allocate() for _ in range((ctx + 15) // 16)], ctx - 1)
+    meta = kv.prepare_step([(s, 1) for s in range(n)])
+    for layer in range(L):
+        ops.reshape_and_cache(dev(c["k_new"][layer], dt), dev(c["v_new"][layer], dt),
+                              m.k_pool[layer], m.v_pool[layer], meta.slot_mapping, m.err)
+    torch.cuda.synchronize()
+    assert C.digest(*host(m.k_cache, dt), *host(m.v_cache, dt)) == g["pools_after_append_sha256"]
+    for s in range(n):
+        kv._len[s] = int(c["ctx"][s])
+    for i, s in enumerate(c["forked"]):
+        s = int(s)
+        for b in kv.block_tables[s]:
+            m.incref(b)
+        kv.add_sequence(n + i, list(kv.block_tables[s]), kv.seq_len(s))
+        kv.ensure_writable_tail(n + i)
+    assert [list(p) for p in m.pending_copies] == g["pairs"]
+    m.flush_copies()
+    torch.cuda.synchronize()
+    assert m.copies_launched == 1
+    assert C.digest(*host(m.k_cache, dt), *host(m.v_cache, dt)) == g["pools_after_cow_sha256"]
+    m.check_errors()
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_reshape_and_cache_matches_oracle(oracle_mod, dt):
+    rng = np.random.default_rng(7)
+    nb = 64
+    kp = C.to_dtype(rng.standard_normal((nb, 16, 2, 64), dtype=np.float32), dt)
+    vp = C.to_dtype(rng.standard_normal((nb, 16, 2, 64), dtype=np.float32), dt)
+    T = 300
+    k = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32), dt)
+    v = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32), dt)
+    slots = rng.permutation(nb * 16)[:T].astype(np.int64)
+    slots[::7] = -1  # padding tokens are skipped
+    kd, vd = dev(kp, dt), dev(vp, dt)
+    err = ops.new_error_flags("cuda")
+    ops.reshape_and_cache(dev(k, dt), dev(v, dt), kd, vd, torch.from_numpy(slots).cuda(), err)
+    assert oracle_mod.reshape_and_cache(kp, vp, k, v, slots, dt) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(host(kd, dt), kp) and np.array_equal(host(vd, dt), vp)
+    assert int(err.item()) == 0
+
+
+def test_reshape_and_cache_strided_input(oracle_mod):
+    """K/V as strided views of a fused [T, (14+2+2)*64] projection output."""
+    rng = np.random.default_rng(8)
+    T, nb = 40, 8
+    qkv = torch.randn(T, 18 * 64, dtype=torch.float16, device="cuda")
+    k = qkv[:, 14 * 64:16 * 64].view(T, 2, 64)
+    v = qkv[:, 16 * 64:].view(T, 2, 64)
+    kp = torch.zeros(nb, 16, 2, 64, dtype=torch.float16, device="cuda")
+    vp = torch.zeros_like(kp)
+    slots = torch.from_numpy(rng.permutation(nb * 16)[:T].astype(np.int64)).cuda()
+    ops.reshape_and_cache(k, v, kp, vp, slots)
+    ref_k, ref_v = torch.zeros_like(kp).view(-1, 2, 64), torch.zeros_like(vp).view(-1, 2, 64)
+    ref_k[slots] = k
+    ref_v[slots] = v
+    assert torch.equal(kp.view(-1, 2, 64), ref_k) and torch.equal(vp.view(-1, 2, 64), ref_v)
+
+
+def test_reshape_and_cache_flags_bad_slot():
+    kp = torch.zeros(4, 16, 2, 64, dtype=torch.float16, device="cuda")
+    vp = torch.zeros_like(kp)
+    k = torch.ones(3, 2, 64, dtype=torch.float16, device="cuda")
+    slots = torch.tensor([0, 4 * 16, 5], dtype=torch.int64, device="cuda")  # middle one out of range
+    err = ops.new_error_flags("cuda")
+    ops.reshape_and_cache(k, k, kp, vp, slots, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_SLOT_OUT_OF_RANGE
+    flat = kp.view(-1, 2, 64)
+    assert flat[0].eq(1).all() and flat[5].eq(1).all() and flat[1].eq(0).all()
+
+
+def test_copy_blocks_flags_bad_pair():
+    kc = torch.randn(2, 8, 16, 2, 64, dtype=torch.float16, device="cuda")
+    vc = torch.randn_like(kc)
+    k0, v0 = kc.clone(), vc.clone()
+    pairs = torch.tensor([[1, 2], [3, 99]], dtype=torch.int32, device="cuda")
+    err = ops.new_error_flags("cuda")
+    ops.copy_blocks(kc, vc, pairs, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_BLOCK_OUT_OF_RANGE
+    assert torch.equal(kc[:, 2], k0[:, 1]) and torch.equal(vc[:, 2], v0[:, 1])
+    assert torch.equal(kc[:, 3], k0[:, 3])
+
+
+# ---------------------------------------------------------------- decode
+
+@pytest.mark.parametrize("dt", DTS)
+def test_decode_config1(oracle_mod, decode_impl, dt):
+    c = C.make_decode_case(1, 8, 32, 600, 512, dt)
+    out, _, _, err = run_decode_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_decode_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+    assert max_abs_diff(out, golden(f"decode_c1_{dt}.npz")["out"], dt) <= PRODUCT_ATOL[dt]
+
+
+@pytest.mark.parametrize("dt", DTS)
+def test_decode_edge_contexts(oracle_mod, decode_impl, dt):
+    c = C.make_decode_case(11, 9, 0, 0, 128, dt, ctx_list=[1, 2, 15, 16, 17, 31, 32, 33, 600])
+    out, _, _, err = run_decode_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_decode_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+    assert max_abs_diff(out, golden(f"decode_edge_{dt}.npz")["out"], dt) <= PRODUCT_ATOL[dt]
+
+
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_decode_config3_full(oracle_mod, decode_impl, dt):
+    """BASELINE config 3 at full size (B=256, lognormal contexts to 8192)."""
+    c = C.make_decode_case(3, 256, 16, 8192, 0, dt, lognormal_median=1024.0, pool_slack=1.1)
+    out, _, _, err = run_decode_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_decode_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+    if dt == "f16":
+        assert max_abs_diff(out, golden("decode_c3_f16.npz")["out"], dt) <= PRODUCT_ATOL[dt]
+
+
+def test_decode_many_short_and_long(oracle_mod, decode_impl):
+    """Ragged batch: many 1-block sequences around a few very long ones, so
+    the stream-K ranges split sequences at every kind of boundary."""
+    rng = np.random.default_rng(31)
+    ctx = rng.integers(1, 40, size=700).tolist()
+    ctx[5], ctx[300], ctx[699] = 8192, 5000, 4097
+    c = C.make_decode_case(31, len(ctx), 0, 0, sum((x + 15) // 16 for x in ctx) + 5, "f16",
+                           ctx_list=ctx)
+    out, _, _, err = run_decode_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_decode_case(c)
+    assert max_abs_diff(out, ref, "f16") <= PRODUCT_ATOL["f16"]
+
+
+def test_decode_repeated_launches_reuse_workspace(oracle_mod):
+    """The fused combine leaves its counters at zero: ten launches on one
+    workspace give identical outputs."""
+    c = C.make_decode_case(3, 256, 16, 8192, 0, "f16", lognormal_median=1024.0, pool_slack=1.1)
+    kp, vp = dev(c["k_pool"], "f16"), dev(c["v_pool"], "f16")
+    ops.reshape_and_cache(dev(c["k_new"], "f16"), dev(c["v_new"], "f16"), kp, vp,
+                          torch.from_numpy(C.decode_slots(c)).cuda())
+    q, tabs, ctx = dev(c["q"], "f16"), dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
+    ws = ops.new_decode_workspace(256, 14, 64, "cuda")
+    outs = [ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, workspace=ws).clone()
+            for _ in range(10)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    counters = ws[-((256 * 4 + 255) // 256 * 256):].view(torch.int32)
+    assert int(counters.abs().sum().item()) == 0
+
+
+def test_decode_zero_context_and_flags(decode_impl):
+    kp = torch.randn(8, 16, 2, 64, dtype=torch.float16, device="cuda")
+    vp = torch.randn_like(kp)
+    q = torch.randn(3, 14, 64, dtype=torch.float16, device="cuda")
+    tabs = torch.tensor([[0, 1], [2, 3], [4, 5]], dtype=torch.int32, device="cuda")
+    ctx = torch.tensor([20, 0, 5], dtype=torch.int32, device="cuda")
+    err = ops.new_error_flags("cuda")
+    out = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert out[1].eq(0).all() and torch.isfinite(out).all()
+    # context beyond the table: flagged and clamped, no fault
+    ctx = torch.tensor([20, 40, 5], dtype=torch.int32, device="cuda")
+    ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_CONTEXT_EXCEEDS_TABLE
+    # block id outside the pool: flagged, no fault
+    err.zero_()
+    bad = torch.tensor([[0, 1], [2, 77], [4, 5]], dtype=torch.int32, device="cuda")
+    ops.paged_decode_attention(q, kp, vp, bad, torch.tensor([20, 30, 5], dtype=torch.int32,
+                                                            device="cuda"), 0.125, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_BLOCK_OUT_OF_RANGE
+
+
+# ---------------------------------------------------------------- prefill
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("name,args", [
+    ("prefill_small", (21, [1, 7, 33, 64, 16], [0, 5, 37, 100, 11], 48, 256)),
+    ("prefill_noshare", (22, [20, 3, 48], [0, 16, 1], 0, 64)),
+])
+def test_prefill_small(oracle_mod, dt, name, args):
+    c = C.make_prefill_case(*args, dt)
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_prefill_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+    assert max_abs_diff(out, golden(f"{name}_{dt}.npz")["out"], dt) <= PRODUCT_ATOL[dt]
+
+
+def test_prefill_config4_full(oracle_mod):
+    c = C.make_c4_case()
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_prefill_case(c)
+    assert max_abs_diff(out, ref, "f16") <= PRODUCT_ATOL["f16"]
+    g = golden("prefill_c4_f16_rows.npz")
+    assert max_abs_diff(out[g["rows"]], g["out"], "f16") <= PRODUCT_ATOL["f16"]
+
+
+# ---------------------------------------------------------------- operator surface
+
+def test_append_and_fetch_roundtrip_reference_scenario():
+    """The reference's test_paged_write_read_roundtrip (test_block_manager.py:37-55),
+    fp32, block_size 4, 1 kv head, head_dim 2, through the CUDA pools."""
+    with open(f"{GOLDEN}/block_manager_ref.json") as f:
+        g = json.load(f)["roundtrip"]
+    m = BlockManager(8, 4, 2, 1, 2, device="cuda", dtype=torch.float32)
+    kv = PagedKVCache(m)
+    table = [m.allocate() for _ in range(3)]
+    kv.add_sequence(0, table, 0)
+    k1 = torch.arange(10, dtype=torch.float32, device="cuda").reshape(5, 1, 2)
+    for layer in range(2):
+        k, v, prior = kv.append_and_fetch(layer, 0, k1, k1 * 10)
+        assert prior == g["step1"][layer]["prior"]
+        assert k.cpu().tolist() == g["step1"][layer]["k"] and v.cpu().tolist() == g["step1"][layer]["v"]
+    k2 = torch.arange(100, 106, dtype=torch.float32, device="cuda").reshape(3, 1, 2)
+    for layer in range(2):
+        k, v, prior = kv.append_and_fetch(layer, 0, k2, k2 * 10)
+        assert prior == g["step2"][layer]["prior"]
+        assert k.cpu().tolist() == g["step2"][layer]["k"] and v.cpu().tolist() == g["step2"][layer]["v"]
+    assert kv.seq_len(0) == g["seq_len"]
+    m.check_errors()
+
+
+def test_cow_isolates_shared_tail_reference_scenario():
+    """test_block_manager.py:58-83 on the GPU pools (COW through copy_blocks)."""
+    with open(f"{GOLDEN}/block_manager_ref.json") as f:
+        g = json.load(f)["cow"]
+    m = BlockManager(8, 4, 2, 1, 2, device="cuda", dtype=torch.float32)
+    kv = PagedKVCache(m)
+    table = [m.allocate()]
+    kv.add_sequence(0, table, 0)
+    k = torch.ones(2, 1, 2, device="cuda")
+    for layer in range(2):
+        kv.append_and_fetch(layer, 0, k, k)
+    for b in table:
+        m.incref(b)
+    kv.add_sequence(1, list(table), 2)
+    kv.ensure_writable_tail(1)
+    k_new = torch.full((1, 1, 2), 7.0, device="cuda")
+    for layer in range(2):
+        kv.append_and_fetch(layer, 1, k_new, k_new)
+    z = torch.zeros(0, 1, 2, device="cuda")
+    k0, _, _ = kv.append_and_fetch(0, 0, z, z)
+    k1, _, _ = kv.append_and_fetch(0, 1, z, z)
+    assert k0.cpu().tolist() == g["k_seq0"] and k1.cpu().tolist() == g["k_seq1"]
+    assert [p.cpu().tolist() for p in m.k_pool] == g["k_pool"]
+    assert [p.cpu().tolist() for p in m.v_pool] == g["v_pool"]
+
+
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_forward_layer_mixed_batch(oracle_mod, dt):
+    """prepare_step + forward_layer on a batch of decodes followed by chunks:
+    one append launch, one decode launch, one prefill launch."""
+    rng = np.random.default_rng(41)
+    L, nb = 2, 256
+    m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=TORCH_DT[dt])
+    pools_k = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
+    pools_v = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
+    m.k_cache.copy_(dev(pools_k, dt))
+    m.v_cache.copy_(dev(pools_v, dt))
+    kv = PagedKVCache(m)
+    plan = [(0, 100, 1), (1, 17, 1), (2, 0, 1), (3, 48, 30), (4, 5, 64), (5, 31, 1)]
+    for s, prior, n in plan:
+        kv.add_sequence(s, [m.allocate() for _ in range((prior + n + 15) // 16)], prior)
+    meta = kv.prepare_step([(s, n) for s, _, n in plan])
+    assert meta.n_decode == 3
+    T = meta.n_tokens
+    for layer in range(L):
+        q = C.to_dtype(rng.standard_normal((T, 14, 64), dtype=np.float32), dt)
+        k = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32), dt)
+        v = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32), dt)
+        out = kv.forward_layer(layer, dev(q, dt), dev(k, dt), dev(v, dt), meta, 0.125)
+        torch.cuda.synchronize()
+        slots = np.concatenate([kv._slots(kv.block_tables[s], p, n) for s, p, n in plan])
+        assert oracle_mod.reshape_and_cache(pools_k[layer], pools_v[layer], k, v, slots, dt) == 0
+        qsl = np.concatenate([[0], np.cumsum([n for _, _, n in plan])]).astype(np.int32)
+        tabs = C.pad_tables([kv.block_tables[s] for s, _, _ in plan])
+        ref = oracle_mod.paged_attention(q, pools_k[layer], pools_v[layer], tabs, qsl,
+                                         np.array([p for _, p, _ in plan], dtype=np.int32), dt)
+        assert max_abs_diff(host(out, dt), ref, dt) <= PRODUCT_ATOL[dt]
+    assert [kv.seq_len(s) for s, _, _ in plan] == [p + n for _, p, n in plan]
+    m.check_errors()

@@ -1,0 +1,178 @@
+"""Host-side bookkeeping of pagedkv.BlockManager / PagedKVCache against the
+reference's behaviour (no GPU needed: bookkeeping-only managers, device=None).
+
+The reference scenarios are mini_engine tests/test_block_manager.py:16-83 and
+the config-2 fork/COW flow; their recorded outcomes live in tests/golden.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from conftest import GOLDEN
+from pagedkv import BlockManager, OutOfBlocks, PagedKVCache
+from pagedkv import ops
+
+
+def mgr(num_blocks=8, block_size=4, layers=2, heads=1, dim=2):
+    return BlockManager(num_blocks, block_size, layers, heads, dim, device=None)
+
+
+def test_allocate_free_cycle():
+    """test_block_manager.py:16-24"""
+    m = mgr(num_blocks=4)
+    blocks = [m.allocate() for _ in range(4)]
+    assert blocks == [0, 1, 2, 3]  # LIFO over range(n-1, -1, -1)
+    assert m.num_free == 0
+    with pytest.raises(OutOfBlocks):
+        m.allocate()
+    for b in blocks:
+        m.decref(b)
+    assert m.num_free == 4
+
+
+def test_ref_counting_delays_free():
+    """test_block_manager.py:27-34"""
+    m = mgr()
+    b = m.allocate()
+    m.incref(b)
+    m.decref(b)
+    assert m.ref_count[b] == 1 and b not in m.free_list
+    m.decref(b)
+    assert m.num_free == m.num_blocks
+
+
+def test_asserts_on_free_blocks():
+    m = mgr()
+    with pytest.raises(AssertionError):
+        m.decref(3)
+    with pytest.raises(AssertionError):
+        m.incref(3)
+
+
+def test_reference_scenarios_bookkeeping():
+    """Tables, free list and COW outcome of the reference's own unit scenarios."""
+    with open(f"{GOLDEN}/block_manager_ref.json") as f:
+        g = json.load(f)
+    m = mgr()
+    kv = PagedKVCache(m)
+    table = [m.allocate() for _ in range(3)]
+    assert table == g["roundtrip"]["table"]
+    kv.add_sequence(0, table, 0)
+    assert list(m.free_list) == g["roundtrip"]["free_list"]
+
+    m = mgr()
+    kv = PagedKVCache(m)
+    table = [m.allocate()]
+    kv.add_sequence(0, table, 2)
+    for b in table:
+        m.incref(b)
+    kv.add_sequence(1, list(table), 2)
+    kv.ensure_writable_tail(1)
+    assert {str(k): v for k, v in kv.block_tables.items()} == g["cow"]["tables_after_cow"]
+    assert list(m.ref_count) == g["cow"]["ref_count"]
+    assert list(m.free_list) == g["cow"]["free_list"]
+    assert m.pending_copies == [(table[0], kv.block_tables[1][0])]
+
+
+def test_config2_cow_pairs_match_reference():
+    """The fork flow of config 2 allocates the same COW destinations, in the
+    same order, as the reference's LIFO allocator over the seeded free list."""
+    c = C.make_append_cow_case()
+    with open(f"{GOLDEN}/append_cow_c2_f16.json") as f:
+        g = json.load(f)
+    m = BlockManager(c["num_blocks"], C.BS, c["n_layers"], C.HKV, C.D, device=None)
+    m.free_list = list(c["free_list"])
+    kv = PagedKVCache(m)
+    n = len(c["ctx"])
+    for s in range(n):
+        ctx = int(c["ctx"][s])
+        kv.add_sequence(s, [m.allocate() for _ in range((ctx + 15) // 16)], ctx)
+    assert [kv.block_tables[s] for s in range(n)] == g["tables"]
+    for i, s in enumerate(c["forked"]):
+        s = int(s)
+        for b in kv.block_tables[s]:
+            m.incref(b)
+        kv.add_sequence(n + i, list(kv.block_tables[s]), kv.seq_len(s))
+        kv.ensure_writable_tail(n + i)
+    assert [list(p) for p in m.pending_copies] == g["pairs"]
+    assert {str(k): v for k, v in kv.block_tables.items() if k >= n} == g["child_tables"]
+    assert list(m.ref_count) == g["ref_count"]
+    assert list(m.free_list) == g["free_list"]
+    assert m.flushes == 0  # 32 independent pairs fit one copy_blocks launch
+
+
+def test_cow_queue_flushes_on_conflict():
+    """A freed COW source that is re-allocated as a destination in the same
+    step must not share a launch with the copy that reads it."""
+    m = mgr(num_blocks=8)
+    a = m.allocate()           # 0
+    b = m.allocate()           # 1
+    m.incref(a)                # shared
+    d1 = m.copy_block(a)       # (0 -> 2) queued
+    m.decref(a)
+    m.decref(a)                # block 0 free again, top of the free list
+    d2 = m.copy_block(b)       # allocates block 0, which the queued pair still reads
+    assert d1 == 2 and d2 == a
+    assert m.flushes == 1
+    assert m.pending_copies == [(b, d2)]
+
+
+def test_step_arrays_slots_tables_and_split():
+    m = mgr(num_blocks=64, block_size=16)
+    kv = PagedKVCache(m)
+    kv.add_sequence(10, [m.allocate() for _ in range(3)], 33)   # decode at position 33
+    kv.add_sequence(11, [m.allocate() for _ in range(2)], 15)   # decode at 15 (block edge)
+    kv.add_sequence(12, [m.allocate() for _ in range(2)], 5)    # 20-token chunk
+    kv.add_sequence(13, [m.allocate()], 0)                      # 3-token prompt
+    a = kv.step_arrays([(10, 1), (11, 1), (12, 20), (13, 3)])
+    assert a["n_decode"] == 2 and a["n_tokens"] == 25 and a["max_query_len"] == 20
+    B, W = a["B"], a["W"]
+    ints = a["ints"]
+    tabs = ints[:B * W].reshape(B, W)
+    assert tabs[0, :3].tolist() == kv.block_tables[10]
+    assert ints[B * W:B * W + B].tolist() == [34, 16, 25, 3]
+    assert ints[B * W + B:B * W + 2 * B].tolist() == [33, 15, 5, 0]
+    assert ints[B * W + 2 * B:].tolist() == [0, 20, 23]
+
+    # slots: the reference's scatter writes position p to table[p // bs], offset p % bs
+    def ref_slots(seq, start, n):
+        t = kv.block_tables[seq]
+        return [t[p // 16] * 16 + p % 16 for p in range(start, start + n)]
+
+    expect = ref_slots(10, 33, 1) + ref_slots(11, 15, 1) + ref_slots(12, 5, 20) + ref_slots(13, 0, 3)
+    assert a["slots"].tolist() == expect
+
+
+def test_step_arrays_capacity_assert():
+    m = mgr(num_blocks=8, block_size=16)
+    kv = PagedKVCache(m)
+    kv.add_sequence(0, [m.allocate()], 16)
+    with pytest.raises(AssertionError):
+        kv.step_arrays([(0, 1)])
+
+
+def test_no_cpu_pools():
+    with pytest.raises(RuntimeError):
+        BlockManager(8, 16, 1, 2, 64, device="cpu")
+
+
+def test_ops_refuse_cpu_tensors():
+    k = torch.zeros(2, 2, 64, dtype=torch.float16)
+    pool = torch.zeros(4, 16, 2, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.reshape_and_cache(k, k, pool, pool, torch.zeros(2, dtype=torch.int64))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.paged_decode_attention(torch.zeros(2, 14, 64, dtype=torch.float16), pool, pool,
+                                   torch.zeros(2, 1, dtype=torch.int32),
+                                   torch.ones(2, dtype=torch.int32), 0.125)
+
+
+def test_to_dtype_bf16_matches_torch():
+    x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 37.0
+    ours = C.to_dtype(x, "bf16")
+    theirs = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(ours, theirs)
