@@ -97,7 +97,7 @@ int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, in
 
 /*
  * Bytes of device workspace pkv_paged_decode_attention needs for n_seqs
- * sequences (split-K partials and per-sequence arrival counters).
+ * sequences (split-K partials; no initialisation required).
  */
 size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim);
 
@@ -109,8 +109,9 @@ size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim);
  * over the context_lens[s] tokens of sequence s, read in place through
  * block_tables[s] (G = n_q_heads / n_kv_heads).  The new token must already
  * have been written (pkv_reshape_and_cache).  context_lens[s] == 0 gives a
- * zero row.  `workspace` must be zero-filled before its first use; every
- * launch leaves its counters at zero again (re-zero it after an error flag).
+ * zero row.  `workspace` (pkv_decode_workspace_bytes) carries split-K
+ * partials from the decode kernel to the merge kernel of the same call; calls
+ * that may overlap on the GPU need separate workspaces.
  */
 int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
                                int64_t q_row_stride, const void* k_pool, const void* v_pool,

@@ -17,6 +17,11 @@ __global__ void __launch_bounds__(256) reshape_and_cache_vec16(
     const char* __restrict__ k, const char* __restrict__ v, int64_t k_stride_b,
     int64_t v_stride_b, char* __restrict__ k_pool, char* __restrict__ v_pool,
     const int64_t* __restrict__ slots, int n_tokens, int64_t n_slots, int row_bytes, int* err) {
+  // launched with programmatic serialization: wait for the preceding grid
+  // (its reads of the pool and writes of k / v), then let the next kernel's
+  // prologue start
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n_tokens) return;
@@ -74,10 +79,19 @@ cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_str
                    ((v_stride * esize) % 16 == 0) && al16(k) && al16(v) && al16(k_pool) &&
                    al16(v_pool);
   if (vec) {
-    reshape_and_cache_vec16<<<grid, threads, 0, stream>>>(
-        static_cast<const char*>(k), static_cast<const char*>(v), k_stride * esize,
-        v_stride * esize, static_cast<char*>(k_pool), static_cast<char*>(v_pool), slots,
-        n_tokens, n_slots, row_bytes, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, reshape_and_cache_vec16, static_cast<const char*>(k),
+                              static_cast<const char*>(v), k_stride * esize, v_stride * esize,
+                              static_cast<char*>(k_pool), static_cast<char*>(v_pool), slots,
+                              n_tokens, n_slots, row_bytes, err);
   } else if (esize == 4) {
     reshape_and_cache_elem<uint32_t><<<grid, threads, 0, stream>>>(
         static_cast<const uint32_t*>(k), static_cast<const uint32_t*>(v), k_stride, v_stride,

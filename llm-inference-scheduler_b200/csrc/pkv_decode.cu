@@ -13,16 +13,22 @@
 //    of each 16-token block, one 16x64 tile per KV head for K and for V,
 //    into a kStages-deep shared-memory ring guarded by mbarriers
 //    (full: transaction bytes; empty: one arrival per consumer warp).
-//  * Consumer warp h (one per KV head): S = Q K^T and O += P V with the
-//    m16n8k16 tensor-core MMA.  The M=16 rows are the G <= 8 query heads of
-//    the GQA group, so all 7 Qwen2 query heads consume each K/V tile from one
-//    shared-memory read.  Online softmax in fp32 (exp2 domain).
+//  * Consumer warp h (one per KV head) runs m16n8k16 tensor-core MMAs with
+//    the 16 tokens of a block as M and the G <= 8 query heads of the GQA
+//    group as N: S^T = K Q^T, then O^T += V^T P^T with P^T transposed in
+//    registers (movmatrix).  All 7 Qwen2 query heads of a group consume each
+//    K/V tile from one shared-memory read.  Online softmax in fp32 (exp2).
 //  * Sequences fully inside one CTA's range are normalised and stored
 //    directly.  A sequence split across CTAs leaves (m, l, O) partials in the
-//    workspace; the CTA that arrives last on the sequence's counter (atomic,
-//    no spinning) merges them and resets the counter to zero.
+//    workspace, merged by a second small kernel (one CTA per sequence) that
+//    is launched right behind the decode kernel.
+//  * Programmatic dependent launch chains append -> decode -> merge: each
+//    kernel's prologue (context scan, block-table reads) runs before
+//    griddepcontrol.wait and overlaps its predecessor; pool, q, out and
+//    workspace are touched only after the wait.
 #include <float.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -31,7 +37,13 @@
 
 namespace pkv {
 
-constexpr int kDecStages = 6;
+#ifndef PKV_DEC_STAGES
+#define PKV_DEC_STAGES 8
+#endif
+#ifndef PKV_DEC_MIN_CTAS
+#define PKV_DEC_MIN_CTAS 3
+#endif
+constexpr int kDecStages = PKV_DEC_STAGES;
 constexpr int kDecMaxCtas = 1024;
 constexpr int kDecMaxSeqs = 2048;
 constexpr int kDecMinBlocksPerCta = 4;
@@ -54,15 +66,16 @@ struct DecodeParams {
   int group;  // q heads per kv head
   float scale_log2;
   float* part_o;   // [2*kDecMaxCtas][n_q_heads][64]
-  float* part_ml;  // [2*kDecMaxCtas][n_q_heads][2]
-  int* counters;   // [n_seqs]
+  float* part_ml;  // [2*kDecMaxCtas][ml_stride]: (m, l) per query head
+  int ml_stride;   // floats per slot: 2*n_q_heads rounded up to 4 (16 bytes)
   int* err;
 };
 
 size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
-  const size_t parts = static_cast<size_t>(2) * kDecMaxCtas * n_q_heads * (head_dim + 2) * 4;
-  const size_t cnt = static_cast<size_t>(n_seqs) * 4;
-  return ((parts + 255) & ~static_cast<size_t>(255)) + ((cnt + 255) & ~static_cast<size_t>(255));
+  (void)n_seqs;
+  const size_t parts = static_cast<size_t>(2) * kDecMaxCtas *
+                       (n_q_heads * head_dim + ((2 * n_q_heads + 3) & ~3)) * 4;
+  return (parts + 255) & ~static_cast<size_t>(255);
 }
 
 bool decode_fast_supported(const AttnArgs& a) {
@@ -74,14 +87,13 @@ bool decode_fast_supported(const AttnArgs& a) {
          al(a.q, 4) && al(a.out, 4) && al(a.k_pool, 16) && al(a.v_pool, 16);
 }
 
-// exclusive scan of n values in smem (in place), result total returned to all threads
+// exclusive scan of n values in smem (in place); returns the total to all threads
 __device__ __forceinline__ int block_exclusive_scan(int* vals, int n, int* scratch) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int per = (n + nt - 1) / nt;
   const int lo = min(n, tid * per), hi = min(n, lo + per);
   int sum = 0;
   for (int i = lo; i < hi; ++i) sum += vals[i];
-  // inclusive scan of per-thread sums across the block
   const int lane = tid & 31, wid = tid >> 5, nw = (nt + 31) >> 5;
   int x = sum;
 #pragma unroll
@@ -114,6 +126,7 @@ __device__ __forceinline__ int find_seq(const int* prefix, int n, int x) {
   return lo;
 }
 
+// Q^T fragments of this warp's GQA group: qa[kk] = Q[head g][16kk + 2t (+8)]
 template <typename T>
 __device__ __forceinline__ void load_q_frag(uint32_t (&qa)[4][2], const DecodeParams& p, int s,
                                             int h, int lane) {
@@ -132,27 +145,32 @@ __device__ __forceinline__ void load_q_frag(uint32_t (&qa)[4][2], const DecodePa
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                           const __grid_constant__ CUtensorMap vmap,
-                                                           const DecodeParams p) {
+// workspace slot of CTA c's partial for a sequence whose blocks start at blk_lo
+__device__ __forceinline__ int partial_slot(int c, int per, int blk_lo) {
+  return (blk_lo > c * per) ? 2 * c + 1 : 2 * c;
+}
+
+template <typename T, int NKV>
+__global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nkv = p.n_kv_heads;
+  constexpr int nkv = NKV;
   const int B = p.n_seqs;
 
   // ---- shared memory carve-up (tiles 1024-byte aligned for the 128B swizzle)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  const int stage_bytes = 2 * nkv * kDecTile;  // K tiles then V tiles
+  constexpr int stage_bytes = 2 * nkv * kDecTile;  // K tiles then V tiles
   uint8_t* tiles = base;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tiles + kDecStages * stage_bytes);
   uint64_t* empty_bar = full_bar + kDecStages;
-  int* misc = reinterpret_cast<int*>(empty_bar + kDecStages);  // [0]: last flag; [1..33] scan scratch
-  int* prefix = misc + 40;                                     // [B+1]
-  int* ctxs = prefix + (B + 1);                                // [B]
+  int* misc = reinterpret_cast<int*>(empty_bar + kDecStages);  // [1..9]: scan scratch
+  int* prefix = misc + 40;                           // [B+1]
+  int* ctxs = prefix + (B + 1);                      // [B]
 
-  // ---- prologue: clamp contexts, count blocks, prefix-sum them
+  // ---- prologue (reads only metadata): clamp contexts, prefix-sum block counts
   const int cap_tokens = p.max_blocks * 16;
   for (int s = tid; s < B; s += blockDim.x) {
     int c = p.context_lens[s];
@@ -172,17 +190,12 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
   const int per = max((total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x),
                       kDecMinBlocksPerCta);
   const int n_active = (total + per - 1) / per;
+  const bool active = static_cast<int>(blockIdx.x) < n_active;
 
-  // zero rows for empty sequences (CTA 0 only; nobody else writes them)
-  if (blockIdx.x == 0) {
-    const int row = p.n_q_heads * 64;
-    for (int s = 0; s < B; ++s) {
-      if (prefix[s + 1] != prefix[s]) continue;
-      T* o = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
-      for (int i = tid; i < row; i += blockDim.x) o[i] = Elem<T>::from_f(0.f);
-    }
-  }
-  if (static_cast<int>(blockIdx.x) >= n_active) return;
+  // the merge kernel behind this one may be scheduled now: it waits for this
+  // grid's completion before it reads anything this grid writes
+  if (tid == 0) pdl_trigger();
+  if (!active) return;
 
   const int r0 = blockIdx.x * per;
   const int r1 = min(r0 + per, total);
@@ -202,7 +215,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
-    bool dead = false;
+    bool dead = false, waited = false;
     int i = 0;
     for (int b0 = r0; b0 < r1; b0 += 32) {
       const int gb = b0 + lane;
@@ -216,6 +229,10 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
           id = 0;
         }
       }
+      if (!waited) {
+        pdl_wait();  // the pool may still be written by the preceding kernel
+        waited = true;
+      }
       const int n = min(32, r1 - b0);
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
@@ -227,6 +244,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
           } else {
             uint8_t* stg = tiles + st * stage_bytes;
             mbar_arrive_expect_tx(&full_bar[st], stage_bytes);
+#pragma unroll
             for (int hk = 0; hk < nkv; ++hk) {
               tma_load_3d(stg + hk * kDecTile, &kmap, &full_bar[st], 0, hk, blk * 16);
               tma_load_3d(stg + (nkv + hk) * kDecTile, &vmap, &full_bar[st], 0, hk, blk * 16);
@@ -239,11 +257,19 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
   }
 
   // ======================= consumer warps (warp = kv head) =======================
+  // Fragment layout (m16n8k16): g = lane / 4, t = lane % 4.
+  //   S^T = K Q^T   : A = K tile (16 tokens x 16 dims per k-step, ldmatrix),
+  //                   B = Q^T (16 dims x 8 heads; heads >= G are zero),
+  //                   C holds tokens {g, g+8} x heads {2t, 2t+1}.
+  //   O^T += V^T P^T: A = V^T (16 dims x 16 tokens, ldmatrix.trans) per
+  //                   16-dim tile, B = P^T from C via movmatrix.trans,
+  //                   C holds dims {16mt+g, 16mt+g+8} x heads {2t, 2t+1}.
+  pdl_wait();
   const int h = warp;
   const int g = lane >> 2, t = lane & 3;
-  const bool row_ok = g < p.group;
-  const int qh = h * p.group + g;
-  const int cons_threads = nkv * 32;
+  const int G = p.group;
+  const bool ok0 = 2 * t < G, ok1 = 2 * t + 1 < G;  // this lane's two heads exist
+  const int qh0 = h * G + 2 * t;                    // its first query head
   bool dead = false;
 
   int s = find_seq(prefix, B, r0);
@@ -261,10 +287,10 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
     if (seg_end < r1) load_q_frag<T>(qn, p, s_next, h, lane);
 
     const int ctx = ctxs[s];
-    float m = -INFINITY, l = 0.f;
-    float o[8][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[4][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int j = 0; j < 4; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
     for (int jb = jb0; jb < jb0 + (seg_end - pos); ++jb, ++i) {
       const int st = i % kDecStages;
@@ -274,112 +300,95 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
       }
       const uint32_t kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
       const uint32_t vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
-      // ---- S = Q K^T : rows = query heads of the group, cols = 16 tokens
-      float sc[2][4];
-#pragma unroll
-      for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+      // ---- S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int mi = lane >> 3;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const int row = (lane & 7) + ((lane >> 4) << 3);
-        const int chunk = 2 * kk + ((lane >> 3) & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1, b2, b3);
-        const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
-        mma16816<T>(sc[0], a, b0, b1);
-        mma16816<T>(sc[1], a, b2, b3);
-      }
-      // ---- online softmax (exp2 domain), tokens >= valid are masked
-      const int valid = min(16, ctx - jb * 16);
-      float x[4] = {sc[0][0] * p.scale_log2, sc[0][1] * p.scale_log2, sc[1][0] * p.scale_log2,
-                    sc[1][1] * p.scale_log2};
-      if (2 * t >= valid) x[0] = -INFINITY;
-      if (2 * t + 1 >= valid) x[1] = -INFINITY;
-      if (8 + 2 * t >= valid) x[2] = -INFINITY;
-      if (9 + 2 * t >= valid) x[3] = -INFINITY;
-      float mloc = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-      mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-      mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-      const float m_new = fmaxf(m, mloc);
-      const float corr = exp2f(m - m_new);
-      const float p0 = exp2f(x[0] - m_new), p1 = exp2f(x[1] - m_new);
-      const float p2 = exp2f(x[2] - m_new), p3 = exp2f(x[3] - m_new);
-      l = l * corr + (p0 + p1) + (p2 + p3);
-      m = m_new;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { o[j][0] *= corr; o[j][1] *= corr; }
-      // ---- O += P V : P (rows = heads, k = 16 tokens) straight from the S fragments
-      const uint32_t pa[4] = {pack2<T>(p0, p1), 0u, pack2<T>(p2, p3), 0u};
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int mi = lane >> 3;
         const int row = (lane & 7) + ((mi & 1) << 3);
-        const int chunk = 2 * jj + (mi >> 1);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), v0, v1, v2, v3);
-        mma16816<T>(o[2 * jj], pa, v0, v1);
-        mma16816<T>(o[2 * jj + 1], pa, v2, v3);
+        const int chunk = 2 * kk + (mi >> 1);
+        uint32_t a[4];
+        ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        mma16816<T>(sc, a, qa[kk][0], qa[kk][1]);
+      }
+      // ---- online softmax per head (exp2 domain); tokens >= valid masked
+      const int valid = min(16, ctx - jb * 16);
+      float x0 = sc[0] * p.scale_log2, x1 = sc[1] * p.scale_log2;  // token g
+      float x2 = sc[2] * p.scale_log2, x3 = sc[3] * p.scale_log2;  // token g + 8
+      if (g >= valid) x0 = x1 = -INFINITY;
+      if (g + 8 >= valid) x2 = x3 = -INFINITY;
+      float ma = fmaxf(x0, x2), mb = fmaxf(x1, x3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
+        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+      }
+      const float mna = fmaxf(m0, ma), mnb = fmaxf(m1, mb);
+      const float ca = exp2f(m0 - mna), cb = exp2f(m1 - mnb);
+      const float p0 = exp2f(x0 - mna), p2 = exp2f(x2 - mna);
+      const float p1 = exp2f(x1 - mnb), p3 = exp2f(x3 - mnb);
+      l0 = l0 * ca + (p0 + p2);
+      l1 = l1 * cb + (p1 + p3);
+      m0 = mna;
+      m1 = mnb;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { o[j][0] *= ca; o[j][1] *= cb; o[j][2] *= ca; o[j][3] *= cb; }
+      // ---- P^T fragments: transpose (token x head) 8x8 tiles to (head x token)
+      const uint32_t b0 = movmatrix_t(pack2<T>(p0, p1));  // tokens 0-7
+      const uint32_t b1 = movmatrix_t(pack2<T>(p2, p3));  // tokens 8-15
+      // ---- O^T += V^T P^T, 4 tiles of 16 dims
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const int row = (lane & 7) + ((mi >> 1) << 3);
+        const int chunk = 2 * mt + (mi & 1);
+        uint32_t a[4];
+        ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        mma16816<T>(o[mt], a, b0, b1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[st]);
     }
 
-    // ---- segment epilogue
-    float lt = l + __shfl_xor_sync(0xffffffffu, l, 1);
-    lt += __shfl_xor_sync(0xffffffffu, lt, 2);
-    if (complete) {
-      if (row_ok) {
-        const float inv = 1.f / lt;
-        T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride +
-                  static_cast<int64_t>(qh) * 64;
+    // ---- segment epilogue: per-head sums over the 8 token groups
+    float lt0 = l0, lt1 = l1;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t) = pack2<T>(o[j][0] * inv, o[j][1] * inv);
+    for (int off = 4; off < 32; off <<= 1) {
+      lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
+      lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
+    }
+    if (complete) {
+      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride +
+                static_cast<int64_t>(qh0) * 64;
+      const float i0 = 1.f / lt0, i1 = 1.f / lt1;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        if (ok0) {
+          orow[16 * mt + g] = Elem<T>::from_f(o[mt][0] * i0);
+          orow[16 * mt + g + 8] = Elem<T>::from_f(o[mt][2] * i0);
+        }
+        if (ok1) {
+          orow[64 + 16 * mt + g] = Elem<T>::from_f(o[mt][1] * i1);
+          orow[64 + 16 * mt + g + 8] = Elem<T>::from_f(o[mt][3] * i1);
+        }
       }
     } else {
-      const int slot = (prefix[s] <= r0) ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-      if (row_ok) {
-        float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh) * 64;
+      const int slot = partial_slot(blockIdx.x, per, prefix[s]);
+      float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh0) * 64;
+      float* pml = p.part_ml + static_cast<int64_t>(slot) * p.ml_stride + qh0 * 2;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float2*>(po + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
-        if (t == 0) {
-          float* pml = p.part_ml + (static_cast<int64_t>(slot) * p.n_q_heads + qh) * 2;
-          pml[0] = m;
-          pml[1] = lt;
+      for (int mt = 0; mt < 4; ++mt) {
+        if (ok0) {
+          po[16 * mt + g] = o[mt][0];
+          po[16 * mt + g + 8] = o[mt][2];
+        }
+        if (ok1) {
+          po[64 + 16 * mt + g] = o[mt][1];
+          po[64 + 16 * mt + g + 8] = o[mt][3];
         }
       }
-      __threadfence();
-      named_bar_sync(1, cons_threads);
-      if (tid == 0) {
-        const int c_first = prefix[s] / per, c_last = (prefix[s + 1] - 1) / per;
-        const int old = atomicAdd(p.counters + s, 1);
-        const int last = (old == c_last - c_first) ? 1 : 0;
-        if (last) p.counters[s] = 0;
-        misc[0] = last;
-      }
-      named_bar_sync(1, cons_threads);
-      if (misc[0]) {
-        __threadfence();
-        const int c_first = prefix[s] / per, c_last = (prefix[s + 1] - 1) / per;
-        const int n_out = p.n_q_heads * 64;
-        for (int idx = tid; idx < n_out; idx += cons_threads) {
-          const int hh = idx >> 6;
-          float M = -INFINITY;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int sl = (c == c_first && prefix[s] > c * per) ? 2 * c + 1 : 2 * c;
-            M = fmaxf(M, __ldcg(p.part_ml + (static_cast<int64_t>(sl) * p.n_q_heads + hh) * 2));
-          }
-          float L = 0.f, acc = 0.f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int sl = (c == c_first && prefix[s] > c * per) ? 2 * c + 1 : 2 * c;
-            const float* pml = p.part_ml + (static_cast<int64_t>(sl) * p.n_q_heads + hh) * 2;
-            const float w = exp2f(__ldcg(pml) - M);
-            L += w * __ldcg(pml + 1);
-            acc += w * __ldcg(p.part_o + static_cast<int64_t>(sl) * p.n_q_heads * 64 + idx);
-          }
-          T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
-          orow[idx] = Elem<T>::from_f(acc / L);
-        }
+      if (g == 0) {
+        if (ok0) { pml[0] = m0; pml[1] = lt0; }
+        if (ok1) { pml[2] = m1; pml[3] = lt1; }
       }
     }
     pos = seg_end;
@@ -391,6 +400,77 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(const __grid_constant
   }
 }
 
+// Split-K merge: CTA s finishes sequence s.  If the decode kernel split it
+// over CTAs c_first..c_last (stream-K ranges of `per` blocks), the partials
+// (m, l, O) are merged: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// Sequences inside one decode CTA were written by that CTA; empty sequences
+// get a zero row.  Warp w merges query heads w, w+4, ...; lane holds dims
+// 2*lane, 2*lane+1.  The block-count scan runs before griddepcontrol.wait and
+// overlaps the decode kernel.
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(const DecodeParams p,
+                                                                 int decode_grid) {
+  __shared__ int red[2][4];
+  const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cap = p.max_blocks * 16;
+  int before = 0, total = 0;
+  for (int i = tid; i < p.n_seqs; i += 128) {
+    const int c = min(max(p.context_lens[i], 0), cap);
+    const int nb = (c + 15) >> 4;
+    total += nb;
+    if (i < s) before += nb;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    before += __shfl_xor_sync(0xffffffffu, before, off);
+    total += __shfl_xor_sync(0xffffffffu, total, off);
+  }
+  if (lane == 0) { red[0][warp] = before; red[1][warp] = total; }
+  __syncthreads();
+  before = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+  total = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+  const int nb_s = (min(max(p.context_lens[s], 0), cap) + 15) >> 4;
+  const int per = max((total + decode_grid - 1) / decode_grid, kDecMinBlocksPerCta);
+
+  pdl_wait();  // the decode grid's partials and outputs are complete and visible
+  if (tid == 0) pdl_trigger();
+  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
+  if (nb_s == 0) {
+    for (int i = tid; i < p.n_q_heads * 64; i += 128) orow[i] = Elem<T>::from_f(0.f);
+    return;
+  }
+  const int blk_lo = before, blk_hi = before + nb_s;
+  const int c_first = blk_lo / per, c_last = (blk_hi - 1) / per;
+  if (c_first == c_last) return;
+  for (int hh = warp; hh < p.n_q_heads; hh += 4) {
+    float M = -INFINITY, L = 0.f, a0 = 0.f, a1 = 0.f;
+    for (int c0 = c_first; c0 <= c_last; c0 += 4) {
+      float2 ml[4], o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k <= c_last) {
+          const int64_t sl = partial_slot(c0 + k, per, blk_lo);
+          ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + sl * p.ml_stride + hh * 2));
+          o[k] = __ldcg(reinterpret_cast<const float2*>(p.part_o + (sl * p.n_q_heads + hh) * 64 + 2 * lane));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k <= c_last) {
+          const float mn = fmaxf(M, ml[k].x);
+          const float wa = exp2f(M - mn), wb = exp2f(ml[k].x - mn);
+          L = L * wa + ml[k].y * wb;
+          a0 = a0 * wa + o[k].x * wb;
+          a1 = a1 * wa + o[k].y * wb;
+          M = mn;
+        }
+      }
+    }
+    const float inv = 1.f / L;
+    *reinterpret_cast<uint32_t*>(orow + hh * 64 + 2 * lane) = pack2<T>(a0 * inv, a1 * inv);
+  }
+}
+
 size_t decode_smem_bytes(int nkv, int n_seqs) {
   return 1024 + static_cast<size_t>(kDecStages) * 2 * nkv * kDecTile +
          2 * kDecStages * sizeof(uint64_t) + 40 * sizeof(int) +
@@ -399,18 +479,28 @@ size_t decode_smem_bytes(int nkv, int n_seqs) {
 
 namespace {
 struct OccKey {
-  int dev, dtype, smem, threads;
+  int dev, kind, smem, threads;
   bool operator==(const OccKey& o) const {
-    return dev == o.dev && dtype == o.dtype && smem == o.smem && threads == o.threads;
+    return dev == o.dev && kind == o.kind && smem == o.smem && threads == o.threads;
   }
 };
 struct OccHash {
   size_t operator()(const OccKey& k) const {
-    return (static_cast<size_t>(k.dev) * 131 + k.dtype) * 1000003u + k.smem * 7 + k.threads;
+    return (static_cast<size_t>(k.dev) * 131 + k.kind) * 1000003u + k.smem * 7 + k.threads;
   }
 };
 std::mutex g_occ_mu;
 std::unordered_map<OccKey, int, OccHash> g_occ;
+
+using DecodeKernel = void (*)(const CUtensorMap, const CUtensorMap, const DecodeParams);
+
+DecodeKernel pick_kernel(int dtype, int nkv) {
+  if (dtype == PKV_DTYPE_F16)
+    return nkv == 1 ? paged_decode_kernel<__half, 1>
+         : nkv == 2 ? paged_decode_kernel<__half, 2> : paged_decode_kernel<__half, 4>;
+  return nkv == 1 ? paged_decode_kernel<__nv_bfloat16, 1>
+       : nkv == 2 ? paged_decode_kernel<__nv_bfloat16, 2> : paged_decode_kernel<__nv_bfloat16, 4>;
+}
 }  // namespace
 
 cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
@@ -422,18 +512,19 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  auto kern = a.dtype == PKV_DTYPE_F16 ? paged_decode_kernel<__half> : paged_decode_kernel<__nv_bfloat16>;
+  DecodeKernel kern = pick_kernel(a.dtype, nkv);
+  const int kind = a.dtype * 8 + nkv;
   int grid = 0;
   {
     std::lock_guard<std::mutex> lk(g_occ_mu);
-    const OccKey key{dev, a.dtype, static_cast<int>(smem), threads};
+    const OccKey key{dev, kind, static_cast<int>(smem), threads};
     auto it = g_occ.find(key);
     if (it == g_occ.end()) {
       // one opt-in size per (device, kernel): the largest any call can need
-      const OccKey attr_key{dev, a.dtype, -1, 0};
+      const OccKey attr_key{dev, kind, -1, 0};
       if (g_occ.find(attr_key) == g_occ.end()) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(decode_smem_bytes(4, kDecMaxSeqs)));
+                                 static_cast<int>(decode_smem_bytes(nkv, kDecMaxSeqs)));
         if (e != cudaSuccess) return e;
         g_occ.emplace(attr_key, 0);
       }
@@ -462,14 +553,32 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.group = a.n_q_heads / nkv;
   p.scale_log2 = a.scale * kLog2e;
   const size_t parts_o = static_cast<size_t>(2) * kDecMaxCtas * a.n_q_heads * 64 * 4;
-  const size_t parts_ml = static_cast<size_t>(2) * kDecMaxCtas * a.n_q_heads * 2 * 4;
+  p.ml_stride = (2 * a.n_q_heads + 3) & ~3;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float*>(ws + parts_o);
-  p.counters = reinterpret_cast<int*>(ws + ((parts_o + parts_ml + 255) & ~static_cast<size_t>(255)));
   p.err = a.err;
-  kern<<<grid, threads, smem, stream>>>(*kmap, *vmap, p);
-  return cudaGetLastError();
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, *kmap, *vmap, p);
+  if (e != cudaSuccess) return e;
+
+  cudaLaunchConfig_t mcfg = cfg;
+  mcfg.gridDim = dim3(a.n_seqs);
+  mcfg.blockDim = dim3(128);
+  mcfg.dynamicSmemBytes = 0;
+  if (a.dtype == PKV_DTYPE_F16)
+    return cudaLaunchKernelEx(&mcfg, paged_decode_merge_kernel<__half>, p, grid);
+  return cudaLaunchKernelEx(&mcfg, paged_decode_merge_kernel<__nv_bfloat16>, p, grid);
 }
 
 }  // namespace pkv

@@ -62,7 +62,8 @@ _lib: ctypes.CDLL | None = None
 
 
 def lib_path() -> str:
-    return _build.LIB
+    """The in-tree build, unless PAGEDKV_LIB names another build of the same ABI."""
+    return os.environ.get("PAGEDKV_LIB") or _build.LIB
 
 
 def load() -> ctypes.CDLL:

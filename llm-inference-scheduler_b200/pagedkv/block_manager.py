@@ -306,7 +306,7 @@ class PagedKVCache:
     def decode_workspace(self, n_seqs: int, n_q_heads: int, head_dim: int) -> torch.Tensor:
         need = ops.decode_workspace_bytes(n_seqs, n_q_heads, head_dim)
         if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = torch.zeros(need, dtype=torch.uint8, device=self.mgr.device)
+            self._workspace = torch.empty(need, dtype=torch.uint8, device=self.mgr.device)
         return self._workspace
 
     def forward_layer(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,

@@ -113,8 +113,8 @@ def decode_workspace_bytes(n_seqs: int, n_q_heads: int, head_dim: int) -> int:
 
 
 def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device) -> torch.Tensor:
-    """Zero-filled workspace; the decode kernel keeps its counters at zero."""
-    return torch.zeros(decode_workspace_bytes(n_seqs, n_q_heads, head_dim), dtype=torch.uint8,
+    """Split-K scratch of paged_decode_attention (any initial contents)."""
+    return torch.empty(decode_workspace_bytes(n_seqs, n_q_heads, head_dim), dtype=torch.uint8,
                        device=device)
 
 

@@ -223,20 +223,21 @@ def test_decode_many_short_and_long(oracle_mod, decode_impl):
 
 
 def test_decode_repeated_launches_reuse_workspace(oracle_mod):
-    """The fused combine leaves its counters at zero: ten launches on one
-    workspace give identical outputs."""
+    """The workspace needs no initialisation and carries nothing between
+    calls: ten launches on one garbage-filled workspace give identical outputs."""
     c = C.make_decode_case(3, 256, 16, 8192, 0, "f16", lognormal_median=1024.0, pool_slack=1.1)
     kp, vp = dev(c["k_pool"], "f16"), dev(c["v_pool"], "f16")
     ops.reshape_and_cache(dev(c["k_new"], "f16"), dev(c["v_new"], "f16"), kp, vp,
                           torch.from_numpy(C.decode_slots(c)).cuda())
     q, tabs, ctx = dev(c["q"], "f16"), dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
-    ws = ops.new_decode_workspace(256, 14, 64, "cuda")
+    ws = torch.randint(0, 255, (ops.decode_workspace_bytes(256, 14, 64),), dtype=torch.uint8,
+                       device="cuda")
     outs = [ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, workspace=ws).clone()
             for _ in range(10)]
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
-    counters = ws[-((256 * 4 + 255) // 256 * 256):].view(torch.int32)
-    assert int(counters.abs().sum().item()) == 0
+    ref, _, _ = oracle_mod.run_decode_case(c)
+    assert max_abs_diff(host(outs[0], "f16"), ref, "f16") <= PRODUCT_ATOL["f16"]
 
 
 def test_decode_zero_context_and_flags(decode_impl):
