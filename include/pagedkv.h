@@ -48,6 +48,7 @@ extern "C" {
 #define PKV_ERR_MISALIGNED (-5)
 #define PKV_ERR_UNSUPPORTED (-6)
 #define PKV_ERR_DRIVER (-7)
+#define PKV_ERR_SCRATCH_LIMIT (-8)
 
 /* device-side error flag bits (atomicOr into *err_flags) */
 #define PKV_FLAG_SLOT_OUT_OF_RANGE 1
@@ -55,6 +56,10 @@ extern "C" {
 #define PKV_FLAG_CONTEXT_EXCEEDS_TABLE 4
 #define PKV_FLAG_PIPELINE_TIMEOUT 8
 #define PKV_FLAG_BAD_QUERY_LAYOUT 16
+
+/* size of the device-resident scratch array behind
+ * pkv_paged_decode_attention_noalloc (per GPU, held until the process exits) */
+#define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /* decode-attention kernel choice (pkv_set_decode_impl) */
 #define PKV_DECODE_AUTO 0
@@ -121,6 +126,38 @@ int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
                                int n_kv_heads, int head_dim, int block_size, float scale,
                                int dtype, void* workspace, size_t workspace_bytes,
                                int* err_flags, pkv_stream_t stream);
+
+/*
+ * Paged decode attention for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some hosts of this library cannot call
+ * cudaMalloc (or any allocating routine) at the point where they run decode
+ * attention -- for example a thin FFI layer that only forwards pointers it
+ * was handed, or a process whose device memory is entirely owned by another
+ * allocator -- so they cannot provide the split-K workspace that
+ * pkv_paged_decode_attention requires.  This entry point takes the same
+ * arguments minus the workspace and computes the same result, keeping its
+ * split-K partials in a fixed array of PKV_NOALLOC_SCRATCH_BYTES (8 MiB) that
+ * is part of the library's device image: every GPU that loads the library
+ * holds it until the process exits.  Nothing is allocated per call.
+ *  - The first call on each device looks up that array's device address
+ *    (cudaGetSymbolAddress, with that device current); make this first call
+ *    before any stream capture.
+ *  - Problems whose partials exceed the array (pkv_decode_workspace_bytes >
+ *    PKV_NOALLOC_SCRATCH_BYTES, e.g. more than 15 query heads at head_dim 64)
+ *    are rejected with PKV_ERR_SCRATCH_LIMIT before anything is launched.
+ *  - All calls on a device share the one array and it keeps whatever the
+ *    last call left there; nothing in it needs to start at zero (every
+ *    partial is written before it is read within a call).  Calls that can
+ *    overlap on the GPU (different streams, no ordering) race on it.
+ */
+int pkv_paged_decode_attention_noalloc(void* out, int64_t out_row_stride, const void* q,
+                                       int64_t q_row_stride, const void* k_pool,
+                                       const void* v_pool, int num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       int max_blocks_per_seq, const int32_t* context_lens,
+                                       int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                       int block_size, float scale, int dtype, int* err_flags,
+                                       pkv_stream_t stream);
 
 /*
  * Paged chunked-prefill attention.  Replaces the per-sequence gather +

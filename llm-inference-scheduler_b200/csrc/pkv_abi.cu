@@ -99,6 +99,20 @@ int check_attn(const void* out, int64_t out_stride, const void* q, int64_t q_str
 
 }  // namespace
 
+// Shared with the allocation-free decode entry point (pkv_decode_noalloc.cu).
+int validate_attention_args(const void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                            const void* k_pool, const void* v_pool, int num_blocks,
+                            const int32_t* tables, int64_t bt_stride, int max_blocks,
+                            int n_q_heads, int n_kv_heads, int head_dim, int block_size, int dtype) {
+  return check_attn(out, out_stride, q, q_stride, k_pool, v_pool, num_blocks, tables, bt_stride,
+                    max_blocks, n_q_heads, n_kv_heads, head_dim, block_size, dtype);
+}
+int pool_tensormap(CUtensorMap* out, const void* pool, int num_blocks, int block_size,
+                   int n_kv_heads, int head_dim, int dtype) {
+  return cached_pool_map(out, pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+}
+int decode_impl_setting() { return g_decode_impl.load(); }
+
 int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, int block_size,
                           int n_kv_heads, int head_dim, int dtype) {
   auto enc = encoder();
@@ -135,6 +149,9 @@ const char* pkv_status_string(int status) {
     case PKV_ERR_MISALIGNED: return "pointer or stride misaligned for this kernel";
     case PKV_ERR_UNSUPPORTED: return "combination of arguments not supported";
     case PKV_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or failed";
+    case PKV_ERR_SCRATCH_LIMIT:
+      return "problem needs more split-K scratch than the allocation-free decode entry point's "
+             "fixed PKV_NOALLOC_SCRATCH_BYTES array holds; use pkv_paged_decode_attention";
     default: break;
   }
   if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));

@@ -65,4 +65,14 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
 int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, int block_size,
                           int n_kv_heads, int head_dim, int dtype);
 
+// Argument checks, TMA-descriptor cache and kernel selection of pkv_abi.cu,
+// reused by the allocation-free decode entry point.
+int validate_attention_args(const void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                            const void* k_pool, const void* v_pool, int num_blocks,
+                            const int32_t* tables, int64_t bt_stride, int max_blocks,
+                            int n_q_heads, int n_kv_heads, int head_dim, int block_size, int dtype);
+int pool_tensormap(CUtensorMap* out, const void* pool, int num_blocks, int block_size,
+                   int n_kv_heads, int head_dim, int dtype);
+int decode_impl_setting();
+
 }  // namespace pkv

@@ -22,6 +22,10 @@ ERR_WORKSPACE_TOO_SMALL = -4
 ERR_MISALIGNED = -5
 ERR_UNSUPPORTED = -6
 ERR_DRIVER = -7
+ERR_SCRATCH_LIMIT = -8
+
+# device-resident scratch of pkv_paged_decode_attention_noalloc
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 FLAG_SLOT_OUT_OF_RANGE = 1
 FLAG_BLOCK_OUT_OF_RANGE = 2
@@ -45,6 +49,8 @@ SIGNATURES = {
     "pkv_paged_prefill_attention": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _P, _I,
                                          _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "pkv_set_decode_impl": (_I, [_I]),
+    "pkv_paged_decode_attention_noalloc": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _I,
+                                                _I, _I, _I, _I, _F, _I, _P, _P]),
 }
 
 
