@@ -83,8 +83,9 @@ bool decode_fast_supported(const AttnArgs& a) {
   auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
   return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
          a.block_size == 16 && (a.n_kv_heads == 1 || a.n_kv_heads == 2 || a.n_kv_heads == 4) &&
-         G <= 8 && a.n_seqs <= kDecMaxSeqs && (a.q_stride % 2) == 0 && (a.out_stride % 2) == 0 &&
-         al(a.q, 4) && al(a.out, 4) && al(a.k_pool, 16) && al(a.v_pool, 16);
+         G <= 8 && a.n_q_heads <= 32 && a.n_seqs <= kDecMaxSeqs && (a.q_stride % 2) == 0 &&
+         (a.out_stride % 4) == 0 && al(a.q, 4) && al(a.out, 8) && al(a.k_pool, 16) &&
+         al(a.v_pool, 16);
 }
 
 // exclusive scan of n values in smem (in place); returns the total to all threads
@@ -404,17 +405,27 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
 // over CTAs c_first..c_last (stream-K ranges of `per` blocks), the partials
 // (m, l, O) are merged: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
 // Sequences inside one decode CTA were written by that CTA; empty sequences
-// get a zero row.  Warp w merges query heads w, w+4, ...; lane holds dims
-// 2*lane, 2*lane+1.  The block-count scan runs before griddepcontrol.wait and
-// overlaps the decode kernel.
+// get a zero row.  Contributors are taken in chunks of kMergeChunk: all
+// (m, l) of a chunk are loaded at once into shared memory, per-head weights
+// are formed there, then each thread accumulates one float4 of the output
+// from independent 16-byte loads, so a chunk costs two memory round trips.
+// The block-count scan runs before griddepcontrol.wait and overlaps the
+// decode kernel.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeChunk = 32;
+constexpr int kMergeMaxHeads = 32;
+
 template <typename T>
-__global__ void __launch_bounds__(128) paged_decode_merge_kernel(const DecodeParams p,
-                                                                 int decode_grid) {
-  __shared__ int red[2][4];
+__global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const DecodeParams p,
+                                                                           int decode_grid) {
+  __shared__ float s_m[kMergeChunk][kMergeMaxHeads];
+  __shared__ float s_l[kMergeChunk][kMergeMaxHeads];
+  __shared__ float s_run_m[kMergeMaxHeads], s_run_l[kMergeMaxHeads], s_scale[kMergeMaxHeads];
+  __shared__ int red[2][kMergeThreads / 32];
   const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cap = p.max_blocks * 16;
   int before = 0, total = 0;
-  for (int i = tid; i < p.n_seqs; i += 128) {
+  for (int i = tid; i < p.n_seqs; i += kMergeThreads) {
     const int c = min(max(p.context_lens[i], 0), cap);
     const int nb = (c + 15) >> 4;
     total += nb;
@@ -427,47 +438,98 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const DecodePar
   }
   if (lane == 0) { red[0][warp] = before; red[1][warp] = total; }
   __syncthreads();
-  before = red[0][0] + red[0][1] + red[0][2] + red[0][3];
-  total = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+  before = 0;
+  total = 0;
+#pragma unroll
+  for (int w = 0; w < kMergeThreads / 32; ++w) { before += red[0][w]; total += red[1][w]; }
   const int nb_s = (min(max(p.context_lens[s], 0), cap) + 15) >> 4;
   const int per = max((total + decode_grid - 1) / decode_grid, kDecMinBlocksPerCta);
 
   pdl_wait();  // the decode grid's partials and outputs are complete and visible
   if (tid == 0) pdl_trigger();
+  const int Hq = p.n_q_heads;
   T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
   if (nb_s == 0) {
-    for (int i = tid; i < p.n_q_heads * 64; i += 128) orow[i] = Elem<T>::from_f(0.f);
+    for (int i = tid; i < Hq * 64; i += kMergeThreads) orow[i] = Elem<T>::from_f(0.f);
     return;
   }
   const int blk_lo = before, blk_hi = before + nb_s;
   const int c_first = blk_lo / per, c_last = (blk_hi - 1) / per;
   if (c_first == c_last) return;
-  for (int hh = warp; hh < p.n_q_heads; hh += 4) {
-    float M = -INFINITY, L = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int c0 = c_first; c0 <= c_last; c0 += 4) {
-      float2 ml[4], o[4];
+
+  // this thread's outputs: float4 number j of the sequence row (head j / 16)
+  constexpr int kOutPerThread = kMergeMaxHeads * 16 / kMergeThreads;  // 2
+  float4 acc[kOutPerThread];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (c0 + k <= c_last) {
-          const int64_t sl = partial_slot(c0 + k, per, blk_lo);
-          ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + sl * p.ml_stride + hh * 2));
-          o[k] = __ldcg(reinterpret_cast<const float2*>(p.part_o + (sl * p.n_q_heads + hh) * 64 + 2 * lane));
-        }
+  for (int r = 0; r < kOutPerThread; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < Hq) { s_run_m[tid] = -INFINITY; s_run_l[tid] = 0.f; }
+  for (int c0 = c_first; c0 <= c_last; c0 += kMergeChunk) {
+    const int n = min(kMergeChunk, c_last - c0 + 1);
+    for (int idx = tid; idx < n * Hq; idx += kMergeThreads) {
+      const int k = idx / Hq, hh = idx - k * Hq;
+      const int64_t sl = partial_slot(c0 + k, per, blk_lo);
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + sl * p.ml_stride + hh * 2));
+      s_m[k][hh] = ml.x;
+      s_l[k][hh] = ml.y;
+    }
+    __syncthreads();
+    if (tid < Hq) {  // running max / sum per head; s_m becomes the weight 2^(m_k - M)
+      float mx = s_run_m[tid];
+      for (int k = 0; k < n; ++k) mx = fmaxf(mx, s_m[k][tid]);
+      const float sc = exp2f(s_run_m[tid] - mx);
+      float l = s_run_l[tid] * sc;
+      for (int k = 0; k < n; ++k) {
+        const float w = exp2f(s_m[k][tid] - mx);
+        s_m[k][tid] = w;
+        l += w * s_l[k][tid];
       }
+      s_run_m[tid] = mx;
+      s_run_l[tid] = l;
+      s_scale[tid] = sc;
+    }
+    __syncthreads();
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (c0 + k <= c_last) {
-          const float mn = fmaxf(M, ml[k].x);
-          const float wa = exp2f(M - mn), wb = exp2f(ml[k].x - mn);
-          L = L * wa + ml[k].y * wb;
-          a0 = a0 * wa + o[k].x * wb;
-          a1 = a1 * wa + o[k].y * wb;
-          M = mn;
+    for (int r = 0; r < kOutPerThread; ++r) {
+      const int j = tid + r * kMergeThreads;
+      if (j < Hq * 16) {
+        const int hh = j >> 4;
+        const float sc = s_scale[hh];
+        float4 a = make_float4(acc[r].x * sc, acc[r].y * sc, acc[r].z * sc, acc[r].w * sc);
+        for (int k0 = 0; k0 < n; k0 += 8) {
+          float4 o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (k0 + k < n) {
+              const int64_t sl = partial_slot(c0 + k0 + k, per, blk_lo);
+              o[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + sl * Hq * 64) + j);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (k0 + k < n) {
+              const float w = s_m[k0 + k][hh];
+              a.x += w * o[k].x;
+              a.y += w * o[k].y;
+              a.z += w * o[k].z;
+              a.w += w * o[k].w;
+            }
+          }
         }
+        acc[r] = a;
       }
     }
-    const float inv = 1.f / L;
-    *reinterpret_cast<uint32_t*>(orow + hh * 64 + 2 * lane) = pack2<T>(a0 * inv, a1 * inv);
+    __syncthreads();  // s_m / s_scale are rewritten by the next chunk
+  }
+#pragma unroll
+  for (int r = 0; r < kOutPerThread; ++r) {
+    const int j = tid + r * kMergeThreads;
+    if (j < Hq * 16) {
+      const float inv = 1.f / s_run_l[j >> 4];
+      uint2 v;
+      v.x = pack2<T>(acc[r].x * inv, acc[r].y * inv);
+      v.y = pack2<T>(acc[r].z * inv, acc[r].w * inv);
+      *reinterpret_cast<uint2*>(orow + 4 * j) = v;
+    }
   }
 }
 
@@ -574,7 +636,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
 
   cudaLaunchConfig_t mcfg = cfg;
   mcfg.gridDim = dim3(a.n_seqs);
-  mcfg.blockDim = dim3(128);
+  mcfg.blockDim = dim3(kMergeThreads);
   mcfg.dynamicSmemBytes = 0;
   if (a.dtype == PKV_DTYPE_F16)
     return cudaLaunchKernelEx(&mcfg, paged_decode_merge_kernel<__half>, p, grid);
