@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
+                    help="decode = BASELINE config 3 (headline); prefill = config 4")
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
     ap.add_argument("--strong", action="store_true")
@@ -390,10 +392,145 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def peaks_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops_sustained"]), "measured (sustained)"
+    except (OSError, KeyError, ValueError):
+        return 1400.0, "fallback (sustained)"
+
+
+def run_prefill(args):
+    """BASELINE config 4 per GPU: 16 sequences x 512-token chunks over a
+    48-token shared prefix + private prior U[0, 4096]; per layer one append of
+    the 8192 chunk tokens and one chunked-prefill launch (tcgen05 kernel)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from pagedkv import BlockManager, ops
+    from pagedkv import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    L, scale, dt = args.layers, 0.125, torch.float16
+    prior, chunk = W.config4_layout(seed=4 + rank)
+    B, T = len(prior), int(chunk.sum())
+    need = int(((prior + chunk + 15) // 16).sum())
+    nb = int(need * 1.1) + 8
+    tabs_np = W.prefill_tables(prior, chunk, 48, nb, seed=200 + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + rank)
+    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=dt)
+    for layer in range(L):
+        mgr.k_pool[layer].normal_(generator=g)
+        mgr.v_pool[layer].normal_(generator=g)
+    q = torch.randn((L, T, 14, 64), generator=g, device=dev, dtype=dt)
+    kn = torch.randn((L, T, 2, 64), generator=g, device=dev, dtype=dt)
+    vn = torch.randn((L, T, 2, 64), generator=g, device=dev, dtype=dt)
+    out = torch.empty_like(q)
+    slots = []
+    for i in range(B):
+        pos = np.arange(prior[i], prior[i] + chunk[i])
+        slots.append(tabs_np[i, pos // 16].astype(np.int64) * 16 + pos % 16)
+    slots = torch.from_numpy(np.concatenate(slots)).to(dev)
+    tabs = torch.from_numpy(tabs_np).to(dev)
+    qsl = torch.from_numpy(np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)).to(dev)
+    prior_d = torch.from_numpy(prior.astype(np.int32)).to(dev)
+    err = ops.new_error_flags(dev)
+    appends = [ops.bind_reshape_and_cache(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], slots, err)
+               for l in range(L)]
+    prefills = [ops.bind_paged_prefill_attention(q[l], mgr.k_pool[l], mgr.v_pool[l], tabs, qsl,
+                                                 prior_d, int(chunk.max()), scale, out[l], err)
+                for l in range(L)]
+    flops = W.prefill_flops(prior, chunk)
+
+    def step(ev=None):
+        for layer in range(L):
+            appends[layer]()
+            if ev is not None:
+                ev[layer][0].record()
+            prefills[layer]()
+            if ev is not None:
+                ev[layer][1].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_flags(err, "prefill warm-up")
+    if args.profile_steps:
+        for _ in range(args.profile_steps):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    every = 10
+    ev_steps = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(L)] for _ in range((args.steps + every - 1) // every)]
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    start.record()
+    for i in range(args.steps):
+        step(ev_steps[i // every] if i % every == 0 else None)
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    barrier()
+    if sampler:
+        sampler.stop()
+    ops.check_flags(err, "prefill timed region")
+    ms = W.max_over_ranks(start.elapsed_time(end) / args.steps)
+    ker = [a.elapsed_time(b) for evs in ev_steps for (a, b) in evs]
+    ker_ms = W.max_over_ranks(sum(ker) / len(ker))
+    total_flops = W.sum_over_ranks(L * flops)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, kind = peaks_tflops()
+    achieved = flops / (ker_ms * 1e-3) / 1e12
+    line = {
+        "metric": "paged chunked-prefill attention TFLOP/s (config 4)",
+        "value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded normal Q/K/V)",
+        "config": {"workload": "config4: 16 seqs x 512-token chunk over 48-token shared prefix + "
+                               "private prior U[0,4096], 24 layers x (append + prefill), 14q/2kv, d64",
+                   "sum_prior": int(prior.sum()), "flops_per_layer": flops, "layers": L},
+        "roofline": {"kernel": "paged_prefill_tc_kernel<half>", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": kind,
+                     "avg_launch_ms": round(ker_ms, 5)},
+        "gpu_launches": 2 * L * args.steps,
+        "clocks": sampler.summary(t0, t1) if sampler else None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)
 

@@ -131,6 +131,24 @@ int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, in
   return r == CUDA_SUCCESS ? 0 : PKV_ERR_DRIVER;
 }
 
+int encode_q_tensormap(CUtensorMap* map, const void* q, int64_t q_stride, int n_tokens,
+                       int n_q_heads, int head_dim, int dtype) {
+  auto enc = encoder();
+  if (enc == nullptr) return PKV_ERR_DRIVER;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(n_q_heads),
+                              static_cast<cuuint64_t>(n_tokens)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2,
+                                 static_cast<cuuint64_t>(q_stride) * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), 1u, 128u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUresult r = enc(map, dt, 3, const_cast<void*>(q), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : PKV_ERR_DRIVER;
+}
+
 }  // namespace pkv
 
 using namespace pkv;
@@ -290,7 +308,18 @@ int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q
   a.scale = scale;
   a.dtype = dtype;
   a.err = err_flags;
-  return status_of(launch_generic_attention(a, static_cast<cudaStream_t>(stream)));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_decode_impl.load() == PKV_DECODE_AUTO && prefill_fast_supported(a)) {
+    CUtensorMap qm, km, vm;
+    rc = encode_q_tensormap(&qm, q, q_row_stride, n_tokens, n_q_heads, head_dim, dtype);
+    if (rc != 0) return rc;
+    rc = cached_pool_map(&km, k_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+    if (rc != 0) return rc;
+    rc = cached_pool_map(&vm, v_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
+    if (rc != 0) return rc;
+    return status_of(launch_prefill_fast(a, &qm, &km, &vm, st));
+  }
+  return status_of(launch_generic_attention(a, st));
 }
 
 }  // extern "C"

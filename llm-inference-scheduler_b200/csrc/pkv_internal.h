@@ -65,6 +65,17 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
 int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, int block_size,
                           int n_kv_heads, int head_dim, int dtype);
 
+// Chunked prefill on tcgen05 tensor cores: fp16/bf16, head_dim 64, block 16,
+// 16-byte aligned q / out rows.
+bool prefill_fast_supported(const AttnArgs& a);
+cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, const CUtensorMap* kmap,
+                                const CUtensorMap* vmap, cudaStream_t stream);
+// TMA descriptor for q viewed as [n_tokens][n_q_heads][head_dim] (row stride
+// q_stride elements) with one (head_dim x 1 head x 128 tokens) box, 128-byte
+// swizzle.  Returns 0 or PKV_ERR_DRIVER.
+int encode_q_tensormap(CUtensorMap* map, const void* q, int64_t q_stride, int n_tokens,
+                       int n_q_heads, int head_dim, int dtype);
+
 // Argument checks, TMA-descriptor cache and kernel selection of pkv_abi.cu,
 // reused by the allocation-free decode entry point.
 int validate_attention_args(const void* out, int64_t out_stride, const void* q, int64_t q_stride,

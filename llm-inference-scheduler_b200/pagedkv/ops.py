@@ -191,15 +191,8 @@ def bind_paged_decode_attention(q, k_pool, v_pool, block_tables, context_lens, s
                        (q, k_pool, v_pool, block_tables, context_lens, workspace, out, err))
 
 
-def paged_prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
-                            block_tables: torch.Tensor, query_start_loc: torch.Tensor,
-                            num_prior: torch.Tensor, max_query_len: int, scale: float,
-                            out: torch.Tensor | None = None,
-                            err: torch.Tensor | None = None) -> torch.Tensor:
-    """Chunked prefill: sequence s owns q rows [qsl[s], qsl[s+1]); its new token
-    i attends to keys 0 .. num_prior[s] + i through block_tables[s].
-    Reference: qwen2.py:98-128 causal mask with the num_prior offset.
-    """
+def _prefill_args(q, k_pool, v_pool, block_tables, query_start_loc, num_prior, max_query_len,
+                  scale, out, err):
     for t, n in ((q, "q"), (k_pool, "k_pool"), (v_pool, "v_pool"),
                  (query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
         _cuda(t, n)
@@ -216,13 +209,38 @@ def paged_prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch
         raise ValueError("pagedkv: q / query_start_loc / num_prior / block_tables shapes disagree")
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    rc = _lib.load().pkv_paged_prefill_attention(
-        out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
-        v_pool.data_ptr(), nb, block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
-        query_start_loc.data_ptr(), num_prior.data_ptr(), B, T, int(max_query_len), hq, hkv, d, bs,
-        float(scale), dtype_code(q.dtype), _ptr(err), _stream(q))
-    _lib.check(rc, "pkv_paged_prefill_attention")
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), nb, block_tables.data_ptr(), block_tables.stride(0),
+            block_tables.shape[1], query_start_loc.data_ptr(), num_prior.data_ptr(), B, T,
+            int(max_query_len), hq, hkv, d, bs, float(scale), dtype_code(q.dtype), _ptr(err),
+            _stream(q))
+    return args, out
+
+
+def paged_prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                            block_tables: torch.Tensor, query_start_loc: torch.Tensor,
+                            num_prior: torch.Tensor, max_query_len: int, scale: float,
+                            out: torch.Tensor | None = None,
+                            err: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked prefill: sequence s owns q rows [qsl[s], qsl[s+1]); its new token
+    i attends to keys 0 .. num_prior[s] + i through block_tables[s].
+    max_query_len must be >= every chunk length.
+    Reference: qwen2.py:98-128 causal mask with the num_prior offset.
+    """
+    args, out = _prefill_args(q, k_pool, v_pool, block_tables, query_start_loc, num_prior,
+                              max_query_len, scale, out, err)
+    if args[13] == 0:
+        return out
+    _lib.check(_lib.load().pkv_paged_prefill_attention(*args), "pkv_paged_prefill_attention")
     return out
+
+
+def bind_paged_prefill_attention(q, k_pool, v_pool, block_tables, query_start_loc, num_prior,
+                                 max_query_len, scale, out, err=None) -> BoundLaunch:
+    args, out = _prefill_args(q, k_pool, v_pool, block_tables, query_start_loc, num_prior,
+                              max_query_len, scale, out, err)
+    return BoundLaunch(_lib.load().pkv_paged_prefill_attention, args, "pkv_paged_prefill_attention",
+                       (q, k_pool, v_pool, block_tables, query_start_loc, num_prior, out, err))
 
 
 def set_decode_impl(impl: int) -> None:

@@ -104,3 +104,39 @@ def sum_over_ranks(value: float, group=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
     return float(t.item())
+
+
+def config4_layout(seed: int = 4, n_seqs: int = 16, chunk: int = 512, prior_hi: int = 4096,
+                   shared: int = 48):
+    """Config 4: n_seqs chunks of `chunk` queries over a `shared`-token radix
+    prefix (same physical blocks in every table) plus a private prior ~ U[0, prior_hi]."""
+    rng = np.random.default_rng(seed + 1000)
+    priv = rng.integers(0, prior_hi + 1, size=n_seqs).astype(np.int64)
+    prior = shared + priv
+    return prior, np.full(n_seqs, chunk, dtype=np.int64)
+
+
+def prefill_flops(prior: np.ndarray, chunk: np.ndarray, n_q_heads: int = N_Q_HEADS,
+                  head_dim: int = HEAD_DIM) -> int:
+    """Algorithmic FLOPs of one chunked-prefill launch: QK^T and PV over the
+    visible (query, key) pairs only, 2 * 2 * head_dim per pair and head.
+    Query i of a chunk sees prior + i + 1 keys."""
+    pairs = sum(int(c) * int(p) + int(c) * (int(c) + 1) // 2 for p, c in zip(prior, chunk))
+    return 4 * head_dim * n_q_heads * pairs
+
+
+def prefill_tables(prior: np.ndarray, chunk: np.ndarray, shared: int, num_blocks: int, seed: int,
+                   block_size: int = BLOCK_SIZE):
+    """Tables whose first shared // 16 blocks are common to all sequences
+    (a radix-cache hit) followed by private blocks from a seeded permutation."""
+    rng = np.random.default_rng(seed)
+    n_shared = shared // block_size
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    need = (prior + chunk + block_size - 1) // block_size
+    tab = np.zeros((len(prior), int(need.max())), dtype=np.int32)
+    o = n_shared
+    for i, n in enumerate(need):
+        tab[i, :n_shared] = perm[:n_shared]
+        tab[i, n_shared:n] = perm[o:o + n - n_shared]
+        o += n - n_shared
+    return tab

@@ -272,7 +272,7 @@ def test_decode_zero_context_and_flags(decode_impl):
     ("prefill_small", (21, [1, 7, 33, 64, 16], [0, 5, 37, 100, 11], 48, 256)),
     ("prefill_noshare", (22, [20, 3, 48], [0, 16, 1], 0, 64)),
 ])
-def test_prefill_small(oracle_mod, dt, name, args):
+def test_prefill_small(oracle_mod, decode_impl, dt, name, args):
     c = C.make_prefill_case(*args, dt)
     out, err = run_prefill_gpu(c)
     assert err == 0
@@ -281,7 +281,18 @@ def test_prefill_small(oracle_mod, dt, name, args):
     assert max_abs_diff(out, golden(f"{name}_{dt}.npz")["out"], dt) <= PRODUCT_ATOL[dt]
 
 
-def test_prefill_config4_full(oracle_mod):
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_prefill_ragged_multi_tile(oracle_mod, decode_impl, dt):
+    """Chunks spanning several 128-query tiles with ragged ends, priors that
+    are not block aligned, and a one-token chunk behind them."""
+    c = C.make_prefill_case(23, [300, 129, 1, 257], [37, 0, 500, 1000], 32, 512, dt)
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_prefill_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+
+
+def test_prefill_config4_full(oracle_mod, decode_impl):
     c = C.make_c4_case()
     out, err = run_prefill_gpu(c)
     assert err == 0
