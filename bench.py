@@ -81,6 +81,21 @@ def traffic_from_profiles():
 
 # --------------------------------------------------------------- clock sampling
 
+def smi_ids(cuda_indices) -> str:
+    """nvidia-smi ids (UUIDs) of this process's CUDA devices, so the sampler
+    watches the GPUs the job runs on whatever CUDA_VISIBLE_DEVICES maps."""
+    import torch
+
+    ids = []
+    for i in cuda_indices:
+        try:
+            u = str(torch.cuda.get_device_properties(i).uuid)
+            ids.append(u if u.startswith("GPU-") else "GPU-" + u)
+        except Exception:  # noqa: BLE001 - fall back to the index
+            ids.append(str(i))
+    return ",".join(ids)
+
+
 class ClockSampler:
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -92,7 +107,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50", "-i", ",".join(str(i) for i in gpu_indices)],
+                 "-lms", "50", "-i", smi_ids(gpu_indices)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -163,7 +178,8 @@ def cpu_sample(seconds: float, n_seqs_subset: int | None = None, max_reps: int |
     qsl = np.arange(B + 1, dtype=np.int32)
     prior = (ctx - 1).astype(np.int32)
     bytes_per = W.decode_bytes(ctx) + W.append_bytes(B)
-    threads = oracle.num_threads()
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    threads = max(1, len(os.sched_getaffinity(0)))
     reps, t0 = 0, time.perf_counter()
     while True:
         oracle.reshape_and_cache(kp, vp, kn, vn, slots, "f16")
