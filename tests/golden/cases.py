@@ -225,3 +225,56 @@ def make_append_cow_case(seed: int = 2, n_seqs: int = 64, num_blocks: int = 4096
 def append_cow_digest(c) -> str:
     return digest(np.asarray(c["free_list"]), c["ctx"], c["forked"], c["k_pools"],
                   c["v_pools"], c["k_new"], c["v_new"])
+
+
+# --------------------------------------------------------------------------
+# end-to-end greedy decoding (BASELINE config 5 geometry, shortened runs)
+# --------------------------------------------------------------------------
+
+E2E_SEED = 5
+E2E_FINAL_NORM_SCALE = 4.0  # spreads the tied-embedding logits (well-separated argmax)
+E2E_VOCAB = 151936
+
+
+def e2e_scenarios():
+    """Two scheduler runs over the same seeded random-init Qwen2.5-0.5B weights.
+
+    "prefix": 4 requests sharing a 48-token prompt prefix, prefix cache on,
+    max_batched_tokens small enough that prompts are prefilled in chunks,
+    followed by a second turn of request 0 (its prompt + answer + new tokens)
+    that hits the radix cache.
+    "preempt": 3 requests on an 11-block pool with the prefix cache off, which
+    forces recompute preemption (the reference's test_scheduler.py:104-128
+    setup).
+    """
+    rng = np.random.default_rng(E2E_SEED)
+    shared = rng.integers(0, E2E_VOCAB, size=48).tolist()
+    prompts = [shared + rng.integers(0, E2E_VOCAB, size=n).tolist() for n in (22, 61, 103, 7)]
+    turn2_extra = rng.integers(0, E2E_VOCAB, size=19).tolist()
+    pre = [rng.integers(0, E2E_VOCAB, size=n).tolist() for n in (30, 41, 25)]
+    return {
+        "prefix": dict(num_blocks=256, max_num_seqs=4, max_batched_tokens=48, prefix_cache=True,
+                       prompts=prompts, max_new_tokens=12, turn2_extra=turn2_extra),
+        "preempt": dict(num_blocks=11, max_num_seqs=3, max_batched_tokens=64, prefix_cache=False,
+                        prompts=pre, max_new_tokens=48, turn2_extra=None),
+    }
+
+
+# --------------------------------------------------------------------------
+# scheduler decisions with a deterministic stand-in model (no attention)
+# --------------------------------------------------------------------------
+
+def fake_next_token(last_id: int, position: int) -> int:
+    """Deterministic 'greedy' token of the stand-in model used to compare
+    scheduling decisions: depends only on the last fed token and its position."""
+    return (last_id * 31 + position * 7) % 997 + 3
+
+
+def sched_scenario():
+    """Admission under a tight pool with the prefix cache on: shared prompt
+    prefixes, chunked prefill, radix eviction, preemption, a second turn."""
+    rng = np.random.default_rng(77)
+    shared = rng.integers(3, 1000, size=40).tolist()
+    prompts = [shared + rng.integers(3, 1000, size=n).tolist() for n in (9, 30, 55, 17, 70, 3)]
+    return dict(num_blocks=20, max_num_seqs=4, max_batched_tokens=40, prompts=prompts,
+                max_new_tokens=[20, 35, 12, 40, 25, 30], turn2=[0, 3])
