@@ -34,7 +34,7 @@ sys.path.insert(0, os.path.join(ROOT, "llm-inference-scheduler_b200"))
 
 METRIC = "paged decode attn KV GB/s (% of HBM peak) and decode tok/s at 1/2/4/8 B200"
 UNIT = "GB/s"
-WORKLOAD = ("config3: paged decode step, 24 layers x (append + decode attention), "
+WORKLOAD = ("config3: paged decode step, 24 layers x (append + decode attention, one fused call), "
             "B=256 seqs/GPU, ctx lognormal(median 1024, sigma 0.5) in [16,8192], 14q/2kv, d64, fp16 KV")
 FALLBACK_HBM_GBS = 6650.0
 
@@ -45,8 +45,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
-                    help="decode = BASELINE config 3 (headline); prefill = config 4")
+    ap.add_argument("--workload", choices=("decode", "prefill", "e2e"), default="decode",
+                    help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5")
+    ap.add_argument("--conversations", type=int, default=64, help="config 5: conversations")
+    ap.add_argument("--rate", type=float, default=40.0, help="config 5: Poisson arrivals per second")
+    ap.add_argument("--max-num-seqs", type=int, default=128)
+    ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
     ap.add_argument("--strong", action="store_true")
@@ -261,10 +265,10 @@ def run_ours(args):
     ws = ops.new_decode_workspace(B, 14, 64, dev)
     err = ops.new_error_flags(dev)
 
-    appends = [ops.bind_reshape_and_cache(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], slots, err)
+    # one call per layer: the decode kernel appends the new token itself
+    decodes = [ops.bind_paged_decode_append_attention(q[l], kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
+                                                      tabs, ctx_d, scale, ws, out[l], err)
                for l in range(L)]
-    decodes = [ops.bind_paged_decode_attention(q[l], mgr.k_pool[l], mgr.v_pool[l], tabs, ctx_d, scale,
-                                               ws, out[l], err) for l in range(L)]
 
     dec_bytes = W.decode_bytes(ctx)
     app_bytes = W.append_bytes(B)
@@ -272,7 +276,6 @@ def run_ours(args):
 
     def step(ev=None):
         for layer in range(L):
-            appends[layer]()
             if ev is not None:
                 ev[layer][0].record()
             decodes[layer]()
@@ -369,7 +372,7 @@ def run_ours(args):
         return
 
     peak, peak_kind = peaks()
-    achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+    achieved = (dec_bytes + app_bytes) / (dec_ms * 1e-3) / 1e9
     clocks = sampler.summary(t_wall0, t_wall1) if sampler else None
     line = {
         "metric": METRIC,
@@ -393,12 +396,12 @@ def run_ours(args):
         "roofline": {"kernel": "paged_decode_kernel<half>", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic_from_profiles(), "bytes_per_launch": dec_bytes,
+                     "traffic": traffic_from_profiles(), "bytes_per_launch": dec_bytes + app_bytes,
                      "avg_launch_ms": round(dec_ms, 5)},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4), "api": "PagedKVCache.prepare_step + forward_layer"},
-        "gpu_launches": 2 * L * args.steps,
+        "gpu_launches": 2 * L * args.steps,  # decode kernel + split-K merge per layer
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:
@@ -541,8 +544,94 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def run_e2e(args):
+    """continuous-batching greedy decoding of a random-init
+    Qwen2.5-0.5B-shaped model (fp16) with the paged-KV path, fed by Poisson
+    arrivals of two-turn conversations: prompts of random token ids, 64-512
+    tokens sharing a 48-token prefix, 128 output tokens per turn; turn two
+    (prompt + answer + 16-64 new tokens) arrives when turn one finishes."""
+    import numpy as np
+    import torch
+
+    from pagedkv import BlockManager
+    from pagedkv.model import PagedQwen2Model, Qwen2Config, random_weights
+    from pagedkv.scheduler import Request, Scheduler
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    rank = int(os.environ.get("RANK", "0"))
+    cfg = Qwen2Config()
+    model = PagedQwen2Model(cfg, random_weights(cfg, seed=5, final_norm_scale=4.0), device="cuda",
+                            dtype=torch.float16)
+    rng = np.random.default_rng(50 + rank)
+    V = cfg.vocab_size
+    shared = rng.integers(0, V, size=48).tolist()
+    n = args.conversations
+    prompts = [shared + rng.integers(0, V, size=int(rng.integers(16, 465))).tolist() for _ in range(n)]
+    extra = [rng.integers(0, V, size=int(rng.integers(16, 65))).tolist() for _ in range(n)]
+    gaps = rng.exponential(1.0 / args.rate, size=n)
+    arrivals = np.cumsum(gaps) - gaps[0]
+    out_len = 128
+    num_blocks = 24000  # 4.7 GB of fp16 KV for 24 layers
+    mgr = BlockManager(num_blocks, 16, cfg.num_hidden_layers, 2, 64, device="cuda", dtype=torch.float16)
+    sched = Scheduler(model, mgr, max_num_seqs=args.max_num_seqs,
+                      max_batched_tokens=args.max_batched_tokens, enable_prefix_cache=True,
+                      eos_ids=set())
+
+    def drive(n_conv, arr):
+        pending = list(range(n_conv))
+        reqs, turn2 = {}, {}
+        t0 = time.perf_counter()
+        while pending or sched.has_work:
+            now = time.perf_counter() - t0
+            while pending and arr[pending[0]] <= now:
+                i = pending.pop(0)
+                reqs[i] = Request(i, list(prompts[i]), max_new_tokens=out_len)
+                sched.add_request(reqs[i])
+            if not sched.has_work:
+                time.sleep(min(1e-3, max(0.0, arr[pending[0]] - now)))
+                continue
+            sched.step()
+            for i, r in list(reqs.items()):
+                if r.finish_reason and i not in turn2:
+                    turn2[i] = Request(n_conv + i, r.prompt_ids + r.output_ids + extra[i],
+                                       max_new_tokens=out_len)
+                    sched.add_request(turn2[i])
+        torch.cuda.synchronize()
+        return time.perf_counter() - t0, list(reqs.values()) + list(turn2.values())
+
+    drive(min(4, n), np.zeros(n))  # warm-up: rope tables, TMA descriptors, allocator
+    sched.radix.evict(num_blocks)   # forget the warm-up prefixes
+    for k in list(sched.metrics):
+        sched.metrics[k] = 0
+    wall, done = drive(n, arrivals)
+    mgr.check_errors()
+    gen = sum(len(r.output_ids) for r in done)
+    ttft = [r.first_token_at - r.arrived_at for r in done]
+    itl = [(r.finished_at - r.first_token_at) / max(1, len(r.output_ids) - 1) for r in done]
+    pct = lambda xs, q: round(1e3 * float(np.percentile(xs, q)), 2)  # noqa: E731
+    line = {
+        "metric": "end-to-end continuous-batching decode tok/s (config 5)",
+        "value": round(gen / wall, 1), "unit": "tok/s", "n_gpus": 1, "steps": sched.metrics["steps"],
+        "warmup": 1, "ms_per_step": round(1e3 * wall / max(1, sched.metrics["steps"]), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: random-init Qwen2.5-0.5B-shaped weights (seed 5), random token-id prompts",
+        "config": {"workload": "config5: Poisson arrivals of 2-turn conversations, prompts 64-512 "
+                               "tokens with a shared 48-token prefix, 128 greedy output tokens/turn",
+                   "conversations": n, "rate_per_s": args.rate, "max_num_seqs": args.max_num_seqs,
+                   "max_batched_tokens": args.max_batched_tokens, "num_blocks": num_blocks},
+        "generated_tokens": gen, "wall_s": round(wall, 3),
+        "ttft_ms": {"p50": pct(ttft, 50), "p99": pct(ttft, 99)},
+        "itl_ms": {"p50": pct(itl, 50), "p99": pct(itl, 99)},
+        "scheduler": dict(sched.metrics),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "e2e" and args.impl == "ours":
+        run_e2e(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "prefill":

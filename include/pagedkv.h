@@ -128,6 +128,28 @@ int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
                                int* err_flags, pkv_stream_t stream);
 
 /*
+ * Decode step of one layer in one call: append + paged decode attention.
+ * Replaces PagedKVCache.append_and_fetch (block_manager.py:111-141: scatter,
+ * length update, gather) followed by Qwen2Model._attention with num_new == 1
+ * (qwen2.py:98-128).  For every sequence s with context_lens[s] >= 1, the
+ * new token's K and V rows (k_new[s], v_new[s]: [n_seqs][n_kv_heads][head_dim]
+ * with the given row strides) are written to position context_lens[s] - 1 of
+ * the sequence, the slot taken from block_tables[s]; then out[s] is the
+ * attention over context_lens[s] tokens as in pkv_paged_decode_attention.
+ * The tensor-core kernel performs the append itself (one launch plus the
+ * split-K merge); other shapes run a separate append kernel first.
+ */
+int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const void* q,
+                                      int64_t q_row_stride, const void* k_new, const void* v_new,
+                                      int64_t k_new_row_stride, int64_t v_new_row_stride,
+                                      void* k_pool, void* v_pool, int num_blocks,
+                                      const int32_t* block_tables, int64_t block_table_stride,
+                                      int max_blocks_per_seq, const int32_t* context_lens,
+                                      int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                      int block_size, float scale, int dtype, void* workspace,
+                                      size_t workspace_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
  * Paged decode attention for callers that cannot allocate device memory.
  * No counterpart in the reference.  Some hosts of this library cannot call
  * cudaMalloc (or any allocating routine) at the point where they run decode

@@ -106,6 +106,58 @@ cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_str
   return cudaGetLastError();
 }
 
+// Append one token per sequence at position context_lens[s] - 1, the slot
+// taken from the sequence's block table (the decode step's append; used when
+// the fused decode kernel does not serve the shape).  One warp per sequence.
+template <typename E>
+__global__ void __launch_bounds__(256) append_at_context_end(
+    const E* __restrict__ k, const E* __restrict__ v, int64_t k_stride, int64_t v_stride,
+    E* __restrict__ k_pool, E* __restrict__ v_pool, const int32_t* __restrict__ tables,
+    int64_t bt_stride, int max_blocks, const int32_t* __restrict__ context_lens, int n_seqs,
+    int num_blocks, int block_size, int row_elems, int* err) {
+  const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= n_seqs) return;
+  const int ctx = context_lens[s];
+  if (ctx <= 0) return;
+  if (ctx > max_blocks * block_size) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+    return;
+  }
+  const int blk = tables[static_cast<int64_t>(s) * bt_stride + (ctx - 1) / block_size];
+  if (blk < 0 || blk >= num_blocks) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t row = static_cast<int64_t>(blk) * block_size + (ctx - 1) % block_size;
+  for (int i = lane; i < row_elems; i += 32) {
+    k_pool[row * row_elems + i] = k[s * k_stride + i];
+    v_pool[row * row_elems + i] = v[s * v_stride + i];
+  }
+}
+
+cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k_stride,
+                                         int64_t v_stride, void* k_pool, void* v_pool,
+                                         const int32_t* tables, int64_t bt_stride, int max_blocks,
+                                         const int32_t* context_lens, int n_seqs, int num_blocks,
+                                         int block_size, int n_kv_heads, int head_dim, int esize,
+                                         int* err, cudaStream_t stream) {
+  if (n_seqs == 0) return cudaSuccess;
+  const int grid = (n_seqs + 7) / 8;
+  const int row = n_kv_heads * head_dim;
+  if (esize == 4)
+    append_at_context_end<uint32_t><<<grid, 256, 0, stream>>>(
+        static_cast<const uint32_t*>(k), static_cast<const uint32_t*>(v), k_stride, v_stride,
+        static_cast<uint32_t*>(k_pool), static_cast<uint32_t*>(v_pool), tables, bt_stride,
+        max_blocks, context_lens, n_seqs, num_blocks, block_size, row, err);
+  else
+    append_at_context_end<uint16_t><<<grid, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), k_stride, v_stride,
+        static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool), tables, bt_stride,
+        max_blocks, context_lens, n_seqs, num_blocks, block_size, row, err);
+  return cudaGetLastError();
+}
+
 // Copy: CTA (pair p, layer l) copies K block then V block of that layer.
 // Reference: BlockManager.copy_block, mini_engine/paged/block_manager.py:65-71.
 __global__ void __launch_bounds__(256) copy_blocks_vec16(char* __restrict__ k_pools,

@@ -69,6 +69,12 @@ struct DecodeParams {
   float* part_ml;  // [2*kDecMaxCtas][ml_stride]: (m, l) per query head
   int ml_stride;   // floats per slot: 2*n_q_heads rounded up to 4 (16 bytes)
   int* err;
+  // fused append: token context_lens[s] - 1 of sequence s (NULL = none)
+  const uint8_t* k_new;
+  const uint8_t* v_new;
+  int64_t k_new_stride_b, v_new_stride_b;  // bytes between rows
+  uint8_t* k_pool;
+  uint8_t* v_pool;
 };
 
 size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
@@ -81,6 +87,9 @@ size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
 bool decode_fast_supported(const AttnArgs& a) {
   const int G = a.n_q_heads / a.n_kv_heads;
   auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
+  if (a.k_new != nullptr &&
+      (!al(a.k_new, 16) || !al(a.v_new, 16) || (a.k_new_stride * 2) % 16 || (a.v_new_stride * 2) % 16))
+    return false;
   return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
          a.block_size == 16 && (a.n_kv_heads == 1 || a.n_kv_heads == 2 || a.n_kv_heads == 4) &&
          G <= 8 && a.n_q_heads <= 32 && a.n_seqs <= kDecMaxSeqs && (a.q_stride % 2) == 0 &&
@@ -221,22 +230,50 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     for (int b0 = r0; b0 < r1; b0 += 32) {
       const int gb = b0 + lane;
       int id = 0;
+      int app_seq = -1, app_row = 0;  // fused append: this block holds seq's newest token
       if (gb < r1) {
         const int s = find_seq(prefix, B, gb);
         const int jb = gb - prefix[s];
         id = __ldg(p.block_tables + static_cast<int64_t>(s) * p.bt_stride + jb);
         if (id < 0 || id >= p.num_blocks) {
           raise_flag(p.err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
-          id = 0;
+          id = 0;  // read a valid block; never write through a bad id
+        } else if (p.k_new != nullptr && gb == prefix[s + 1] - 1) {
+          app_seq = s;
+          app_row = id * 16 + ((ctxs[s] - 1) & 15);
         }
       }
       if (!waited) {
+        // warm L2 with the first stages' K/V while the preceding kernel ends
+        if (gb < r1 && lane < kDecStages) {
+          prefetch_l2(p.k_pool + static_cast<int64_t>(id) * (nkv * kDecTile), nkv * kDecTile);
+          prefetch_l2(p.v_pool + static_cast<int64_t>(id) * (nkv * kDecTile), nkv * kDecTile);
+        }
         pdl_wait();  // the pool may still be written by the preceding kernel
         waited = true;
       }
       const int n = min(32, r1 - b0);
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
+        const int a_seq = __shfl_sync(0xffffffffu, app_seq, k);
+        if (a_seq >= 0) {
+          // append before the block is loaded: the warp copies the K and V
+          // rows (nkv*128 bytes each) into the pool, then orders those
+          // generic-proxy writes before lane 0's TMA read of the block
+          const int row = __shfl_sync(0xffffffffu, app_row, k);
+          constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
+          for (int v = lane; v < 2 * row_vecs; v += 32) {
+            const bool is_v = v >= row_vecs;
+            const int vi = is_v ? v - row_vecs : v;
+            const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
+                                       : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
+            uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
+            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
+          }
+          fence_proxy_async_global();
+          __syncwarp();
+          if (lane == 0) fence_proxy_async_global();
+        }
         if (lane == 0 && !dead) {
           const int st = i % kDecStages;
           if (!mbar_wait(&empty_bar[st], ((i / kDecStages) & 1) ^ 1)) {
@@ -620,6 +657,12 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float*>(ws + parts_o);
   p.err = a.err;
+  p.k_new = static_cast<const uint8_t*>(a.k_new);
+  p.v_new = static_cast<const uint8_t*>(a.v_new);
+  p.k_new_stride_b = a.k_new_stride * 2;
+  p.v_new_stride_b = a.v_new_stride * 2;
+  p.k_pool = static_cast<uint8_t*>(const_cast<void*>(a.k_pool));
+  p.v_pool = static_cast<uint8_t*>(const_cast<void*>(a.v_pool));
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -35,6 +35,12 @@ struct AttnArgs {
   float scale;
   int dtype;
   int* err;
+  // decode only: the new token of each sequence, written by the decode
+  // kernel at position context_lens[s] - 1 before it is read (NULL = none)
+  const void* k_new = nullptr;
+  const void* v_new = nullptr;
+  int64_t k_new_stride = 0;  // elements between rows
+  int64_t v_new_stride = 0;
 };
 
 cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_stride,
@@ -42,6 +48,13 @@ cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_str
                                      const int64_t* slots, int n_tokens, int num_blocks,
                                      int block_size, int n_kv_heads, int head_dim, int esize,
                                      int* err, cudaStream_t stream);
+
+cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k_stride,
+                                         int64_t v_stride, void* k_pool, void* v_pool,
+                                         const int32_t* tables, int64_t bt_stride, int max_blocks,
+                                         const int32_t* context_lens, int n_seqs, int num_blocks,
+                                         int block_size, int n_kv_heads, int head_dim, int esize,
+                                         int* err, cudaStream_t stream);
 
 cudaError_t launch_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride, int n_layers,
                                const int32_t* pairs, int n_pairs, int num_blocks,

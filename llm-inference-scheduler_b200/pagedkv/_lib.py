@@ -49,6 +49,9 @@ SIGNATURES = {
     "pkv_paged_prefill_attention": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _P, _I,
                                          _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "pkv_set_decode_impl": (_I, [_I]),
+    "pkv_paged_decode_append_attention": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I, _P,
+                                               _I64, _I, _P, _I, _I, _I, _I, _I, _F, _I, _P, _SZ,
+                                               _P, _P]),
     "pkv_paged_decode_attention_noalloc": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _I,
                                                 _I, _I, _I, _I, _F, _I, _P, _P]),
 }

@@ -25,8 +25,9 @@ What differs, and why:
   batched copy equals the reference's sequential one.
 * The hot path is batched: `prepare_step` builds the step's device metadata
   (slot mapping, block tables, context lengths, query offsets) once per step
-  with one host-to-device copy, and `forward_layer` runs one append launch
-  plus at most one decode and one prefill attention launch per layer,
+  with one host-to-device copy, and `forward_layer` runs one fused
+  append + decode-attention call for the leading one-token sequences and one
+  append + one chunked-prefill launch for the rest,
   replacing the per-sequence append_and_fetch + gather + _attention loop of
   mini_engine/model/qwen2.py:158-166.  `append_and_fetch` keeps the
   reference's contract (gathered K/V) for callers that still attend
@@ -318,17 +319,19 @@ class PagedKVCache:
         without moving the lengths (benchmarks re-running one step)."""
         mgr = self.mgr
         mgr.flush_copies()
-        ops.reshape_and_cache(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer], meta.slot_mapping,
-                              mgr.err)
         if out is None:
             out = torch.empty((meta.n_tokens,) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
         nd = meta.n_decode
         if nd:
+            # decode sequences: append fused into the decode kernel
             ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
-            ops.paged_decode_attention(q[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
-                                       meta.block_tables[:nd], meta.context_lens[:nd], scale,
-                                       workspace=ws, out=out[:nd], err=mgr.err)
+            ops.paged_decode_append_attention(q[:nd], k_new[:nd], v_new[:nd], mgr.k_pool[layer],
+                                              mgr.v_pool[layer], meta.block_tables[:nd],
+                                              meta.context_lens[:nd], scale, workspace=ws,
+                                              out=out[:nd], err=mgr.err)
         if nd < meta.n_seqs:
+            ops.reshape_and_cache(k_new[nd:], v_new[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
+                                  meta.slot_mapping[nd:], mgr.err)
             ops.paged_prefill_attention(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
                                         meta.block_tables[nd:], meta.query_start_loc,
                                         meta.num_prior_dev[nd:], meta.max_query_len, scale,

@@ -162,6 +162,41 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     return out
 
 
+def _decode_append_args(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens, scale,
+                        workspace, out, err):
+    args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out,
+                             err)
+    _cuda(k_new, "k_new"), _cuda(v_new, "v_new")
+    nb, bs, hkv, d = k_pool.shape
+    B = q.shape[0]
+    if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+        raise TypeError("pagedkv: k_new / v_new must have the pool dtype")
+    if k_new.shape[0] < B or v_new.shape[0] < B or tuple(k_new.shape[1:]) != (hkv, d) \
+            or tuple(v_new.shape[1:]) != (hkv, d):
+        raise ValueError("pagedkv: k_new / v_new must be [n_seqs, n_kv_heads, head_dim]")
+    # decode-call argument order with the new rows inserted after q
+    args = args[:4] + (k_new.data_ptr(), v_new.data_ptr(), _row_stride(k_new, "k_new"),
+                       _row_stride(v_new, "v_new")) + args[4:]
+    return args, out
+
+
+def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                                  k_pool: torch.Tensor, v_pool: torch.Tensor,
+                                  block_tables: torch.Tensor, context_lens: torch.Tensor,
+                                  scale: float, workspace: torch.Tensor | None = None,
+                                  out: torch.Tensor | None = None,
+                                  err: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of one layer: write k_new[s] / v_new[s] at position
+    context_lens[s] - 1 of sequence s (slot from its block table), then the
+    paged attention over context_lens[s] tokens.  Reference:
+    PagedKVCache.append_and_fetch + Qwen2Model._attention (num_new == 1)."""
+    args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
+                                    scale, workspace, out, err)
+    _lib.check(_lib.load().pkv_paged_decode_append_attention(*args),
+               "pkv_paged_decode_append_attention")
+    return out
+
+
 class BoundLaunch:
     """A validated launch with its C-ABI arguments fixed (pointers, sizes and
     the stream that was current when it was bound).  Calling it re-issues the
@@ -189,6 +224,16 @@ def bind_paged_decode_attention(q, k_pool, v_pool, block_tables, context_lens, s
     args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err)
     return BoundLaunch(_lib.load().pkv_paged_decode_attention, args, "pkv_paged_decode_attention",
                        (q, k_pool, v_pool, block_tables, context_lens, workspace, out, err))
+
+
+def bind_paged_decode_append_attention(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
+                                       scale, workspace, out, err=None) -> BoundLaunch:
+    args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
+                                    scale, workspace, out, err)
+    return BoundLaunch(_lib.load().pkv_paged_decode_append_attention, args,
+                       "pkv_paged_decode_append_attention",
+                       (q, k_new, v_new, k_pool, v_pool, block_tables, context_lens, workspace, out,
+                        err))
 
 
 def _prefill_args(q, k_pool, v_pool, block_tables, query_start_loc, num_prior, max_query_len,

@@ -129,3 +129,18 @@ def test_set_decode_impl_validation():
     L = _lib.load()
     assert L.pkv_set_decode_impl(5) == _lib.ERR_UNSUPPORTED
     assert L.pkv_set_decode_impl(_lib.DECODE_AUTO) == 0
+
+
+def test_decode_append_validation():
+    f = _lib.load().pkv_paged_decode_append_attention
+    base = [FAKE, 896, FAKE, 896, FAKE, FAKE, 128, 128, FAKE, FAKE, 64, FAKE, 8, 8, FAKE, 4, 14, 2,
+            64, 16, 0.125, 1, FAKE, 1 << 30, None, None]
+    a = list(base)
+    a[4] = None  # k_new
+    assert f(*a) == _lib.ERR_NULL_POINTER
+    a = list(base)
+    a[6] = 64  # k_new row stride below n_kv_heads * head_dim
+    assert f(*a) == _lib.ERR_BAD_SHAPE
+    a = list(base)
+    a[15] = 0  # no sequences: nothing to do
+    assert f(*a) == 0

@@ -208,6 +208,31 @@ def test_decode_config3_full(oracle_mod, decode_impl, dt):
         assert max_abs_diff(out, golden("decode_c3_f16.npz")["out"], dt) <= PRODUCT_ATOL[dt]
 
 
+@pytest.mark.parametrize("name,dt,make", [
+    ("c1", "f32", lambda: C.make_decode_case(1, 8, 32, 600, 512, "f32")),
+    ("c1", "bf16", lambda: C.make_decode_case(1, 8, 32, 600, 512, "bf16")),
+    ("edge", "f16", lambda: C.make_decode_case(11, 9, 0, 0, 128, "f16",
+                                              ctx_list=[1, 2, 15, 16, 17, 31, 32, 33, 600])),
+    ("c3", "f16", lambda: C.make_decode_case(3, 256, 16, 8192, 0, "f16", lognormal_median=1024.0,
+                                            pool_slack=1.1)),
+])
+def test_decode_append_fused_matches_oracle(oracle_mod, decode_impl, name, dt, make):
+    """pkv_paged_decode_append_attention: the decode kernel writes the new
+    token itself (slot from the block table); the pools must equal the
+    oracle's bit for bit and the output match within tolerance."""
+    c = make()
+    kp, vp = dev(c["k_pool"], dt), dev(c["v_pool"], dt)
+    err = ops.new_error_flags("cuda")
+    out = ops.paged_decode_append_attention(dev(c["q"], dt), dev(c["k_new"], dt), dev(c["v_new"], dt),
+                                            kp, vp, dev(C.pad_tables(c["tables"])),
+                                            dev(c["ctx"].astype(np.int32)), 0.125, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref, ref_k, ref_v = oracle_mod.run_decode_case(c)
+    assert np.array_equal(host(kp, dt), ref_k) and np.array_equal(host(vp, dt), ref_v)
+    assert max_abs_diff(host(out, dt), ref, dt) <= PRODUCT_ATOL[dt]
+
+
 def test_decode_many_short_and_long(oracle_mod, decode_impl):
     """Ragged batch: many 1-block sequences around a few very long ones, so
     the stream-K ranges split sequences at every kind of boundary."""
