@@ -7,22 +7,41 @@
 // blocks (shared radix-cache blocks included) read in place through the
 // block table.
 //
-// One CTA per (sequence, query head, tile of 128 queries); 6 warps:
-//  * warps 0-3 (softmax): thread r owns query row r.  It reads its row of
-//    S = Q K^T from TMEM (tcgen05.ld), applies the scale, the causal mask and
-//    an online softmax in the exp2 domain, writes P (fp16/bf16) into a
-//    128-byte-swizzled shared tile, and at the end reads O from TMEM,
-//    normalises and stores it.  O is rescaled in TMEM only when the running
-//    maximum grows by more than 8 (2^8 bounds P), so rescaling is rare.
-//  * warp 4 (producer): TMA tensor loads of the Q tile (once) and, per key
-//    tile of 128 keys (8 blocks), the K and V blocks into a 3-stage ring;
+// One CTA per (sequence, query head, pair of 128-query tiles A and B); the two
+// tiles share every K/V tile the CTA loads.  10 warps:
+//  * warps 0-3 / 4-7 (softmax of tile A / tile B): thread r of a group owns
+//    query row r of its tile.  It reads its row of S = Q K^T from TMEM
+//    (tcgen05.ld), applies the causal mask and an online softmax in the exp2
+//    domain, writes its row of P (fp16/bf16 pairs) back into TMEM
+//    (tcgen05.st), and at the end reads O from TMEM, normalises and stores it.
+//    O is rescaled in TMEM only when the running maximum grows by more than 8
+//    (2^8 bounds P), so rescaling is rare.  The two groups run side by side
+//    (two warps per SM sub-partition), so one group's exponentials overlap
+//    the other's tensor-memory traffic and barrier waits.
+//  * warp 8 (producer): TMA tensor loads of the two Q tiles (once) and, per
+//    key tile of 128 keys (8 blocks), the K and V blocks into a 4-stage ring;
 //    blocks past the visible keys are fetched from an out-of-range coordinate
 //    and arrive as zeros.
-//  * warp 5 (MMA): allocates 512 TMEM columns (S double buffer 2 x 128,
-//    O 64) and one thread issues tcgen05.mma kind::f16 (M=128):
-//    S_j = Q K_j^T (N=128, K=64, both K-major), O += P_j V_j (N=64, K=128;
-//    V is the MN-major B operand), committing to mbarriers.  S_{j+1} is issued
-//    before waiting for P_j, so QK^T overlaps the softmax.
+//  * warp 9 (MMA): allocates all 512 TMEM columns (S_A, S_B: 128 fp32 each;
+//    O_A, O_B: 64 fp32 each; P_A, P_B: 64 columns of fp16/bf16 pairs each)
+//    and one thread issues tcgen05.mma kind::f16 (M=128):
+//    S_x = Q_x K_j^T (N=128, K=64, both K-major, from shared memory) and
+//    O_x += P_x V_j (N=64, K=128; A = P_x from tensor memory, B = V the
+//    MN-major shared operand), committing to mbarriers.  S_x of key tile j+1
+//    is issued as soon as the softmax holds S_x of tile j in registers, so
+//    QK^T overlaps the exponentials.  Keeping P in tensor memory halves the
+//    shared-memory traffic of a key tile (no P stores, no P operand reads).
+// Tile B of a CTA may need one key tile more than tile A (its last rows see
+// 128 more keys); that tile is loaded once and only B computes on it.
+//
+// CTA order.  Work items differ in length by up to the whole context, and one
+// CTA fills an SM, so the grid is mapped longest-first: blockIdx.x enumerates
+// sequences by decreasing (prior + new) length, then the later query pair of a
+// sequence, then the head.  The hardware dispatches CTAs in blockIdx order as
+// SMs free up, which makes this a longest-processing-time list schedule.  The
+// rank is computed by every CTA from num_prior / query_start_loc (up to
+// kPfOrderMaxSeqs sequences; natural order beyond).
+//
 // Every wait is bounded; on a timeout the kernel flags PKV_FLAG_PIPELINE_TIMEOUT,
 // stops waiting and still frees its tensor memory.
 #include <float.h>
@@ -35,21 +54,29 @@
 
 namespace pkv {
 
-constexpr int kPfM = 128;                 // query rows per CTA
+constexpr int kPfM = 128;                 // query rows per tile
+constexpr int kPfPair = 2 * kPfM;         // query rows per CTA (tiles A and B)
 constexpr int kPfN = 128;                 // keys per tile (8 blocks of 16)
-constexpr int kPfStages = 3;              // K/V ring depth
+constexpr int kPfStages = 4;              // K/V ring depth
 constexpr int kPfTile = 128 * 64 * 2;     // 16 KB: 128 rows x 64 dims x 2 bytes
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 320;
+constexpr int kPfProducerWarp = 8;
+constexpr int kPfMmaWarp = 9;
 constexpr uint32_t kPfTmemCols = 512;
+constexpr int kPfOrderMaxSeqs = 64;
+
+// tensor-memory columns: S_A, S_B (fp32), O_A, O_B (fp32), P_A, P_B (fp16/bf16 pairs)
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
 
 // shared-memory offsets from the 1024-byte aligned base
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kPfTile;
+constexpr int kOffQ = 0;                               // Q_A, Q_B
+constexpr int kOffK = kOffQ + 2 * kPfTile;
 constexpr int kOffV = kOffK + kPfStages * kPfTile;
-constexpr int kOffP = kOffV + kPfStages * kPfTile;   // 2 buffers x (2 sub-tiles x 16 KB)
-constexpr int kOffBar = kOffP + 2 * 2 * kPfTile;
-constexpr int kNumBars = 1 + 2 * kPfStages + 2 + 2 + 2 + 2;
-constexpr int kPfSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
+constexpr int kOffBar = kOffV + kPfStages * kPfTile;
+constexpr int kNumBars = 1 + 2 * kPfStages + 4 * 2;
+constexpr int kOffSched = kOffBar + kNumBars * 8;      // tmem slot, work item, length keys
+constexpr int kSchedInts = 4 + kPfOrderMaxSeqs;
+constexpr int kPfSmemBytes = 1024 + kOffSched + kSchedInts * 4;
 
 struct PrefillParams {
   void* out;
@@ -61,6 +88,10 @@ struct PrefillParams {
   const int32_t* num_prior;
   int num_blocks;
   int n_tokens;
+  int n_seqs;
+  int n_q_heads;
+  int n_pairs;         // query pairs per sequence in the grid: ceil(max_query_len / 256)
+  int order_by_length;
   int group;
   float scale_log2;
   int* err;
@@ -72,30 +103,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                             const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
-  const int qt = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  const int q_begin = p.qsl[s];
-  const int n_new = p.qsl[s + 1] - q_begin;
-  const int q0 = qt * kPfM;
-  if (qt == static_cast<int>(gridDim.x) - 1 && n_new > static_cast<int>(gridDim.x) * kPfM && tid == 0)
-    raise_flag(p.err, PKV_FLAG_BAD_QUERY_LAYOUT);  // max_query_len below a chunk length
-  if (q_begin < 0 || n_new < 0 || q_begin + n_new > p.n_tokens) {
-    if (qt == 0 && h == 0 && tid == 0) raise_flag(p.err, PKV_FLAG_BAD_QUERY_LAYOUT);
-    return;
-  }
-  if (n_new == 0 || q0 >= n_new) return;  // uniform: before any barrier or allocation
-  const int prior = max(p.num_prior[s], 0);
-  const int rows = min(kPfM, n_new - q0);
-  int kv_len = prior + q0 + rows;  // keys visible to this tile's last row
-  const int cap = p.max_blocks * 16;
-  if (kv_len > cap) {
-    if (tid == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
-    kv_len = cap;
-  }
-  const int n_tiles = (kv_len + kPfN - 1) / kPfN;
-  const int nb_needed = (kv_len + 15) >> 4;
-  const int g = h / p.group;
 
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -103,14 +111,41 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + kPfStages;
-  uint64_t* s_full = kv_empty + kPfStages;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_done = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  uint64_t* s_full = kv_empty + kPfStages;  // [tile]: S_x of the current key tile is in TMEM
+  uint64_t* s_empty = s_full + 2;           // [tile]: the softmax holds S_x in registers
+  uint64_t* p_full = s_empty + 2;           // [tile]: P_x is in tensor memory
+  uint64_t* o_done = p_full + 2;            // [tile]: O_x += P_x V has completed
+  int* sched = reinterpret_cast<int*>(base + kOffSched);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sched);
   const uint32_t sbase = smem_u32(base);
 
-  if (tid == 0) {
+  // ---- work item of this CTA (warp 0), barriers (warp 1), TMEM (MMA warp)
+  if (warp == 0) {
+    const int per_seq = p.n_pairs * p.n_q_heads;
+    const int rho = static_cast<int>(blockIdx.x) / per_seq;
+    const int rem = static_cast<int>(blockIdx.x) - rho * per_seq;
+    if (lane == 0) {
+      sched[1] = rho;
+      sched[2] = p.n_pairs - 1 - rem / p.n_q_heads;
+      sched[3] = rem % p.n_q_heads;
+    }
+    if (p.order_by_length) {
+      // rank of sequence t: how many sequences are longer, ties by index
+      int* keys = sched + 4;
+      for (int t = lane; t < p.n_seqs; t += 32)
+        keys[t] = max(p.num_prior[t], 0) + (p.qsl[t + 1] - p.qsl[t]);
+      __syncwarp();
+      for (int t = lane; t < p.n_seqs; t += 32) {
+        const int kt = keys[t];
+        int rank = 0;
+        for (int u = 0; u < p.n_seqs; ++u) {
+          const int ku = keys[u];
+          rank += (ku > kt) || (ku == kt && u < t);
+        }
+        if (rank == rho) sched[1] = t;  // ranks are a permutation: one writer
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < kPfStages; ++i) {
       mbar_init(&kv_full[i], 1);
@@ -123,25 +158,59 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
+  } else if (warp == kPfMmaWarp) {
+    tmem_alloc(tmem_slot, kPfTmemCols);
   }
-  if (warp == 5) tmem_alloc(tmem_slot, kPfTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t t_o = tbase + 256;
+  const int s = sched[1], qp = sched[2], h = sched[3];
 
-  if (warp == 4) {
+  const int q_begin = p.qsl[s];
+  const int n_new = p.qsl[s + 1] - q_begin;
+  const int q0 = qp * kPfPair;
+  bool skip = false;
+  if (qp == p.n_pairs - 1 && h == 0 && n_new > p.n_pairs * kPfPair && tid == 0)
+    raise_flag(p.err, PKV_FLAG_BAD_QUERY_LAYOUT);  // max_query_len below a chunk length
+  if (q_begin < 0 || n_new < 0 || q_begin + n_new > p.n_tokens) {
+    if (qp == 0 && h == 0 && tid == 0) raise_flag(p.err, PKV_FLAG_BAD_QUERY_LAYOUT);
+    skip = true;
+  }
+  if (skip || n_new == 0 || q0 >= n_new) {  // uniform over the CTA
+    if (warp == kPfMmaWarp) tmem_dealloc(tbase, kPfTmemCols);
+    return;
+  }
+  const int prior = max(p.num_prior[s], 0);
+  const int cap = p.max_blocks * 16;
+  // tile x covers queries q0 + 128 x ...; kv[x] keys are visible to its last row
+  int rows[2], kv[2], nt[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    rows[x] = min(max(n_new - (q0 + x * kPfM), 0), kPfM);
+    kv[x] = rows[x] > 0 ? prior + q0 + x * kPfM + rows[x] : 0;
+    if (kv[x] > cap) {
+      if (tid == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+      kv[x] = cap;
+    }
+    nt[x] = (kv[x] + kPfN - 1) / kPfN;
+  }
+  const int n_kv_tiles = max(nt[0], nt[1]);
+  const int nb_needed = (max(kv[0], kv[1]) + 15) >> 4;
+  const int g = h / p.group;
+
+  if (warp == kPfProducerWarp) {
     // ======================= producer =======================
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(q_full, kPfTile);
+      mbar_arrive_expect_tx(q_full, rows[1] > 0 ? 2 * kPfTile : kPfTile);
       tma_load_3d(base + kOffQ, &qmap, q_full, 0, h, q_begin + q0);
+      if (rows[1] > 0) tma_load_3d(base + kOffQ + kPfTile, &qmap, q_full, 0, h, q_begin + q0 + kPfM);
     }
     bool dead = false;
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < n_kv_tiles; ++j) {
       int tok = p.num_blocks * 16;  // out of range: TMA fills zeros
       if (lane < 8) {
         const int jb = j * 8 + lane;
@@ -174,77 +243,115 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kPfMmaWarp) {
     // ======================= MMA issuer (one thread) =======================
     if (lane == 0) {
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_s = mma_idesc_f16(fmt, 0, 0, kPfN, kPfM);
       constexpr uint32_t idesc_o = mma_idesc_f16(fmt, 0, 1, 64, kPfM);
       bool dead = !mbar_wait(q_full, 0);
-      auto issue_qk = [&](int j) {
-        const int st = j % kPfStages, sb = j & 1;
-        if (!dead && !mbar_wait(&kv_full[st], (j / kPfStages) & 1)) dead = true;
-        if (!dead && !mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1)) dead = true;
-        if (dead) return;
+      auto issue_qk = [&](int x, int j) {
         tc_fence_after();
-        const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + st * kPfTile;
+        const uint32_t qa = sbase + kOffQ + x * kPfTile;
+        const uint32_t ka = sbase + kOffK + (j % kPfStages) * kPfTile;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc_mma_f16(tbase + sb * 128, smem_desc(qa + kk * 32, 16, 1024),
+          tc_mma_f16(tbase + kColS + x * 128, smem_desc(qa + kk * 32, 16, 1024),
                      smem_desc(ka + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[sb]);
+        tc_commit(&s_full[x]);
       };
-      issue_qk(0);
-      for (int j = 0; j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) issue_qk(j + 1);
-        const int st = j % kPfStages, pb = j & 1;
-        if (!dead && !mbar_wait(&p_full[pb], (j >> 1) & 1)) dead = true;
-        if (dead) break;
+      auto issue_pv = [&](int x, int j) {
         tc_fence_after();
-        const uint32_t pa = sbase + kOffP + pb * 2 * kPfTile, va = sbase + kOffV + st * kPfTile;
+        const uint32_t va = sbase + kOffV + (j % kPfStages) * kPfTile;
+        // A = P_x from tensor memory: 16 keys (8 columns) per instruction
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16(t_o, smem_desc(pa + (kk >> 2) * kPfTile + (kk & 3) * 32, 16, 1024),
-                     smem_desc(va + kk * 2048, 16, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&o_done[pb]);
-        tc_commit(&kv_empty[st]);
+          tc_mma_f16_ts(tbase + kColO + x * 64, tbase + kColP + x * 64 + kk * 8,
+                        smem_desc(va + kk * 2048, 16, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[x]);
+      };
+      if (!dead && !mbar_wait(&kv_full[0], 0)) dead = true;
+      if (!dead) {
+        if (nt[0] > 0) issue_qk(0, 0);
+        if (nt[1] > 0) issue_qk(1, 0);
+      }
+      for (int j = 0; j < n_kv_tiles && !dead; ++j) {
+        // S of key tile j+1 once the softmax has read S of tile j
+        if (j + 1 < n_kv_tiles && !mbar_wait(&kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1)) {
+          dead = true;
+          break;
+        }
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (j + 1 >= nt[x]) continue;
+          if (!mbar_wait(&s_empty[x], j & 1)) {
+            dead = true;
+            break;
+          }
+          issue_qk(x, j + 1);
+        }
+        if (dead) break;
+        // O_x += P_x V_j once the softmax has written P_x
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (j >= nt[x]) continue;
+          if (!mbar_wait(&p_full[x], j & 1)) {
+            dead = true;
+            break;
+          }
+          issue_pv(x, j);
+        }
+        if (dead) break;
+        tc_commit(&kv_empty[j % kPfStages]);
       }
       if (dead) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
     }
   } else {
     // ======================= softmax / epilogue (thread = query row) =======================
-    const int r = tid;
-    const bool row_valid = r < rows;
-    const int lim = row_valid ? min(prior + q0 + r + 1, kv_len) : 0;  // keys [0, lim) visible
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int x = warp >> 2;
+    const int r = tid & 127;
+    const int ntx = x ? nt[1] : nt[0];  // selects keep the per-tile arrays in registers
+    const bool row_valid = r < (x ? rows[1] : rows[0]);
+    const int lim = row_valid ? min(prior + q0 + x * kPfM + r + 1, x ? kv[1] : kv[0]) : 0;  // keys [0, lim)
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tbase + kColS + x * 128 + lane_off;
+    const uint32_t t_o = tbase + kColO + x * 64 + lane_off;
+    const uint32_t t_p = tbase + kColP + x * 64 + lane_off;
+    const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool dead = false;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      if (!dead && !mbar_wait(&s_full[sb], (j >> 1) & 1)) dead = true;
+    for (int j = 0; j < ntx; ++j) {
+      if (!dead && !mbar_wait(&s_full[x], j & 1)) dead = true;
       __syncwarp();  // tcgen05.ld is warp-collective
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tbase + sb * 128 + lane_off + c4 * 32, sr[c4]);
-      tmem_wait_ld();
+      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(t_s + c4 * 32, sr[c4]);
+      tmem_wait_ld_regs(sr[0]);
+      reg_after_wait(sr[1]);
+      reg_after_wait(sr[2]);
+      reg_after_wait(sr[3]);
       tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
+      mbar_arrive(&s_empty[x]);
 
-      // scale > 0 (checked on the host), so the row max is taken on raw
-      // scores and scaled once; only tiles crossing the causal limit mask
+      // keys at or past this row's causal limit become -inf (exp2 -> 0)
       const int kbase = j * kPfN;
-      const bool full_tile = kbase + kPfN <= lim;
-      float mt = -INFINITY;
-      if (full_tile) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mt = fmaxf(mt, __uint_as_float(sr[c >> 5][c & 31]));
-      } else {
+      if (kbase + kPfN > lim) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
-          if (kbase + c < lim) mt = fmaxf(mt, __uint_as_float(sr[c >> 5][c & 31]));
+          if (kbase + c >= lim) sr[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      mt *= p.scale_log2;
+      // row max on raw scores (scale > 0 is checked on the host): four
+      // independent chains of three-input max
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          m4[q] = fmax3(m4[q], __uint_as_float(sr[c >> 5][(c & 31) + 2 * q]),
+                        __uint_as_float(sr[c >> 5][(c & 31) + 2 * q + 1]));
+      }
+      const float mt = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
       float factor = 1.f;
       if (mt > m_used + 8.f) {
         factor = exp2f(m_used - mt);  // 0 while nothing was visible yet
@@ -255,82 +362,76 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // any of its rows needs it; rows that do not use factor 1
       const bool rescale = __any_sync(0xffffffffu, factor != 1.f) && j > 0;
       const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
-      const float sl2 = p.scale_log2;
-      uint32_t pk[64];
-      float lsum = 0.f;
-      if (full_tile) {
+      // P in two halves of 64 keys: the first half covers the wait for the
+      // PV of tile j-1 (which last read P_x and last wrote O_x)
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
 #pragma unroll
-        for (int c2 = 0; c2 < 64; ++c2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[(2 * c2) >> 5][(2 * c2) & 31]), sl2, nm));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[(2 * c2 + 1) >> 5][(2 * c2 + 1) & 31]), sl2, nm));
-          lsum += p0 + p1;
-          pk[c2] = pack2<T>(p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int c2 = 0; c2 < 64; ++c2) {
-          const int c = 2 * c2;
-          const float p0 = kbase + c < lim ? ex2_approx(fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm)) : 0.f;
-          const float p1 = kbase + c + 1 < lim ? ex2_approx(fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm)) : 0.f;
-          lsum += p0 + p1;
-          pk[c2] = pack2<T>(p0, p1);
-        }
+      for (int c2 = 0; c2 < 32; ++c2) {
+        const int c = 2 * c2;
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm));
+        ls[c2 & 3] += p0 + p1;
+        pk[c2] = pack2<T>(p0, p1);
       }
-      l += lsum;
-      // P buffer sb was last read by PV_{j-2}; O must be current before a rescale
-      if (j >= 2 && !dead && !mbar_wait(&o_done[sb], ((j >> 1) - 1) & 1)) dead = true;
+      if (j >= 1 && !dead && !mbar_wait(&o_done[x], (j - 1) & 1)) dead = true;
+      __syncwarp();
+      tc_fence_after();
       if (rescale) {
-        if (!dead && !mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) dead = true;
-        __syncwarp();
-        tc_fence_after();
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t orr[32];
-          tmem_ld32(t_o + lane_off + c2 * 32, orr);
-          tmem_wait_ld();
+          tmem_ld32(t_o + c2 * 32, orr);
+          tmem_wait_ld_regs(orr);
 #pragma unroll
           for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * factor);
-          tmem_st32(t_o + lane_off + c2 * 32, orr);
-        }
-        tmem_wait_st();
-      }
-      // row r of P: two 64-key sub-tiles of 128-byte swizzled rows
-      uint8_t* prow = base + kOffP + sb * 2 * kPfTile + r * 128;
-#pragma unroll
-      for (int sub = 0; sub < 2; ++sub) {
-#pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {
-          const int w = sub * 32 + c16 * 4;
-          *reinterpret_cast<uint4*>(prow + sub * kPfTile + ((c16 ^ (r & 7)) << 4)) =
-              make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
+          tmem_st32(t_o + c2 * 32, orr);
         }
       }
-      fence_proxy_async_smem();
+      // row r of P: 64 columns of packed (even key, odd key) pairs
+      tmem_st32(t_p, pk);
+#pragma unroll
+      for (int c2 = 32; c2 < 64; ++c2) {
+        const int c = 2 * c2;
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm));
+        ls[c2 & 3] += p0 + p1;
+        pk[c2 - 32] = pack2<T>(p0, p1);
+      }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tmem_st32(t_p + 32, pk);
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[sb]);
+      mbar_arrive(&p_full[x]);
     }
     // ---- epilogue: O / l -> out
-    const int lastb = (n_tiles - 1) & 1;
-    if (!dead && !mbar_wait(&o_done[lastb], ((n_tiles - 1) >> 1) & 1)) dead = true;
-    __syncwarp();
-    tc_fence_after();
     uint32_t o0[32], o1[32];
-    tmem_ld32(t_o + lane_off, o0);
-    tmem_ld32(t_o + lane_off + 32, o1);
-    tmem_wait_ld();
+    if (ntx > 0) {
+      if (!dead && !mbar_wait(&o_done[x], (ntx - 1) & 1)) dead = true;
+      __syncwarp();
+      tc_fence_after();
+      tmem_ld32(t_o, o0);
+      tmem_ld32(t_o + 32, o1);
+      tmem_wait_ld_regs(o0);
+      reg_after_wait(o1);
+    }
     if (dead && r == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
     if (row_valid) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(q_begin + q0 + r) * p.out_stride +
+      // no visible key (a table of zero blocks): the row is zeros
+      const float inv = (ntx > 0 && l > 0.f) ? 1.f / l : 0.f;
+      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(q_begin + q0 + x * kPfM + r) * p.out_stride +
                 static_cast<int64_t>(h) * 64;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         const uint32_t* src = c8 < 4 ? o0 + c8 * 8 : o1 + (c8 - 4) * 8;
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = inv == 0.f ? 0.f : __uint_as_float(src[i]) * inv;
         uint4 v;
-        v.x = pack2<T>(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-        v.y = pack2<T>(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-        v.z = pack2<T>(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-        v.w = pack2<T>(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        v.x = pack2<T>(f[0], f[1]);
+        v.y = pack2<T>(f[2], f[3]);
+        v.z = pack2<T>(f[4], f[5]);
+        v.w = pack2<T>(f[6], f[7]);
         *reinterpret_cast<uint4*>(orow + c8 * 8) = v;
       }
     }
@@ -338,7 +439,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // ---- teardown: every tcgen05 access of this CTA is done before the dealloc
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kPfMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tbase, kPfTmemCols);
   }
@@ -346,11 +447,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
 bool prefill_fast_supported(const AttnArgs& a) {
   auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
+  const int64_t pairs = (static_cast<int64_t>(a.max_query_len) + kPfPair - 1) / kPfPair;
   return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
-         a.block_size == 16 && a.n_seqs <= 65535 && a.n_q_heads <= 65535 && a.max_query_len > 0 &&
+         a.block_size == 16 && a.max_query_len > 0 &&
+         pairs * a.n_q_heads * a.n_seqs < (int64_t{1} << 31) &&
          (a.q_stride * 2) % 16 == 0 && (a.out_stride * 2) % 16 == 0 && al(a.q, 16) &&
          al(a.out, 16) && al(a.k_pool, 16) && al(a.v_pool, 16) &&
-         a.scale > 0.f && static_cast<int64_t>(a.n_tokens) + kPfM < (int64_t{1} << 31);
+         a.scale > 0.f && static_cast<int64_t>(a.n_tokens) + kPfPair < (int64_t{1} << 31);
 }
 
 namespace {
@@ -385,10 +488,14 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
   p.num_prior = a.num_prior;
   p.num_blocks = a.num_blocks;
   p.n_tokens = a.n_tokens;
+  p.n_seqs = a.n_seqs;
+  p.n_q_heads = a.n_q_heads;
+  p.n_pairs = (a.max_query_len + kPfPair - 1) / kPfPair;
+  p.order_by_length = a.n_seqs <= kPfOrderMaxSeqs ? 1 : 0;
   p.group = a.n_q_heads / a.n_kv_heads;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = a.err;
-  const dim3 grid((a.max_query_len + kPfM - 1) / kPfM, a.n_q_heads, a.n_seqs);
+  const dim3 grid(static_cast<unsigned>(p.n_pairs * a.n_q_heads * a.n_seqs));
   kern<<<grid, kPfThreads, kPfSmemBytes, stream>>>(*qmap, *kmap, *vmap, p);
   return cudaGetLastError();
 }

@@ -9,8 +9,13 @@ on the GPU: every attention call goes through prepare_step / forward_layer
 radix cache, copies from copy_blocks.
 
 * fp32: the token streams and the scheduler metrics must be identical.
-* fp16 (the tensor-core decode and tcgen05 prefill kernels): the streams are
-  compared too, and the first divergence, if any, is reported.
+* fp16 (the tensor-core decode and tcgen05 prefill kernels): an fp16 forward
+  moves a top-1/top-2 logit gap by up to ~0.026 on these weights, so a stream
+  may part from the fp32 reference only at a near-tie: every request is
+  identical up to its first divergence, and the reference's margin at that
+  token (tests/golden/e2e_margins.json, make_golden_margins.py) is below
+  FP16_NEAR_TIE.  Tokens after a divergence continue a different prefix and
+  are not compared.
 """
 
 import json
@@ -26,10 +31,18 @@ from pagedkv.scheduler import Request, Scheduler
 
 pytestmark = pytest.mark.gpu
 
+FP16_NEAR_TIE = 0.05  # logits: about twice the largest fp16-vs-fp32 gap error measured
+
 
 @pytest.fixture(scope="module")
 def golden_e2e():
     with open(f"{GOLDEN}/e2e_greedy.json") as f:
+        return json.load(f)
+
+
+@pytest.fixture(scope="module")
+def margins():
+    with open(f"{GOLDEN}/e2e_margins.json") as f:
         return json.load(f)
 
 
@@ -88,12 +101,18 @@ def test_fp32_greedy_streams_identical_to_reference(golden_e2e, weights, scenari
 
 
 @pytest.mark.parametrize("scenario", ["prefix", "preempt"])
-def test_fp16_greedy_streams_match_reference(golden_e2e, weights, scenario):
+def test_fp16_greedy_streams_match_reference(golden_e2e, margins, weights, scenario):
     sc = C.e2e_scenarios()[scenario]
     g = golden_e2e[scenario]
     model = PagedQwen2Model(Qwen2Config(), weights, device="cuda", dtype=torch.float16)
     reqs, sched = run_engine(model, sc, torch.float16)
-    div = {r.req_id: first_divergence(r.output_ids, ref) for r, ref in zip(reqs, g["outputs"])}
-    assert all(v is None for v in div.values()), f"first divergence per request: {div}"
-    assert sched.metrics["preemptions"] == g["metrics"]["preemptions"]
-    assert sched.metrics["prefix_cache_hit_tokens"] == g["metrics"]["prefix_cache_hit_tokens"]
+    for r, ref, marg in zip(reqs, g["outputs"], margins[scenario]):
+        d = first_divergence(r.output_ids, ref)
+        if d is None:
+            continue
+        assert d < len(ref) and len(r.output_ids) == len(ref), f"req {r.req_id}: length differs"
+        assert marg[d] < FP16_NEAR_TIE, (
+            f"req {r.req_id}: token {d} differs where the reference's margin is {marg[d]}")
+    if all(first_divergence(r.output_ids, ref) is None for r, ref in zip(reqs, g["outputs"])):
+        assert sched.metrics["preemptions"] == g["metrics"]["preemptions"]
+        assert sched.metrics["prefix_cache_hit_tokens"] == g["metrics"]["prefix_cache_hit_tokens"]

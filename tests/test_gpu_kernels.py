@@ -317,6 +317,26 @@ def test_prefill_ragged_multi_tile(oracle_mod, decode_impl, dt):
     assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
 
 
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_prefill_equal_lengths_and_many_sequences(oracle_mod, dt):
+    """The tensor-core kernel maps CTAs longest-sequence-first: five sequences
+    of the same total length (ties ranked by index) beside a longer one, and
+    a batch of 70 sequences, beyond the ranked limit (natural order)."""
+    c = C.make_prefill_case(24, [100, 100, 100, 100, 50, 260], [10, 10, 10, 10, 60, 0], 16, 256, dt)
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_prefill_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+    rng = np.random.default_rng(25)
+    chunks = rng.integers(1, 300, size=70).tolist()
+    priors = rng.integers(0, 200, size=70).tolist()
+    c = C.make_prefill_case(25, chunks, priors, 32, 4096, dt)
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref, _, _ = oracle_mod.run_prefill_case(c)
+    assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
+
+
 def test_prefill_config4_full(oracle_mod, decode_impl):
     c = C.make_c4_case()
     out, err = run_prefill_gpu(c)

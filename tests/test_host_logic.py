@@ -176,3 +176,18 @@ def test_to_dtype_bf16_matches_torch():
     ours = C.to_dtype(x, "bf16")
     theirs = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(ours, theirs)
+
+
+def test_e2e_margin_fixture_matches_streams():
+    """Every reference token of the e2e golden has its top-1/top-2 margin."""
+    import json
+
+    from conftest import GOLDEN
+
+    with open(f"{GOLDEN}/e2e_greedy.json") as f:
+        g = json.load(f)
+    with open(f"{GOLDEN}/e2e_margins.json") as f:
+        m = json.load(f)
+    for name in ("prefix", "preempt"):
+        assert [len(x) for x in m[name]] == [len(o) for o in g[name]["outputs"]]
+        assert all(v >= 0 for x in m[name] for v in x)
