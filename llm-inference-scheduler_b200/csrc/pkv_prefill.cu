@@ -8,7 +8,7 @@
 // block table.
 //
 // One CTA per (sequence, query head, pair of 128-query tiles A and B); the two
-// tiles share every K/V tile the CTA loads.  10 warps:
+// tiles share every K/V tile the CTA loads.  12 warps (three warpgroups):
 //  * warps 0-3 / 4-7 (softmax of tile A / tile B): thread r of a group owns
 //    query row r of its tile.  It reads its row of S = Q K^T from TMEM
 //    (tcgen05.ld), applies the causal mask and an online softmax in the exp2
@@ -42,6 +42,13 @@
 // rank is computed by every CTA from num_prior / query_start_loc (up to
 // kPfOrderMaxSeqs sequences; natural order beyond).
 //
+// Registers.  The 384 threads launch with 168 registers each (64,512 in all).
+// The third warpgroup (producer, MMA, two idle warps) gives registers back with
+// setmaxnreg.dec to 56 and the two softmax warpgroups raise theirs to 224:
+// 128 x 56 + 256 x 224 = 64,512, the launch total.  The host checks the compiled
+// register count against that sum before the first launch (a split above the
+// launch total would leave setmaxnreg.inc waiting).
+//
 // Every wait is bounded; on a timeout the kernel flags PKV_FLAG_PIPELINE_TIMEOUT,
 // stops waiting and still frees its tensor memory.
 #include <float.h>
@@ -59,7 +66,10 @@ constexpr int kPfPair = 2 * kPfM;         // query rows per CTA (tiles A and B)
 constexpr int kPfN = 128;                 // keys per tile (8 blocks of 16)
 constexpr int kPfStages = 4;              // K/V ring depth
 constexpr int kPfTile = 128 * 64 * 2;     // 16 KB: 128 rows x 64 dims x 2 bytes
-constexpr int kPfThreads = 320;
+constexpr int kPfThreads = 384;
+constexpr int kPfRegsSoftmax = 224;       // per thread, warpgroups 0 and 1
+constexpr int kPfRegsOther = 56;          // per thread, warpgroup 2
+constexpr int kPfRegSplit = 256 * kPfRegsSoftmax + 128 * kPfRegsOther;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
 constexpr uint32_t kPfTmemCols = 512;
@@ -199,6 +209,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int nb_needed = (max(kv[0], kv[1]) + 15) >> 4;
   const int g = h / p.group;
 
+  if (warp >= 8) {
+  // third warpgroup: producer, MMA issuer, two idle warps
+  setmaxnreg_dec<kPfRegsOther>();
   if (warp == kPfProducerWarp) {
     // ======================= producer =======================
     if (lane == 0) {
@@ -306,7 +319,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       if (dead) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
     }
+  }
   } else {
+    setmaxnreg_inc<kPfRegsSoftmax>();
     // ======================= softmax / epilogue (thread = query row) =======================
     const int x = warp >> 2;
     const int r = tid & 127;
@@ -458,7 +473,7 @@ bool prefill_fast_supported(const AttnArgs& a) {
 
 namespace {
 std::mutex g_pf_mu;
-bool g_pf_attr[64][2] = {};
+int g_pf_state[64][2] = {};  // 0 unchecked, 1 ready, -1 register split does not fit
 }  // namespace
 
 cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, const CUtensorMap* kmap,
@@ -472,11 +487,21 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
   {
     std::lock_guard<std::mutex> lk(g_pf_mu);
     const int k = a.dtype == PKV_DTYPE_F16 ? 0 : 1;
-    if (dev < 64 && !g_pf_attr[dev][k]) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+    int state = dev < 64 ? g_pf_state[dev][k] : 0;
+    if (state == 0) {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, kern);
       if (e != cudaSuccess) return e;
-      g_pf_attr[dev][k] = true;
+      state = fa.numRegs * kPfThreads >= kPfRegSplit ? 1 : -1;
+      if (state == 1) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+        if (e != cudaSuccess) return e;
+      }
+      if (dev < 64) g_pf_state[dev][k] = state;
     }
+    // a build whose launch register count cannot fund the split runs the
+    // CUDA-core kernel instead
+    if (state != 1) return launch_generic_attention(a, stream);
   }
   PrefillParams p;
   p.out = a.out;
