@@ -329,6 +329,20 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// One leader lane of a converged warp (elect.sync over all 32 lanes; the same
+// lane every time).  Issuing tcgen05.mma / TMA under this predicate from
+// warp-converged code keeps their operands on the uniform datapath; under a
+// per-lane test (lane == 0) every operand is moved there instruction by
+// instruction, which costs several times the tensor core's own time for
+// N <= 128 instructions.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // three-input maximum (one instruction on sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

@@ -24,7 +24,7 @@
 //    and arrive as zeros.
 //  * warp 9 (MMA): allocates all 512 TMEM columns (S_A, S_B: 128 fp32 each;
 //    O_A, O_B: 64 fp32 each; P_A, P_B: 64 columns of fp16/bf16 pairs each)
-//    and one thread issues tcgen05.mma kind::f16 (M=128):
+//    and one elected lane issues tcgen05.mma kind::f16 (M=128):
 //    S_x = Q_x K_j^T (N=128, K=64, both K-major, from shared memory) and
 //    O_x += P_x V_j (N=64, K=128; A = P_x from tensor memory, B = V the
 //    MN-major shared operand), committing to mbarriers.  S_x of key tile j+1
@@ -214,7 +214,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   setmaxnreg_dec<kPfRegsOther>();
   if (warp == kPfProducerWarp) {
     // ======================= producer =======================
-    if (lane == 0) {
+    // warp-converged; one elected lane issues the TMA loads
+    if (elect_one()) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_load_3d(base + kOffQ, &qmap, q_full, 0, h, q_begin + q0);
       if (rows[1] > 0) tma_load_3d(base + kOffQ + kPfTile, &qmap, q_full, 0, h, q_begin + q0 + kPfM);
     }
-    bool dead = false;
+    __syncwarp();
     for (int j = 0; j < n_kv_tiles; ++j) {
       int tok = p.num_blocks * 16;  // out of range: TMA fills zeros
       if (lane < 8) {
@@ -239,86 +240,106 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int toks[8];
 #pragma unroll
       for (int b = 0; b < 8; ++b) toks[b] = __shfl_sync(0xffffffffu, tok, b);
-      if (lane == 0 && !dead) {
-        const int st = j % kPfStages;
-        if (!mbar_wait(&kv_empty[st], ((j / kPfStages) & 1) ^ 1)) {
-          raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
-          dead = true;
-        } else {
-          mbar_arrive_expect_tx(&kv_full[st], 2 * kPfTile);
-          uint8_t* kd = base + kOffK + st * kPfTile;
-          uint8_t* vd = base + kOffV + st * kPfTile;
+      const int st = j % kPfStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / kPfStages) & 1) ^ 1))) {
+        if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+        break;
+      }
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kPfTile);
+        uint8_t* kd = base + kOffK + st * kPfTile;
+        uint8_t* vd = base + kOffV + st * kPfTile;
 #pragma unroll
-          for (int b = 0; b < 8; ++b) {
-            tma_load_3d(kd + b * 2048, &kmap, &kv_full[st], 0, g, toks[b]);
-            tma_load_3d(vd + b * 2048, &vmap, &kv_full[st], 0, g, toks[b]);
-          }
+        for (int b = 0; b < 8; ++b) {
+          tma_load_3d(kd + b * 2048, &kmap, &kv_full[st], 0, g, toks[b]);
+          tma_load_3d(vd + b * 2048, &vmap, &kv_full[st], 0, g, toks[b]);
         }
       }
+      __syncwarp();
     }
   } else if (warp == kPfMmaWarp) {
-    // ======================= MMA issuer (one thread) =======================
-    if (lane == 0) {
-      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t idesc_s = mma_idesc_f16(fmt, 0, 0, kPfN, kPfM);
-      constexpr uint32_t idesc_o = mma_idesc_f16(fmt, 0, 1, 64, kPfM);
-      bool dead = !mbar_wait(q_full, 0);
-      auto issue_qk = [&](int x, int j) {
+    // ======================= MMA issuer =======================
+    // The whole warp runs the loop, so descriptors and tensor-memory
+    // addresses are warp-uniform values; one elected lane (the same lane every
+    // time) issues every tcgen05.mma and tcgen05.commit (a commit tracks the
+    // operations of the thread that issues it).
+    constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+    constexpr uint32_t idesc_s = mma_idesc_f16(fmt, 0, 0, kPfN, kPfM);
+    constexpr uint32_t idesc_o = mma_idesc_f16(fmt, 0, 1, 64, kPfM);
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+    };
+    auto issue_qk = [&](int x, int j) {
+      const uint32_t qa = sbase + kOffQ + x * kPfTile;
+      const uint32_t ka = sbase + kOffK + (j % kPfStages) * kPfTile;
+      uint64_t ad[4], bd[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ad[kk] = smem_desc(qa + kk * 32, 16, 1024);
+        bd[kk] = smem_desc(ka + kk * 32, 16, 1024);
+      }
+      if (elect_one()) {
         tc_fence_after();
-        const uint32_t qa = sbase + kOffQ + x * kPfTile;
-        const uint32_t ka = sbase + kOffK + (j % kPfStages) * kPfTile;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc_mma_f16(tbase + kColS + x * 128, smem_desc(qa + kk * 32, 16, 1024),
-                     smem_desc(ka + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tbase + kColS + x * 128, ad[kk], bd[kk], idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(&s_full[x]);
-      };
-      auto issue_pv = [&](int x, int j) {
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int x, int j) {
+      // A = P_x from tensor memory: 16 keys (8 columns) per instruction
+      const uint32_t va = sbase + kOffV + (j % kPfStages) * kPfTile;
+      uint64_t bd[8];
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) bd[kk] = smem_desc(va + kk * 2048, 16, 1024);
+      if (elect_one()) {
         tc_fence_after();
-        const uint32_t va = sbase + kOffV + (j % kPfStages) * kPfTile;
-        // A = P_x from tensor memory: 16 keys (8 columns) per instruction
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16_ts(tbase + kColO + x * 64, tbase + kColP + x * 64 + kk * 8,
-                        smem_desc(va + kk * 2048, 16, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tbase + kColO + x * 64, tbase + kColP + x * 64 + kk * 8, bd[kk], idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&o_done[x]);
-      };
-      if (!dead && !mbar_wait(&kv_full[0], 0)) dead = true;
-      if (!dead) {
-        if (nt[0] > 0) issue_qk(0, 0);
-        if (nt[1] > 0) issue_qk(1, 0);
       }
-      for (int j = 0; j < n_kv_tiles && !dead; ++j) {
-        // S of key tile j+1 once the softmax has read S of tile j
-        if (j + 1 < n_kv_tiles && !mbar_wait(&kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1)) {
+      __syncwarp();
+    };
+    bool dead = !wait_all(q_full, 0);
+    if (!dead && !wait_all(&kv_full[0], 0)) dead = true;
+    if (!dead) {
+      if (nt[0] > 0) issue_qk(0, 0);
+      if (nt[1] > 0) issue_qk(1, 0);
+    }
+    for (int j = 0; j < n_kv_tiles && !dead; ++j) {
+      // S of key tile j+1 once the softmax has read S of tile j
+      if (j + 1 < n_kv_tiles && !wait_all(&kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1)) {
+        dead = true;
+        break;
+      }
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (j + 1 >= nt[x]) continue;
+        if (!wait_all(&s_empty[x], j & 1)) {
           dead = true;
           break;
         }
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          if (j + 1 >= nt[x]) continue;
-          if (!mbar_wait(&s_empty[x], j & 1)) {
-            dead = true;
-            break;
-          }
-          issue_qk(x, j + 1);
-        }
-        if (dead) break;
-        // O_x += P_x V_j once the softmax has written P_x
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          if (j >= nt[x]) continue;
-          if (!mbar_wait(&p_full[x], j & 1)) {
-            dead = true;
-            break;
-          }
-          issue_pv(x, j);
-        }
-        if (dead) break;
-        tc_commit(&kv_empty[j % kPfStages]);
+        issue_qk(x, j + 1);
       }
-      if (dead) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+      if (dead) break;
+      // O_x += P_x V_j once the softmax has written P_x
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (j >= nt[x]) continue;
+        if (!wait_all(&p_full[x], j & 1)) {
+          dead = true;
+          break;
+        }
+        issue_pv(x, j);
+      }
+      if (dead) break;
+      if (elect_one()) tc_commit(&kv_empty[j % kPfStages]);
+      __syncwarp();
     }
+    if (dead && lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
   }
   } else {
     setmaxnreg_inc<kPfRegsSoftmax>();
