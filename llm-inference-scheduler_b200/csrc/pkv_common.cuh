@@ -187,6 +187,9 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 
 // ----------------------------------------------------------------------------
@@ -341,6 +344,26 @@ __device__ __forceinline__ bool elect_one() {
       "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}"
       : "=r"(pred));
   return pred != 0;
+}
+
+// 2^x on the FMA pipe, for x <= ~16 (used beside ex2.approx to share the
+// exponentials of a softmax between the MUFU and FMA pipes).
+// Cody-Waite range reduction: t = x + 1.5 * 2^23 rounds x to the nearest
+// integer n, held in t's low mantissa bits; f = x - n lies in [-1/2, 1/2].
+// 2^f is a degree-3 polynomial fitted by Remez exchange to minimise the
+// relative error on [-1/2, 1/2] (7.5e-5, against 4.9e-4 for rounding to
+// fp16); 2^n is applied by adding n to the exponent field.  x is clamped at
+// -125 so that the exponent field stays positive (p(f) can be below 1).
+constexpr float kExp2C0 = 0x1.fff692p-1f;
+constexpr float kExp2C1 = 0x1.62f31ap-1f;
+constexpr float kExp2C2 = 0x1.f0de1ap-3f;
+constexpr float kExp2C3 = 0x1.c3f760p-5f;
+__device__ __forceinline__ float exp2_poly3(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  const float p = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // three-input maximum (one instruction on sm_100)

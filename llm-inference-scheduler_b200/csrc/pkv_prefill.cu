@@ -74,6 +74,11 @@ constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfOrderMaxSeqs = 64;
+#ifndef PKV_PF_POLY_EVERY
+#define PKV_PF_POLY_EVERY 8
+#endif
+// one key pair in kPfPolyEvery takes the FMA-pipe exp2 (0: all on the MUFU)
+constexpr int kPfPolyEvery = PKV_PF_POLY_EVERY;
 
 // tensor-memory columns: S_A, S_B (fp32), O_A, O_B (fp32), P_A, P_B (fp16/bf16 pairs)
 constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
@@ -377,17 +382,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (kbase + c >= lim) sr[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      // row max on raw scores (scale > 0 is checked on the host): four
+      // row max on raw scores (scale > 0 is checked on the host): eight
       // independent chains of three-input max
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float m8[8];
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
+      for (int q = 0; q < 8; ++q) m8[q] = fmaxf(__uint_as_float(sr[0][q]), __uint_as_float(sr[0][q + 8]));
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          m4[q] = fmax3(m4[q], __uint_as_float(sr[c >> 5][(c & 31) + 2 * q]),
-                        __uint_as_float(sr[c >> 5][(c & 31) + 2 * q + 1]));
+      for (int c = 16; c < 128; c += 16) {  // columns c + q and c + 8 + q
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          m8[q] = fmax3(m8[q], __uint_as_float(sr[c >> 5][(c & 31) + q]),
+                        __uint_as_float(sr[(c + 8) >> 5][((c + 8) & 31) + q]));
       }
-      const float mt = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
+      const float mt = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                             fmaxf(m8[6], m8[7])) * sl2;
       float factor = 1.f;
       if (mt > m_used + 8.f) {
         factor = exp2f(m_used - mt);  // 0 while nothing was visible yet
@@ -401,41 +409,40 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // P in two halves of 64 keys: the first half covers the wait for the
       // PV of tile j-1 (which last read P_x and last wrote O_x)
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];
 #pragma unroll
-      for (int c2 = 0; c2 < 32; ++c2) {
-        const int c = 2 * c2;
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm));
-        ls[c2 & 3] += p0 + p1;
-        pk[c2] = pack2<T>(p0, p1);
-      }
-      if (j >= 1 && !dead && !mbar_wait(&o_done[x], (j - 1) & 1)) dead = true;
-      __syncwarp();
-      tc_fence_after();
-      if (rescale) {
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          uint32_t orr[32];
-          tmem_ld32(t_o + c2 * 32, orr);
-          tmem_wait_ld_regs(orr);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * factor);
-          tmem_st32(t_o + c2 * 32, orr);
+        for (int i = 0; i < 32; ++i) {
+          const int c2 = half * 32 + i, c = 2 * c2;
+          const float x0 = fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm);
+          const float x1 = fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm);
+          const bool poly = kPfPolyEvery > 0 && (c2 % (kPfPolyEvery > 0 ? kPfPolyEvery : 1)) == kPfPolyEvery - 1;
+          const float p0 = poly ? exp2_poly3(x0) : ex2_approx(x0);
+          const float p1 = poly ? exp2_poly3(x1) : ex2_approx(x1);
+          ls[i & 3] += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
         }
-      }
-      // row r of P: 64 columns of packed (even key, odd key) pairs
-      tmem_st32(t_p, pk);
+        if (half == 0) {
+          if (j >= 1 && !dead && !mbar_wait(&o_done[x], (j - 1) & 1)) dead = true;
+          __syncwarp();
+          tc_fence_after();
+          if (rescale) {
 #pragma unroll
-      for (int c2 = 32; c2 < 64; ++c2) {
-        const int c = 2 * c2;
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm));
-        ls[c2 & 3] += p0 + p1;
-        pk[c2 - 32] = pack2<T>(p0, p1);
+            for (int c2 = 0; c2 < 2; ++c2) {
+              uint32_t orr[32];
+              tmem_ld32(t_o + c2 * 32, orr);
+              tmem_wait_ld_regs(orr);
+#pragma unroll
+              for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * factor);
+              tmem_st32(t_o + c2 * 32, orr);
+            }
+          }
+        }
+        // row r of P: 64 columns of packed (even key, odd key) pairs
+        tmem_st32(t_p + half * 32, pk);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tmem_st32(t_p + 32, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);

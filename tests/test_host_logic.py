@@ -6,6 +6,7 @@ the config-2 fork/COW flow; their recorded outcomes live in tests/golden.
 """
 
 import json
+import os
 
 import numpy as np
 import pytest
@@ -191,3 +192,36 @@ def test_e2e_margin_fixture_matches_streams():
     for name in ("prefix", "preempt"):
         assert [len(x) for x in m[name]] == [len(o) for o in g[name]["outputs"]]
         assert all(v >= 0 for x in m[name] for v in x)
+
+
+def test_exp2_polynomial_error_bound():
+    """exp2_poly3 (csrc/pkv_common.cuh), the FMA-pipe 2^x that takes a quarter
+    of the prefill softmax's exponentials, restated step by step in float32:
+    relative error below 1e-4 on [-125, 16] (fp16 rounding is 4.9e-4), and
+    2^n exact at integers."""
+    import re
+
+    import numpy as np
+
+    from conftest import ROOT
+
+    src = open(os.path.join(ROOT, "llm-inference-scheduler_b200", "csrc", "pkv_common.cuh")).read()
+    c = {int(k): np.float32(float.fromhex(v))
+         for k, v in re.findall(r"kExp2C(\d) = (0x[0-9a-fp.+-]+)f;", src)}
+    assert sorted(c) == [0, 1, 2, 3]
+    f32 = np.float32
+
+    def fma(a, b, d):  # a*b is exact in float64; one rounding to float32 after the add
+        return (a.astype(np.float64) * b + d).astype(np.float32)
+
+    x = np.concatenate([np.linspace(-125, 16, 2_000_001, dtype=np.float32),
+                        np.arange(-125, 17, dtype=np.float32)])
+    xc = np.maximum(x, f32(-125))
+    t = (xc + f32(12582912.0)).astype(np.float32)
+    f = (xc - (t - f32(12582912.0)).astype(np.float32)).astype(np.float32)
+    assert np.all(np.abs(f) <= 0.5)
+    p = fma(fma(fma(np.full_like(f, c[3]), f, c[2]), f, c[1]), f, c[0])
+    bits = (p.view(np.int32).astype(np.int64) + (t.view(np.int32).astype(np.int64) << 23)) & 0xFFFFFFFF
+    y = bits.astype(np.uint32).view(np.float32).astype(np.float64)
+    rel = np.abs(y / np.exp2(xc.astype(np.float64)) - 1)
+    assert rel.max() < 1e-4, rel.max()
