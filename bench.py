@@ -45,8 +45,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "prefill", "e2e"), default="decode",
-                    help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5")
+    ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops"), default="decode",
+                    help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5; "
+                         "cache_ops = reshape_and_cache and copy_blocks at bandwidth-sized batches")
+    ap.add_argument("--append-tokens", type=int, nargs="+", default=[8192, 65536],
+                    help="cache_ops: tokens appended per reshape_and_cache launch")
+    ap.add_argument("--copy-pairs", type=int, default=4096, help="cache_ops: (src, dst) block pairs")
     ap.add_argument("--conversations", type=int, default=64, help="config 5: conversations")
     ap.add_argument("--rate", type=float, default=40.0, help="config 5: Poisson arrivals per second")
     ap.add_argument("--max-num-seqs", type=int, default=128)
@@ -627,6 +631,85 @@ def run_e2e(args):
     print(json.dumps(line), flush=True)
 
 
+def run_cache_ops(args):
+    """reshape_and_cache and copy_blocks at batches large enough to measure HBM
+    bandwidth (one GPU).  Append: T tokens of K and V per launch scattered
+    to a random permutation of pool slots, one pool per layer (the working
+    set of the L layers exceeds L2).  Copy: copy_blocks of P (src, dst) block
+    pairs over all L layers in one launch, src and dst disjoint and random
+    (a COW fork / preemption-sized batch).  GB/s counts algorithmic bytes:
+    every K/V byte read once and written once, plus the slot / pair indices."""
+    import numpy as np
+    import torch
+
+    from pagedkv import ops
+    from pagedkv import workloads as W
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L, dt = args.layers, torch.float16
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    rng = np.random.default_rng(99)
+    err = ops.new_error_flags(dev)
+    peak, kind = peaks()
+
+    def time_calls(calls, reps):
+        """Device time per launch of back-to-back launches: each round of
+        len(calls) launches is queued behind a short GPU sleep, so the host's
+        launch cost does not open gaps between them; one event pair per round."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for _ in range(args.warmup):
+            for c in calls:
+                c()
+        torch.cuda.synchronize()
+        for a, b in evs:
+            torch.cuda._sleep(4_000_000)  # ~2 ms of GPU time covers the queueing of the round
+            a.record()
+            for c in calls:
+                c()
+            b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / (len(evs) * len(calls))
+
+    results = []
+    for T in args.append_tokens:
+        nb = (T + 15) // 16 + 16
+        kp = torch.empty((L, nb, 16, 2, 64), device=dev, dtype=dt)
+        vp = torch.empty_like(kp)
+        kn = torch.randn((L, T, 2, 64), generator=g, device=dev, dtype=dt)
+        vn = torch.randn_like(kn)
+        slots = torch.from_numpy(rng.permutation(nb * 16)[:T].astype(np.int64)).to(dev)
+        calls = [ops.bind_reshape_and_cache(kn[l], vn[l], kp[l], vp[l], slots, err) for l in range(L)]
+        ms = time_calls(calls, max(3, args.steps // L))
+        nbytes = W.append_bytes(T)
+        results.append({"kernel": "pkv::reshape_and_cache_vec16", "tokens": T, "bytes_per_launch": nbytes,
+                        "us": round(ms * 1e3, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                        "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)})
+        del kp, vp, kn, vn
+    P = args.copy_pairs
+    nb = 2 * P + 16
+    kc = torch.randn((L, nb, 16, 2, 64), generator=g, device=dev, dtype=dt)
+    vc = torch.randn_like(kc)
+    perm = rng.permutation(nb)[:2 * P].astype(np.int32)
+    pairs = torch.from_numpy(np.stack([perm[:P], perm[P:]], axis=1).copy()).to(dev)
+    ms = time_calls([lambda: ops.copy_blocks(kc, vc, pairs, err)], max(3, args.steps // 50))
+    block_bytes = 16 * 2 * 64 * 2
+    nbytes = 2 * 2 * L * P * block_bytes + P * 8
+    results.append({"kernel": "pkv::copy_blocks_vec16", "pairs": P, "layers": L, "bytes_per_launch": nbytes,
+                    "us": round(ms * 1e3, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                    "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)})
+    ops.check_flags(err, "cache_ops")
+    line = {"metric": "KV append (reshape_and_cache) and copy_blocks HBM GB/s", "value": results[-2]["gbs"],
+            "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f16",
+            "data": "synthetic (seeded normal K/V, random slots and pairs)",
+            "config": {"workload": "cache_ops: append T tokens/launch x 24 layer pools; copy_blocks P pairs x 24 layers",
+                       "append_tokens": args.append_tokens, "copy_pairs": P, "layers": L},
+            "peak": peak, "peak_kind": kind, "kernels": results, "gpu_launches": None}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.workload == "e2e" and args.impl == "ours":
@@ -636,6 +719,8 @@ def main():
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "cache_ops":
+        run_cache_ops(args)
     else:
         run_ours(args)
 
