@@ -169,31 +169,100 @@ class StepMetadata:
     context_lens: torch.Tensor      # int32 [B] = num_prior + num_new
     query_start_loc: torch.Tensor   # int32 [B - n_decode + 1], relative to the prefill rows
     num_prior_dev: torch.Tensor     # int32 [B]
+    decode_plan: ops.DecodeAppendPlan | None = None  # built by the first forward_layer
 
     @property
     def n_seqs(self) -> int:
         return len(self.seq_ids)
 
 
+class _TableMirror:
+    """Host int32 copy of the live block tables: one zero-padded row per
+    sequence in a 2-D buffer, so that a step's table matrix and decode slots
+    are single vectorised gathers instead of per-sequence list conversions.
+
+    A row follows its Python list by length: entries appended since the last
+    step are copied in; a list replaced by a new object, one that shrank, or
+    one whose last entry disagrees with the row is copied in full.  Entries
+    rewritten in place other than the last must go through
+    PagedKVCache.ensure_writable_tail (which updates the row) or a new
+    add_sequence."""
+
+    def __init__(self):
+        self.buf = np.zeros((64, 64), dtype=np.int32)
+        self.state: dict[int, list] = {}  # seq_id -> [row, synced length, list object, last entry]
+        self.free_rows: list[int] = []
+        self.next_row = 0
+
+    def _fit(self, rows: int, cols: int):
+        r, c = self.buf.shape
+        if rows > r or cols > c:
+            nb = np.zeros((max(r, 1 << (rows - 1).bit_length()), max(c, 1 << (cols - 1).bit_length())),
+                          dtype=np.int32)
+            nb[:r, :c] = self.buf
+            self.buf = nb
+
+    def add(self, seq_id: int, table: list[int]):
+        if seq_id in self.state:
+            self.remove(seq_id)
+        if self.free_rows:
+            row = self.free_rows.pop()
+        else:
+            row = self.next_row
+            self.next_row += 1
+            self._fit(row + 1, 1)
+        self.state[seq_id] = [row, 0, table, None]
+
+    def remove(self, seq_id: int):
+        st = self.state.pop(seq_id, None)
+        if st is not None:
+            self.buf[st[0], : st[1]] = 0
+            self.free_rows.append(st[0])
+
+    def set(self, seq_id: int, idx: int, block: int):
+        st = self.state.get(seq_id)
+        if st is not None and idx < st[1]:
+            self.buf[st[0], idx] = block
+            if idx == st[1] - 1:
+                st[3] = block
+
+    def resync(self, st: list, table: list[int]):
+        row, k = st[0], st[1]
+        n = len(table)
+        self._fit(row + 1, n)
+        self.buf[row, :k] = 0
+        self.buf[row, :n] = table
+        st[1], st[2], st[3] = n, table, (table[-1] if n else None)
+
 class PagedKVCache:
     """The model-facing adapter: same append_and_fetch contract as the
     reference's ContiguousKVCache / PagedKVCache, plus the batched
-    prepare_step / forward_layer path that the paged model uses."""
+    prepare_step / forward_layer path that the paged model uses.
+
+    Block tables are the caller's lists (the reference's contract).  A live
+    sequence's table grows by appending; copy-on-write replaces its tail
+    block through ensure_writable_tail; any other rewrite of an existing entry
+    is followed by add_sequence (the reference scheduler does exactly this)."""
 
     def __init__(self, manager: BlockManager):
         self.mgr = manager
         self.block_tables: dict[int, list[int]] = {}
         self._len: dict[int, int] = {}
         self._workspace: torch.Tensor | None = None
+        self._mirror = _TableMirror()
+        self._stage_ring: list = [[None, None] for _ in range(4)]
+        self._stage_next = 0
 
     def add_sequence(self, seq_id: int, block_table: list[int], num_cached_tokens: int):
         """num_cached_tokens = tokens already present via prefix-cache reuse."""
         self.block_tables[seq_id] = block_table
         self._len[seq_id] = num_cached_tokens
+        self._mirror.add(seq_id, block_table)
 
     def free_sequence(self, seq_id: int):
         self.block_tables.pop(seq_id, None)
         self._len.pop(seq_id, None)
+        self._mirror.remove(seq_id)
 
     def seq_len(self, seq_id: int) -> int:
         return self._len[seq_id]
@@ -208,6 +277,7 @@ class PagedKVCache:
             block = table[idx]
             if self.mgr.ref_count[block] > 1:
                 table[idx] = self.mgr.copy_block(block)
+                self._mirror.set(seq_id, idx, table[idx])
                 self.mgr.decref(block)
 
     # ---- reference contract: one sequence, one layer -----------------------
@@ -248,57 +318,115 @@ class PagedKVCache:
     def step_arrays(self, seqs: list[tuple[int, int]]) -> dict:
         """Host half of prepare_step (no device work): numpy arrays of the step.
 
-        Returns dict(ints=int32 [B*W + 2B + n_prefill + 1] = block tables (B x W,
-        zero padded) | context lens | num_prior | prefill query_start_loc,
+        Returns dict(ints=int32 [B*W + 2B + n_prefill + 1] = block tables (B x W;
+        row s holds the sequence's first ceil(len/16) blocks, the entries after
+        them are unspecified) | context lens | num_prior | prefill query_start_loc,
         slots=int64 [T], plus the scalar fields of StepMetadata).
         """
         bs = self.mgr.block_size
         B = len(seqs)
         seq_ids = [s for s, _ in seqs]
-        num_new = [int(n) for _, n in seqs]
-        num_prior = [self._len[s] for s in seq_ids]
-        totals = [p + n for p, n in zip(num_prior, num_new)]
-        used = [(t + bs - 1) // bs for t in totals]
-        for s, t in zip(seq_ids, totals):
-            assert t <= len(self.block_tables[s]) * bs, (
-                f"seq {s}: {t} tokens but only {len(self.block_tables[s])} blocks allocated")
-        W = max(1, max(used, default=1))
-        n_dec = 0
-        while n_dec < B and num_new[n_dec] == 1:
-            n_dec += 1
+        mirror, tables, lens = self._mirror, self.block_tables, self._len
+        rows, n_blocks, prior = [0] * B, [0] * B, [0] * B
+        state, buf = mirror.state, mirror.buf
+        for i, s_id in enumerate(seq_ids):
+            st = state[s_id]
+            table = tables[s_id]
+            n, k = len(table), st[1]
+            if table is not st[2] or n < k or (n == k and n and table[-1] != st[3]):
+                mirror.resync(st, table)
+                buf = mirror.buf
+            elif n > k:
+                mirror._fit(st[0] + 1, n)
+                buf = mirror.buf
+                buf[st[0], k:n] = table[k:]
+                st[1], st[3] = n, table[-1]
+            rows[i], n_blocks[i], prior[i] = st[0], n, lens[s_id]
+        rows = np.asarray(rows, dtype=np.int64)
+        num_new = np.fromiter((n for _, n in seqs), dtype=np.int64, count=B)
+        num_prior = np.asarray(prior, dtype=np.int64)
+        n_blocks = np.asarray(n_blocks, dtype=np.int64)
+        totals = num_prior + num_new
+        bad = np.nonzero(totals > n_blocks * bs)[0]
+        assert not len(bad), (f"seq {seq_ids[bad[0]]}: {totals[bad[0]]} tokens but only "
+                              f"{n_blocks[bad[0]]} blocks allocated")
+        used = (totals + bs - 1) // bs
+        W = max(1, int(used.max(initial=1)))
+        ones = num_new == 1
+        n_dec = B if ones.all() else int(np.argmin(ones))
         pre_new = num_new[n_dec:]
         n_pre = B - n_dec
         ints = np.zeros(B * W + 2 * B + n_pre + 1, dtype=np.int32)
         tabs = ints[: B * W].reshape(B, W)
-        for i, (s, u) in enumerate(zip(seq_ids, used)):
-            tabs[i, :u] = self.block_tables[s][:u]
+        mirror._fit(1, W)
+        # entries past a sequence's used blocks are left as the mirror holds
+        # them (allocated-ahead block ids or zeros): no kernel reads them
+        tabs[:] = mirror.buf[rows, :W]
         ints[B * W: B * W + B] = totals
         ints[B * W + B: B * W + 2 * B] = num_prior
         if n_pre:
             ints[B * W + 2 * B + 1:] = np.cumsum(pre_new)
-        T = sum(num_new)
+        T = int(num_new.sum())
         slots = np.empty(T, dtype=np.int64)
-        o = 0
-        for s, p, n in zip(seq_ids, num_prior, num_new):
-            slots[o:o + n] = self._slots(self.block_tables[s], p, n)
+        # decode sequences: one slot each, gathered in one step
+        pos = num_prior[:n_dec]
+        slots[:n_dec] = mirror.buf[rows[:n_dec], pos // bs].astype(np.int64) * bs + pos % bs
+        o = n_dec
+        for i in range(n_dec, B):
+            n = int(num_new[i])
+            pos = np.arange(num_prior[i], num_prior[i] + n, dtype=np.int64)
+            slots[o:o + n] = mirror.buf[rows[i], pos // bs].astype(np.int64) * bs + pos % bs
             o += n
-        return dict(ints=ints, slots=slots, seq_ids=seq_ids, num_new=num_new, num_prior=num_prior,
-                    n_tokens=T, n_decode=n_dec, max_query_len=max(pre_new, default=0), B=B, W=W)
+        return dict(ints=ints, slots=slots, seq_ids=seq_ids, num_new=num_new.tolist(),
+                    num_prior=num_prior.tolist(), n_tokens=T, n_decode=n_dec,
+                    max_query_len=int(pre_new.max(initial=0)), B=B, W=W)
+
+    def _staging(self, nbytes: int) -> torch.Tensor:
+        """A pinned host buffer of >= nbytes from a small ring; waits (normally
+        not at all) until the copy last issued from that buffer has finished."""
+        ring = self._stage_ring
+        i = self._stage_next = (self._stage_next + 1) % len(ring)
+        buf, ev = ring[i]
+        if ev is not None:
+            ev.synchronize()
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 16, 2 * (0 if buf is None else buf.numel())),
+                              dtype=torch.uint8).pin_memory()
+        ring[i] = [buf, None]
+        return i, buf
 
     def prepare_step(self, seqs: list[tuple[int, int]]) -> StepMetadata:
-        """Build the device metadata of a step with one pinned host-to-device
-        copy of the int32 arrays and one of the slot mapping.  seqs =
-        [(seq_id, num_new)] in flat-batch order.  Flushes queued COW copies."""
+        """Build the device metadata of a step with one host-to-device copy:
+        the int32 arrays and the int64 slot mapping packed in one pinned
+        staging buffer.  seqs = [(seq_id, num_new)] in flat-batch order.
+        Flushes queued COW copies."""
         self.mgr.flush_copies()
         a = self.step_arrays(seqs)
         B, W = a["B"], a["W"]
         dev = self.mgr.device
-        ints_d = torch.from_numpy(a["ints"]).pin_memory().to(dev, non_blocking=True)
-        slots_d = torch.from_numpy(a["slots"]).pin_memory().to(dev, non_blocking=True)
+        ints, slots = a["ints"], a["slots"]
+        n_int = ints.nbytes
+        off = (n_int + 15) // 16 * 16  # the slots start 16-byte aligned
+        nbytes = off + slots.nbytes
+        if dev.type == "cuda":
+            i, stage = self._staging(nbytes)
+            host = stage.numpy()
+            host[:n_int] = ints.view(np.uint8)
+            host[off:nbytes] = slots.view(np.uint8)
+            dbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            dbuf.copy_(stage[:nbytes], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(dev))
+            self._stage_ring[i][1] = ev
+        else:
+            dbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            dbuf[:n_int] = torch.from_numpy(ints.view(np.uint8))
+            dbuf[off:nbytes] = torch.from_numpy(slots.view(np.uint8))
+        ints_d = dbuf[:n_int].view(torch.int32)
         return StepMetadata(
             seq_ids=a["seq_ids"], num_new=a["num_new"], num_prior=a["num_prior"],
             n_tokens=a["n_tokens"], n_decode=a["n_decode"], max_query_len=a["max_query_len"],
-            slot_mapping=slots_d,
+            slot_mapping=dbuf[off:nbytes].view(torch.int64),
             block_tables=ints_d[: B * W].view(B, W),
             context_lens=ints_d[B * W: B * W + B],
             num_prior_dev=ints_d[B * W + B: B * W + 2 * B],
@@ -323,12 +451,17 @@ class PagedKVCache:
             out = torch.empty((meta.n_tokens,) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
         nd = meta.n_decode
         if nd:
-            # decode sequences: append fused into the decode kernel
-            ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
-            ops.paged_decode_append_attention(q[:nd], k_new[:nd], v_new[:nd], mgr.k_pool[layer],
-                                              mgr.v_pool[layer], meta.block_tables[:nd],
-                                              meta.context_lens[:nd], scale, workspace=ws,
-                                              out=out[:nd], err=mgr.err)
+            # decode sequences: append fused into the decode kernel; the
+            # step's plan validates once and then only swaps layer pointers
+            plan = meta.decode_plan
+            if plan is None or plan.scale != scale:
+                ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
+                plan = meta.decode_plan = ops.DecodeAppendPlan(
+                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err)
+            whole = nd == meta.n_tokens
+            plan(q if whole else q[:nd], k_new if whole else k_new[:nd],
+                 v_new if whole else v_new[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
+                 out if whole else out[:nd])
         if nd < meta.n_seqs:
             ops.reshape_and_cache(k_new[nd:], v_new[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
                                   meta.slot_mapping[nd:], mgr.err)

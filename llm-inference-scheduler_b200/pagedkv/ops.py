@@ -197,6 +197,45 @@ def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: t
     return out
 
 
+class DecodeAppendPlan:
+    """pkv_paged_decode_append_attention for the layers of one step, which
+    share block tables, context lengths, scale, workspace and error word.
+
+    The first call (and any call whose tensors differ in dtype, shape, stride
+    or stream from the previous one) builds the arguments through the regular
+    validating path; the others reuse them and only fill in the layer's
+    pointers (q, k_new, v_new, pools, out), so a layer costs one ctypes call
+    and a few attribute reads instead of a full argument check."""
+
+    _PTRS = (0, 2, 4, 5, 8, 9)  # out, q, k_new, v_new, k_pool, v_pool in the C argument list
+
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None):
+        self._static = (block_tables, context_lens, scale, workspace, err)
+        self.scale = scale
+        self._key = None
+        self._args: list = []
+        self._fn = _lib.load().pkv_paged_decode_append_attention
+
+    def __call__(self, q, k_new, v_new, k_pool, v_pool, out) -> torch.Tensor:
+        key = (q.dtype, k_new.dtype, v_new.dtype, k_pool.dtype, v_pool.dtype, out.dtype,
+               q.shape, q.stride(), k_new.shape, k_new.stride(), v_new.shape, v_new.stride(),
+               k_pool.shape, v_pool.shape, out.shape, out.stride(), q.device,
+               torch.cuda.current_stream(q.device).cuda_stream)
+        if key != self._key or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+            tables, ctx, scale, ws, err = self._static
+            args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, tables, ctx, scale, ws,
+                                            out, err)
+            self._args, self._key = list(args), key
+        else:
+            a = self._args
+            a[0], a[2], a[4], a[5], a[8], a[9] = (out.data_ptr(), q.data_ptr(), k_new.data_ptr(),
+                                                  v_new.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr())
+        rc = self._fn(*self._args)
+        if rc:
+            _lib.check(rc, "pkv_paged_decode_append_attention")
+        return out
+
+
 class BoundLaunch:
     """A validated launch with its C-ABI arguments fixed (pointers, sizes and
     the stream that was current when it was bound).  Calling it re-issues the

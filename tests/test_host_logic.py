@@ -225,3 +225,87 @@ def test_exp2_polynomial_error_bound():
     y = bits.astype(np.uint32).view(np.float32).astype(np.float64)
     rel = np.abs(y / np.exp2(xc.astype(np.float64)) - 1)
     assert rel.max() < 1e-4, rel.max()
+
+
+def _step_arrays_direct(kv, seqs):
+    """The step arrays built directly from the block-table lists, sequence by
+    sequence, zero padded (what PagedKVCache.step_arrays computes through its
+    mirror, whose padding is unspecified)."""
+    bs = kv.mgr.block_size
+    B = len(seqs)
+    num_new = [n for _, n in seqs]
+    num_prior = [kv.seq_len(s) for s, _ in seqs]
+    totals = [p + n for p, n in zip(num_prior, num_new)]
+    used = [(t + bs - 1) // bs for t in totals]
+    W = max(1, max(used))
+    n_dec = 0
+    while n_dec < B and num_new[n_dec] == 1:
+        n_dec += 1
+    ints = np.zeros(B * W + 2 * B + (B - n_dec) + 1, dtype=np.int32)
+    for i, ((s, _), u) in enumerate(zip(seqs, used)):
+        ints[i * W: i * W + u] = kv.block_tables[s][:u]
+    ints[B * W: B * W + B] = totals
+    ints[B * W + B: B * W + 2 * B] = num_prior
+    if B - n_dec:
+        ints[B * W + 2 * B + 1:] = np.cumsum(num_new[n_dec:])
+    slots = np.concatenate([kv._slots(kv.block_tables[s], p, n)
+                            for (s, n), p in zip(seqs, num_prior)])
+    return ints, slots, n_dec, W
+
+
+def test_step_arrays_track_table_changes():
+    """PagedKVCache.step_arrays (host mirror of the tables) equals the arrays
+    built directly from the lists while tables grow, fork, copy-on-write,
+    are replaced, freed and re-added, over mixed decode / chunk steps."""
+    rng = np.random.default_rng(7)
+    mgr = BlockManager(4096, 16, 1, 1, 1, device=None)
+    kv = PagedKVCache(mgr)
+    live = {}
+    next_id = 0
+    for it in range(300):
+        op = rng.integers(0, 10)
+        if op < 3 or not live:  # new sequence with a fresh table
+            n = int(rng.integers(0, 40))
+            table = [mgr.allocate() for _ in range((n + 16) // 16 + 1)]
+            kv.add_sequence(next_id, table, n)
+            live[next_id] = table
+            next_id += 1
+        elif op == 3:  # fork a sequence (shared blocks), then copy-on-write its tail
+            s = int(rng.choice(list(live)))
+            for b in kv.block_tables[s]:
+                mgr.incref(b)
+            kv.add_sequence(next_id, list(kv.block_tables[s]), kv.seq_len(s))
+            live[next_id] = kv.block_tables[next_id]
+            kv.ensure_writable_tail(next_id)
+            next_id += 1
+        elif op == 4 and len(live) > 1:  # free
+            s = int(rng.choice(list(live)))
+            for b in kv.block_tables[s]:
+                mgr.decref(b)
+            kv.free_sequence(s)
+            del live[s]
+        elif op == 5:  # the caller replaces a table with a new list object
+            s = int(rng.choice(list(live)))
+            kv.block_tables[s] = list(kv.block_tables[s])
+        # one step over a random subset: decodes first, then chunks
+        ids = [int(x) for x in rng.permutation(list(live))[: int(rng.integers(1, len(live) + 1))]]
+        seqs = []
+        for s in ids:
+            n = 1 if rng.random() < 0.7 else int(rng.integers(2, 40))
+            need = (kv.seq_len(s) + n + 15) // 16
+            while len(kv.block_tables[s]) < need:
+                kv.block_tables[s].append(mgr.allocate())  # the scheduler grows tables in place
+            seqs.append((s, n))
+        seqs.sort(key=lambda x: x[1] != 1)
+        a = kv.step_arrays(seqs)
+        ints, slots, n_dec, W = _step_arrays_direct(kv, seqs)
+        assert a["n_decode"] == n_dec and a["W"] == W
+        B = len(seqs)
+        got, want = a["ints"][: B * W].reshape(B, W), ints[: B * W].reshape(B, W)
+        for i, (s, n) in enumerate(seqs):  # the used blocks of each row (the rest is unspecified)
+            u = (kv.seq_len(s) + n + 15) // 16
+            np.testing.assert_array_equal(got[i, :u], want[i, :u])
+        np.testing.assert_array_equal(a["ints"][B * W:], ints[B * W:])
+        np.testing.assert_array_equal(a["slots"], slots)
+        for s, n in seqs:  # advance, as the last layer of forward_layer does
+            kv._len[s] += n
