@@ -272,10 +272,17 @@ def test_decode_zero_context_and_flags(decode_impl):
     tabs = torch.tensor([[0, 1], [2, 3], [4, 5]], dtype=torch.int32, device="cuda")
     ctx = torch.tensor([20, 0, 5], dtype=torch.int32, device="cuda")
     err = ops.new_error_flags("cuda")
-    out = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err)
+    out = torch.full_like(q, 7.0)  # rows of empty sequences must be overwritten with zeros
+    ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, out=out, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    assert out[1].eq(0).all() and torch.isfinite(out).all()
+    assert out[1].eq(0).all() and torch.isfinite(out).all() and not out[0].eq(7.0).any()
+    # every sequence empty: no KV block to stream, all rows zero
+    out = torch.full_like(q, 7.0)
+    ops.paged_decode_attention(q, kp, vp, tabs, torch.zeros(3, dtype=torch.int32, device="cuda"),
+                               0.125, out=out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and out.eq(0).all()
     # context beyond the table: flagged and clamped, no fault
     ctx = torch.tensor([20, 40, 5], dtype=torch.int32, device="cuda")
     ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err)
