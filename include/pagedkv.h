@@ -56,6 +56,7 @@ extern "C" {
 #define PKV_FLAG_CONTEXT_EXCEEDS_TABLE 4
 #define PKV_FLAG_PIPELINE_TIMEOUT 8
 #define PKV_FLAG_BAD_QUERY_LAYOUT 16
+#define PKV_FLAG_POSITION_OUT_OF_RANGE 32
 
 /* size of the device-resident scratch array behind
  * pkv_paged_decode_attention_noalloc (per GPU, held until the process exits) */
@@ -99,6 +100,33 @@ int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride,
 int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
                     const int32_t* block_pairs, int n_pairs, int num_blocks,
                     int64_t block_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
+ * Rotary embedding of q and k fused with the KV append (one launch per
+ * layer).  Replaces the RoPE of the projected q and k in Qwen2Model.forward
+ * (mini_engine/model/qwen2.py:152-158; K is cached post-RoPE) followed by the
+ * scatter of PagedKVCache.append_and_fetch (block_manager.py:121-131).
+ *   qkv[t]  : one row per token, [q heads | k heads | v heads] x head_dim
+ *             (the fused q/k/v projection), qkv_row_stride elements apart;
+ *   q_out[t]: the rotated q, [n_q_heads][head_dim], q_out_row_stride apart;
+ *   k_pool / v_pool at slot_mapping[t] (as pkv_reshape_and_cache): the
+ *             rotated k and the unrotated v.
+ * Rotation of the half-split pairs (i, i + head_dim/2) with the caller's
+ * tables cos_table / sin_table [max_position][head_dim] (the model dtype),
+ * row positions[t]; each product and the sum are rounded to the element type
+ * as separate elementwise multiply and add operations round them, so the
+ * result equals that unfused computation bit for bit.  A position outside
+ * [0, max_position) sets PKV_FLAG_POSITION_OUT_OF_RANGE and the token is
+ * skipped; slot -1 writes only q; a slot past the pool sets
+ * PKV_FLAG_SLOT_OUT_OF_RANGE.  head_dim must be even.
+ */
+int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                               int64_t qkv_row_stride, const int64_t* positions,
+                               const void* cos_table, const void* sin_table, int max_position,
+                               void* k_pool, void* v_pool, const int64_t* slot_mapping,
+                               int n_tokens, int num_blocks, int block_size, int n_q_heads,
+                               int n_kv_heads, int head_dim, int dtype, int* err_flags,
+                               pkv_stream_t stream);
 
 /*
  * Bytes of device workspace pkv_paged_decode_attention needs for n_seqs

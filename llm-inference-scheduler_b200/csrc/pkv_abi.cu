@@ -199,6 +199,48 @@ int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride, in
                                             static_cast<cudaStream_t>(stream)));
 }
 
+int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                               int64_t qkv_row_stride, const int64_t* positions,
+                               const void* cos_table, const void* sin_table, int max_position,
+                               void* k_pool, void* v_pool, const int64_t* slot_mapping,
+                               int n_tokens, int num_blocks, int block_size, int n_q_heads,
+                               int n_kv_heads, int head_dim, int dtype, int* err_flags,
+                               pkv_stream_t stream) {
+  if (n_tokens < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_tokens == 0) return PKV_OK;
+  if (!q_out || !qkv || !positions || !cos_table || !sin_table || !k_pool || !v_pool ||
+      !slot_mapping)
+    return PKV_ERR_NULL_POINTER;
+  if (!valid_dtype(dtype)) return PKV_ERR_BAD_DTYPE;
+  if (num_blocks <= 0 || block_size <= 0 || n_q_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 ||
+      (head_dim & 1) || max_position <= 0)
+    return PKV_ERR_BAD_SHAPE;
+  if (q_out_row_stride < static_cast<int64_t>(n_q_heads) * head_dim ||
+      qkv_row_stride < static_cast<int64_t>(n_q_heads + 2 * n_kv_heads) * head_dim)
+    return PKV_ERR_BAD_SHAPE;
+  RopeArgs a{};
+  a.q_out = q_out;
+  a.q_out_stride = q_out_row_stride;
+  a.qkv = qkv;
+  a.qkv_stride = qkv_row_stride;
+  a.positions = positions;
+  a.cos_t = cos_table;
+  a.sin_t = sin_table;
+  a.max_pos = max_position;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.slots = slot_mapping;
+  a.n_tokens = n_tokens;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.dtype = dtype;
+  a.err = err_flags;
+  return status_of(launch_rope_reshape_and_cache(a, static_cast<cudaStream_t>(stream)));
+}
+
 int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
                     const int32_t* block_pairs, int n_pairs, int num_blocks, int64_t block_bytes,
                     int* err_flags, pkv_stream_t stream) {

@@ -9,6 +9,23 @@
 
 namespace pkv {
 
+struct RopeArgs {
+  void* q_out;
+  int64_t q_out_stride;  // elements between token rows
+  const void* qkv;
+  int64_t qkv_stride;
+  const int64_t* positions;
+  const void* cos_t;
+  const void* sin_t;
+  int max_pos;
+  void* k_pool;
+  void* v_pool;
+  const int64_t* slots;
+  int n_tokens, num_blocks, block_size, n_q_heads, n_kv_heads, head_dim, dtype;
+  int* err;
+};
+cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream);
+
 struct AttnArgs {
   void* out;
   int64_t out_stride;  // elements between token rows of out

@@ -1,0 +1,130 @@
+// pkv_rope.cu -- rotary embedding of q and k fused with the KV append.
+//
+// Replaces, per layer, the reference's RoPE of the projected q and k
+// (mini_engine/model/qwen2.py:152-158: K is stored post-RoPE) followed by the
+// scatter of k and v into the block pool (PagedKVCache.append_and_fetch,
+// mini_engine/paged/block_manager.py:121-131).  Input is the fused q|k|v
+// projection row of each token; output is the rotated q (for the attention
+// kernels) and the rotated k plus v written at the token's slot.
+//
+// Rotation (half-split pairs, as the reference and Hugging Face Qwen2):
+//   out[i]        = x[i] * cos[p, i]        - x[i + D/2] * sin[p, i]
+//   out[i + D/2]  = x[i + D/2] * cos[p, i + D/2] + x[i] * sin[p, i + D/2]
+// with the model's own cos/sin tables (computed in fp32, stored in the model
+// dtype).  Each product and the sum are rounded to the element type exactly
+// as the separate elementwise operations of the unfused path round them
+// (multiply in fp32, round; add in fp32, round; no fused multiply-add), so
+// the result is bit-identical to that path for fp32, fp16 and bf16.
+//
+// One warp per token; lane l owns the pairs (i, i + D/2) for i = l, l + 32,
+// ... of every head, so each head's loads and stores are coalesced.
+#include "pkv_common.cuh"
+#include "pkv_internal.h"
+
+namespace pkv {
+
+template <typename E> __device__ __forceinline__ E rnd(float x);
+template <> __device__ __forceinline__ float rnd<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half rnd<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 rnd<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <typename E> __device__ __forceinline__ float tof(E x) { return static_cast<float>(x); }
+template <> __device__ __forceinline__ float tof<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+// a * c + b * s with the unfused path's rounding: each product rounded to E,
+// then the sum rounded to E
+template <typename E>
+__device__ __forceinline__ E rot_term(float a, float c, float b, float s) {
+  const float p = tof<E>(rnd<E>(__fmul_rn(a, c)));
+  const float q = tof<E>(rnd<E>(__fmul_rn(b, s)));
+  return rnd<E>(__fadd_rn(p, q));
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256) rope_reshape_and_cache_kernel(
+    E* __restrict__ q_out, int64_t q_out_stride, const E* __restrict__ qkv, int64_t qkv_stride,
+    const int64_t* __restrict__ positions, const E* __restrict__ cos_t,
+    const E* __restrict__ sin_t, int64_t max_pos, E* __restrict__ k_pool, E* __restrict__ v_pool,
+    const int64_t* __restrict__ slots, int64_t n_slots, int n_tokens, int hq, int hkv, int d,
+    int* err) {
+  // launched with programmatic serialization: wait for the preceding grid
+  // (it may still read the pool or write qkv), then let the next kernel's
+  // prologue start
+  pdl_wait();
+  pdl_trigger();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const int64_t pos = __ldg(positions + t);
+  if (pos < 0 || pos >= max_pos) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t slot = __ldg(slots + t);
+  if (slot >= n_slots) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
+  }
+  const bool store_kv = slot >= 0 && slot < n_slots;  // slot -1: padding token
+  const E* row = qkv + static_cast<int64_t>(t) * qkv_stride;
+  const E* cr = cos_t + pos * d;
+  const E* sr = sin_t + pos * d;
+  const int half = d >> 1;
+  E* qrow = q_out + static_cast<int64_t>(t) * q_out_stride;
+  E* krow = store_kv ? k_pool + slot * (static_cast<int64_t>(hkv) * d) : nullptr;
+  for (int i = lane; i < half; i += 32) {
+    const float c1 = tof<E>(__ldg(cr + i)), c2 = tof<E>(__ldg(cr + i + half));
+    const float s1 = tof<E>(__ldg(sr + i)), s2 = tof<E>(__ldg(sr + i + half));
+    for (int h = 0; h < hq + hkv; ++h) {
+      const E* x = row + h * d;
+      const float x1 = tof<E>(__ldg(x + i)), x2 = tof<E>(__ldg(x + i + half));
+      const E o1 = rot_term<E>(x1, c1, -x2, s1);
+      const E o2 = rot_term<E>(x2, c2, x1, s2);
+      if (h < hq) {
+        qrow[h * d + i] = o1;
+        qrow[h * d + i + half] = o2;
+      } else if (store_kv) {
+        krow[(h - hq) * d + i] = o1;
+        krow[(h - hq) * d + i + half] = o2;
+      }
+    }
+  }
+  if (store_kv) {
+    const E* vsrc = row + (hq + hkv) * d;
+    E* vdst = v_pool + slot * (static_cast<int64_t>(hkv) * d);
+    for (int i = lane; i < hkv * d; i += 32) vdst[i] = __ldg(vsrc + i);
+  }
+}
+
+cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream) {
+  if (a.n_tokens == 0) return cudaSuccess;
+  const int threads = 256;
+  const int grid = (a.n_tokens + 7) / 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int64_t n_slots = static_cast<int64_t>(a.num_blocks) * a.block_size;
+  auto go = [&](auto tag) {
+    using E = decltype(tag);
+    return cudaLaunchKernelEx(&cfg, rope_reshape_and_cache_kernel<E>, static_cast<E*>(a.q_out),
+                              a.q_out_stride, static_cast<const E*>(a.qkv), a.qkv_stride,
+                              a.positions, static_cast<const E*>(a.cos_t),
+                              static_cast<const E*>(a.sin_t), static_cast<int64_t>(a.max_pos),
+                              static_cast<E*>(a.k_pool), static_cast<E*>(a.v_pool), a.slots, n_slots,
+                              a.n_tokens, a.n_q_heads, a.n_kv_heads, a.head_dim, a.err);
+  };
+  if (a.dtype == PKV_DTYPE_F32) return go(float{});
+  if (a.dtype == PKV_DTYPE_F16) return go(__half{});
+  return go(__nv_bfloat16{});
+}
+
+}  // namespace pkv

@@ -32,6 +32,7 @@ FLAG_BLOCK_OUT_OF_RANGE = 2
 FLAG_CONTEXT_EXCEEDS_TABLE = 4
 FLAG_PIPELINE_TIMEOUT = 8
 FLAG_BAD_QUERY_LAYOUT = 16
+FLAG_POSITION_OUT_OF_RANGE = 32
 
 DECODE_AUTO = 0
 DECODE_GENERIC = 1
@@ -43,6 +44,8 @@ SIGNATURES = {
     "pkv_status_string": (ctypes.c_char_p, [_I]),
     "pkv_reshape_and_cache": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "pkv_copy_blocks": (_I, [_P, _P, _I64, _I, _P, _I, _I, _I64, _P, _P]),
+    "pkv_rope_reshape_and_cache": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I,
+                                        _I, _I, _I, _I, _P, _P]),
     "pkv_decode_workspace_bytes": (_SZ, [_I, _I, _I]),
     "pkv_paged_decode_attention": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _I, _I,
                                         _I, _I, _I, _F, _I, _P, _SZ, _P, _P]),

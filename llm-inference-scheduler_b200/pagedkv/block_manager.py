@@ -170,6 +170,7 @@ class StepMetadata:
     query_start_loc: torch.Tensor   # int32 [B - n_decode + 1], relative to the prefill rows
     num_prior_dev: torch.Tensor     # int32 [B]
     decode_plan: ops.DecodeAppendPlan | None = None  # built by the first forward_layer
+    decode_plain_plan: ops.DecodePlan | None = None   # built by the first forward_layer_qkv
 
     @property
     def n_seqs(self) -> int:
@@ -465,6 +466,41 @@ class PagedKVCache:
         if nd < meta.n_seqs:
             ops.reshape_and_cache(k_new[nd:], v_new[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
                                   meta.slot_mapping[nd:], mgr.err)
+            ops.paged_prefill_attention(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
+                                        meta.block_tables[nd:], meta.query_start_loc,
+                                        meta.num_prior_dev[nd:], meta.max_query_len, scale,
+                                        out=out[nd:], err=mgr.err)
+        if advance and layer == mgr.num_layers - 1:
+            for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
+                self._len[s] = p + n
+        return out
+
+    def forward_layer_qkv(self, layer: int, qkv: torch.Tensor, positions: torch.Tensor,
+                          cos: torch.Tensor, sin: torch.Tensor, meta: StepMetadata, scale: float,
+                          out: torch.Tensor | None = None, advance: bool = True) -> torch.Tensor:
+        """forward_layer for the rows of the fused q|k|v projection, qkv
+        [T, (Hq + 2 Hkv) D]: one launch rotates q and k at `positions` (RoPE
+        tables cos/sin [max_pos, D]) and appends the rotated k and v; then the
+        step's attention launches (decode without a second append, chunked
+        prefill).  Returns out [T, Hq, D].  Same results as rotating q and k
+        with Rope.rotate and calling forward_layer."""
+        mgr = self.mgr
+        mgr.flush_copies()
+        q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer], mgr.v_pool[layer],
+                                       meta.slot_mapping, err=mgr.err)
+        if out is None:
+            out = torch.empty_like(q)
+        nd = meta.n_decode
+        if nd:
+            plan = meta.decode_plain_plan
+            if plan is None or plan.scale != scale:
+                ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
+                plan = meta.decode_plain_plan = ops.DecodePlan(
+                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err)
+            whole = nd == meta.n_tokens
+            plan(q if whole else q[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
+                 out if whole else out[:nd])
+        if nd < meta.n_seqs:
             ops.paged_prefill_attention(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
                                         meta.block_tables[nd:], meta.query_start_loc,
                                         meta.num_prior_dev[nd:], meta.max_query_len, scale,

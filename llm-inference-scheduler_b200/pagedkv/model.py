@@ -8,13 +8,15 @@ final RMSNorm -> tied LM head on the last new token of each sequence.  The
 weights use the reference's (Hugging Face) names, so one weight dict drives
 both this model and the reference's.
 
-What changes is only the attention call site (qwen2.py:158-166): instead of a
-Python loop of append_and_fetch + _attention per sequence, each layer calls
-PagedKVCache.forward_layer once with the step metadata built by prepare_step
-(one append launch, one decode launch for the leading one-token sequences,
-one chunked-prefill launch for the rest).  The q/k/v projections are one
-fused GEMM; RMSNorm, RoPE, the MLP and the LM head stay torch operations (out
-of scope of the KV path).
+What changes is the attention call site (qwen2.py:152-166): instead of RoPE
+on q and k and a Python loop of append_and_fetch + _attention per sequence,
+each layer makes one fused q/k/v projection GEMM and calls
+PagedKVCache.forward_layer_qkv with the step metadata built by prepare_step:
+one launch rotates q and k and appends k and v (bit-identical to the torch
+RoPE + append), then one decode launch for the leading one-token sequences
+and one chunked-prefill launch for the rest.  fused_rope=False keeps RoPE as
+torch operations and calls forward_layer (the same results).  RMSNorm, the
+MLP and the LM head stay torch operations (out of scope of the KV path).
 """
 
 from __future__ import annotations
@@ -127,8 +129,9 @@ class PagedQwen2Model:
     """Qwen2 forward over a flat token batch with paged attention."""
 
     def __init__(self, cfg: Qwen2Config, weights: dict[str, torch.Tensor], device="cuda",
-                 dtype=torch.float16):
+                 dtype=torch.float16, fused_rope: bool = True):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        self.fused_rope = fused_rope
         dev = self.device
         w = {k: v.to(device=dev, dtype=dtype) for k, v in weights.items()}
         self.embed = w["model.embed_tokens.weight"]
@@ -160,19 +163,21 @@ class PagedQwen2Model:
         pos_np = np.concatenate([s.positions for s in seq_infos]).astype(np.int64)
         positions = torch.from_numpy(pos_np).pin_memory().to(self.device, non_blocking=True)
         cos_t, sin_t = self.rope.tables(int(pos_np.max()) + 1)
-        cos, sin = cos_t[positions].unsqueeze(1), sin_t[positions].unsqueeze(1)
+        if not self.fused_rope:
+            cos, sin = cos_t[positions].unsqueeze(1), sin_t[positions].unsqueeze(1)
         h = self.embed[input_ids]
         T = h.shape[0]
         for li, lw in enumerate(self.layers):
             residual = h
             x = rms_norm(h, lw["ln1"], cfg.rms_norm_eps)
             qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
-            q = qkv[:, : hq * d].view(T, hq, d)
-            k = qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d)
-            v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
-            q = Rope.rotate(q, cos, sin)
-            k = Rope.rotate(k, cos, sin)
-            attn = kv_cache.forward_layer(li, q, k, v, meta, self.scale)
+            if self.fused_rope:
+                attn = kv_cache.forward_layer_qkv(li, qkv, positions, cos_t, sin_t, meta, self.scale)
+            else:
+                q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), cos, sin)
+                k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), cos, sin)
+                v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+                attn = kv_cache.forward_layer(li, q, k, v, meta, self.scale)
             h = residual + F.linear(attn.view(T, hq * d), lw["wo"])
             residual = h
             x = rms_norm(h, lw["ln2"], cfg.rms_norm_eps)

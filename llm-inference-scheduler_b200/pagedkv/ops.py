@@ -118,6 +118,55 @@ def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device) -> 
                        device=device)
 
 
+def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor,
+                           sin: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                           slot_mapping: torch.Tensor, q_out: torch.Tensor | None = None,
+                           err: torch.Tensor | None = None) -> torch.Tensor:
+    """Rotary embedding of q and k fused with the append.
+
+    qkv: [T, (Hq + 2 Hkv) * D] rows of the fused q/k/v projection (unit inner
+    stride); positions: int64 [T]; cos, sin: [max_pos, D] tables in the pool
+    dtype.  Writes the rotated k and the v of token t to the pools at
+    slot_mapping[t] (-1 skips) and returns the rotated q [T, Hq, D] (into
+    q_out when given).  Bit-identical to rotating q and k with separate
+    elementwise multiply/add operations (pagedkv.model.Rope.rotate) followed
+    by reshape_and_cache.  Reference: qwen2.py:152-158 (RoPE before the
+    append, K cached post-RoPE) + block_manager.py:121-131.
+    """
+    for t, n in ((qkv, "qkv"), (positions, "positions"), (cos, "cos"), (sin, "sin"),
+                 (k_pool, "k_pool"), (v_pool, "v_pool"), (slot_mapping, "slot_mapping")):
+        _cuda(t, n)
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("pagedkv: qkv must be [tokens, (n_q + 2 n_kv) * head_dim] with unit inner stride")
+    if positions.dtype != torch.int64 or slot_mapping.dtype != torch.int64 or \
+            not positions.is_contiguous() or not slot_mapping.is_contiguous():
+        raise TypeError("pagedkv: positions and slot_mapping must be contiguous int64 tensors")
+    if not (k_pool.is_contiguous() and v_pool.is_contiguous() and cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("pagedkv: pools and rope tables must be contiguous")
+    dt = qkv.dtype
+    if any(t.dtype != dt for t in (cos, sin, k_pool, v_pool)):
+        raise TypeError("pagedkv: qkv, the rope tables and the pools must share one dtype")
+    nb, bs, hkv, d = k_pool.shape
+    T, W = qkv.shape
+    hq = W // d - 2 * hkv if W % d == 0 else 0
+    if hq <= 0 or cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != d or \
+            positions.shape[0] != T or slot_mapping.shape[0] != T:
+        raise ValueError("pagedkv: qkv / tables / positions / slot_mapping shapes disagree")
+    if q_out is None:
+        q_out = torch.empty((T, hq, d), dtype=dt, device=qkv.device)
+    elif q_out.dtype != dt or tuple(q_out.shape) != (T, hq, d):
+        raise ValueError("pagedkv: q_out must be [tokens, n_q_heads, head_dim] in the qkv dtype")
+    if T == 0:
+        return q_out
+    rc = _lib.load().pkv_rope_reshape_and_cache(
+        q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),
+        positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], k_pool.data_ptr(),
+        v_pool.data_ptr(), slot_mapping.data_ptr(), T, nb, bs, hq, hkv, d, dtype_code(dt), _ptr(err),
+        _stream(qkv))
+    _lib.check(rc, "pkv_rope_reshape_and_cache")
+    return q_out
+
+
 def _check_tables(block_tables: torch.Tensor) -> None:
     _cuda(block_tables, "block_tables")
     if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.stride(1) != 1:
@@ -233,6 +282,32 @@ class DecodeAppendPlan:
         rc = self._fn(*self._args)
         if rc:
             _lib.check(rc, "pkv_paged_decode_append_attention")
+        return out
+
+
+class DecodePlan(DecodeAppendPlan):
+    """pkv_paged_decode_attention (no append: the step's K/V are already in
+    the pools) for the layers of one step, with the same reuse of validated
+    arguments as DecodeAppendPlan."""
+
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None):
+        super().__init__(block_tables, context_lens, scale, workspace, err)
+        self._fn = _lib.load().pkv_paged_decode_attention
+
+    def __call__(self, q, k_pool, v_pool, out) -> torch.Tensor:
+        key = (q.dtype, k_pool.dtype, v_pool.dtype, out.dtype, q.shape, q.stride(), k_pool.shape,
+               v_pool.shape, out.shape, out.stride(), q.device,
+               torch.cuda.current_stream(q.device).cuda_stream)
+        if key != self._key or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+            tables, ctx, scale, ws, err = self._static
+            args, out = _decode_args(q, k_pool, v_pool, tables, ctx, scale, ws, out, err)
+            self._args, self._key = list(args), key
+        else:
+            a = self._args
+            a[0], a[2], a[4], a[5] = out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
+        rc = self._fn(*self._args)
+        if rc:
+            _lib.check(rc, "pkv_paged_decode_attention")
         return out
 
 

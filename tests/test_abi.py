@@ -46,7 +46,7 @@ def test_header_constants_match_binding():
                  "UNSUPPORTED", "DRIVER"):
         assert d[f"PKV_ERR_{name}"] == getattr(_lib, f"ERR_{name}")
     for name in ("SLOT_OUT_OF_RANGE", "BLOCK_OUT_OF_RANGE", "CONTEXT_EXCEEDS_TABLE",
-                 "PIPELINE_TIMEOUT", "BAD_QUERY_LAYOUT"):
+                 "PIPELINE_TIMEOUT", "BAD_QUERY_LAYOUT", "POSITION_OUT_OF_RANGE"):
         assert d[f"PKV_FLAG_{name}"] == getattr(_lib, f"FLAG_{name}")
 
 
@@ -144,3 +144,29 @@ def test_decode_append_validation():
     a = list(base)
     a[15] = 0  # no sequences: nothing to do
     assert f(*a) == 0
+
+
+def test_rope_reshape_and_cache_validation():
+    f = _lib.load().pkv_rope_reshape_and_cache
+    # q_out, q_stride, qkv, qkv_stride, positions, cos, sin, max_pos, k_pool, v_pool, slots,
+    # n_tokens, num_blocks, block_size, hq, hkv, d, dtype, err, stream
+    base = [FAKE, 896, FAKE, 1152, FAKE, FAKE, FAKE, 4096, FAKE, FAKE, FAKE, 8, 64, 16, 14, 2, 64, 1,
+            None, None]
+    a = list(base)
+    a[11] = 0  # no tokens: nothing to do
+    assert f(*a) == 0
+    a = list(base)
+    a[4] = None  # positions
+    assert f(*a) == _lib.ERR_NULL_POINTER
+    a = list(base)
+    a[3] = 1151  # qkv row shorter than (14 + 2 * 2) * 64
+    assert f(*a) == _lib.ERR_BAD_SHAPE
+    a = list(base)
+    a[16] = 63  # odd head_dim
+    assert f(*a) == _lib.ERR_BAD_SHAPE
+    a = list(base)
+    a[7] = 0  # no table rows
+    assert f(*a) == _lib.ERR_BAD_SHAPE
+    a = list(base)
+    a[17] = 9
+    assert f(*a) == _lib.ERR_BAD_DTYPE

@@ -100,6 +100,19 @@ def test_fp32_greedy_streams_identical_to_reference(golden_e2e, weights, scenari
     assert [r.preemptions for r in reqs] == g["preemptions"]
 
 
+def test_fp32_unfused_rope_path_identical_to_reference(golden_e2e, weights):
+    """The same fp32 parity through the unfused path (torch RoPE +
+    forward_layer with the decode kernel's own append)."""
+    sc = C.e2e_scenarios()["prefix"]
+    g = golden_e2e["prefix"]
+    model = PagedQwen2Model(Qwen2Config(), weights, device="cuda", dtype=torch.float32,
+                            fused_rope=False)
+    reqs, _ = run_engine(model, sc, torch.float32)
+    for r, ref in zip(reqs, g["outputs"]):
+        assert r.output_ids == ref, (
+            f"req {r.req_id}: first divergence at token {first_divergence(r.output_ids, ref)}")
+
+
 @pytest.mark.parametrize("scenario", ["prefix", "preempt"])
 def test_fp16_greedy_streams_match_reference(golden_e2e, margins, weights, scenario):
     sc = C.e2e_scenarios()[scenario]

@@ -438,3 +438,93 @@ def test_forward_layer_mixed_batch(oracle_mod, dt):
         assert max_abs_diff(host(out, dt), ref, dt) <= PRODUCT_ATOL[dt]
     assert [kv.seq_len(s) for s, _, _ in plan] == [p + n for _, p, n in plan]
     m.check_errors()
+
+
+# ---------------------------------------------------------------- fused RoPE + append
+
+@pytest.mark.parametrize("dt", DTS)
+def test_rope_reshape_and_cache_bit_identical_to_torch_rope(dt):
+    """pkv_rope_reshape_and_cache against the unfused path it replaces:
+    Rope.rotate on q and k (separate torch multiply / add) then
+    reshape_and_cache.  Rotated q and both pools must be identical bit for
+    bit; a padding slot (-1) writes q only; a position outside the tables is
+    flagged and that token skipped."""
+    from pagedkv.model import Rope
+
+    tdt = TORCH_DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(61)
+    T, hq, hkv, d, nb = 200, 14, 2, 64, 64
+    rope = Rope(d, 1e6, "cuda", tdt)
+    cos, sin = rope.tables(5000)
+    qkv = torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda").to(tdt)
+    pos = torch.randint(0, 5000, (T,), generator=g, device="cuda")
+    slots = torch.randperm(nb * 16, generator=g, device="cuda")[:T]
+    slots[7] = -1
+    kp = torch.randn((nb, 16, hkv, d), generator=g, device="cuda").to(tdt)
+    vp = torch.randn_like(kp)
+    kp_ref, vp_ref = kp.clone(), vp.clone()
+    err = ops.new_error_flags("cuda")
+    q = ops.rope_reshape_and_cache(qkv, pos, cos, sin, kp, vp, slots, err=err)
+    c, s = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+    q_ref = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), c, s)
+    k_ref = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), c, s)
+    v_ref = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+    ops.reshape_and_cache(k_ref.contiguous(), v_ref.contiguous(), kp_ref, vp_ref, slots)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(q, q_ref)
+    assert torch.equal(kp, kp_ref) and torch.equal(vp, vp_ref)
+    # a position past the tables: flagged, token skipped, the rest written
+    pos[3] = 5000
+    q2 = torch.zeros_like(q)
+    ops.rope_reshape_and_cache(qkv, pos, cos, sin, kp, vp, slots, q_out=q2, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_POSITION_OUT_OF_RANGE
+    assert q2[3].eq(0).all() and torch.equal(q2[4:], q_ref[4:])
+
+
+@pytest.mark.parametrize("dt", ("f16", "f32"))
+def test_forward_layer_qkv_equals_forward_layer(dt):
+    """The fused RoPE + append path (forward_layer_qkv: rope kernel, decode
+    without append, prefill) gives the same outputs and pools as rotating in
+    torch and calling forward_layer (decode kernel with the fused append)."""
+    from pagedkv.model import Rope
+
+    tdt = TORCH_DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(62)
+    L, nb, hq, hkv, d = 2, 256, 14, 2, 64
+    plan = [(0, 100, 1), (1, 17, 1), (2, 0, 1), (3, 48, 30), (4, 5, 64), (5, 31, 1)]
+    caches = []
+    for _ in range(2):
+        m = BlockManager(nb, 16, L, hkv, d, device="cuda", dtype=tdt)
+        kv = PagedKVCache(m)
+        o = 0
+        for s, prior, n in plan:  # disjoint consecutive blocks
+            nblk = (prior + n + 15) // 16
+            kv.add_sequence(s, list(range(o, o + nblk)), prior)
+            o += nblk
+        caches.append((m, kv))
+    base_k = torch.randn((L, nb, 16, hkv, d), generator=g, device="cuda").to(tdt)
+    base_v = torch.randn_like(base_k)
+    for m, _ in caches:
+        m.k_cache.copy_(base_k)
+        m.v_cache.copy_(base_v)
+    metas = [kv.prepare_step([(s, n) for s, _, n in plan]) for _, kv in caches]
+    T = metas[0].n_tokens
+    pos = torch.from_numpy(np.concatenate([np.arange(p, p + n) for _, p, n in plan])).cuda()
+    rope = Rope(d, 1e6, "cuda", tdt)
+    cos, sin = rope.tables(4096)
+    for layer in range(L):
+        qkv = torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda").to(tdt)
+        out_a = caches[0][1].forward_layer_qkv(layer, qkv, pos, cos, sin, metas[0], 0.125)
+        c, s_ = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+        q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), c, s_)
+        k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), c, s_)
+        v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+        out_b = caches[1][1].forward_layer(layer, q, k, v, metas[1], 0.125)
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, out_b)
+    assert torch.equal(caches[0][0].k_cache, caches[1][0].k_cache)
+    assert torch.equal(caches[0][0].v_cache, caches[1][0].v_cache)
+    for m, _ in caches:
+        m.check_errors()
