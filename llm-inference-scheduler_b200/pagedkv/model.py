@@ -132,6 +132,9 @@ class PagedQwen2Model:
                  dtype=torch.float16, fused_rope: bool = True):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         self.fused_rope = fused_rope
+        # when a list: forward() appends (step start, step end, [(attn start,
+        # attn end) per layer]) CUDA events -- the attention share diagnostic
+        self.timing: list | None = None
         dev = self.device
         w = {k: v.to(device=dev, dtype=dtype) for k, v in weights.items()}
         self.embed = w["model.embed_tokens.weight"]
@@ -165,12 +168,20 @@ class PagedQwen2Model:
         cos_t, sin_t = self.rope.tables(int(pos_np.max()) + 1)
         if not self.fused_rope:
             cos, sin = cos_t[positions].unsqueeze(1), sin_t[positions].unsqueeze(1)
+        timing = self.timing
+        if timing is not None:
+            ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+            t_step = (ev(), ev())
+            t_attn = [(ev(), ev()) for _ in self.layers]
+            t_step[0].record()
         h = self.embed[input_ids]
         T = h.shape[0]
         for li, lw in enumerate(self.layers):
             residual = h
             x = rms_norm(h, lw["ln1"], cfg.rms_norm_eps)
             qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
+            if timing is not None:
+                t_attn[li][0].record()
             if self.fused_rope:
                 attn = kv_cache.forward_layer_qkv(li, qkv, positions, cos_t, sin_t, meta, self.scale)
             else:
@@ -178,6 +189,8 @@ class PagedQwen2Model:
                 k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), cos, sin)
                 v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
                 attn = kv_cache.forward_layer(li, q, k, v, meta, self.scale)
+            if timing is not None:
+                t_attn[li][1].record()
             h = residual + F.linear(attn.view(T, hq * d), lw["wo"])
             residual = h
             x = rms_norm(h, lw["ln2"], cfg.rms_norm_eps)
@@ -185,4 +198,8 @@ class PagedQwen2Model:
                                     lw["wdown"])
         h = rms_norm(h, self.final_norm, cfg.rms_norm_eps)
         last = torch.tensor([s.flat_start + s.num_tokens - 1 for s in seq_infos], device=self.device)
-        return F.linear(h[last], self.embed)
+        logits = F.linear(h[last], self.embed)
+        if timing is not None:
+            t_step[1].record()
+            timing.append((t_step, t_attn))
+        return logits
