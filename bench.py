@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops", "decode_fp8"),
+                    default="decode",
                     help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5; "
                          "cache_ops = reshape_and_cache and copy_blocks at bandwidth-sized batches")
     ap.add_argument("--append-tokens", type=int, nargs="+", default=[8192, 65536],
@@ -679,6 +680,97 @@ def run_e2e(args):
     print(json.dumps(line), flush=True)
 
 
+def run_decode_fp8(args):
+    """The config-3 decode step (same contexts, tables, 24 layers) over fp8
+    e4m3 pools with per-(token, KV head) fp32 scales: per layer the fp8 append
+    of the step's token (pkv_reshape_and_cache_fp8) and the fp8 decode.  One
+    GPU; fp16 q / out."""
+    import numpy as np
+    import torch
+
+    from pagedkv import BlockManager, ops
+    from pagedkv import workloads as W
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L, scale, dt = args.layers, 0.125, torch.float16
+    ctx = W.shard_contexts(args.batch, 0, 1)
+    B = len(ctx)
+    nblk = (ctx + 15) // 16
+    nb = int(math.ceil(1.1 * nblk.sum()))
+    tabs_np = W.make_tables(ctx, nb, seed=100)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=torch.float8_e4m3fn)
+    err = ops.new_error_flags(dev)
+    all_slots = torch.arange(nb * 16, device=dev, dtype=torch.int64)
+    fill = torch.empty((nb * 16, 2, 64), device=dev, dtype=dt)
+    for layer in range(L):  # every slot quantised from N(0,1) rows
+        fill.normal_(generator=g)
+        ops.reshape_and_cache_fp8(fill, fill, mgr.k_pool[layer], mgr.v_pool[layer], mgr.k_scale[layer],
+                                  mgr.v_scale[layer], all_slots, err)
+    del fill
+    q = torch.randn((L, B, 14, 64), generator=g, device=dev, dtype=dt)
+    kn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+    vn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+    out = torch.empty_like(q)
+    pos = ctx - 1
+    slots = torch.from_numpy(tabs_np[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16).to(dev)
+    tabs = torch.from_numpy(tabs_np).to(dev)
+    ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    ws = ops.new_decode_workspace(B, 14, 64, dev)
+    launches = []
+    for l in range(L):
+        launches.append(ops.bind_reshape_and_cache_fp8(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
+                                                       mgr.k_scale[l], mgr.v_scale[l], slots, err))
+        launches.append(ops.bind_paged_decode_attention_fp8(q[l], mgr.k_pool[l], mgr.v_pool[l],
+                                                            mgr.k_scale[l], mgr.v_scale[l], tabs, ctx_d,
+                                                            scale, ws, out[l], err))
+    tot = int(ctx.sum())
+    dec_bytes = (tot * 2 * 64 * 2 + tot * 2 * 2 * 4 + B * 14 * 64 * 2 * 2 + int(nblk.sum()) * 4 + B * 4)
+    app_bytes = B * (2 * 2 * 64 * 2 + 2 * 2 * 64 + 2 * 2 * 4 + 8)
+    step_bytes = L * (dec_bytes + app_bytes)
+
+    def step():
+        for f in launches:
+            f()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_flags(err, "fp8 warm-up")
+    sampler = ClockSampler([0])
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    sampler.stop()
+    ops.check_flags(err, "fp8 timed region")
+    ms = start.elapsed_time(end) / args.steps
+    peak, kind = peaks()
+    line = {
+        "metric": "paged decode attn KV GB/s and decode tok/s with fp8 e4m3 KV (config-3 shape)",
+        "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "dtype": "fp8 e4m3 KV (fp32 row scales), f16 q/out",
+        "data": "synthetic (seeded normal rows quantised on the device; lognormal contexts)",
+        "config": {"workload": "config3 shape: B=256, ctx lognormal(1024, 0.5) in [16,8192], 24 layers x "
+                               "(fp8 append + fp8 decode), 14q/2kv, d64", "sum_ctx": tot,
+                   "bytes_per_token": 2 * 64 * 2 + 2 * 2 * 4},
+        "decode_tok_s": round(B / (ms * 1e-3), 1),
+        "hbm_frac_step": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak": peak, "peak_kind": kind,
+        "gpu_launches": 3 * L * args.steps,  # fp8 append, decode, split-K merge per layer
+        "clocks": sampler.summary(t0, t1),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_cache_ops(args):
     """reshape_and_cache and copy_blocks at batches large enough to measure HBM
     bandwidth (one GPU).  Append: T tokens of K and V per launch scattered
@@ -784,6 +876,8 @@ def main():
         run_prefill(args)
     elif args.workload == "cache_ops":
         run_cache_ops(args)
+    elif args.workload == "decode_fp8":
+        run_decode_fp8(args)
     else:
         run_ours(args)
 

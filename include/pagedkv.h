@@ -235,6 +235,47 @@ int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q
  */
 int pkv_set_decode_impl(int impl);
 
+/*
+ * fp8 e4m3 KV pools.  No counterpart in the reference (its quant.py notes fp8
+ * KV as the next step after its group-wise absmax int8 weights, with the same
+ * math).  Pools hold one byte per element in the reference layout
+ * [num_blocks][block_size][n_kv_heads][head_dim]; each (slot, KV head) row has
+ * an fp32 scale in k_scale / v_scale [num_blocks * block_size][n_kv_heads]:
+ *   scale = absmax(row) / 448 (1 for an all-zero row),
+ *   byte  = e4m3(x / scale), round to nearest even, saturated at +-448,
+ *   value = e4m3_to_float(byte) * scale.
+ * q, out and the arithmetic stay in `dtype`; e4m3 values are exact in fp16.
+ */
+
+/* reshape_and_cache into fp8 pools: k, v in `dtype`, quantised per row. */
+int pkv_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_row_stride,
+                              int64_t v_row_stride, void* k_pool, void* v_pool, float* k_scale,
+                              float* v_scale, const int64_t* slot_mapping, int n_tokens,
+                              int num_blocks, int block_size, int n_kv_heads, int head_dim,
+                              int dtype, int* err_flags, pkv_stream_t stream);
+
+/* pkv_paged_decode_attention over fp8 pools (the new token already
+ * appended by pkv_reshape_and_cache_fp8); same workspace contract. */
+int pkv_paged_decode_attention_fp8(void* out, int64_t out_row_stride, const void* q,
+                                   int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                   const float* k_scale, const float* v_scale, int num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                                   float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                   int* err_flags, pkv_stream_t stream);
+
+/* pkv_paged_prefill_attention over fp8 pools (CUDA-core kernel). */
+int pkv_paged_prefill_attention_fp8(void* out, int64_t out_row_stride, const void* q,
+                                    int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                    const float* k_scale, const float* v_scale, int num_blocks,
+                                    const int32_t* block_tables, int64_t block_table_stride,
+                                    int max_blocks_per_seq, const int32_t* query_start_loc,
+                                    const int32_t* num_prior, int n_seqs, int n_tokens,
+                                    int max_query_len, int n_q_heads, int n_kv_heads, int head_dim,
+                                    int block_size, float scale, int dtype, int* err_flags,
+                                    pkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

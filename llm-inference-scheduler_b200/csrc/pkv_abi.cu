@@ -97,6 +97,25 @@ int check_attn(const void* out, int64_t out_stride, const void* q, int64_t q_str
   return PKV_OK;
 }
 
+// tensor-core decode when the shape allows it (16-bit or fp8 pools), else the
+// CUDA-core kernel
+int decode_dispatch(AttnArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a)) {
+    if (!workspace) return PKV_ERR_NULL_POINTER;
+    if (workspace_bytes < decode_workspace_bytes(a.n_seqs, a.n_q_heads, a.head_dim))
+      return PKV_ERR_WORKSPACE_TOO_SMALL;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return PKV_ERR_MISALIGNED;
+    const int fmt = a.k_scale != nullptr ? kPoolFp8 : a.dtype;
+    CUtensorMap km, vm;
+    int rc = cached_pool_map(&km, a.k_pool, a.num_blocks, a.block_size, a.n_kv_heads, a.head_dim, fmt);
+    if (rc != 0) return rc;
+    rc = cached_pool_map(&vm, a.v_pool, a.num_blocks, a.block_size, a.n_kv_heads, a.head_dim, fmt);
+    if (rc != 0) return rc;
+    return status_of(launch_decode_fast(a, &km, &vm, workspace, st));
+  }
+  return status_of(launch_generic_attention(a, st));
+}
+
 }  // namespace
 
 // Shared with the allocation-free decode entry point (pkv_decode_noalloc.cu).
@@ -117,16 +136,22 @@ int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, in
                           int n_kv_heads, int head_dim, int dtype) {
   auto enc = encoder();
   if (enc == nullptr) return PKV_ERR_DRIVER;
+  // 16-bit pools: 128-byte rows with the 128-byte swizzle (ldmatrix reads them
+  // in place); fp8 pools: 64-byte rows, unswizzled (converted by the consumers)
+  const bool fp8 = dtype == kPoolFp8;
+  const cuuint64_t es = fp8 ? 1 : 2;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(n_kv_heads),
                               static_cast<cuuint64_t>(num_blocks) * block_size};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2,
-                                 static_cast<cuuint64_t>(n_kv_heads) * head_dim * 2};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * es,
+                                 static_cast<cuuint64_t>(n_kv_heads) * head_dim * es};
   const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), 1u, static_cast<cuuint32_t>(block_size)};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUtensorMapDataType dt =
-      dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType dt = fp8                      ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUresult r = enc(map, dt, 3, const_cast<void*>(pool), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : PKV_ERR_DRIVER;
 }
@@ -197,6 +222,25 @@ int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride, in
                                             slot_mapping, n_tokens, num_blocks, block_size,
                                             n_kv_heads, head_dim, esize_of(dtype), err_flags,
                                             static_cast<cudaStream_t>(stream)));
+}
+
+int pkv_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_row_stride,
+                              int64_t v_row_stride, void* k_pool, void* v_pool, float* k_scale,
+                              float* v_scale, const int64_t* slot_mapping, int n_tokens,
+                              int num_blocks, int block_size, int n_kv_heads, int head_dim,
+                              int dtype, int* err_flags, pkv_stream_t stream) {
+  if (n_tokens < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_tokens == 0) return PKV_OK;
+  if (!k || !v || !k_pool || !v_pool || !k_scale || !v_scale || !slot_mapping)
+    return PKV_ERR_NULL_POINTER;
+  if (!valid_dtype(dtype)) return PKV_ERR_BAD_DTYPE;
+  if (num_blocks <= 0 || block_size <= 0 || n_kv_heads <= 0 || head_dim <= 0) return PKV_ERR_BAD_SHAPE;
+  const int64_t row = static_cast<int64_t>(n_kv_heads) * head_dim;
+  if (k_row_stride < row || v_row_stride < row) return PKV_ERR_BAD_SHAPE;
+  return status_of(launch_reshape_and_cache_fp8(k, v, k_row_stride, v_row_stride, k_pool, v_pool,
+                                                k_scale, v_scale, slot_mapping, n_tokens, num_blocks,
+                                                block_size, n_kv_heads, head_dim, dtype, err_flags,
+                                                static_cast<cudaStream_t>(stream)));
 }
 
 int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void* qkv,
@@ -297,20 +341,49 @@ int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
   a.scale = scale;
   a.dtype = dtype;
   a.err = err_flags;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a)) {
-    if (!workspace) return PKV_ERR_NULL_POINTER;
-    if (workspace_bytes < decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
-      return PKV_ERR_WORKSPACE_TOO_SMALL;
-    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return PKV_ERR_MISALIGNED;
-    CUtensorMap km, vm;
-    rc = cached_pool_map(&km, k_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
-    if (rc != 0) return rc;
-    rc = cached_pool_map(&vm, v_pool, num_blocks, block_size, n_kv_heads, head_dim, dtype);
-    if (rc != 0) return rc;
-    return status_of(launch_decode_fast(a, &km, &vm, workspace, st));
-  }
-  return status_of(launch_generic_attention(a, st));
+  return decode_dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int pkv_paged_decode_attention_fp8(void* out, int64_t out_row_stride, const void* q,
+                                   int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                   const float* k_scale, const float* v_scale, int num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                                   float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                   int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!context_lens || !k_scale || !v_scale) return PKV_ERR_NULL_POINTER;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.context_lens = context_lens;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_seqs;
+  a.max_query_len = 1;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  return decode_dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const void* q,
@@ -430,6 +503,52 @@ int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q
     return status_of(launch_prefill_fast(a, &qm, &km, &vm, st));
   }
   return status_of(launch_generic_attention(a, st));
+}
+
+int pkv_paged_prefill_attention_fp8(void* out, int64_t out_row_stride, const void* q,
+                                    int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                    const float* k_scale, const float* v_scale, int num_blocks,
+                                    const int32_t* block_tables, int64_t block_table_stride,
+                                    int max_blocks_per_seq, const int32_t* query_start_loc,
+                                    const int32_t* num_prior, int n_seqs, int n_tokens,
+                                    int max_query_len, int n_q_heads, int n_kv_heads, int head_dim,
+                                    int block_size, float scale, int dtype, int* err_flags,
+                                    pkv_stream_t stream) {
+  if (n_seqs < 0 || n_tokens < 0 || max_query_len < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0 || n_tokens == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!query_start_loc || !num_prior || !k_scale || !v_scale) return PKV_ERR_NULL_POINTER;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.query_start_loc = query_start_loc;
+  a.num_prior = num_prior;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_tokens;
+  a.max_query_len = max_query_len;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  // the CUDA-core kernel (dequantise on load); the tensor-core prefill reads
+  // 16-bit pools only
+  return status_of(launch_generic_attention(a, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -7,8 +7,12 @@
 // head_dim/32 output dims per lane.  Semantics follow the reference's gather
 // + _attention (mini_engine/paged/block_manager.py:136-141,
 // mini_engine/model/qwen2.py:98-128): key j is visible to new token i of a
-// sequence iff j <= num_prior + i.
+// sequence iff j <= num_prior + i.  With fp8 e4m3 pools (AttnArgs::k_scale
+// set) every K/V element is dequantised as e4m3(byte) * scale of its (slot,
+// KV head) row before it enters the fp32 arithmetic.
 #include <float.h>
+
+#include <type_traits>
 
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
@@ -18,7 +22,18 @@ namespace pkv {
 constexpr int kGenericWarps = 4;
 constexpr int kGenericMaxDPerLane = 8;  // head_dim <= 256
 
-template <typename T>
+// K/V element d of pool row `row` (slot * n_kv_heads + head), as fp32
+template <typename T, bool FP8>
+__device__ __forceinline__ float kv_elem(const void* pool, const float* scales, int64_t row,
+                                         int D, int d) {
+  if constexpr (FP8) {
+    return fp8_to_float(static_cast<const uint8_t*>(pool)[row * D + d]) * __ldg(scales + row);
+  } else {
+    return Elem<T>::to_f(static_cast<const T*>(pool)[row * D + d]);
+  }
+}
+
+template <typename T, bool FP8>
 __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(AttnArgs a) {
   extern __shared__ float qs_all[];
   const int lane = threadIdx.x & 31;
@@ -67,11 +82,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(A
   for (int d = lane; d < D; d += 32) qs[d] = Elem<T>::to_f(q[d]);
   __syncwarp();
 
-  const T* kp = static_cast<const T*>(a.k_pool);
-  const T* vp = static_cast<const T*>(a.v_pool);
   const int32_t* table = a.block_tables + static_cast<int64_t>(s) * a.bt_stride;
-  const int64_t head_off = static_cast<int64_t>(g) * D;
-  const int64_t tok_stride = static_cast<int64_t>(a.n_kv_heads) * D;
 
   float m = -FLT_MAX, l = 0.f;
   float acc[kGenericMaxDPerLane];
@@ -85,9 +96,9 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(A
     if (j < limit) {
       int blk = table[j / a.block_size];
       if (blk < 0 || blk >= a.num_blocks) { bad_block = true; blk = 0; }
-      const T* krow = kp + (static_cast<int64_t>(blk) * a.block_size + j % a.block_size) * tok_stride + head_off;
+      const int64_t krow = (static_cast<int64_t>(blk) * a.block_size + j % a.block_size) * a.n_kv_heads + g;
       float dot = 0.f;
-      for (int d = 0; d < D; ++d) dot = fmaf(qs[d], Elem<T>::to_f(krow[d]), dot);
+      for (int d = 0; d < D; ++d) dot = fmaf(qs[d], kv_elem<T, FP8>(a.k_pool, a.k_scale, krow, D, d), dot);
       sj = dot * a.scale;
     }
     float mc = sj;
@@ -108,11 +119,11 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(A
       const int key = j0 + jj;
       int blk = table[key / a.block_size];
       if (blk < 0 || blk >= a.num_blocks) blk = 0;
-      const T* vrow = vp + (static_cast<int64_t>(blk) * a.block_size + key % a.block_size) * tok_stride + head_off;
+      const int64_t vrow = (static_cast<int64_t>(blk) * a.block_size + key % a.block_size) * a.n_kv_heads + g;
 #pragma unroll
       for (int r = 0; r < kGenericMaxDPerLane; ++r) {
         const int d = lane + 32 * r;
-        if (d < D) acc[r] = fmaf(p, Elem<T>::to_f(vrow[d]), acc[r]);
+        if (d < D) acc[r] = fmaf(p, kv_elem<T, FP8>(a.v_pool, a.v_scale, vrow, D, d), acc[r]);
       }
     }
     m = m_new;
@@ -136,15 +147,21 @@ cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream) {
   const int64_t grid = (warps + kGenericWarps - 1) / kGenericWarps;
   if (grid > 0x7fffffff) return cudaErrorInvalidConfiguration;
   const size_t smem = sizeof(float) * kGenericWarps * a.head_dim;
+  const unsigned g = static_cast<unsigned>(grid);
+  auto go = [&](auto tag, auto fp8) {
+    using T = decltype(tag);
+    generic_attention_kernel<T, decltype(fp8)::value><<<g, kGenericWarps * 32, smem, stream>>>(a);
+  };
+  const bool fp8 = a.k_scale != nullptr;
   switch (a.dtype) {
     case PKV_DTYPE_F32:
-      generic_attention_kernel<float><<<static_cast<unsigned>(grid), kGenericWarps * 32, smem, stream>>>(a);
+      fp8 ? go(float{}, std::true_type{}) : go(float{}, std::false_type{});
       break;
     case PKV_DTYPE_F16:
-      generic_attention_kernel<__half><<<static_cast<unsigned>(grid), kGenericWarps * 32, smem, stream>>>(a);
+      fp8 ? go(__half{}, std::true_type{}) : go(__half{}, std::false_type{});
       break;
     default:
-      generic_attention_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), kGenericWarps * 32, smem, stream>>>(a);
+      fp8 ? go(__nv_bfloat16{}, std::true_type{}) : go(__nv_bfloat16{}, std::false_type{});
       break;
   }
   return cudaGetLastError();

@@ -136,6 +136,72 @@ __global__ void __launch_bounds__(256) append_at_context_end(
   }
 }
 
+// fp8 e4m3 append: K and V rows quantised per (token, KV head) with scale =
+// absmax / 448 (1 for an all-zero row), value = e4m3(x / scale) rounded to
+// nearest even and saturated; the byte goes to the pool, the scale to the
+// parallel fp32 scale array [slots][n_kv_heads].  One warp per token.
+template <typename E>
+__global__ void __launch_bounds__(256) reshape_and_cache_fp8_kernel(
+    const E* __restrict__ k, const E* __restrict__ v, int64_t k_stride, int64_t v_stride,
+    uint8_t* __restrict__ k_pool, uint8_t* __restrict__ v_pool, float* __restrict__ k_scale,
+    float* __restrict__ v_scale, const int64_t* __restrict__ slots, int n_tokens, int64_t n_slots,
+    int hkv, int d, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const int64_t slot = __ldg(slots + t);
+  if (slot < 0) return;  // padding token
+  if (slot >= n_slots) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
+    return;
+  }
+  for (int which = 0; which < 2; ++which) {
+    const E* src = which ? v + t * v_stride : k + t * k_stride;
+    uint8_t* dst = (which ? v_pool : k_pool) + slot * hkv * d;
+    float* sc = (which ? v_scale : k_scale) + slot * hkv;
+    for (int h = 0; h < hkv; ++h) {
+      float amax = 0.f;
+      for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(Elem<E>::to_f(src[h * d + i])));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float s = fp8_row_scale(amax);
+      for (int i = lane; i < d; i += 32) dst[h * d + i] = fp8_quantize(Elem<E>::to_f(src[h * d + i]), s);
+      if (lane == 0) sc[h] = s;
+    }
+  }
+}
+
+cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,
+                                         int64_t v_stride, void* k_pool, void* v_pool,
+                                         float* k_scale, float* v_scale, const int64_t* slots,
+                                         int n_tokens, int num_blocks, int block_size,
+                                         int n_kv_heads, int head_dim, int src_dtype, int* err,
+                                         cudaStream_t stream) {
+  if (n_tokens == 0) return cudaSuccess;
+  const int64_t n_slots = static_cast<int64_t>(num_blocks) * block_size;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((n_tokens + 7) / 8);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto go = [&](auto tag) {
+    using E = decltype(tag);
+    return cudaLaunchKernelEx(&cfg, reshape_and_cache_fp8_kernel<E>, static_cast<const E*>(k),
+                              static_cast<const E*>(v), k_stride, v_stride,
+                              static_cast<uint8_t*>(k_pool), static_cast<uint8_t*>(v_pool), k_scale,
+                              v_scale, slots, n_tokens, n_slots, n_kv_heads, head_dim, err);
+  };
+  if (src_dtype == PKV_DTYPE_F32) return go(float{});
+  if (src_dtype == PKV_DTYPE_F16) return go(__half{});
+  return go(__nv_bfloat16{});
+}
+
 cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k_stride,
                                          int64_t v_stride, void* k_pool, void* v_pool,
                                          const int32_t* tables, int64_t bt_stride, int max_blocks,

@@ -9,6 +9,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -364,6 +365,20 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
   const float p = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// ---- fp8 e4m3 KV: one scale per (token, KV head) row, absmax / 448
+constexpr float kFp8Max = 448.f;  // largest finite e4m3 value
+__device__ __forceinline__ float fp8_row_scale(float absmax) {
+  return absmax > 0.f ? __fdiv_rn(absmax, kFp8Max) : 1.f;
+}
+// round to nearest even, saturating at +-448 (CUDA's conversion)
+__device__ __forceinline__ uint8_t fp8_quantize(float x, float scale) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(__fdiv_rn(x, scale), __NV_SATFINITE, __NV_E4M3));
+}
+// exact: every e4m3 value is representable in fp16
+__device__ __forceinline__ float fp8_to_float(uint8_t b) {
+  return __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E4M3)));
 }
 
 // three-input maximum (one instruction on sm_100)

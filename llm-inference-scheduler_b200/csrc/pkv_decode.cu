@@ -22,6 +22,13 @@
 //    directly.  A sequence split across CTAs leaves (m, l, O) partials in the
 //    workspace, merged by a second small kernel (one CTA per sequence) that
 //    is launched right behind the decode kernel.
+//  * fp8 e4m3 pools (FP8 instantiation): the ring stage holds each head's
+//    16 x 64-byte fp8 K and V tiles plus the block's per-(token, KV head)
+//    fp32 scales (TMA + two bulk copies).  Each consumer warp converts its
+//    head's tiles into a 16-bit staging tile laid out exactly as the 16-bit
+//    TMA tiles (so the ldmatrix/MMA path is shared), releases the stage, and
+//    applies the scales outside the MMAs: K's to the token's scores, V's
+//    folded into P after the softmax sums.  e4m3 -> fp16/bf16 is exact.
 //  * Programmatic dependent launch chains append -> decode -> merge: each
 //    kernel's prologue (context scan, block-table reads) runs before
 //    griddepcontrol.wait and overlaps its predecessor; pool, q, out and
@@ -48,6 +55,7 @@ constexpr int kDecMaxCtas = 1024;
 constexpr int kDecMaxSeqs = 2048;
 constexpr int kDecMinBlocksPerCta = 4;
 constexpr int kDecTile = 2048;  // 16 tokens x 64 dims x 2 bytes
+constexpr int kDecTile8 = 1024;  // 16 tokens x 64 dims x 1 byte (fp8)
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -75,7 +83,29 @@ struct DecodeParams {
   int64_t k_new_stride_b, v_new_stride_b;  // bytes between rows
   uint8_t* k_pool;
   uint8_t* v_pool;
+  // fp8 pools: fp32 scale per (slot, KV head)
+  const float* k_scale;
+  const float* v_scale;
 };
+
+// 16 fp8 e4m3 values -> 16 values of T (exact), low byte first
+template <typename T> __device__ __forceinline__ uint32_t fp8x2_to(uint32_t two);
+template <> __device__ __forceinline__ uint32_t fp8x2_to<__half>(uint32_t two) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+template <> __device__ __forceinline__ uint32_t fp8x2_to<__nv_bfloat16>(uint32_t two) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+  const float2 f = __half22float2(__half2(h));
+  return pack2<__nv_bfloat16>(f.x, f.y);
+}
+template <typename T>
+__device__ __forceinline__ void fp8x16_to(const uint4& in, uint4& lo, uint4& hi) {
+  lo = make_uint4(fp8x2_to<T>(in.x & 0xffffu), fp8x2_to<T>(in.x >> 16), fp8x2_to<T>(in.y & 0xffffu),
+                  fp8x2_to<T>(in.y >> 16));
+  hi = make_uint4(fp8x2_to<T>(in.z & 0xffffu), fp8x2_to<T>(in.z >> 16), fp8x2_to<T>(in.w & 0xffffu),
+                  fp8x2_to<T>(in.w >> 16));
+}
 
 size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
   (void)n_seqs;
@@ -89,6 +119,9 @@ bool decode_fast_supported(const AttnArgs& a) {
   auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
   if (a.k_new != nullptr &&
       (!al(a.k_new, 16) || !al(a.v_new, 16) || (a.k_new_stride * 2) % 16 || (a.v_new_stride * 2) % 16))
+    return false;
+  // fp8 pools: no fused append; the scale rows are bulk-copied (16-byte aligned)
+  if (a.k_scale != nullptr && (a.k_new != nullptr || !al(a.k_scale, 16) || !al(a.v_scale, 16)))
     return false;
   return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
          a.block_size == 16 && (a.n_kv_heads == 1 || a.n_kv_heads == 2 || a.n_kv_heads == 4) &&
@@ -160,7 +193,7 @@ __device__ __forceinline__ int partial_slot(int c, int per, int blk_lo) {
   return (blk_lo > c * per) ? 2 * c + 1 : 2 * c;
 }
 
-template <typename T, int NKV>
+template <typename T, int NKV, bool FP8>
 __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
@@ -172,8 +205,14 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   // ---- shared memory carve-up (tiles 1024-byte aligned for the 128B swizzle)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  constexpr int stage_bytes = 2 * nkv * kDecTile;  // K tiles then V tiles
-  uint8_t* tiles = base;
+  // stage: K tiles, V tiles (fp8: then the K and V scale rows of the block)
+  constexpr int tile_bytes = FP8 ? kDecTile8 : kDecTile;
+  constexpr int scale_bytes = FP8 ? 16 * nkv * 4 : 0;
+  constexpr int stage_bytes = 2 * nkv * tile_bytes + 2 * scale_bytes;
+  // fp8: per consumer warp a 16-bit K and V staging tile ahead of the ring
+  constexpr int staging_bytes = FP8 ? nkv * 2 * kDecTile : 0;
+  uint8_t* staging = base;
+  uint8_t* tiles = base + staging_bytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tiles + kDecStages * stage_bytes);
   uint64_t* empty_bar = full_bar + kDecStages;
   int* misc = reinterpret_cast<int*>(empty_bar + kDecStages);  // [1..9]: scan scratch
@@ -238,7 +277,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         if (id < 0 || id >= p.num_blocks) {
           raise_flag(p.err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
           id = 0;  // read a valid block; never write through a bad id
-        } else if (p.k_new != nullptr && gb == prefix[s + 1] - 1) {
+        } else if (!FP8 && p.k_new != nullptr && gb == prefix[s + 1] - 1) {
           app_seq = s;
           app_row = id * 16 + ((ctxs[s] - 1) & 15);
         }
@@ -246,8 +285,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       if (!waited) {
         // warm L2 with the first stages' K/V while the preceding kernel ends
         if (gb < r1 && lane < kDecStages) {
-          prefetch_l2(p.k_pool + static_cast<int64_t>(id) * (nkv * kDecTile), nkv * kDecTile);
-          prefetch_l2(p.v_pool + static_cast<int64_t>(id) * (nkv * kDecTile), nkv * kDecTile);
+          prefetch_l2(p.k_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
+          prefetch_l2(p.v_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
         }
         pdl_wait();  // the pool may still be written by the preceding kernel
         waited = true;
@@ -256,7 +295,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
         const int a_seq = __shfl_sync(0xffffffffu, app_seq, k);
-        if (a_seq >= 0) {
+        if (!FP8 && a_seq >= 0) {
           // append before the block is loaded: the warp copies the K and V
           // rows (nkv*128 bytes each) into the pool, then orders those
           // generic-proxy writes before lane 0's TMA read of the block
@@ -284,8 +323,14 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
             mbar_arrive_expect_tx(&full_bar[st], stage_bytes);
 #pragma unroll
             for (int hk = 0; hk < nkv; ++hk) {
-              tma_load_3d(stg + hk * kDecTile, &kmap, &full_bar[st], 0, hk, blk * 16);
-              tma_load_3d(stg + (nkv + hk) * kDecTile, &vmap, &full_bar[st], 0, hk, blk * 16);
+              tma_load_3d(stg + hk * tile_bytes, &kmap, &full_bar[st], 0, hk, blk * 16);
+              tma_load_3d(stg + (nkv + hk) * tile_bytes, &vmap, &full_bar[st], 0, hk, blk * 16);
+            }
+            if constexpr (FP8) {
+              bulk_load(stg + 2 * nkv * tile_bytes, p.k_scale + static_cast<int64_t>(blk) * 16 * nkv,
+                        scale_bytes, &full_bar[st]);
+              bulk_load(stg + 2 * nkv * tile_bytes + scale_bytes,
+                        p.v_scale + static_cast<int64_t>(blk) * 16 * nkv, scale_bytes, &full_bar[st]);
             }
           }
         }
@@ -336,8 +381,46 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
         dead = true;
       }
-      const uint32_t kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
-      const uint32_t vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
+      uint32_t kt, vt;
+      float ks0 = 1.f, ks1 = 1.f, vs0 = 1.f, vs1 = 1.f;  // fp8 scales of tokens g, g + 8
+      if constexpr (FP8) {
+        // this head's fp8 tiles -> 16-bit staging tiles in the swizzled layout
+        // of the 16-bit TMA tiles; rows past the context are zeros (an unused
+        // slot may hold any bytes, and 0 x NaN would reach O)
+        const int valid8 = min(16, ctx - jb * 16);
+        const uint8_t* stg = tiles + st * stage_bytes;
+        const uint8_t* k8 = stg + h * kDecTile8;
+        const uint8_t* v8 = stg + (nkv + h) * kDecTile8;
+        const float* ksc = reinterpret_cast<const float*>(stg + 2 * nkv * kDecTile8);
+        const float* vsc = ksc + 16 * nkv;
+        uint8_t* kst = staging + h * 2 * kDecTile;
+        uint8_t* vst = kst + kDecTile;
+#pragma unroll
+        for (int c = lane; c < 64; c += 32) {
+          const int r = c >> 2, part = c & 3;
+          uint4 rk = *reinterpret_cast<const uint4*>(k8 + c * 16);
+          uint4 rv = *reinterpret_cast<const uint4*>(v8 + c * 16);
+          if (r >= valid8) rk = rv = make_uint4(0u, 0u, 0u, 0u);
+          uint4 lo, hi;
+          fp8x16_to<T>(rk, lo, hi);
+          *reinterpret_cast<uint4*>(kst + r * 128 + (((2 * part) ^ (r & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(kst + r * 128 + (((2 * part + 1) ^ (r & 7)) << 4)) = hi;
+          fp8x16_to<T>(rv, lo, hi);
+          *reinterpret_cast<uint4*>(vst + r * 128 + (((2 * part) ^ (r & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(vst + r * 128 + (((2 * part + 1) ^ (r & 7)) << 4)) = hi;
+        }
+        ks0 = g < valid8 ? ksc[g * nkv + h] : 0.f;
+        ks1 = g + 8 < valid8 ? ksc[(g + 8) * nkv + h] : 0.f;
+        vs0 = g < valid8 ? vsc[g * nkv + h] : 0.f;
+        vs1 = g + 8 < valid8 ? vsc[(g + 8) * nkv + h] : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);  // the fp8 stage is free once converted
+        kt = smem_u32(kst);
+        vt = smem_u32(vst);
+      } else {
+        kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
+        vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
+      }
       // ---- S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
       float sc[4] = {0.f, 0.f, 0.f, 0.f};
       const int mi = lane >> 3;
@@ -351,8 +434,10 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       }
       // ---- online softmax per head (exp2 domain); tokens >= valid masked
       const int valid = min(16, ctx - jb * 16);
-      float x0 = sc[0] * p.scale_log2, x1 = sc[1] * p.scale_log2;  // token g
-      float x2 = sc[2] * p.scale_log2, x3 = sc[3] * p.scale_log2;  // token g + 8
+      const float sa = FP8 ? p.scale_log2 * ks0 : p.scale_log2;
+      const float sb = FP8 ? p.scale_log2 * ks1 : p.scale_log2;
+      float x0 = sc[0] * sa, x1 = sc[1] * sa;  // token g
+      float x2 = sc[2] * sb, x3 = sc[3] * sb;  // token g + 8
       if (g >= valid) x0 = x1 = -INFINITY;
       if (g + 8 >= valid) x2 = x3 = -INFINITY;
       float ma = fmaxf(x0, x2), mb = fmaxf(x1, x3);
@@ -372,8 +457,9 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
 #pragma unroll
       for (int j = 0; j < 4; ++j) { o[j][0] *= ca; o[j][1] *= cb; o[j][2] *= ca; o[j][3] *= cb; }
       // ---- P^T fragments: transpose (token x head) 8x8 tiles to (head x token)
-      const uint32_t b0 = movmatrix_t(pack2<T>(p0, p1));  // tokens 0-7
-      const uint32_t b1 = movmatrix_t(pack2<T>(p2, p3));  // tokens 8-15
+      // (fp8: V's per-token scale folded into P; l above sums the unscaled P)
+      const uint32_t b0 = movmatrix_t(pack2<T>(p0 * vs0, p1 * vs0));  // tokens 0-7
+      const uint32_t b1 = movmatrix_t(pack2<T>(p2 * vs1, p3 * vs1));  // tokens 8-15
       // ---- O^T += V^T P^T, 4 tiles of 16 dims
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
@@ -383,8 +469,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
         mma16816<T>(o[mt], a, b0, b1);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[st]);
+      __syncwarp();  // (fp8: every lane is done with the staging tiles)
+      if (!FP8 && lane == 0) mbar_arrive(&empty_bar[st]);
     }
 
     // ---- segment epilogue: per-head sums over the 8 token groups
@@ -570,8 +656,10 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
   }
 }
 
-size_t decode_smem_bytes(int nkv, int n_seqs) {
-  return 1024 + static_cast<size_t>(kDecStages) * 2 * nkv * kDecTile +
+size_t decode_smem_bytes(int nkv, int n_seqs, bool fp8) {
+  const size_t stage = fp8 ? 2 * nkv * kDecTile8 + 2 * 16 * nkv * 4 : 2 * nkv * kDecTile;
+  const size_t staging = fp8 ? static_cast<size_t>(nkv) * 2 * kDecTile : 0;
+  return 1024 + staging + static_cast<size_t>(kDecStages) * stage +
          2 * kDecStages * sizeof(uint64_t) + 40 * sizeof(int) +
          (2 * static_cast<size_t>(n_seqs) + 1) * sizeof(int);
 }
@@ -593,12 +681,17 @@ std::unordered_map<OccKey, int, OccHash> g_occ;
 
 using DecodeKernel = void (*)(const CUtensorMap, const CUtensorMap, const DecodeParams);
 
-DecodeKernel pick_kernel(int dtype, int nkv) {
+template <bool FP8>
+DecodeKernel pick_kernel_t(int dtype, int nkv) {
   if (dtype == PKV_DTYPE_F16)
-    return nkv == 1 ? paged_decode_kernel<__half, 1>
-         : nkv == 2 ? paged_decode_kernel<__half, 2> : paged_decode_kernel<__half, 4>;
-  return nkv == 1 ? paged_decode_kernel<__nv_bfloat16, 1>
-       : nkv == 2 ? paged_decode_kernel<__nv_bfloat16, 2> : paged_decode_kernel<__nv_bfloat16, 4>;
+    return nkv == 1 ? paged_decode_kernel<__half, 1, FP8>
+         : nkv == 2 ? paged_decode_kernel<__half, 2, FP8> : paged_decode_kernel<__half, 4, FP8>;
+  return nkv == 1 ? paged_decode_kernel<__nv_bfloat16, 1, FP8>
+       : nkv == 2 ? paged_decode_kernel<__nv_bfloat16, 2, FP8>
+                  : paged_decode_kernel<__nv_bfloat16, 4, FP8>;
+}
+DecodeKernel pick_kernel(int dtype, int nkv, bool fp8) {
+  return fp8 ? pick_kernel_t<true>(dtype, nkv) : pick_kernel_t<false>(dtype, nkv);
 }
 }  // namespace
 
@@ -607,12 +700,13 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   if (a.n_seqs == 0) return cudaSuccess;
   const int nkv = a.n_kv_heads;
   const int threads = 32 * (nkv + 1);
-  const size_t smem = decode_smem_bytes(nkv, a.n_seqs);
+  const bool fp8 = a.k_scale != nullptr;
+  const size_t smem = decode_smem_bytes(nkv, a.n_seqs, fp8);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  DecodeKernel kern = pick_kernel(a.dtype, nkv);
-  const int kind = a.dtype * 8 + nkv;
+  DecodeKernel kern = pick_kernel(a.dtype, nkv, fp8);
+  const int kind = a.dtype * 8 + nkv + (fp8 ? 64 : 0);
   int grid = 0;
   {
     std::lock_guard<std::mutex> lk(g_occ_mu);
@@ -623,7 +717,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
       const OccKey attr_key{dev, kind, -1, 0};
       if (g_occ.find(attr_key) == g_occ.end()) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(decode_smem_bytes(nkv, kDecMaxSeqs)));
+                                 static_cast<int>(decode_smem_bytes(nkv, kDecMaxSeqs, fp8)));
         if (e != cudaSuccess) return e;
         g_occ.emplace(attr_key, 0);
       }
@@ -663,6 +757,8 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.v_new_stride_b = a.v_new_stride * 2;
   p.k_pool = static_cast<uint8_t*>(const_cast<void*>(a.k_pool));
   p.v_pool = static_cast<uint8_t*>(const_cast<void*>(a.v_pool));
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

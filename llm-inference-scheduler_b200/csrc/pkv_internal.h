@@ -9,6 +9,10 @@
 
 namespace pkv {
 
+// pool format code (internal; not an ABI dtype) of fp8 e4m3 pools, for
+// encode_pool_tensormap / pool_tensormap
+constexpr int kPoolFp8 = 100;
+
 struct RopeArgs {
   void* q_out;
   int64_t q_out_stride;  // elements between token rows
@@ -58,7 +62,17 @@ struct AttnArgs {
   const void* v_new = nullptr;
   int64_t k_new_stride = 0;  // elements between rows
   int64_t v_new_stride = 0;
+  // fp8 e4m3 pools: one fp32 scale per (slot, KV head); NULL = 16/32-bit pools
+  // of `dtype` (q, out and the dequantised arithmetic stay in `dtype`)
+  const float* k_scale = nullptr;
+  const float* v_scale = nullptr;
 };
+cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,
+                                         int64_t v_stride, void* k_pool, void* v_pool,
+                                         float* k_scale, float* v_scale, const int64_t* slots,
+                                         int n_tokens, int num_blocks, int block_size,
+                                         int n_kv_heads, int head_dim, int src_dtype, int* err,
+                                         cudaStream_t stream);
 
 cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_stride,
                                      int64_t v_stride, void* k_pool, void* v_pool,

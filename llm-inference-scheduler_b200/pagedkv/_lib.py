@@ -57,6 +57,12 @@ SIGNATURES = {
                                                _P, _P]),
     "pkv_paged_decode_attention_noalloc": (_I, [_P, _I64, _P, _I64, _P, _P, _I, _P, _I64, _I, _P, _I,
                                                 _I, _I, _I, _I, _F, _I, _P, _P]),
+    "pkv_reshape_and_cache_fp8": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                       _P, _P]),
+    "pkv_paged_decode_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _I64, _I, _P,
+                                            _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _P]),
+    "pkv_paged_prefill_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _I64, _I, _P,
+                                             _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
 }
 
 

@@ -49,6 +49,14 @@ class OutOfBlocks(Exception):
 
 
 class BlockManager:
+    """Block pools in HBM plus the reference's host-side allocator.
+
+    dtype=torch.float8_e4m3fn keeps fp8 e4m3 pools (no counterpart in the
+    reference): k_cache / v_cache hold the bytes (uint8) and k_scale_cache /
+    v_scale_cache [L, NB, block_size, n_kv_heads] one fp32 scale per (slot,
+    KV head) row; copy_block copies both.
+    """
+
     def __init__(self, num_blocks: int, block_size: int, num_layers: int, num_kv_heads: int,
                  head_dim: int, device="cuda", dtype=torch.float16):
         self.num_blocks = num_blocks
@@ -57,6 +65,9 @@ class BlockManager:
         self.num_kv_heads = num_kv_heads
         self.head_dim = head_dim
         self.dtype = dtype
+        self.fp8 = dtype == torch.float8_e4m3fn
+        self.k_scale_cache = self.v_scale_cache = None
+        self.k_scale = self.v_scale = None
         if device is None:
             self.device = None
             self.k_cache = self.v_cache = None
@@ -67,10 +78,19 @@ class BlockManager:
                 raise RuntimeError(
                     "pagedkv.BlockManager keeps its pools in GPU memory; pass a CUDA device "
                     "(or device=None for a bookkeeping-only manager)")
-            ops.dtype_code(dtype)
             shape = (num_layers, num_blocks, block_size, num_kv_heads, head_dim)
-            self.k_cache = torch.zeros(shape, device=self.device, dtype=dtype)
-            self.v_cache = torch.zeros(shape, device=self.device, dtype=dtype)
+            if self.fp8:
+                pool_dt = torch.uint8
+                sshape = shape[:-1]
+                self.k_scale_cache = torch.zeros(sshape, device=self.device, dtype=torch.float32)
+                self.v_scale_cache = torch.zeros(sshape, device=self.device, dtype=torch.float32)
+                self.k_scale = [self.k_scale_cache[layer] for layer in range(num_layers)]
+                self.v_scale = [self.v_scale_cache[layer] for layer in range(num_layers)]
+            else:
+                ops.dtype_code(dtype)
+                pool_dt = dtype
+            self.k_cache = torch.zeros(shape, device=self.device, dtype=pool_dt)
+            self.v_cache = torch.zeros(shape, device=self.device, dtype=pool_dt)
             self.k_pool = [self.k_cache[layer] for layer in range(num_layers)]
             self.v_pool = [self.v_cache[layer] for layer in range(num_layers)]
             self.err = ops.new_error_flags(self.device)
@@ -89,7 +109,7 @@ class BlockManager:
     @property
     def block_bytes(self) -> int:
         """Bytes of one block of one layer's K (or V) pool."""
-        esize = torch.tensor([], dtype=self.dtype).element_size()
+        esize = 1 if self.fp8 else torch.tensor([], dtype=self.dtype).element_size()
         return self.block_size * self.num_kv_heads * self.head_dim * esize
 
     def allocate(self) -> int:
@@ -140,6 +160,8 @@ class BlockManager:
         host = torch.tensor(pairs, dtype=torch.int32).pin_memory()
         dev = host.to(self.device, non_blocking=True)
         ops.copy_blocks(self.k_cache, self.v_cache, dev, self.err)
+        if self.fp8:  # the rows' scales travel with their bytes
+            ops.copy_blocks(self.k_scale_cache, self.v_scale_cache, dev, self.err)
         self.copies_launched += 1
 
     def check_errors(self):
@@ -304,14 +326,23 @@ class PagedKVCache:
         mgr.flush_copies()
         if n_new:
             slots = torch.from_numpy(self._slots(table, num_prior, n_new)).to(mgr.device)
-            ops.reshape_and_cache(k_new.to(mgr.dtype), v_new.to(mgr.dtype), mgr.k_pool[layer],
-                                  mgr.v_pool[layer], slots, mgr.err)
+            if mgr.fp8:
+                ops.reshape_and_cache_fp8(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer],
+                                          mgr.k_scale[layer], mgr.v_scale[layer], slots, mgr.err)
+            else:
+                ops.reshape_and_cache(k_new.to(mgr.dtype), v_new.to(mgr.dtype), mgr.k_pool[layer],
+                                      mgr.v_pool[layer], slots, mgr.err)
         if layer == mgr.num_layers - 1:
             self._len[seq_id] = total
         used = (total + bs - 1) // bs
         idx = torch.tensor(table[:used], device=mgr.device, dtype=torch.long)
         k = mgr.k_pool[layer][idx].reshape(used * bs, *k_new.shape[1:])[:total]
         v = mgr.v_pool[layer][idx].reshape(used * bs, *v_new.shape[1:])[:total]
+        if mgr.fp8:  # dequantised, in the dtype of the new rows
+            ks = mgr.k_scale[layer][idx].reshape(used * bs, -1, 1)[:total]
+            vs = mgr.v_scale[layer][idx].reshape(used * bs, -1, 1)[:total]
+            k = (k.view(torch.float8_e4m3fn).float() * ks).to(k_new.dtype)
+            v = (v.view(torch.float8_e4m3fn).float() * vs).to(v_new.dtype)
         return k, v, num_prior
 
     # ---- batched hot path ---------------------------------------------------
@@ -450,6 +481,8 @@ class PagedKVCache:
         mgr.flush_copies()
         if out is None:
             out = torch.empty((meta.n_tokens,) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
+        if mgr.fp8:
+            return self._forward_layer_fp8(layer, q, k_new, v_new, meta, scale, out, advance)
         nd = meta.n_decode
         if nd:
             # decode sequences: append fused into the decode kernel; the
@@ -475,6 +508,29 @@ class PagedKVCache:
                 self._len[s] = p + n
         return out
 
+    def _forward_layer_fp8(self, layer, q, k_new, v_new, meta, scale, out, advance):
+        """forward_layer over fp8 pools: the quantising append of every token,
+        then decode and chunked prefill over the fp8 pools."""
+        mgr = self.mgr
+        ks, vs = mgr.k_scale[layer], mgr.v_scale[layer]
+        ops.reshape_and_cache_fp8(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
+                                  meta.slot_mapping, mgr.err)
+        nd = meta.n_decode
+        if nd:
+            ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
+            ops.paged_decode_attention_fp8(q[:nd], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
+                                           meta.block_tables[:nd], meta.context_lens[:nd], scale,
+                                           workspace=ws, out=out[:nd], err=mgr.err)
+        if nd < meta.n_seqs:
+            ops.paged_prefill_attention_fp8(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
+                                            meta.block_tables[nd:], meta.query_start_loc,
+                                            meta.num_prior_dev[nd:], meta.max_query_len, scale,
+                                            out=out[nd:], err=mgr.err)
+        if advance and layer == mgr.num_layers - 1:
+            for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
+                self._len[s] = p + n
+        return out
+
     def forward_layer_qkv(self, layer: int, qkv: torch.Tensor, positions: torch.Tensor,
                           cos: torch.Tensor, sin: torch.Tensor, meta: StepMetadata, scale: float,
                           out: torch.Tensor | None = None, advance: bool = True) -> torch.Tensor:
@@ -485,6 +541,9 @@ class PagedKVCache:
         prefill).  Returns out [T, Hq, D].  Same results as rotating q and k
         with Rope.rotate and calling forward_layer."""
         mgr = self.mgr
+        if mgr.fp8:
+            raise NotImplementedError("pagedkv: forward_layer_qkv writes 16-bit pools; with fp8 "
+                                      "pools rotate q and k and call forward_layer")
         mgr.flush_copies()
         q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer], mgr.v_pool[layer],
                                        meta.slot_mapping, err=mgr.err)

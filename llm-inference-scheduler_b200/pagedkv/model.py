@@ -166,7 +166,8 @@ class PagedQwen2Model:
         pos_np = np.concatenate([s.positions for s in seq_infos]).astype(np.int64)
         positions = torch.from_numpy(pos_np).pin_memory().to(self.device, non_blocking=True)
         cos_t, sin_t = self.rope.tables(int(pos_np.max()) + 1)
-        if not self.fused_rope:
+        fused = self.fused_rope and not kv_cache.mgr.fp8  # the fused kernel writes 16-bit pools
+        if not fused:
             cos, sin = cos_t[positions].unsqueeze(1), sin_t[positions].unsqueeze(1)
         timing = self.timing
         if timing is not None:
@@ -182,7 +183,7 @@ class PagedQwen2Model:
             qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
             if timing is not None:
                 t_attn[li][0].record()
-            if self.fused_rope:
+            if fused:
                 attn = kv_cache.forward_layer_qkv(li, qkv, positions, cos_t, sin_t, meta, self.scale)
             else:
                 q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), cos, sin)

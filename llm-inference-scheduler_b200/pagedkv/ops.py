@@ -246,6 +246,103 @@ def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: t
     return out
 
 
+# ---------------------------------------------------------------- fp8 e4m3 pools
+
+def _check_fp8_pools(k_pool, v_pool, k_scale, v_scale):
+    for t, n in ((k_pool, "k_pool"), (v_pool, "v_pool"), (k_scale, "k_scale"), (v_scale, "v_scale")):
+        _cuda(t, n)
+    if k_pool.dtype != torch.uint8 or v_pool.dtype != torch.uint8:
+        raise TypeError("pagedkv: fp8 pools are uint8 tensors of e4m3 bytes")
+    if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32:
+        raise TypeError("pagedkv: fp8 pool scales are float32")
+    if not all(t.is_contiguous() for t in (k_pool, v_pool, k_scale, v_scale)):
+        raise ValueError("pagedkv: fp8 pools and scales must be contiguous")
+    nb, bs, hkv, d = k_pool.shape
+    if tuple(v_pool.shape) != (nb, bs, hkv, d) or tuple(k_scale.shape) != (nb, bs, hkv) or \
+            tuple(v_scale.shape) != (nb, bs, hkv):
+        raise ValueError("pagedkv: fp8 pools [nb, bs, hkv, d] and scales [nb, bs, hkv] disagree")
+    return nb, bs, hkv, d
+
+
+def reshape_and_cache_fp8(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
+                          v_pool: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
+                          slot_mapping: torch.Tensor, err: torch.Tensor | None = None) -> None:
+    """reshape_and_cache into fp8 e4m3 pools: each (token, KV head) row of
+    k / v ([T, Hkv, D], fp32/fp16/bf16) is quantised with scale =
+    absmax / 448, byte = e4m3(x / scale) (nearest even, saturated); the bytes
+    go to k_pool / v_pool (uint8 [NB, bs, Hkv, D]) and the scales to
+    k_scale / v_scale (fp32 [NB, bs, Hkv]) at slot_mapping[t] (-1 skips)."""
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    for t, n in ((k, "k"), (v, "v"), (slot_mapping, "slot_mapping")):
+        _cuda(t, n)
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise TypeError("pagedkv: slot_mapping must be a contiguous int64 tensor")
+    T = slot_mapping.shape[0]
+    if k.dtype != v.dtype or k.shape[0] != T or v.shape[0] != T or tuple(k.shape[1:]) != (hkv, d) \
+            or tuple(v.shape[1:]) != (hkv, d):
+        raise ValueError("pagedkv: k/v shape does not match the pool and slot_mapping")
+    if T == 0:
+        return
+    rc = _lib.load().pkv_reshape_and_cache_fp8(
+        k.data_ptr(), v.data_ptr(), _row_stride(k, "k"), _row_stride(v, "v"), k_pool.data_ptr(),
+        v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), slot_mapping.data_ptr(), T, nb, bs,
+        hkv, d, dtype_code(k.dtype), _ptr(err), _stream(k))
+    _lib.check(rc, "pkv_reshape_and_cache_fp8")
+
+
+def paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
+                               scale, workspace=None, out=None, err=None) -> torch.Tensor:
+    """paged_decode_attention over fp8 e4m3 pools (value = e4m3(byte) *
+    scale of its row); q / out in fp16, bf16 or fp32."""
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    _cuda(q, "q"), _cuda(context_lens, "context_lens")
+    _check_tables(block_tables)
+    if context_lens.dtype != torch.int32 or not context_lens.is_contiguous():
+        raise TypeError("pagedkv: context_lens must be a contiguous int32 tensor")
+    B, hq, dq = q.shape
+    if dq != d or block_tables.shape[0] < B or context_lens.shape[0] < B:
+        raise ValueError("pagedkv: q / block_tables / context_lens shapes disagree")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if workspace is None:
+        workspace = new_decode_workspace(B, hq, d, q.device)
+    if B == 0:
+        return out
+    rc = _lib.load().pkv_paged_decode_attention_fp8(
+        out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
+        v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb, block_tables.data_ptr(),
+        block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(), B, hq, hkv, d, bs,
+        float(scale), dtype_code(q.dtype), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
+    _lib.check(rc, "pkv_paged_decode_attention_fp8")
+    return out
+
+
+def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
+                                num_prior, max_query_len, scale, out=None, err=None) -> torch.Tensor:
+    """paged_prefill_attention over fp8 e4m3 pools (CUDA-core kernel)."""
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    for t, n in ((q, "q"), (query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
+        _cuda(t, n)
+    _check_tables(block_tables)
+    T, hq, dq = q.shape
+    n_seqs = query_start_loc.shape[0] - 1
+    if dq != d or num_prior.shape[0] < n_seqs:
+        raise ValueError("pagedkv: q / num_prior shapes disagree")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if T == 0 or n_seqs == 0:
+        return out
+    rc = _lib.load().pkv_paged_prefill_attention_fp8(
+        out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
+        v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb, block_tables.data_ptr(),
+        block_tables.stride(0), block_tables.shape[1], query_start_loc.data_ptr(), num_prior.data_ptr(),
+        n_seqs, T, int(max_query_len), hq, hkv, d, bs, float(scale), dtype_code(q.dtype), _ptr(err),
+        _stream(q))
+    _lib.check(rc, "pkv_paged_prefill_attention_fp8")
+    return out
+
+
 class DecodeAppendPlan:
     """pkv_paged_decode_append_attention for the layers of one step, which
     share block tables, context lengths, scale, workspace and error word.
@@ -404,3 +501,31 @@ def bind_paged_prefill_attention(q, k_pool, v_pool, block_tables, query_start_lo
 
 def set_decode_impl(impl: int) -> None:
     _lib.check(_lib.load().pkv_set_decode_impl(int(impl)), "pkv_set_decode_impl")
+
+
+def bind_reshape_and_cache_fp8(k, v, k_pool, v_pool, k_scale, v_scale, slot_mapping,
+                               err=None) -> BoundLaunch:
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    reshape_and_cache_fp8(k, v, k_pool, v_pool, k_scale, v_scale, slot_mapping, err)  # validates
+    args = (k.data_ptr(), v.data_ptr(), _row_stride(k, "k"), _row_stride(v, "v"), k_pool.data_ptr(),
+            v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), slot_mapping.data_ptr(),
+            slot_mapping.shape[0], nb, bs, hkv, d, dtype_code(k.dtype), _ptr(err), _stream(k))
+    return BoundLaunch(_lib.load().pkv_reshape_and_cache_fp8, args, "pkv_reshape_and_cache_fp8",
+                       (k, v, k_pool, v_pool, k_scale, v_scale, slot_mapping, err))
+
+
+def bind_paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
+                                    scale, workspace, out, err=None) -> BoundLaunch:
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens, scale,
+                               workspace, out, err)  # validates (and runs once)
+    B, hq, _ = q.shape
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            context_lens.data_ptr(), B, hq, hkv, d, bs, float(scale), dtype_code(q.dtype),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
+    return BoundLaunch(_lib.load().pkv_paged_decode_attention_fp8, args,
+                       "pkv_paged_decode_attention_fp8",
+                       (q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens, workspace,
+                        out, err))

@@ -96,6 +96,57 @@ def paged_attention(q, k_pool, v_pool, tables_padded, qsl, num_prior, dt: str,
     return out
 
 
+# ---- fp8 e4m3 KV (no reference counterpart: the reference's quant.py names
+# fp8 KV as its next step).  Restated from the e4m3 format -- 1 sign bit, 4
+# exponent bits (bias 7), 3 mantissa bits, no infinities, S.1111.111 = NaN,
+# largest finite 448 -- and this library's row quantisation rule: scale =
+# absmax(row) / 448 (1 for an all-zero row), byte = e4m3(x / scale) rounded
+# to nearest with ties to the even mantissa, saturated at +-448.
+
+def e4m3_decode(b: np.ndarray) -> np.ndarray:
+    b = np.asarray(b).astype(np.int64)
+    s, e, m = (b >> 7) & 1, (b >> 3) & 15, b & 7
+    val = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * np.exp2(e - 7.0))
+    val = np.where((e == 15) & (m == 7), np.nan, val)
+    return np.where(s == 1, -val, val).astype(np.float32)
+
+
+_E4M3_POS = e4m3_decode(np.arange(127))  # codes 0..126: the non-negative finite values, ascending
+
+
+def e4m3_encode(x: np.ndarray) -> np.ndarray:
+    x = np.asarray(x, dtype=np.float32)
+    a = np.minimum(np.abs(x), np.float32(448.0))
+    hi = np.clip(np.searchsorted(_E4M3_POS, a, side="left"), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    dlo = a - _E4M3_POS[lo]
+    dhi = _E4M3_POS[hi] - a
+    code = np.where(dhi < dlo, hi, np.where(dlo < dhi, lo, np.where(hi % 2 == 0, hi, lo)))
+    code = np.where(a == _E4M3_POS[hi], hi, code)
+    return (code | (np.signbit(x).astype(np.int64) << 7)).astype(np.uint8)
+
+
+def fp8_quantize_rows(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """x [..., D] (fp32 values of the source rows) -> (bytes [..., D], scale [...])."""
+    x = np.asarray(x, dtype=np.float32)
+    amax = np.abs(x).max(axis=-1)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    return e4m3_encode(x / scale[..., None]), scale
+
+
+def fp8_dequantize(b: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    return (e4m3_decode(b) * np.asarray(scale, dtype=np.float32)[..., None]).astype(np.float32)
+
+
+def paged_attention_fp8(q32, k_bytes, v_bytes, k_scale, v_scale, tables_padded, qsl, num_prior,
+                        scale: float = 0.125, threads: int = 0) -> np.ndarray:
+    """Attention over fp8 pools: dequantised to fp32, then the fp32 oracle."""
+    return paged_attention(np.ascontiguousarray(q32, dtype=np.float32),
+                           np.ascontiguousarray(fp8_dequantize(k_bytes, k_scale)),
+                           np.ascontiguousarray(fp8_dequantize(v_bytes, v_scale)),
+                           tables_padded, qsl, num_prior, "f32", scale, threads)
+
+
 # ---- whole-case runners (mirror the reference's append-then-attend order) ----
 
 def run_decode_case(c, threads: int = 0):

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 import cases as C
-from conftest import GOLDEN, PRODUCT_ATOL, golden, max_abs_diff
+from conftest import GOLDEN, PRODUCT_ATOL, as_f32, golden, max_abs_diff
 from pagedkv import BlockManager, PagedKVCache, _lib, ops
 
 pytestmark = pytest.mark.gpu
@@ -528,3 +528,151 @@ def test_forward_layer_qkv_equals_forward_layer(dt):
     assert torch.equal(caches[0][0].v_cache, caches[1][0].v_cache)
     for m, _ in caches:
         m.check_errors()
+
+
+# ---------------------------------------------------------------- fp8 e4m3 pools
+
+def _fp8_case(seed, ctx, src_dt, nb=None):
+    """Pools filled through pkv_reshape_and_cache_fp8 with every context token
+    of every sequence (random block tables); returns the device pools plus the
+    source rows, tables and slots."""
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, dtype=np.int64)
+    nblk = (ctx + 15) // 16
+    nb = nb or int(nblk.sum()) + 8
+    perm = rng.permutation(nb).astype(np.int32)
+    tables, o = [], 0
+    for n in nblk:
+        tables.append(perm[o:o + n].tolist())
+        o += n
+    T = int(ctx.sum())
+    k = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32) * 3, src_dt)
+    v = C.to_dtype(rng.standard_normal((T, 2, 64), dtype=np.float32), src_dt)
+    slots = np.concatenate([np.array(t, np.int64)[np.arange(c) // 16] * 16 + np.arange(c) % 16
+                            for t, c in zip(tables, ctx)])
+    kp = torch.zeros((nb, 16, 2, 64), dtype=torch.uint8, device="cuda")
+    vp = torch.zeros_like(kp)
+    ks = torch.zeros((nb, 16, 2), dtype=torch.float32, device="cuda")
+    vs = torch.zeros_like(ks)
+    err = ops.new_error_flags("cuda")
+    ops.reshape_and_cache_fp8(dev(k, src_dt), dev(v, src_dt), kp, vp, ks, vs,
+                              torch.from_numpy(slots).cuda(), err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return dict(ctx=ctx, tables=tables, k=k, v=v, slots=slots, kp=kp, vp=vp, ks=ks, vs=vs, nb=nb, rng=rng)
+
+
+@pytest.mark.parametrize("src_dt", DTS)
+def test_reshape_and_cache_fp8_matches_oracle(oracle_mod, src_dt):
+    """Quantisation on the device equals the oracle's restatement bit for bit:
+    the e4m3 bytes and the per-(token, KV head) scales, from fp32 / fp16 /
+    bf16 rows; a padding slot writes nothing."""
+    c = _fp8_case(71, [37, 300, 5, 129], src_dt)
+    for name, rows in (("k", c["k"]), ("v", c["v"])):
+        b, s = oracle_mod.fp8_quantize_rows(as_f32(rows, src_dt))
+        pool = (c["kp"] if name == "k" else c["vp"]).view(-1, 2, 64).cpu().numpy()[c["slots"]]
+        sc = (c["ks"] if name == "k" else c["vs"]).view(-1, 2).cpu().numpy()[c["slots"]]
+        assert np.array_equal(pool, b), f"{name} bytes differ at {np.argwhere(pool != b)[:4]}"
+        assert np.array_equal(sc, s), f"{name} scales differ"
+    # slot -1: skipped
+    kp0 = c["kp"].clone()
+    ones = torch.ones((1, 2, 64), dtype=TORCH_DT[src_dt], device="cuda")
+    ops.reshape_and_cache_fp8(ones, ones, c["kp"], c["vp"], c["ks"], c["vs"],
+                              torch.tensor([-1], dtype=torch.int64, device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.equal(kp0, c["kp"])
+
+
+@pytest.mark.parametrize("q_dt", ("f16", "bf16"))
+def test_decode_fp8_matches_oracle(oracle_mod, decode_impl, q_dt):
+    """Decode over fp8 pools (tensor-core kernel and CUDA-core kernel) against
+    the oracle's attention over the dequantised pools, with the 16-bit
+    tolerance of the query dtype."""
+    ctx = [1, 15, 16, 17, 33, 600, 1000, 2047, 64, 5000, 3, 250]
+    c = _fp8_case(72, ctx, "f16")
+    B = len(ctx)
+    q = C.to_dtype(c["rng"].standard_normal((B, 14, 64), dtype=np.float32), q_dt)
+    tabs = C.pad_tables(c["tables"])
+    err = ops.new_error_flags("cuda")
+    out = ops.paged_decode_attention_fp8(dev(q, q_dt), c["kp"], c["vp"], c["ks"], c["vs"], dev(tabs),
+                                         dev(c["ctx"].astype(np.int32)), 0.125, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    qsl = np.arange(B + 1, dtype=np.int32)
+    prior = (c["ctx"] - 1).astype(np.int32)
+    q32 = as_f32(q, q_dt)
+    ref = oracle_mod.paged_attention_fp8(q32, c["kp"].cpu().numpy(), c["vp"].cpu().numpy(),
+                                         c["ks"].cpu().numpy(), c["vs"].cpu().numpy(), tabs, qsl, prior)
+    got = as_f32(host(out, q_dt), q_dt)
+    assert np.abs(got - ref).max() <= PRODUCT_ATOL[q_dt]
+
+
+def test_prefill_fp8_matches_oracle(oracle_mod):
+    """Chunked prefill over fp8 pools (CUDA-core kernel): chunks over a prior."""
+    prior = np.array([48, 0, 300, 17], dtype=np.int64)
+    chunk = np.array([64, 130, 1, 40], dtype=np.int64)
+    c = _fp8_case(73, prior + chunk, "f16")
+    T = int(chunk.sum())
+    q = C.to_dtype(c["rng"].standard_normal((T, 14, 64), dtype=np.float32), "f16")
+    tabs = C.pad_tables(c["tables"])
+    qsl = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    err = ops.new_error_flags("cuda")
+    out = ops.paged_prefill_attention_fp8(dev(q, "f16"), c["kp"], c["vp"], c["ks"], c["vs"], dev(tabs),
+                                          dev(qsl), dev(prior.astype(np.int32)), int(chunk.max()), 0.125,
+                                          err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = oracle_mod.paged_attention_fp8(q.astype(np.float32), c["kp"].cpu().numpy(),
+                                         c["vp"].cpu().numpy(), c["ks"].cpu().numpy(),
+                                         c["vs"].cpu().numpy(), tabs, qsl, prior.astype(np.int32))
+    assert np.abs(host(out, "f16").astype(np.float32) - ref).max() <= PRODUCT_ATOL["f16"]
+
+
+def test_forward_layer_fp8_pools_and_cow(oracle_mod):
+    """BlockManager(dtype=float8_e4m3fn) + forward_layer on a mixed batch
+    (decodes then chunks): outputs against the oracle over the pools it left
+    (dequantised), and a copy-on-write copies bytes and scales."""
+    L, nb = 2, 128
+    m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=torch.float8_e4m3fn)
+    assert m.fp8 and m.k_cache.dtype == torch.uint8 and m.block_bytes == 16 * 2 * 64
+    kv = PagedKVCache(m)
+    g = torch.Generator(device="cuda").manual_seed(74)
+    plan = [(0, 40, 1), (1, 17, 1), (2, 48, 30), (3, 5, 20)]
+    for s, prior, n in plan:
+        kv.add_sequence(s, [m.allocate() for _ in range((prior + n + 15) // 16)], 0)
+    # prefill the priors through the same path (chunks only), then the mixed step
+    meta0 = kv.prepare_step([(s, prior) for s, prior, _ in plan])
+    T0 = meta0.n_tokens
+    for layer in range(L):
+        q = torch.randn((T0, 14, 64), generator=g, device="cuda", dtype=torch.float16)
+        k = torch.randn((T0, 2, 64), generator=g, device="cuda", dtype=torch.float16)
+        kv.forward_layer(layer, q, k, k * 0.5, meta0, 0.125)
+    meta = kv.prepare_step([(s, n) for s, _, n in plan])
+    assert meta.n_decode == 2
+    T = meta.n_tokens
+    qsl = np.concatenate([[0], np.cumsum([n for _, _, n in plan])]).astype(np.int32)
+    tabs = C.pad_tables([kv.block_tables[s] for s, _, _ in plan])
+    for layer in range(L):
+        q = torch.randn((T, 14, 64), generator=g, device="cuda", dtype=torch.float16)
+        k = torch.randn((T, 2, 64), generator=g, device="cuda", dtype=torch.float16)
+        v = torch.randn((T, 2, 64), generator=g, device="cuda", dtype=torch.float16)
+        out = kv.forward_layer(layer, q, k, v, meta, 0.125)
+        torch.cuda.synchronize()
+        ref = oracle_mod.paged_attention_fp8(
+            q.float().cpu().numpy(), m.k_pool[layer].cpu().numpy(), m.v_pool[layer].cpu().numpy(),
+            m.k_scale[layer].cpu().numpy(), m.v_scale[layer].cpu().numpy(), tabs, qsl,
+            np.array([p for _, p, _ in plan], dtype=np.int32))
+        assert np.abs(out.float().cpu().numpy() - ref).max() <= PRODUCT_ATOL["f16"]
+    m.check_errors()
+    # fork sequence 2 and copy-on-write its partial tail block: bytes and scales follow
+    s = 2
+    for b in kv.block_tables[s]:
+        m.incref(b)
+    kv.add_sequence(9, list(kv.block_tables[s]), kv.seq_len(s))
+    kv.ensure_writable_tail(9)
+    m.flush_copies()
+    torch.cuda.synchronize()
+    src, dst = kv.block_tables[s][-1], kv.block_tables[9][-1]
+    assert src != dst
+    assert torch.equal(m.k_cache[:, dst], m.k_cache[:, src])
+    assert torch.equal(m.v_scale_cache[:, dst], m.v_scale_cache[:, src])

@@ -106,3 +106,18 @@ def test_oracle_rejects_bad_block(oracle_mod):
     with pytest.raises(ValueError):
         oracle_mod.paged_attention(c["q"], c["k_pool"], c["v_pool"], tabs,
                                    np.arange(3, dtype=np.int32), (c["ctx"] - 1).astype(np.int32), "f32")
+
+
+def test_e4m3_codec(oracle_mod):
+    """The oracle's fp8 e4m3 codec: every finite code round-trips, the largest
+    value is 448, ties round to the even mantissa, magnitudes saturate."""
+    codes = np.arange(256, dtype=np.uint8)
+    vals = oracle_mod.e4m3_decode(codes)
+    fin = ~np.isnan(vals)
+    assert fin.sum() == 254 and vals[fin].max() == 448.0 and vals[1] == 2.0 ** -9
+    assert np.array_equal(oracle_mod.e4m3_decode(oracle_mod.e4m3_encode(vals[fin])), vals[fin])
+    x = np.array([1.0625, 1.1875, 2.0 ** -10, 3 * 2.0 ** -10, 500.0, -1e9, -2.5], np.float32)
+    assert oracle_mod.e4m3_decode(oracle_mod.e4m3_encode(x)).tolist() == \
+        [1.0, 1.25, 0.0, 2.0 ** -8, 448.0, -448.0, -2.5]
+    b, s = oracle_mod.fp8_quantize_rows(np.array([[0.0, 0.0], [1.0, -3.5]], np.float32))
+    assert s.tolist() == [1.0, np.float32(3.5) / np.float32(448.0)] and b[1, 1] == 0xFE
