@@ -532,6 +532,17 @@ def test_forward_layer_qkv_equals_forward_layer(dt):
 
 # ---------------------------------------------------------------- fp8 e4m3 pools
 
+def fp8_atol(dt: str, ref: np.ndarray) -> float:
+    """Tolerance of attention over fp8 pools against the fp32 oracle over the
+    dequantised pools.  fp8 KV has no reference path to emulate, so the oracle
+    keeps every step in fp32; the kernels compute in the query dtype and
+    round one extra product to it -- P times the token's V scale -- so the bar
+    is the 16-bit tolerance of that dtype plus one rounding (2^-8 relative for
+    bf16, 2^-10 for fp16) of the largest output."""
+    eps = {"f16": 2.0 ** -10, "bf16": 2.0 ** -8, "f32": 0.0}[dt]
+    return PRODUCT_ATOL[dt] + eps * float(np.abs(ref).max())
+
+
 def _fp8_case(seed, ctx, src_dt, nb=None):
     """Pools filled through pkv_reshape_and_cache_fp8 with every context token
     of every sequence (random block tables); returns the device pools plus the
@@ -604,7 +615,7 @@ def test_decode_fp8_matches_oracle(oracle_mod, decode_impl, q_dt):
     ref = oracle_mod.paged_attention_fp8(q32, c["kp"].cpu().numpy(), c["vp"].cpu().numpy(),
                                          c["ks"].cpu().numpy(), c["vs"].cpu().numpy(), tabs, qsl, prior)
     got = as_f32(host(out, q_dt), q_dt)
-    assert np.abs(got - ref).max() <= PRODUCT_ATOL[q_dt]
+    assert np.abs(got - ref).max() <= fp8_atol(q_dt, ref)
 
 
 def test_prefill_fp8_matches_oracle(oracle_mod):
@@ -625,7 +636,7 @@ def test_prefill_fp8_matches_oracle(oracle_mod):
     ref = oracle_mod.paged_attention_fp8(q.astype(np.float32), c["kp"].cpu().numpy(),
                                          c["vp"].cpu().numpy(), c["ks"].cpu().numpy(),
                                          c["vs"].cpu().numpy(), tabs, qsl, prior.astype(np.int32))
-    assert np.abs(host(out, "f16").astype(np.float32) - ref).max() <= PRODUCT_ATOL["f16"]
+    assert np.abs(host(out, "f16").astype(np.float32) - ref).max() <= fp8_atol("f16", ref)
 
 
 def test_forward_layer_fp8_pools_and_cow(oracle_mod):
@@ -662,7 +673,7 @@ def test_forward_layer_fp8_pools_and_cow(oracle_mod):
             q.float().cpu().numpy(), m.k_pool[layer].cpu().numpy(), m.v_pool[layer].cpu().numpy(),
             m.k_scale[layer].cpu().numpy(), m.v_scale[layer].cpu().numpy(), tabs, qsl,
             np.array([p for _, p, _ in plan], dtype=np.int32))
-        assert np.abs(out.float().cpu().numpy() - ref).max() <= PRODUCT_ATOL["f16"]
+        assert np.abs(out.float().cpu().numpy() - ref).max() <= fp8_atol("f16", ref)
     m.check_errors()
     # fork sequence 2 and copy-on-write its partial tail block: bytes and scales follow
     s = 2
