@@ -23,12 +23,17 @@
 //    workspace, merged by a second small kernel (one CTA per sequence) that
 //    is launched right behind the decode kernel.
 //  * fp8 e4m3 pools (FP8 instantiation): the ring stage holds each head's
-//    16 x 64-byte fp8 K and V tiles plus the block's per-(token, KV head)
-//    fp32 scales (TMA + two bulk copies).  Each consumer warp converts its
-//    head's tiles into a 16-bit staging tile laid out exactly as the 16-bit
-//    TMA tiles (so the ldmatrix/MMA path is shared), releases the stage, and
-//    applies the scales outside the MMAs: K's to the token's scores, V's
-//    folded into P after the softmax sums.  e4m3 -> fp16/bf16 is exact.
+//    16 x 64-byte fp8 K and V tiles (row-major, unswizzled) plus the block's
+//    per-(token, KV head) fp32 scales (TMA + two bulk copies).  Each lane
+//    loads the fp8 bytes of its own MMA fragments straight into registers
+//    (K: 2 x 16 bytes, V: 4 x 8 bytes, bank-conflict free), releases the
+//    stage, and converts them there (cvt e4m3x2 -> f16x2; exact).  That works
+//    because the head dimension may be permuted: S sums over it, so K and Q
+//    use the order in which lane t's four k-steps read 16 contiguous bytes,
+//    and O's rows use the order in which lane g owns 8 contiguous dims (the
+//    epilogue writes them back in natural order).  Scales are applied
+//    outside the MMAs: K's to the token's scores, V's folded into P after
+//    the softmax sums.
 //  * Programmatic dependent launch chains append -> decode -> merge: each
 //    kernel's prologue (context scan, block-table reads) runs before
 //    griddepcontrol.wait and overlaps its predecessor; pool, q, out and
@@ -37,6 +42,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "pkv_common.cuh"
@@ -99,6 +105,25 @@ template <> __device__ __forceinline__ uint32_t fp8x2_to<__nv_bfloat16>(uint32_t
   const float2 f = __half22float2(__half2(h));
   return pack2<__nv_bfloat16>(f.x, f.y);
 }
+// fp8 -> f16 on the integer pipes (the fp16 instantiation): the e4m3 fields
+// moved into f16 position, which is the value times 2^-8 (exact, e4m3
+// subnormals included: they land on f16 subnormals).  The 2^8 is folded into
+// the K and V scales.  The NaN encodings 0x7f / 0xff map to +-480; the
+// quantising append never stores them.  Keeps the conversions off the
+// transcendental pipe, which the softmax's exp2 also needs.
+#ifndef PKV_FP8_ALU_CVT
+#define PKV_FP8_ALU_CVT 1
+#endif
+// bytes 1 and 3 of x -> f16x2 (byte 1 in the low half)
+__device__ __forceinline__ uint32_t e4m3_odd_h2(uint32_t x) {
+  return (x & 0x80008000u) | ((x >> 1) & 0x3f803f80u);
+}
+// bytes 0 and 2 of x -> f16x2 (byte 0 in the low half)
+__device__ __forceinline__ uint32_t e4m3_even_h2(uint32_t x) {
+  const uint32_t z = (x << 7) & 0x7f807f80u;  // sign lands on bit 14 / 30
+  return z + (z & 0x40004000u);               // ... and is carried to bit 15 / 31
+}
+
 template <typename T>
 __device__ __forceinline__ void fp8x16_to(const uint4& in, uint4& lo, uint4& hi) {
   lo = make_uint4(fp8x2_to<T>(in.x & 0xffffu), fp8x2_to<T>(in.x >> 16), fp8x2_to<T>(in.y & 0xffffu),
@@ -169,8 +194,12 @@ __device__ __forceinline__ int find_seq(const int* prefix, int n, int x) {
   return lo;
 }
 
-// Q^T fragments of this warp's GQA group: qa[kk] = Q[head g][16kk + 2t (+8)]
-template <typename T>
+// Q^T fragments of this warp's GQA group, in the dim order of the K
+// fragments (QL): 0 natural, qa[kk] = Q[head g][16kk + 2t (+8)]; 1 (fp8,
+// cvt) k-step kk's k indices 2t, 2t + 1, 2t + 8, 2t + 9 are dims
+// 16t + 4kk + {0, 1, 2, 3}; 2 (fp8, integer-pipe conversion) they are dims
+// 16t + 4kk + {0, 2, 1, 3}
+template <typename T, int QL>
 __device__ __forceinline__ void load_q_frag(uint32_t (&qa)[4][2], const DecodeParams& p, int s,
                                             int h, int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -179,8 +208,12 @@ __device__ __forceinline__ void load_q_frag(uint32_t (&qa)[4][2], const DecodePa
                    static_cast<int64_t>(h * p.group + g) * 64;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(row + 16 * kk + 2 * t));
-      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(row + 16 * kk + 8 + 2 * t));
+      const int d0 = QL ? 16 * t + 4 * kk : 16 * kk + 2 * t;
+      const int d1 = QL ? d0 + 2 : d0 + 8;
+      const uint32_t u0 = __ldg(reinterpret_cast<const uint32_t*>(row + d0));
+      const uint32_t u1 = __ldg(reinterpret_cast<const uint32_t*>(row + d1));
+      qa[kk][0] = QL == 2 ? __byte_perm(u0, u1, 0x5410) : u0;
+      qa[kk][1] = QL == 2 ? __byte_perm(u0, u1, 0x7632) : u1;
     }
   } else {
 #pragma unroll
@@ -209,10 +242,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   constexpr int tile_bytes = FP8 ? kDecTile8 : kDecTile;
   constexpr int scale_bytes = FP8 ? 16 * nkv * 4 : 0;
   constexpr int stage_bytes = 2 * nkv * tile_bytes + 2 * scale_bytes;
-  // fp8: per consumer warp a 16-bit K and V staging tile ahead of the ring
-  constexpr int staging_bytes = FP8 ? nkv * 2 * kDecTile : 0;
-  uint8_t* staging = base;
-  uint8_t* tiles = base + staging_bytes;
+  uint8_t* tiles = base;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tiles + kDecStages * stage_bytes);
   uint64_t* empty_bar = full_bar + kDecStages;
   int* misc = reinterpret_cast<int*>(empty_bar + kDecStages);  // [1..9]: scan scratch
@@ -350,6 +380,10 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   pdl_wait();
   const int h = warp;
   const int g = lane >> 2, t = lane & 3;
+  // fp8 conversion on the integer pipes (fp16) or by cvt (bf16)
+  constexpr bool kAluCvt = FP8 && PKV_FP8_ALU_CVT && std::is_same<T, __half>::value;
+  constexpr int QL = !FP8 ? 0 : kAluCvt ? 2 : 1;
+  constexpr float kCvt = kAluCvt ? 256.f : 1.f;  // undoes the 2^-8 of the integer conversion
   const int G = p.group;
   const bool ok0 = 2 * t < G, ok1 = 2 * t + 1 < G;  // this lane's two heads exist
   const int qh0 = h * G + 2 * t;                    // its first query head
@@ -357,7 +391,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
 
   int s = find_seq(prefix, B, r0);
   uint32_t qa[4][2];
-  load_q_frag<T>(qa, p, s, h, lane);
+  load_q_frag<T, QL>(qa, p, s, h, lane);
   int pos = r0;
   int i = 0;
   while (pos < r1) {
@@ -367,7 +401,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     int s_next = s + 1;
     while (s_next < B && prefix[s_next + 1] == prefix[s_next]) ++s_next;
     uint32_t qn[4][2];
-    if (seg_end < r1) load_q_frag<T>(qn, p, s_next, h, lane);
+    if (seg_end < r1) load_q_frag<T, QL>(qn, p, s_next, h, lane);
 
     const int ctx = ctxs[s];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
@@ -381,42 +415,43 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
         dead = true;
       }
-      uint32_t kt, vt;
+      uint32_t kt = 0, vt = 0;                           // 16-bit tiles: ldmatrix bases
       float ks0 = 1.f, ks1 = 1.f, vs0 = 1.f, vs1 = 1.f;  // fp8 scales of tokens g, g + 8
+      uint4 kr0, kr1;  // fp8: K rows g and g + 8, bytes 16t .. 16t + 15
+      uint2 vr[4];     // fp8: V rows 2t, 2t + 1, 2t + 8, 2t + 9, bytes 8g .. 8g + 7
       if constexpr (FP8) {
-        // this head's fp8 tiles -> 16-bit staging tiles in the swizzled layout
-        // of the 16-bit TMA tiles; rows past the context are zeros (an unused
-        // slot may hold any bytes, and 0 x NaN would reach O)
         const int valid8 = min(16, ctx - jb * 16);
         const uint8_t* stg = tiles + st * stage_bytes;
         const uint8_t* k8 = stg + h * kDecTile8;
         const uint8_t* v8 = stg + (nkv + h) * kDecTile8;
         const float* ksc = reinterpret_cast<const float*>(stg + 2 * nkv * kDecTile8);
         const float* vsc = ksc + 16 * nkv;
-        uint8_t* kst = staging + h * 2 * kDecTile;
-        uint8_t* vst = kst + kDecTile;
-#pragma unroll
-        for (int c = lane; c < 64; c += 32) {
-          const int r = c >> 2, part = c & 3;
-          uint4 rk = *reinterpret_cast<const uint4*>(k8 + c * 16);
-          uint4 rv = *reinterpret_cast<const uint4*>(v8 + c * 16);
-          if (r >= valid8) rk = rv = make_uint4(0u, 0u, 0u, 0u);
-          uint4 lo, hi;
-          fp8x16_to<T>(rk, lo, hi);
-          *reinterpret_cast<uint4*>(kst + r * 128 + (((2 * part) ^ (r & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(kst + r * 128 + (((2 * part + 1) ^ (r & 7)) << 4)) = hi;
-          fp8x16_to<T>(rv, lo, hi);
-          *reinterpret_cast<uint4*>(vst + r * 128 + (((2 * part) ^ (r & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(vst + r * 128 + (((2 * part + 1) ^ (r & 7)) << 4)) = hi;
-        }
-        ks0 = g < valid8 ? ksc[g * nkv + h] : 0.f;
-        ks1 = g + 8 < valid8 ? ksc[(g + 8) * nkv + h] : 0.f;
-        vs0 = g < valid8 ? vsc[g * nkv + h] : 0.f;
-        vs1 = g + 8 < valid8 ? vsc[(g + 8) * nkv + h] : 0.f;
+        kr0 = *reinterpret_cast<const uint4*>(k8 + g * 64 + t * 16);
+        kr1 = *reinterpret_cast<const uint4*>(k8 + (g + 8) * 64 + t * 16);
+        // lanes with odd t take their row pair in the other order, so that
+        // each 8-byte load's 32 lanes fill all 32 banks (two wavefronts)
+        const int sw = t & 1;
+        const uint2 va = *reinterpret_cast<const uint2*>(v8 + (2 * t + sw) * 64 + 8 * g);
+        const uint2 vb = *reinterpret_cast<const uint2*>(v8 + (2 * t + 1 - sw) * 64 + 8 * g);
+        const uint2 vc = *reinterpret_cast<const uint2*>(v8 + (2 * t + 8 + sw) * 64 + 8 * g);
+        const uint2 vd = *reinterpret_cast<const uint2*>(v8 + (2 * t + 9 - sw) * 64 + 8 * g);
+        ks0 = g < valid8 ? ksc[g * nkv + h] * kCvt : 0.f;
+        ks1 = g + 8 < valid8 ? ksc[(g + 8) * nkv + h] * kCvt : 0.f;
+        vs0 = g < valid8 ? vsc[g * nkv + h] * kCvt : 0.f;
+        vs1 = g + 8 < valid8 ? vsc[(g + 8) * nkv + h] * kCvt : 0.f;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[st]);  // the fp8 stage is free once converted
-        kt = smem_u32(kst);
-        vt = smem_u32(vst);
+        if (lane == 0) mbar_arrive(&empty_bar[st]);  // the stage is free once in registers
+        vr[0] = sw ? vb : va;
+        vr[1] = sw ? va : vb;
+        vr[2] = sw ? vd : vc;
+        vr[3] = sw ? vc : vd;
+        // V rows past the context are zeroed (an unused slot may hold any
+        // bytes, and 0 x NaN would reach O); K rows there are masked below
+        const uint2 z = make_uint2(0u, 0u);
+        if (2 * t >= valid8) vr[0] = z;
+        if (2 * t + 1 >= valid8) vr[1] = z;
+        if (2 * t + 8 >= valid8) vr[2] = z;
+        if (2 * t + 9 >= valid8) vr[3] = z;
       } else {
         kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
         vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
@@ -426,10 +461,27 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       const int mi = lane >> 3;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const int row = (lane & 7) + ((mi & 1) << 3);
-        const int chunk = 2 * kk + (mi >> 1);
         uint32_t a[4];
-        ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        if constexpr (FP8) {
+          // k-step kk: bytes 4kk .. 4kk + 3 of rows g and g + 8
+          const uint32_t w0 = kk == 0 ? kr0.x : kk == 1 ? kr0.y : kk == 2 ? kr0.z : kr0.w;
+          const uint32_t w1 = kk == 0 ? kr1.x : kk == 1 ? kr1.y : kk == 2 ? kr1.z : kr1.w;
+          if constexpr (kAluCvt) {
+            a[0] = e4m3_even_h2(w0);
+            a[1] = e4m3_even_h2(w1);
+            a[2] = e4m3_odd_h2(w0);
+            a[3] = e4m3_odd_h2(w1);
+          } else {
+            a[0] = fp8x2_to<T>(w0 & 0xffffu);
+            a[1] = fp8x2_to<T>(w1 & 0xffffu);
+            a[2] = fp8x2_to<T>(w0 >> 16);
+            a[3] = fp8x2_to<T>(w1 >> 16);
+          }
+        } else {
+          const int row = (lane & 7) + ((mi & 1) << 3);
+          const int chunk = 2 * kk + (mi >> 1);
+          ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        }
         mma16816<T>(sc, a, qa[kk][0], qa[kk][1]);
       }
       // ---- online softmax per head (exp2 domain); tokens >= valid masked
@@ -460,17 +512,41 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       // (fp8: V's per-token scale folded into P; l above sums the unscaled P)
       const uint32_t b0 = movmatrix_t(pack2<T>(p0 * vs0, p1 * vs0));  // tokens 0-7
       const uint32_t b1 = movmatrix_t(pack2<T>(p2 * vs1, p3 * vs1));  // tokens 8-15
-      // ---- O^T += V^T P^T, 4 tiles of 16 dims
+      // ---- O^T += V^T P^T, 4 tiles of 16 dims (fp8: O rows g, g + 8 of tile
+      // mt are dims 8g + 2mt and 8g + 2mt + 1)
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
-        const int row = (lane & 7) + ((mi >> 1) << 3);
-        const int chunk = 2 * mt + (mi & 1);
         uint32_t a[4];
-        ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        if constexpr (FP8) {
+          // interleave tokens (2t, 2t + 1) and (2t + 8, 2t + 9) byte by byte:
+          // the low 16 bits are dim 8g + 2mt, the high 16 bits the next dim
+          // (integer conversion: bytes 0, 2 = dim 8g + 2mt and bytes 1, 3 = the
+          // next dim, tokens 2t / 2t + 1 in bytes 0-1 / 2-3)
+          const uint32_t sel = kAluCvt ? ((mt & 1) ? 0x7632u : 0x5410u) : ((mt & 1) ? 0x7362u : 0x5140u);
+          const uint32_t x01 = __byte_perm(mt < 2 ? vr[0].x : vr[0].y, mt < 2 ? vr[1].x : vr[1].y, sel);
+          const uint32_t x23 = __byte_perm(mt < 2 ? vr[2].x : vr[2].y, mt < 2 ? vr[3].x : vr[3].y, sel);
+          if constexpr (kAluCvt) {
+            a[0] = e4m3_even_h2(x01);
+            a[1] = e4m3_odd_h2(x01);
+            a[2] = e4m3_even_h2(x23);
+            a[3] = e4m3_odd_h2(x23);
+          } else {
+            a[0] = fp8x2_to<T>(x01 & 0xffffu);
+            a[1] = fp8x2_to<T>(x01 >> 16);
+            a[2] = fp8x2_to<T>(x23 & 0xffffu);
+            a[3] = fp8x2_to<T>(x23 >> 16);
+          }
+        } else {
+          const int row = (lane & 7) + ((mi >> 1) << 3);
+          const int chunk = 2 * mt + (mi & 1);
+          ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+        }
         mma16816<T>(o[mt], a, b0, b1);
       }
-      __syncwarp();  // (fp8: every lane is done with the staging tiles)
-      if (!FP8 && lane == 0) mbar_arrive(&empty_bar[st]);
+      if constexpr (!FP8) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);
+      }
     }
 
     // ---- segment epilogue: per-head sums over the 8 token groups
@@ -484,30 +560,58 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride +
                 static_cast<int64_t>(qh0) * 64;
       const float i0 = 1.f / lt0, i1 = 1.f / lt1;
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
+      if constexpr (FP8) {
+        // this lane holds dims 8g .. 8g + 7 of heads 2t and 2t + 1
         if (ok0) {
-          orow[16 * mt + g] = Elem<T>::from_f(o[mt][0] * i0);
-          orow[16 * mt + g + 8] = Elem<T>::from_f(o[mt][2] * i0);
+          *reinterpret_cast<uint2*>(orow + 8 * g) =
+              make_uint2(pack2<T>(o[0][0] * i0, o[0][2] * i0), pack2<T>(o[1][0] * i0, o[1][2] * i0));
+          *reinterpret_cast<uint2*>(orow + 8 * g + 4) =
+              make_uint2(pack2<T>(o[2][0] * i0, o[2][2] * i0), pack2<T>(o[3][0] * i0, o[3][2] * i0));
         }
         if (ok1) {
-          orow[64 + 16 * mt + g] = Elem<T>::from_f(o[mt][1] * i1);
-          orow[64 + 16 * mt + g + 8] = Elem<T>::from_f(o[mt][3] * i1);
+          *reinterpret_cast<uint2*>(orow + 64 + 8 * g) =
+              make_uint2(pack2<T>(o[0][1] * i1, o[0][3] * i1), pack2<T>(o[1][1] * i1, o[1][3] * i1));
+          *reinterpret_cast<uint2*>(orow + 64 + 8 * g + 4) =
+              make_uint2(pack2<T>(o[2][1] * i1, o[2][3] * i1), pack2<T>(o[3][1] * i1, o[3][3] * i1));
+        }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          if (ok0) {
+            orow[16 * mt + g] = Elem<T>::from_f(o[mt][0] * i0);
+            orow[16 * mt + g + 8] = Elem<T>::from_f(o[mt][2] * i0);
+          }
+          if (ok1) {
+            orow[64 + 16 * mt + g] = Elem<T>::from_f(o[mt][1] * i1);
+            orow[64 + 16 * mt + g + 8] = Elem<T>::from_f(o[mt][3] * i1);
+          }
         }
       }
     } else {
       const int slot = partial_slot(blockIdx.x, per, prefix[s]);
       float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh0) * 64;
       float* pml = p.part_ml + static_cast<int64_t>(slot) * p.ml_stride + qh0 * 2;
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
+      if constexpr (FP8) {
         if (ok0) {
-          po[16 * mt + g] = o[mt][0];
-          po[16 * mt + g + 8] = o[mt][2];
+          *reinterpret_cast<float4*>(po + 8 * g) = make_float4(o[0][0], o[0][2], o[1][0], o[1][2]);
+          *reinterpret_cast<float4*>(po + 8 * g + 4) = make_float4(o[2][0], o[2][2], o[3][0], o[3][2]);
         }
         if (ok1) {
-          po[64 + 16 * mt + g] = o[mt][1];
-          po[64 + 16 * mt + g + 8] = o[mt][3];
+          *reinterpret_cast<float4*>(po + 64 + 8 * g) = make_float4(o[0][1], o[0][3], o[1][1], o[1][3]);
+          *reinterpret_cast<float4*>(po + 64 + 8 * g + 4) =
+              make_float4(o[2][1], o[2][3], o[3][1], o[3][3]);
+        }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          if (ok0) {
+            po[16 * mt + g] = o[mt][0];
+            po[16 * mt + g + 8] = o[mt][2];
+          }
+          if (ok1) {
+            po[64 + 16 * mt + g] = o[mt][1];
+            po[64 + 16 * mt + g + 8] = o[mt][3];
+          }
         }
       }
       if (g == 0) {
@@ -658,8 +762,7 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
 
 size_t decode_smem_bytes(int nkv, int n_seqs, bool fp8) {
   const size_t stage = fp8 ? 2 * nkv * kDecTile8 + 2 * 16 * nkv * 4 : 2 * nkv * kDecTile;
-  const size_t staging = fp8 ? static_cast<size_t>(nkv) * 2 * kDecTile : 0;
-  return 1024 + staging + static_cast<size_t>(kDecStages) * stage +
+  return 1024 + static_cast<size_t>(kDecStages) * stage +
          2 * kDecStages * sizeof(uint64_t) + 40 * sizeof(int) +
          (2 * static_cast<size_t>(n_seqs) + 1) * sizeof(int);
 }
