@@ -51,10 +51,14 @@
 namespace pkv {
 
 #ifndef PKV_DEC_STAGES
-#define PKV_DEC_STAGES 8
+#define PKV_DEC_STAGES 3
 #endif
 #ifndef PKV_DEC_MIN_CTAS
 #define PKV_DEC_MIN_CTAS 3
+#endif
+// blocks of each CTA's range prefetched into L2 before griddepcontrol.wait
+#ifndef PKV_DEC_PREFETCH
+#define PKV_DEC_PREFETCH 3
 #endif
 constexpr int kDecStages = PKV_DEC_STAGES;
 constexpr int kDecMaxCtas = 1024;
@@ -63,6 +67,8 @@ constexpr int kDecMinBlocksPerCta = 4;
 constexpr int kDecTile = 2048;  // 16 tokens x 64 dims x 2 bytes
 constexpr int kDecTile8 = 1024;  // 16 tokens x 64 dims x 1 byte (fp8)
 constexpr float kLog2e = 1.4426950408889634f;
+// lazy online-softmax rescale threshold (log2 domain): P <= 2^8
+constexpr float kRescaleSlack = 8.f;
 
 struct DecodeParams {
   void* out;
@@ -313,8 +319,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         }
       }
       if (!waited) {
-        // warm L2 with the first stages' K/V while the preceding kernel ends
-        if (gb < r1 && lane < kDecStages) {
+        // warm L2 with the first blocks' K/V while the preceding kernel ends
+        if (gb < r1 && lane < PKV_DEC_PREFETCH) {
           prefetch_l2(p.k_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
           prefetch_l2(p.v_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
         }
@@ -383,7 +389,16 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   // fp8 conversion on the integer pipes (fp16) or by cvt (bf16)
   constexpr bool kAluCvt = FP8 && PKV_FP8_ALU_CVT && std::is_same<T, __half>::value;
   constexpr int QL = !FP8 ? 0 : kAluCvt ? 2 : 1;
-  constexpr float kCvt = kAluCvt ? 256.f : 1.f;  // undoes the 2^-8 of the integer conversion
+  // the integer conversion yields 2^-8 x the e4m3 values: K's 2^8 goes into
+  // the score scale, V's into O at the segment epilogue
+  constexpr float kCvt = kAluCvt ? 256.f : 1.f;
+  const float sl2 = p.scale_log2 * kCvt;
+  // fp8 V byte interleave (tokens 2t / 2t + 1 of dims 8g + 2mt, + 1); lanes
+  // with sw = 1 loaded the token pair swapped, so their operands swap back
+  const int sw = t & 1;
+  const uint32_t sel_flip = sw ? 0x4444u : 0u;
+  const uint32_t sel_lo = (kAluCvt ? 0x5410u : 0x5140u) ^ sel_flip;  // even mt
+  const uint32_t sel_hi = (kAluCvt ? 0x7632u : 0x7362u) ^ sel_flip;  // odd mt
   const int G = p.group;
   const bool ok0 = 2 * t < G, ok1 = 2 * t + 1 < G;  // this lane's two heads exist
   const int qh0 = h * G + 2 * t;                    // its first query head
@@ -415,12 +430,14 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
         dead = true;
       }
+      // tokens of this block inside the context; only a sequence's last
+      // block has fewer than 16 (warp-uniform)
+      const int valid = min(16, ctx - jb * 16);
       uint32_t kt = 0, vt = 0;                           // 16-bit tiles: ldmatrix bases
       float ks0 = 1.f, ks1 = 1.f, vs0 = 1.f, vs1 = 1.f;  // fp8 scales of tokens g, g + 8
       uint4 kr0, kr1;  // fp8: K rows g and g + 8, bytes 16t .. 16t + 15
-      uint2 vr[4];     // fp8: V rows 2t, 2t + 1, 2t + 8, 2t + 9, bytes 8g .. 8g + 7
+      uint2 vr[4];     // fp8: V rows 2t + sw, 2t + 1 - sw, 2t + 8 + sw, 2t + 9 - sw
       if constexpr (FP8) {
-        const int valid8 = min(16, ctx - jb * 16);
         const uint8_t* stg = tiles + st * stage_bytes;
         const uint8_t* k8 = stg + h * kDecTile8;
         const uint8_t* v8 = stg + (nkv + h) * kDecTile8;
@@ -428,30 +445,30 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         const float* vsc = ksc + 16 * nkv;
         kr0 = *reinterpret_cast<const uint4*>(k8 + g * 64 + t * 16);
         kr1 = *reinterpret_cast<const uint4*>(k8 + (g + 8) * 64 + t * 16);
-        // lanes with odd t take their row pair in the other order, so that
-        // each 8-byte load's 32 lanes fill all 32 banks (two wavefronts)
-        const int sw = t & 1;
-        const uint2 va = *reinterpret_cast<const uint2*>(v8 + (2 * t + sw) * 64 + 8 * g);
-        const uint2 vb = *reinterpret_cast<const uint2*>(v8 + (2 * t + 1 - sw) * 64 + 8 * g);
-        const uint2 vc = *reinterpret_cast<const uint2*>(v8 + (2 * t + 8 + sw) * 64 + 8 * g);
-        const uint2 vd = *reinterpret_cast<const uint2*>(v8 + (2 * t + 9 - sw) * 64 + 8 * g);
-        ks0 = g < valid8 ? ksc[g * nkv + h] * kCvt : 0.f;
-        ks1 = g + 8 < valid8 ? ksc[(g + 8) * nkv + h] * kCvt : 0.f;
-        vs0 = g < valid8 ? vsc[g * nkv + h] * kCvt : 0.f;
-        vs1 = g + 8 < valid8 ? vsc[(g + 8) * nkv + h] * kCvt : 0.f;
+        // lanes with odd t (sw = 1) take their row pair in the other order, so
+        // that each 8-byte load's 32 lanes fill all 32 banks (two wavefronts);
+        // the byte permutes below swap their operands back (sel ^ 0x4444)
+        vr[0] = *reinterpret_cast<const uint2*>(v8 + (2 * t + sw) * 64 + 8 * g);
+        vr[1] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 1 - sw) * 64 + 8 * g);
+        vr[2] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 8 + sw) * 64 + 8 * g);
+        vr[3] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 9 - sw) * 64 + 8 * g);
+        ks0 = ksc[g * nkv + h];
+        ks1 = ksc[(g + 8) * nkv + h];
+        vs0 = vsc[g * nkv + h];
+        vs1 = vsc[(g + 8) * nkv + h];
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[st]);  // the stage is free once in registers
-        vr[0] = sw ? vb : va;
-        vr[1] = sw ? va : vb;
-        vr[2] = sw ? vd : vc;
-        vr[3] = sw ? vc : vd;
-        // V rows past the context are zeroed (an unused slot may hold any
-        // bytes, and 0 x NaN would reach O); K rows there are masked below
-        const uint2 z = make_uint2(0u, 0u);
-        if (2 * t >= valid8) vr[0] = z;
-        if (2 * t + 1 >= valid8) vr[1] = z;
-        if (2 * t + 8 >= valid8) vr[2] = z;
-        if (2 * t + 9 >= valid8) vr[3] = z;
+        if (valid < 16) {
+          // rows past the context: scales 0, V bytes 0 (an unused slot may hold
+          // any bytes, and 0 x NaN would reach O); their scores are masked below
+          if (g >= valid) ks0 = vs0 = 0.f;
+          if (g + 8 >= valid) ks1 = vs1 = 0.f;
+          const uint2 z = make_uint2(0u, 0u);
+          if (2 * t + sw >= valid) vr[0] = z;
+          if (2 * t + 1 - sw >= valid) vr[1] = z;
+          if (2 * t + 8 + sw >= valid) vr[2] = z;
+          if (2 * t + 9 - sw >= valid) vr[3] = z;
+        }
       } else {
         kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
         vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
@@ -484,45 +501,50 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         }
         mma16816<T>(sc, a, qa[kk][0], qa[kk][1]);
       }
-      // ---- online softmax per head (exp2 domain); tokens >= valid masked
-      const int valid = min(16, ctx - jb * 16);
-      const float sa = FP8 ? p.scale_log2 * ks0 : p.scale_log2;
-      const float sb = FP8 ? p.scale_log2 * ks1 : p.scale_log2;
+      // ---- online softmax per head (exp2 domain)
+      const float sa = FP8 ? sl2 * ks0 : sl2;
+      const float sb = FP8 ? sl2 * ks1 : sl2;
       float x0 = sc[0] * sa, x1 = sc[1] * sa;  // token g
       float x2 = sc[2] * sb, x3 = sc[3] * sb;  // token g + 8
-      if (g >= valid) x0 = x1 = -INFINITY;
-      if (g + 8 >= valid) x2 = x3 = -INFINITY;
+      if (valid < 16) {
+        if (g >= valid) x0 = x1 = -INFINITY;
+        if (g + 8 >= valid) x2 = x3 = -INFINITY;
+      }
       float ma = fmaxf(x0, x2), mb = fmaxf(x1, x3);
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
         mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
       }
-      const float mna = fmaxf(m0, ma), mnb = fmaxf(m1, mb);
-      const float ca = exp2f(m0 - mna), cb = exp2f(m1 - mnb);
-      const float p0 = exp2f(x0 - mna), p2 = exp2f(x2 - mna);
-      const float p1 = exp2f(x1 - mnb), p3 = exp2f(x3 - mnb);
-      l0 = l0 * ca + (p0 + p2);
-      l1 = l1 * cb + (p1 + p3);
-      m0 = mna;
-      m1 = mnb;
+      // lazy rescale: the reference max moves only when some head's block max
+      // exceeds it by more than kRescaleSlack, so P stays <= 2^kRescaleSlack
+      // and the (m, l, O) triple stays exact relative to its own m
+      if (__any_sync(0xffffffffu, ma > m0 + kRescaleSlack || mb > m1 + kRescaleSlack)) {
+        const float mna = fmaxf(m0, ma), mnb = fmaxf(m1, mb);
+        const float ca = ex2_approx(m0 - mna), cb = ex2_approx(m1 - mnb);
+        l0 *= ca;
+        l1 *= cb;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { o[j][0] *= ca; o[j][1] *= cb; o[j][2] *= ca; o[j][3] *= cb; }
+        for (int j = 0; j < 4; ++j) { o[j][0] *= ca; o[j][1] *= cb; o[j][2] *= ca; o[j][3] *= cb; }
+        m0 = mna;
+        m1 = mnb;
+      }
+      const float p0 = ex2_approx(x0 - m0), p2 = ex2_approx(x2 - m0);
+      const float p1 = ex2_approx(x1 - m1), p3 = ex2_approx(x3 - m1);
+      l0 += p0 + p2;
+      l1 += p1 + p3;
       // ---- P^T fragments: transpose (token x head) 8x8 tiles to (head x token)
       // (fp8: V's per-token scale folded into P; l above sums the unscaled P)
-      const uint32_t b0 = movmatrix_t(pack2<T>(p0 * vs0, p1 * vs0));  // tokens 0-7
-      const uint32_t b1 = movmatrix_t(pack2<T>(p2 * vs1, p3 * vs1));  // tokens 8-15
+      const uint32_t b0 = movmatrix_t(FP8 ? pack2<T>(p0 * vs0, p1 * vs0) : pack2<T>(p0, p1));  // tokens 0-7
+      const uint32_t b1 = movmatrix_t(FP8 ? pack2<T>(p2 * vs1, p3 * vs1) : pack2<T>(p2, p3));  // tokens 8-15
       // ---- O^T += V^T P^T, 4 tiles of 16 dims (fp8: O rows g, g + 8 of tile
       // mt are dims 8g + 2mt and 8g + 2mt + 1)
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
         uint32_t a[4];
         if constexpr (FP8) {
-          // interleave tokens (2t, 2t + 1) and (2t + 8, 2t + 9) byte by byte:
-          // the low 16 bits are dim 8g + 2mt, the high 16 bits the next dim
-          // (integer conversion: bytes 0, 2 = dim 8g + 2mt and bytes 1, 3 = the
-          // next dim, tokens 2t / 2t + 1 in bytes 0-1 / 2-3)
-          const uint32_t sel = kAluCvt ? ((mt & 1) ? 0x7632u : 0x5410u) : ((mt & 1) ? 0x7362u : 0x5140u);
+          // interleave tokens (2t, 2t + 1) and (2t + 8, 2t + 9) byte by byte
+          const uint32_t sel = (mt & 1) ? sel_hi : sel_lo;
           const uint32_t x01 = __byte_perm(mt < 2 ? vr[0].x : vr[0].y, mt < 2 ? vr[1].x : vr[1].y, sel);
           const uint32_t x23 = __byte_perm(mt < 2 ? vr[2].x : vr[2].y, mt < 2 ? vr[3].x : vr[3].y, sel);
           if constexpr (kAluCvt) {
@@ -559,7 +581,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     if (complete) {
       T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride +
                 static_cast<int64_t>(qh0) * 64;
-      const float i0 = 1.f / lt0, i1 = 1.f / lt1;
+      const float i0 = kCvt / lt0, i1 = kCvt / lt1;
       if constexpr (FP8) {
         // this lane holds dims 8g .. 8g + 7 of heads 2t and 2t + 1
         if (ok0) {
@@ -592,6 +614,10 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh0) * 64;
       float* pml = p.part_ml + static_cast<int64_t>(slot) * p.ml_stride + qh0 * 2;
       if constexpr (FP8) {
+        if constexpr (kAluCvt) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) { o[j][0] *= kCvt; o[j][1] *= kCvt; o[j][2] *= kCvt; o[j][3] *= kCvt; }
+        }
         if (ok0) {
           *reinterpret_cast<float4*>(po + 8 * g) = make_float4(o[0][0], o[0][2], o[1][0], o[1][2]);
           *reinterpret_cast<float4*>(po + 8 * g + 4) = make_float4(o[2][0], o[2][2], o[3][0], o[3][2]);
