@@ -118,7 +118,7 @@ template <> __device__ __forceinline__ uint32_t fp8x2_to<__nv_bfloat16>(uint32_t
 // quantising append never stores them.  Keeps the conversions off the
 // transcendental pipe, which the softmax's exp2 also needs.
 #ifndef PKV_FP8_ALU_CVT
-#define PKV_FP8_ALU_CVT 1
+#define PKV_FP8_ALU_CVT 2  // bit 0: K tiles, bit 1: V tiles (K by cvt measured faster)
 #endif
 // bytes 1 and 3 of x -> f16x2 (byte 1 in the low half)
 __device__ __forceinline__ uint32_t e4m3_odd_h2(uint32_t x) {
@@ -387,18 +387,20 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   const int h = warp;
   const int g = lane >> 2, t = lane & 3;
   // fp8 conversion on the integer pipes (fp16) or by cvt (bf16)
-  constexpr bool kAluCvt = FP8 && PKV_FP8_ALU_CVT && std::is_same<T, __half>::value;
-  constexpr int QL = !FP8 ? 0 : kAluCvt ? 2 : 1;
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  constexpr bool kAluK = FP8 && kF16 && (PKV_FP8_ALU_CVT & 1);
+  constexpr bool kAluV = FP8 && kF16 && (PKV_FP8_ALU_CVT & 2);
+  constexpr int QL = !FP8 ? 0 : kAluK ? 2 : 1;
   // the integer conversion yields 2^-8 x the e4m3 values: K's 2^8 goes into
   // the score scale, V's into O at the segment epilogue
-  constexpr float kCvt = kAluCvt ? 256.f : 1.f;
-  const float sl2 = p.scale_log2 * kCvt;
+  constexpr float kCvt = kAluV ? 256.f : 1.f;
+  const float sl2 = p.scale_log2 * (kAluK ? 256.f : 1.f);
   // fp8 V byte interleave (tokens 2t / 2t + 1 of dims 8g + 2mt, + 1); lanes
   // with sw = 1 loaded the token pair swapped, so their operands swap back
   const int sw = t & 1;
   const uint32_t sel_flip = sw ? 0x4444u : 0u;
-  const uint32_t sel_lo = (kAluCvt ? 0x5410u : 0x5140u) ^ sel_flip;  // even mt
-  const uint32_t sel_hi = (kAluCvt ? 0x7632u : 0x7362u) ^ sel_flip;  // odd mt
+  const uint32_t sel_lo = (kAluV ? 0x5410u : 0x5140u) ^ sel_flip;  // even mt
+  const uint32_t sel_hi = (kAluV ? 0x7632u : 0x7362u) ^ sel_flip;  // odd mt
   const int G = p.group;
   const bool ok0 = 2 * t < G, ok1 = 2 * t + 1 < G;  // this lane's two heads exist
   const int qh0 = h * G + 2 * t;                    // its first query head
@@ -483,7 +485,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
           // k-step kk: bytes 4kk .. 4kk + 3 of rows g and g + 8
           const uint32_t w0 = kk == 0 ? kr0.x : kk == 1 ? kr0.y : kk == 2 ? kr0.z : kr0.w;
           const uint32_t w1 = kk == 0 ? kr1.x : kk == 1 ? kr1.y : kk == 2 ? kr1.z : kr1.w;
-          if constexpr (kAluCvt) {
+          if constexpr (kAluK) {
             a[0] = e4m3_even_h2(w0);
             a[1] = e4m3_even_h2(w1);
             a[2] = e4m3_odd_h2(w0);
@@ -547,7 +549,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
           const uint32_t sel = (mt & 1) ? sel_hi : sel_lo;
           const uint32_t x01 = __byte_perm(mt < 2 ? vr[0].x : vr[0].y, mt < 2 ? vr[1].x : vr[1].y, sel);
           const uint32_t x23 = __byte_perm(mt < 2 ? vr[2].x : vr[2].y, mt < 2 ? vr[3].x : vr[3].y, sel);
-          if constexpr (kAluCvt) {
+          if constexpr (kAluV) {
             a[0] = e4m3_even_h2(x01);
             a[1] = e4m3_odd_h2(x01);
             a[2] = e4m3_even_h2(x23);
@@ -614,7 +616,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh0) * 64;
       float* pml = p.part_ml + static_cast<int64_t>(slot) * p.ml_stride + qh0 * 2;
       if constexpr (FP8) {
-        if constexpr (kAluCvt) {
+        if constexpr (kAluV) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) { o[j][0] *= kCvt; o[j][1] *= kCvt; o[j][2] *= kCvt; o[j][3] *= kCvt; }
         }
