@@ -45,10 +45,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops", "decode_fp8"),
+    ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops", "decode_fp8",
+                                           "migrate"),
                     default="decode",
                     help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5; "
-                         "cache_ops = reshape_and_cache and copy_blocks at bandwidth-sized batches")
+                         "cache_ops = reshape_and_cache and copy_blocks at bandwidth-sized batches; "
+                         "migrate = KV block migration between rank pairs over NVLink (2+ ranks)")
+    ap.add_argument("--migrate-blocks", type=int, default=1024,
+                    help="migrate: blocks per copy launch (x 24 layers, K and V)")
     ap.add_argument("--append-tokens", type=int, nargs="+", default=[8192, 65536],
                     help="cache_ops: tokens appended per reshape_and_cache launch")
     ap.add_argument("--copy-pairs", type=int, default=4096, help="cache_ops: (src, dst) block pairs")
@@ -865,8 +869,114 @@ def run_cache_ops(args):
     print(json.dumps(line), flush=True)
 
 
+def run_migrate(args):
+    """KV block migration between rank pairs (0 -> 1, 2 -> 3, ...) over NVLink.
+    Kernel: one pkv_copy_blocks_peer launch moving P blocks x L layers of K
+    and V (fp16) from the source's pool to fixed destination blocks of the
+    peer's pool, timed with CUDA events on the launching rank.  push: the
+    source launches it (its stores cross NVLink); pull: the destination does
+    (its loads cross).  GB/s = bytes crossing the link / kernel time.  Then
+    the full protocol (allocation, host handshakes, copy, synchronisation) for
+    one 1,024-token sequence (64 blocks), host wall time per migration."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from pagedkv import BlockManager, ops
+    from pagedkv.migration import PeerPools, migrate_blocks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        print(json.dumps({"metric": "KV block migration GB/s over NVLink", "unavailable":
+                          "needs 2 ranks: torchrun --nproc-per-node 2 bench.py --workload migrate"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    L, P = args.layers, args.migrate_blocks
+    nb = P + 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=torch.float16)
+    mgr.k_cache.normal_(generator=g)
+    mgr.v_cache.normal_(generator=g)
+    src_side = rank % 2 == 0
+    peer = rank + 1 if src_side else rank - 1
+    rng = np.random.default_rng(5)
+    perm_src = rng.permutation(nb)[:P].astype(np.int32)
+    perm_dst = rng.permutation(nb)[:P].astype(np.int32)
+    pairs = torch.from_numpy(np.stack([perm_src, perm_dst], axis=1).copy()).to(dev)
+    nbytes = 2 * L * P * mgr.block_bytes
+    res = {}
+    for mode in ("push", "pull"):
+        peers = PeerPools(mgr, mode=mode)
+        launching = src_side == (mode == "push")
+        ms = 0.0
+        if launching:
+            src = peers.refs[rank if src_side else peer]
+            dst = peers.refs[peer if src_side else rank]
+
+            def copy():
+                ops.copy_blocks_peer(dst.k, dst.v, dst.layer_stride, dst.num_blocks, src.k, src.v,
+                                     src.layer_stride, src.num_blocks, L, pairs, dst.block_bytes,
+                                     mgr.err)
+
+            for _ in range(args.warmup):
+                copy()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for a, b in evs:
+                a.record()
+                copy()
+                b.record()
+            torch.cuda.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+            ops.check_flags(mgr.err, "migrate bench")
+        dist.barrier(group=peers.host_group)
+        t = torch.tensor([ms])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=peers.host_group)
+        res[mode] = {"us": round(float(t) * 1e3, 2), "gbs": round(nbytes / (float(t) * 1e-3) / 1e9, 1)}
+        # full protocol for a 1,024-token sequence (64 blocks), host wall time
+        seq_blocks = list(range(64))
+        reps = 20
+        dist.barrier(group=peers.host_group)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            ids = migrate_blocks(peers, rank if src_side else peer, peer if src_side else rank,
+                                 seq_blocks if src_side else None)
+            if not src_side:
+                for b in ids:
+                    mgr.decref(b)
+        res[mode]["protocol_ms_per_seq"] = round((time.perf_counter() - t0) / reps * 1e3, 3)
+        peers.close()
+    link_peak = 770.0  # measured peer copy per direction on this pool (GB/s)
+    if rank == 0:
+        best = max(res.values(), key=lambda r: r["gbs"])
+        print(json.dumps({
+            "metric": "KV block migration GB/s over NVLink (one copy launch, rank pairs)",
+            "value": best["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "dtype": "f16",
+            "data": "synthetic (seeded normal K/V pools, random block pairs)",
+            "config": {"workload": f"migrate: {P} blocks x {L} layers x K,V per launch "
+                                   f"({nbytes / 1e6:.1f} MB), pairs of ranks 0->1, 2->3, ...",
+                       "blocks": P, "layers": L},
+            "modes": res,
+            "roofline": {"bound": "nvlink", "achieved": best["gbs"], "peak": link_peak,
+                         "unit": "GB/s", "frac": round(best["gbs"] / link_peak, 4)},
+            "gpu_launches": args.steps}), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "migrate":
+        run_migrate(args)
+        return
     if args.workload == "e2e" and args.impl == "ours":
         run_e2e(args)
         return

@@ -62,6 +62,9 @@ extern "C" {
  * pkv_paged_decode_attention_noalloc (per GPU, held until the process exits) */
 #define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)
 
+/* Bytes of a CUDA IPC memory handle (pkv_ipc_export / pkv_ipc_open). */
+#define PKV_IPC_HANDLE_BYTES 64
+
 /* decode-attention kernel choice (pkv_set_decode_impl) */
 #define PKV_DECODE_AUTO 0
 #define PKV_DECODE_GENERIC 1
@@ -100,6 +103,41 @@ int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride,
 int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
                     const int32_t* block_pairs, int n_pairs, int num_blocks,
                     int64_t block_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
+ * KV block migration between GPUs (one process per GPU).  Replaces the
+ * reference's recompute preemption (mini_engine/scheduler.py:143-156 frees a
+ * preempted sequence's blocks and recomputes its KV later): a rank copies a
+ * sequence's blocks into another rank's pool over NVLink instead.
+ *
+ * pkv_ipc_export: the CUDA IPC handle (PKV_IPC_HANDLE_BYTES) of the device
+ *   allocation that holds dev_ptr, and dev_ptr's byte offset in it (a pool
+ *   tensor may sit inside a larger allocation of the caller's allocator).
+ * pkv_ipc_open: maps an allocation exported by another process (any GPU of
+ *   this node; peer access is enabled on first use) into this process's
+ *   current device context and returns its base; add the exported offset.
+ *   An allocation is opened once per process.
+ * pkv_ipc_close: unmaps a base returned by pkv_ipc_open.
+ * pkv_copy_blocks_peer: for each (src, dst) pair of block_pairs [n_pairs][2]
+ *   and each of n_layers layers, block dst of the destination K and V pools
+ *   becomes a copy of block src of the source pools.  Either side may be a
+ *   peer GPU's memory opened with pkv_ipc_open (the kernel runs on the
+ *   caller's stream and device).  Layer l of a pool starts l * its layer
+ *   stride after its base.  Ids outside [0, num_blocks) of their pool set
+ *   PKV_FLAG_BLOCK_OUT_OF_RANGE and the pair is skipped.  block_bytes,
+ *   strides and pool bases must be multiples of 16 bytes.  fp8 pools move
+ *   their scale pools by a second call (block_bytes = block_size x n_kv_heads
+ *   x 4).  The caller orders the copy against the other process's use of
+ *   its pool (pagedkv.migration does it with host messages).
+ */
+int pkv_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset);
+int pkv_ipc_open(const void* handle, void** base);
+int pkv_ipc_close(void* base);
+int pkv_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride_bytes,
+                         int dst_num_blocks, const void* src_k, const void* src_v,
+                         int64_t src_layer_stride_bytes, int src_num_blocks, int n_layers,
+                         const int32_t* block_pairs, int n_pairs, int64_t block_bytes,
+                         int* err_flags, pkv_stream_t stream);
 
 /*
  * Rotary embedding of q and k fused with the KV append (one launch per

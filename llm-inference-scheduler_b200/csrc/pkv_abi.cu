@@ -34,6 +34,23 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return g_encode;
 }
 
+PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+std::once_flag g_addr_range_once;
+
+PFN_cuMemGetAddressRange_v3020 address_range() {
+  std::call_once(g_addr_range_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  return g_addr_range;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == PKV_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+
 struct MapKey {
   const void* ptr;
   int num_blocks, block_size, n_kv_heads, head_dim, dtype;
@@ -191,7 +208,9 @@ const char* pkv_status_string(int status) {
     case PKV_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than pkv_decode_workspace_bytes()";
     case PKV_ERR_MISALIGNED: return "pointer or stride misaligned for this kernel";
     case PKV_ERR_UNSUPPORTED: return "combination of arguments not supported";
-    case PKV_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or failed";
+    case PKV_ERR_DRIVER:
+      return "a CUDA driver entry point (cuTensorMapEncodeTiled, cuMemGetAddressRange) is "
+             "unavailable or failed";
     case PKV_ERR_SCRATCH_LIMIT:
       return "problem needs more split-K scratch than the allocation-free decode entry point's "
              "fixed PKV_NOALLOC_SCRATCH_BYTES array holds; use pkv_paged_decode_attention";
@@ -298,6 +317,56 @@ int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, in
   return status_of(launch_copy_blocks(k_pools, v_pools, layer_stride_bytes, n_layers, block_pairs,
                                       n_pairs, num_blocks, block_bytes, err_flags,
                                       static_cast<cudaStream_t>(stream)));
+}
+
+int pkv_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset) {
+  if (!dev_ptr || !handle || !offset) return PKV_ERR_NULL_POINTER;
+  auto range = address_range();
+  if (range == nullptr) return PKV_ERR_DRIVER;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return PKV_ERR_DRIVER;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return status_of(e);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(dev_ptr) - base);
+  return PKV_OK;
+}
+
+int pkv_ipc_open(const void* handle, void** base) {
+  if (!handle || !base) return PKV_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return status_of(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int pkv_ipc_close(void* base) {
+  if (!base) return PKV_ERR_NULL_POINTER;
+  return status_of(cudaIpcCloseMemHandle(base));
+}
+
+int pkv_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride_bytes,
+                         int dst_num_blocks, const void* src_k, const void* src_v,
+                         int64_t src_layer_stride_bytes, int src_num_blocks, int n_layers,
+                         const int32_t* block_pairs, int n_pairs, int64_t block_bytes,
+                         int* err_flags, pkv_stream_t stream) {
+  if (n_pairs < 0 || n_layers < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_pairs == 0 || n_layers == 0) return PKV_OK;
+  if (!dst_k || !dst_v || !src_k || !src_v || !block_pairs) return PKV_ERR_NULL_POINTER;
+  if (dst_num_blocks <= 0 || src_num_blocks <= 0 || block_bytes <= 0) return PKV_ERR_BAD_SHAPE;
+  if (n_layers > 65535) return PKV_ERR_UNSUPPORTED;
+  if (n_layers > 1 && (dst_layer_stride_bytes < static_cast<int64_t>(dst_num_blocks) * block_bytes ||
+                       src_layer_stride_bytes < static_cast<int64_t>(src_num_blocks) * block_bytes))
+    return PKV_ERR_BAD_SHAPE;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (block_bytes % 16 || dst_layer_stride_bytes % 16 || src_layer_stride_bytes % 16 || !al16(dst_k) ||
+      !al16(dst_v) || !al16(src_k) || !al16(src_v))
+    return PKV_ERR_MISALIGNED;
+  return status_of(launch_copy_blocks_peer(dst_k, dst_v, dst_layer_stride_bytes, dst_num_blocks, src_k,
+                                           src_v, src_layer_stride_bytes, src_num_blocks, n_layers,
+                                           block_pairs, n_pairs, block_bytes, err_flags,
+                                           static_cast<cudaStream_t>(stream)));
 }
 
 size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {

@@ -4,6 +4,8 @@
 // elements (256 B for the reference's 2 x 64 fp16) move with 16-byte vector
 // loads/stores, one warp per token (append) or one CTA per (pair, layer)
 // (copy).  Results are bit-exact copies.
+#include <algorithm>
+
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
 
@@ -271,6 +273,68 @@ __global__ void __launch_bounds__(256) copy_blocks_bytes(char* __restrict__ k_po
     k_pools[base + dst * block_bytes + i] = k_pools[base + src * block_bytes + i];
     v_pools[base + dst * block_bytes + i] = v_pools[base + src * block_bytes + i];
   }
+}
+
+// Block copy between two pools that may live on different GPUs: one of them
+// (or both) mapped from a peer process with CUDA IPC, so the loads or the
+// stores cross NVLink.  Used for KV block migration between ranks (a rank
+// pulls a peer's blocks, or pushes its own into a peer's pool) in place of
+// recompute preemption (mini_engine/scheduler.py:143-156 drops the KV and
+// recomputes it).  Plain 16-byte loads and stores only, no TMA.
+// One CTA per (pair, layer); each thread issues all its loads before its
+// stores, so a CTA keeps the whole K and V block in flight over the link.
+constexpr int kPeerVecsPerThread = 4;
+__global__ void __launch_bounds__(256) copy_blocks_peer_vec16(
+    char* __restrict__ dst_k, char* __restrict__ dst_v, int64_t dst_layer_stride, int dst_num_blocks,
+    const char* __restrict__ src_k, const char* __restrict__ src_v, int64_t src_layer_stride,
+    int src_num_blocks, const int32_t* __restrict__ pairs, int64_t block_bytes, int* err) {
+  const int p = blockIdx.x;
+  const int layer = blockIdx.y;
+  const int src = __ldg(pairs + 2 * p), dst = __ldg(pairs + 2 * p + 1);
+  if (src < 0 || dst < 0 || src >= src_num_blocks || dst >= dst_num_blocks) {
+    if (threadIdx.x == 0 && layer == 0) raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t nvec = block_bytes >> 4;
+  const int4* ks = reinterpret_cast<const int4*>(src_k + layer * src_layer_stride + src * block_bytes);
+  const int4* vs = reinterpret_cast<const int4*>(src_v + layer * src_layer_stride + src * block_bytes);
+  int4* kd = reinterpret_cast<int4*>(dst_k + layer * dst_layer_stride + dst * block_bytes);
+  int4* vd = reinterpret_cast<int4*>(dst_v + layer * dst_layer_stride + dst * block_bytes);
+  for (int64_t i0 = threadIdx.x; i0 < nvec; i0 += static_cast<int64_t>(blockDim.x) * kPeerVecsPerThread) {
+    int4 a[kPeerVecsPerThread], b[kPeerVecsPerThread];
+#pragma unroll
+    for (int j = 0; j < kPeerVecsPerThread; ++j) {
+      const int64_t i = i0 + static_cast<int64_t>(j) * blockDim.x;
+      if (i < nvec) {
+        a[j] = ks[i];
+        b[j] = vs[i];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPeerVecsPerThread; ++j) {
+      const int64_t i = i0 + static_cast<int64_t>(j) * blockDim.x;
+      if (i < nvec) {
+        kd[i] = a[j];
+        vd[i] = b[j];
+      }
+    }
+  }
+}
+
+cudaError_t launch_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride,
+                                    int dst_num_blocks, const void* src_k, const void* src_v,
+                                    int64_t src_layer_stride, int src_num_blocks, int n_layers,
+                                    const int32_t* pairs, int n_pairs, int64_t block_bytes, int* err,
+                                    cudaStream_t stream) {
+  if (n_pairs == 0 || n_layers == 0) return cudaSuccess;
+  const int64_t nvec = block_bytes >> 4;
+  // enough threads for the block's vectors, a multiple of a warp, at most 256
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, (nvec + 31) / 32 * 32)));
+  copy_blocks_peer_vec16<<<dim3(n_pairs, n_layers), threads, 0, stream>>>(
+      static_cast<char*>(dst_k), static_cast<char*>(dst_v), dst_layer_stride, dst_num_blocks,
+      static_cast<const char*>(src_k), static_cast<const char*>(src_v), src_layer_stride,
+      src_num_blocks, pairs, block_bytes, err);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride, int n_layers,

@@ -87,6 +87,11 @@ cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k
                                          int block_size, int n_kv_heads, int head_dim, int esize,
                                          int* err, cudaStream_t stream);
 
+cudaError_t launch_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride,
+                                    int dst_num_blocks, const void* src_k, const void* src_v,
+                                    int64_t src_layer_stride, int src_num_blocks, int n_layers,
+                                    const int32_t* pairs, int n_pairs, int64_t block_bytes, int* err,
+                                    cudaStream_t stream);
 cudaError_t launch_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride, int n_layers,
                                const int32_t* pairs, int n_pairs, int num_blocks,
                                int64_t block_bytes, int* err, cudaStream_t stream);

@@ -27,6 +27,9 @@ ERR_SCRATCH_LIMIT = -8
 # device-resident scratch of pkv_paged_decode_attention_noalloc
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
+# bytes of a CUDA IPC memory handle (pkv_ipc_export / pkv_ipc_open)
+IPC_HANDLE_BYTES = 64
+
 FLAG_SLOT_OUT_OF_RANGE = 1
 FLAG_BLOCK_OUT_OF_RANGE = 2
 FLAG_CONTEXT_EXCEEDS_TABLE = 4
@@ -63,6 +66,10 @@ SIGNATURES = {
                                             _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _P]),
     "pkv_paged_prefill_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _I64, _I, _P,
                                              _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
+    "pkv_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
+    "pkv_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "pkv_ipc_close": (_I, [_P]),
+    "pkv_copy_blocks_peer": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I, _P, _I, _I64, _P, _P]),
 }
 
 

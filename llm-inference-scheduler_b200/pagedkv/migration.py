@@ -1,0 +1,272 @@
+"""KV block migration between ranks over NVLink (one process per GPU).
+
+The reference answers memory pressure with recompute preemption
+(mini_engine/scheduler.py:143-156): the victim's blocks are freed and its
+prompt plus generated tokens are prefilled again when it is rescheduled.
+With sequence-sharded ranks (one pool per GPU), a rank can instead hand a
+sequence's KV to a rank that has room.  The blocks cross NVLink once, at
+copy bandwidth, instead of being recomputed.
+
+* `PeerPools(mgr)` is collective over all ranks.
+  - Each rank exports the CUDA IPC handles of its pool allocations: K and V,
+    and the scale pools of fp8 managers.
+  - Ranks on the same node map each other's pools.
+  - A gloo group carries the host-side handshakes.
+* `migrate_blocks(peers, src, dst, blocks)` is collective over the two
+  ranks.
+  - The destination allocates fresh blocks from its own allocator.
+  - One `pkv_copy_blocks_peer` launch copies every layer's K and V block, and
+    one more launch copies the scales of fp8 pools.
+    - mode "push": the source runs it, reading its own pool and writing into
+      the peer's.
+    - mode "pull" (the default): the destination runs it.  Its loads cross
+      NVLink; measured faster than the posted stores of push (752 vs 686 GB/s
+      for 201 MB between two B200s).
+  - The side that launched synchronises its stream before it signals the
+    other, so the source's blocks are never read after the source may reuse
+    them, and the destination reads complete blocks.
+* `migrate_sequence(...)` also carries the token count and returns the
+  destination's block table, ready for `PagedKVCache.add_sequence`.
+
+The copy is plain 16-byte loads and stores between the two HBMs; no TMA
+touches the peer's memory.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import socket
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .block_manager import BlockManager, OutOfBlocks, PagedKVCache
+
+
+@dataclasses.dataclass
+class PoolRef:
+    """One rank's pools as device addresses, valid in this process."""
+
+    k: int
+    v: int
+    layer_stride: int       # bytes between layers of the K (and V) pool
+    block_bytes: int        # bytes of one block of one layer
+    num_blocks: int
+    k_scale: int = 0        # fp8 pools: the scale pools
+    v_scale: int = 0
+    scale_layer_stride: int = 0
+    scale_block_bytes: int = 0
+
+
+class PeerPools:
+    """Every rank's pools mapped into this process (collective over the default
+    process group; call `close()` on every rank before the pools are freed)."""
+
+    def __init__(self, mgr: BlockManager, mode: str = "pull"):
+        if mode not in ("push", "pull"):
+            raise ValueError("mode is 'push' (the source launches the copy) or 'pull'")
+        if not dist.is_initialized():
+            raise RuntimeError("PeerPools needs torch.distributed initialised (one process per GPU)")
+        self.mgr = mgr
+        self.mode = mode
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        # host-side handshakes go through gloo whatever the default backend is
+        self.host_group = dist.new_group(backend="gloo")
+        self.meta = self._describe()
+        metas: list = [None] * self.world
+        dist.all_gather_object(metas, self._export(), group=self.host_group)
+        for r, m in enumerate(metas):
+            if (m["layout"] != metas[self.rank]["layout"]):
+                raise ValueError(f"rank {r}'s pool layout {m['layout']} differs from this rank's "
+                                 f"{metas[self.rank]['layout']}")
+        self.metas = metas
+        self.refs: dict[int, PoolRef] = {self.rank: self._local_ref()}
+        self._opened: list = []
+        for r, m in enumerate(metas):
+            if r != self.rank and m["host"] == metas[self.rank]["host"]:
+                self.refs[r] = self._open(m)
+
+    # ---- what is exchanged --------------------------------------------------
+
+    def _pools(self) -> list[torch.Tensor]:
+        m = self.mgr
+        pools = [m.k_cache, m.v_cache]
+        if m.fp8:
+            pools += [m.k_scale_cache, m.v_scale_cache]
+        return pools
+
+    def _describe(self) -> dict:
+        m = self.mgr
+        layout = (m.num_layers, m.block_size, m.num_kv_heads, m.head_dim, str(m.dtype))
+        return {"layout": layout, "num_blocks": m.num_blocks, "host": socket.gethostname()}
+
+    def _export(self) -> dict:
+        d = dict(self.meta)
+        d["handles"] = [ops.ipc_export(t) for t in self._pools()]
+        return d
+
+    def _local_ref(self) -> PoolRef:
+        return self._ref_from([t.data_ptr() for t in self._pools()], self.mgr.num_blocks)
+
+    def _ref_from(self, addrs: list[int], num_blocks: int) -> PoolRef:
+        m = self.mgr
+        ref = PoolRef(k=addrs[0], v=addrs[1], layer_stride=num_blocks * m.block_bytes,
+                      block_bytes=m.block_bytes, num_blocks=num_blocks)
+        if m.fp8:
+            sbytes = m.block_size * m.num_kv_heads * 4
+            ref.k_scale, ref.v_scale = addrs[2], addrs[3]
+            ref.scale_layer_stride, ref.scale_block_bytes = num_blocks * sbytes, sbytes
+        return ref
+
+    def _open(self, meta: dict) -> PoolRef:
+        bases: dict[bytes, int] = {}
+        addrs = []
+        for handle, offset in meta["handles"]:
+            if handle not in bases:  # one allocation may hold several pools
+                bases[handle] = ops.ipc_open(handle)
+                self._opened.append(bases[handle])
+            addrs.append(bases[handle] + offset)
+        return self._ref_from(addrs, meta["num_blocks"])
+
+    def close(self) -> None:
+        """Collective: unmap the peers' pools once every rank is done copying."""
+        dist.barrier(group=self.host_group)
+        for base in self._opened:
+            ops.ipc_close(base)
+        self._opened = []
+        self.refs = {self.rank: self.refs[self.rank]}
+        dist.barrier(group=self.host_group)
+
+    # ---- the copy (the launching rank's current device and stream) ----------
+
+    def _launch_copy(self, dst: PoolRef, src: PoolRef, pairs: list[tuple[int, int]]) -> None:
+        dev = self.mgr.device
+        t = torch.tensor(pairs, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        L = self.mgr.num_layers
+        ops.copy_blocks_peer(dst.k, dst.v, dst.layer_stride, dst.num_blocks, src.k, src.v,
+                             src.layer_stride, src.num_blocks, L, t, dst.block_bytes, self.mgr.err)
+        if self.mgr.fp8:  # the rows' scales travel with their bytes
+            ops.copy_blocks_peer(dst.k_scale, dst.v_scale, dst.scale_layer_stride, dst.num_blocks,
+                                 src.k_scale, src.v_scale, src.scale_layer_stride, src.num_blocks,
+                                 L, t, dst.scale_block_bytes, self.mgr.err)
+        self._sync()
+        self.mgr.check_errors()
+
+    def _sync(self) -> None:
+        torch.cuda.current_stream(self.mgr.device).synchronize()
+
+    # ---- host messages -------------------------------------------------------
+
+    def _send(self, values: list[int], peer: int) -> None:
+        dist.send(torch.tensor(values, dtype=torch.int64), dst=peer, group=self.host_group)
+
+    def _recv(self, n: int, peer: int) -> list[int]:
+        t = torch.empty(n, dtype=torch.int64)
+        dist.recv(t, src=peer, group=self.host_group)
+        return t.tolist()
+
+
+def migrate_blocks(peers: PeerPools, src: int, dst: int, blocks: list[int] | None = None) -> list[int]:
+    """Copy blocks `blocks` of rank src's pool (all layers, K and V, fp8
+    scales) into freshly allocated blocks of rank dst's pool.
+
+    Collective over ranks src and dst only; `blocks` is read on src.  Returns
+    the destination block ids on both ranks (on dst they are allocated, with
+    ref count 1).  Raises OutOfBlocks on both ranks if dst cannot allocate
+    them all (nothing stays allocated then), and RuntimeError on both ranks
+    if the copy failed (the destination frees the blocks).
+
+    Messages (int64, gloo): src -> dst [n] and the n source ids; dst -> src
+    [status] and the n destination ids; then the launching side reports the
+    copy's status to the other once its stream has synchronised (pull: after
+    src reported that its blocks are complete).
+    """
+    me = peers.rank
+    if src == dst or me not in (src, dst):
+        raise ValueError("migrate_blocks is called by the source and the destination rank")
+    peer = dst if me == src else src
+    if peer not in peers.refs:
+        raise RuntimeError(f"rank {peer}'s pools are not mapped here (another node?)")
+    mgr = peers.mgr
+    push = peers.mode == "push"
+    if me == src:
+        blocks = [int(b) for b in (blocks or [])]
+        n = len(blocks)
+        peers._send([n], dst)
+        if n == 0:
+            return []
+        peers._send(blocks, dst)
+        reply = peers._recv(n + 1, dst)
+        if reply[0] != 0:
+            raise OutOfBlocks()
+        ids = reply[1:]
+        mgr.flush_copies()  # queued COW copies may write the source blocks
+        if push:
+            status = 1
+            try:
+                peers._launch_copy(peers.refs[dst], peers.refs[src], list(zip(blocks, ids)))
+                status = 0
+            finally:
+                peers._send([status], dst)
+        else:
+            peers._sync()  # the source's blocks are complete
+            peers._send([0], dst)
+            if peers._recv(1, dst)[0] != 0:
+                raise RuntimeError("migrate_blocks: the destination's copy failed")
+        return ids
+    # destination
+    n = peers._recv(1, src)[0]
+    if n == 0:
+        return []
+    blocks_src = peers._recv(n, src)
+    ids: list[int] = []
+    try:
+        for _ in range(n):
+            ids.append(mgr.allocate())
+    except OutOfBlocks:
+        for b in ids:
+            mgr.decref(b)
+        peers._send([1] + [0] * n, src)
+        raise
+    peers._send([0] + ids, src)
+    if push:
+        ok = peers._recv(1, src)[0] == 0
+    else:
+        peers._recv(1, src)  # the source's blocks are complete
+        ok = False
+        try:
+            peers._launch_copy(peers.refs[dst], peers.refs[src], list(zip(blocks_src, ids)))
+            ok = True
+        finally:
+            peers._send([0 if ok else 1], src)
+    if not ok:
+        for b in ids:
+            mgr.decref(b)
+        raise RuntimeError("migrate_blocks: the source's copy failed")
+    return ids
+
+
+def migrate_sequence(peers: PeerPools, cache: PagedKVCache, seq_id: int, src: int,
+                     dst: int) -> tuple[int, list[int]]:
+    """Move sequence seq_id's KV from rank src to rank dst.
+
+    Collective over ranks src and dst.  The blocks holding its cached tokens
+    (ceil(len / block_size) of its table) are copied with migrate_blocks; on
+    dst the sequence is registered in `cache` with the new table and the same
+    token count.  Returns (num_tokens, dst_table) on both ranks.  The source
+    keeps its own table and blocks: it releases them as its scheduler
+    releases a preempted sequence's (decref each block, free_sequence)."""
+    me = peers.rank
+    bs = peers.mgr.block_size
+    if me == src:
+        length = cache.seq_len(seq_id)
+        table = cache.block_tables[seq_id][: -(-length // bs)]
+        peers._send([length], dst)
+        ids = migrate_blocks(peers, src, dst, table)
+    else:
+        length = peers._recv(1, src)[0]
+        ids = migrate_blocks(peers, src, dst)
+        cache.add_sequence(seq_id, list(ids), length)
+    return length, list(ids)

@@ -9,6 +9,8 @@ pagedkv._lib.FLAG_*), which callers check with `check_flags` after a sync.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -106,6 +108,51 @@ def copy_blocks(k_cache: torch.Tensor, v_cache: torch.Tensor, pairs: torch.Tenso
         k_cache.data_ptr(), v_cache.data_ptr(), nb * block_bytes, L, pairs.data_ptr(),
         pairs.shape[0], nb, block_bytes, _ptr(err), _stream(k_cache))
     _lib.check(rc, "pkv_copy_blocks")
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """CUDA IPC handle of the device allocation that holds t's data, and the
+    byte offset of t.data_ptr() in it (pkv_ipc_export)."""
+    _cuda(t, "tensor")
+    h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    off = ctypes.c_uint64(0)
+    _lib.check(_lib.load().pkv_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "pkv_ipc_export")
+    return h.raw, int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map an allocation exported by another process; returns its base address
+    on the current device (pkv_ipc_open).  Open each allocation once."""
+    if len(handle) != _lib.IPC_HANDLE_BYTES:
+        raise ValueError(f"pagedkv: an IPC handle has {_lib.IPC_HANDLE_BYTES} bytes")
+    base = ctypes.c_void_p(0)
+    _lib.check(_lib.load().pkv_ipc_open(handle, ctypes.byref(base)), "pkv_ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    _lib.check(_lib.load().pkv_ipc_close(base), "pkv_ipc_close")
+
+
+def copy_blocks_peer(dst_k: int, dst_v: int, dst_layer_stride: int, dst_num_blocks: int,
+                     src_k: int, src_v: int, src_layer_stride: int, src_num_blocks: int,
+                     n_layers: int, pairs: torch.Tensor, block_bytes: int,
+                     err: torch.Tensor | None = None) -> None:
+    """For every (src, dst) row of `pairs` (int32 [N, 2] on the current device)
+    and every layer, block dst of the destination K / V pools becomes a copy of
+    block src of the source pools (pkv_copy_blocks_peer).  Pools are given by
+    device addresses, so either side may be a peer GPU's pool mapped with
+    ipc_open; the kernel runs on the current device's current stream."""
+    _cuda(pairs, "pairs")
+    if pairs.dtype != torch.int32 or not pairs.is_contiguous() or pairs.dim() != 2 or pairs.shape[1] != 2:
+        raise TypeError("pagedkv: pairs must be a contiguous int32 [N, 2] tensor")
+    if pairs.shape[0] == 0:
+        return
+    rc = _lib.load().pkv_copy_blocks_peer(
+        dst_k, dst_v, dst_layer_stride, dst_num_blocks, src_k, src_v, src_layer_stride,
+        src_num_blocks, n_layers, pairs.data_ptr(), pairs.shape[0], block_bytes, _ptr(err),
+        _stream(pairs))
+    _lib.check(rc, "pkv_copy_blocks_peer")
 
 
 def decode_workspace_bytes(n_seqs: int, n_q_heads: int, head_dim: int) -> int:

@@ -79,6 +79,41 @@ def test_copy_blocks_validation():
     assert f(FAKE, FAKE, 8 * 4096, 70000, FAKE, 3, 8, 4096, None, None) == _lib.ERR_UNSUPPORTED
 
 
+def test_copy_blocks_peer_validation():
+    f = _lib.load().pkv_copy_blocks_peer
+    A = ctypes.c_void_p(0x10000)  # 16-byte aligned, never dereferenced
+    ok = dict(dk=A, dv=A, dls=8 * 4096, dnb=8, sk=A, sv=A, sls=8 * 4096, snb=8, L=24, pairs=A,
+              n=3, bb=4096, err=None, stream=None)
+
+    def call(**kw):
+        a = dict(ok)
+        a.update(kw)
+        return f(*a.values())
+
+    assert call(n=0) == 0 and call(L=0) == 0
+    assert call(sv=None) == _lib.ERR_NULL_POINTER
+    assert call(pairs=None) == _lib.ERR_NULL_POINTER
+    assert call(n=-1) == _lib.ERR_BAD_SHAPE
+    assert call(dnb=0) == _lib.ERR_BAD_SHAPE
+    assert call(sls=100) == _lib.ERR_BAD_SHAPE        # layers overlap
+    assert call(L=70000) == _lib.ERR_UNSUPPORTED
+    assert call(bb=4100, dls=8 * 4100, sls=8 * 4100) == _lib.ERR_MISALIGNED
+    assert call(dk=ctypes.c_void_p(0x10008)) == _lib.ERR_MISALIGNED
+
+
+def test_ipc_validation():
+    L = _lib.load()
+    off = ctypes.c_uint64(0)
+    h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    base = ctypes.c_void_p(0)
+    assert L.pkv_ipc_export(None, h, ctypes.byref(off)) == _lib.ERR_NULL_POINTER
+    assert L.pkv_ipc_export(FAKE, None, ctypes.byref(off)) == _lib.ERR_NULL_POINTER
+    assert L.pkv_ipc_open(None, ctypes.byref(base)) == _lib.ERR_NULL_POINTER
+    assert L.pkv_ipc_open(h, None) == _lib.ERR_NULL_POINTER
+    assert L.pkv_ipc_close(None) == _lib.ERR_NULL_POINTER
+    assert header_defines()["PKV_IPC_HANDLE_BYTES"] == _lib.IPC_HANDLE_BYTES
+
+
 def _decode(**kw):
     a = dict(out=FAKE, out_stride=896, q=FAKE, q_stride=896, k_pool=FAKE, v_pool=FAKE,
              num_blocks=64, tables=FAKE, bt_stride=8, max_blocks=8, ctx=FAKE, n_seqs=4, hq=14,
