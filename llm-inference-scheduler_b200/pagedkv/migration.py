@@ -231,20 +231,21 @@ def migrate_blocks(peers: PeerPools, src: int, dst: int, blocks: list[int] | Non
         peers._send([1] + [0] * n, src)
         raise
     peers._send([0] + ids, src)
+    failure: Exception | None = None
     if push:
-        ok = peers._recv(1, src)[0] == 0
+        if peers._recv(1, src)[0] != 0:
+            failure = RuntimeError("migrate_blocks: the source's copy failed")
     else:
         peers._recv(1, src)  # the source's blocks are complete
-        ok = False
         try:
             peers._launch_copy(peers.refs[dst], peers.refs[src], list(zip(blocks_src, ids)))
-            ok = True
-        finally:
-            peers._send([0 if ok else 1], src)
-    if not ok:
+        except Exception as e:  # reported to the source, then re-raised here
+            failure = e
+        peers._send([0 if failure is None else 1], src)
+    if failure is not None:
         for b in ids:
             mgr.decref(b)
-        raise RuntimeError("migrate_blocks: the source's copy failed")
+        raise failure
     return ids
 
 

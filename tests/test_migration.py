@@ -112,15 +112,19 @@ def _cpu_rank(rank, world, port, pools, out_dir):
         except OutOfBlocks:
             res["oob"] = np.array(1)
         res["free_kept"] = np.array(int(mgr.num_free == free_before))
-        # a failed copy on the launching side (push: the source)
+        # a failed copy on the launching side (push: the source; pull: the
+        # destination): both ranks raise, the destination keeps nothing
         Fake.fail_copy = True
-        free_before = mgr.num_free
-        try:
-            migrate_blocks(peers, 0, 1, [3] if rank == 0 else None)
-            res["fail"] = np.array(0)
-        except RuntimeError:
-            res["fail"] = np.array(1)
-        res["fail_freed"] = np.array(int(mgr.num_free == free_before))
+        for mode in ("push", "pull"):
+            fpeers = Fake(mgr, mode=mode)
+            free_before = mgr.num_free
+            try:
+                migrate_blocks(fpeers, 0, 1, [3] if rank == 0 else None)
+                res[f"fail_{mode}"] = np.array(0)
+            except RuntimeError:
+                res[f"fail_{mode}"] = np.array(1)
+            res[f"fail_freed_{mode}"] = np.array(int(mgr.num_free == free_before))
+            fpeers.close()
         Fake.fail_copy = False
         # a whole sequence: 37 tokens in a 4-block table -> 3 blocks move
         cache = PagedKVCache(mgr)
@@ -161,7 +165,9 @@ def test_migration_protocol_two_gloo_ranks(tmp_path):
             for a, b in zip(before[1], pools[1]):
                 assert torch.equal(a[:, d], b[:, d]), d
     assert r0["oob"] == 1 and r1["oob"] == 1 and r1["free_kept"] == 1
-    assert r0["fail"] == 1 and r1["fail"] == 1 and r1["fail_freed"] == 1
+    for mode in ("push", "pull"):
+        assert r0[f"fail_{mode}"] == 1 and r1[f"fail_{mode}"] == 1, mode
+        assert r1[f"fail_freed_{mode}"] == 1, mode
     assert r0["seq_len"] == r1["seq_len"] == 37
     assert len(r1["seq_table"]) == 3 and r0["seq_table"].tolist() == r1["seq_table"].tolist()
     assert r1["seq_registered"].tolist() == [37, 1]
