@@ -17,7 +17,13 @@
 //    the 16 tokens of a block as M and the G <= 8 query heads of the GQA
 //    group as N: S^T = K Q^T, then O^T += V^T P^T with P^T transposed in
 //    registers (movmatrix).  All 7 Qwen2 query heads of a group consume each
-//    K/V tile from one shared-memory read.  Online softmax in fp32 (exp2).
+//    K/V tile from one shared-memory read.  Online softmax in fp32 (exp2)
+//    with a lazy rescale: the reference max of a head moves only when a
+//    block's max exceeds it by more than 2^8 (a warp vote), so most blocks
+//    skip the O / l rescale; masks apply only to a sequence's last block.
+//  * The ring is only 3 stages deep: with 3 stages, 5 CTAs per SM stay
+//    resident (the register limit), and that measured faster than deeper
+//    rings with fewer CTAs.  Two stages starve.
 //  * Sequences fully inside one CTA's range are normalised and stored
 //    directly.  A sequence split across CTAs leaves (m, l, O) partials in the
 //    workspace, merged by a second small kernel (one CTA per sequence) that
@@ -27,7 +33,11 @@
 //    per-(token, KV head) fp32 scales (TMA + two bulk copies).  Each lane
 //    loads the fp8 bytes of its own MMA fragments straight into registers
 //    (K: 2 x 16 bytes, V: 4 x 8 bytes, bank-conflict free), releases the
-//    stage, and converts them there (cvt e4m3x2 -> f16x2; exact).  That works
+//    stage, and converts them there, exactly: K by cvt e4m3x2 -> f16x2 (the
+//    transcendental pipe), V (fp16 build) by moving the e4m3 fields into f16
+//    position on the integer pipes, which yields 2^-8 x the value (the 2^8 is
+//    applied to O at the segment end).  Splitting the work between the two
+//    pipes measured fastest of the four combinations.  That works
 //    because the head dimension may be permuted: S sums over it, so K and Q
 //    use the order in which lane t's four k-steps read 16 contiguous bytes,
 //    and O's rows use the order in which lane g owns 8 contiguous dims (the
@@ -113,10 +123,11 @@ template <> __device__ __forceinline__ uint32_t fp8x2_to<__nv_bfloat16>(uint32_t
 }
 // fp8 -> f16 on the integer pipes (the fp16 instantiation): the e4m3 fields
 // moved into f16 position, which is the value times 2^-8 (exact, e4m3
-// subnormals included: they land on f16 subnormals).  The 2^8 is folded into
-// the K and V scales.  The NaN encodings 0x7f / 0xff map to +-480; the
-// quantising append never stores them.  Keeps the conversions off the
-// transcendental pipe, which the softmax's exp2 also needs.
+// subnormals included: they land on f16 subnormals).  The 2^8 goes into the
+// score scale (K) or into O at the segment end (V).  The NaN encodings
+// 0x7f / 0xff map to +-480; the quantising append never stores them.  Takes
+// conversions off the transcendental pipe, which cvt and the softmax's exp2
+// share.
 #ifndef PKV_FP8_ALU_CVT
 #define PKV_FP8_ALU_CVT 2  // bit 0: K tiles, bit 1: V tiles (K by cvt measured faster)
 #endif
