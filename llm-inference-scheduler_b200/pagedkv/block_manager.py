@@ -347,13 +347,16 @@ class PagedKVCache:
 
     # ---- batched hot path ---------------------------------------------------
 
-    def step_arrays(self, seqs: list[tuple[int, int]]) -> dict:
+    def step_arrays(self, seqs: list[tuple[int, int]], out=None) -> dict:
         """Host half of prepare_step (no device work): numpy arrays of the step.
 
         Returns dict(ints=int32 [B*W + 2B + n_prefill + 1] = block tables (B x W;
         row s holds the sequence's first ceil(len/16) blocks, the entries after
         them are unspecified) | context lens | num_prior | prefill query_start_loc,
-        slots=int64 [T], plus the scalar fields of StepMetadata).
+        slots=int64 [T], plus the scalar fields of StepMetadata).  With
+        out(n_ints, n_slots) -> (int32 array, int64 array), the two arrays are
+        written into the buffers it returns (prepare_step: its pinned staging
+        buffer) instead of fresh ones.
         """
         bs = self.mgr.block_size
         B = len(seqs)
@@ -388,18 +391,22 @@ class PagedKVCache:
         n_dec = B if ones.all() else int(np.argmin(ones))
         pre_new = num_new[n_dec:]
         n_pre = B - n_dec
-        ints = np.zeros(B * W + 2 * B + n_pre + 1, dtype=np.int32)
+        T = int(num_new.sum())
+        n_ints = B * W + 2 * B + n_pre + 1
+        if out is None:
+            ints, slots = np.empty(n_ints, dtype=np.int32), np.empty(T, dtype=np.int64)
+        else:
+            ints, slots = out(n_ints, T)
         tabs = ints[: B * W].reshape(B, W)
         mirror._fit(1, W)
         # entries past a sequence's used blocks are left as the mirror holds
         # them (allocated-ahead block ids or zeros): no kernel reads them
-        tabs[:] = mirror.buf[rows, :W]
+        np.take(mirror.buf[:, :W], rows, axis=0, out=tabs)
         ints[B * W: B * W + B] = totals
         ints[B * W + B: B * W + 2 * B] = num_prior
+        ints[B * W + 2 * B] = 0
         if n_pre:
             ints[B * W + 2 * B + 1:] = np.cumsum(pre_new)
-        T = int(num_new.sum())
-        slots = np.empty(T, dtype=np.int64)
         # decode sequences: one slot each, gathered in one step
         pos = num_prior[:n_dec]
         slots[:n_dec] = mirror.buf[rows[:n_dec], pos // bs].astype(np.int64) * bs + pos % bs
@@ -433,18 +440,25 @@ class PagedKVCache:
         staging buffer.  seqs = [(seq_id, num_new)] in flat-batch order.
         Flushes queued COW copies."""
         self.mgr.flush_copies()
-        a = self.step_arrays(seqs)
-        B, W = a["B"], a["W"]
         dev = self.mgr.device
+        staged = []
+
+        def into_staging(n_ints: int, n_slots: int):
+            # int32 arrays first, then the int64 slots 16-byte aligned
+            off = (4 * n_ints + 15) // 16 * 16
+            i, stage = self._staging(off + 8 * n_slots)
+            host = stage.numpy()
+            staged.append((i, stage, off, off + 8 * n_slots))
+            return host[: 4 * n_ints].view(np.int32), host[off: off + 8 * n_slots].view(np.int64)
+
+        a = self.step_arrays(seqs, out=into_staging if dev.type == "cuda" else None)
+        B, W = a["B"], a["W"]
         ints, slots = a["ints"], a["slots"]
         n_int = ints.nbytes
         off = (n_int + 15) // 16 * 16  # the slots start 16-byte aligned
         nbytes = off + slots.nbytes
         if dev.type == "cuda":
-            i, stage = self._staging(nbytes)
-            host = stage.numpy()
-            host[:n_int] = ints.view(np.uint8)
-            host[off:nbytes] = slots.view(np.uint8)
+            i, stage, _, _ = staged[0]
             dbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             dbuf.copy_(stage[:nbytes], non_blocking=True)
             ev = torch.cuda.Event()
@@ -478,12 +492,20 @@ class PagedKVCache:
         (block_manager.py:133-134 semantics); advance=False replays a step
         without moving the lengths (benchmarks re-running one step)."""
         mgr = self.mgr
-        mgr.flush_copies()
+        if mgr._pending:
+            mgr.flush_copies()
         if out is None:
             out = torch.empty((meta.n_tokens,) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
         if mgr.fp8:
             return self._forward_layer_fp8(layer, q, k_new, v_new, meta, scale, out, advance)
         nd = meta.n_decode
+        plan = meta.decode_plan
+        if nd == meta.n_tokens and plan is not None and plan.scale == scale:
+            # a decode-only step after its first layer: one launch, no slicing
+            plan(q, k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer], out)
+            if advance and layer == mgr.num_layers - 1:
+                self._advance(meta)
+            return out
         if nd:
             # decode sequences: append fused into the decode kernel; the
             # step's plan validates once and then only swaps layer pointers
@@ -504,9 +526,14 @@ class PagedKVCache:
                                         meta.num_prior_dev[nd:], meta.max_query_len, scale,
                                         out=out[nd:], err=mgr.err)
         if advance and layer == mgr.num_layers - 1:
-            for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
-                self._len[s] = p + n
+            self._advance(meta)
         return out
+
+    def _advance(self, meta: StepMetadata):
+        """After the last layer: the step's tokens count as cached
+        (block_manager.py:133-134 semantics)."""
+        for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
+            self._len[s] = p + n
 
     def _forward_layer_fp8(self, layer, q, k_new, v_new, meta, scale, out, advance):
         """forward_layer over fp8 pools: the quantising append of every token,
@@ -527,8 +554,7 @@ class PagedKVCache:
                                             meta.num_prior_dev[nd:], meta.max_query_len, scale,
                                             out=out[nd:], err=mgr.err)
         if advance and layer == mgr.num_layers - 1:
-            for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
-                self._len[s] = p + n
+            self._advance(meta)
         return out
 
     def forward_layer_qkv(self, layer: int, qkv: torch.Tensor, positions: torch.Tensor,
@@ -565,6 +591,5 @@ class PagedKVCache:
                                         meta.num_prior_dev[nd:], meta.max_query_len, scale,
                                         out=out[nd:], err=mgr.err)
         if advance and layer == mgr.num_layers - 1:
-            for s, p, n in zip(meta.seq_ids, meta.num_prior, meta.num_new):
-                self._len[s] = p + n
+            self._advance(meta)
         return out

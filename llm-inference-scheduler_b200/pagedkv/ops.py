@@ -35,6 +35,11 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _raw_stream(t: torch.Tensor) -> int:
+    """The current stream of t's device as a handle (cheaper than _stream)."""
+    return torch._C._cuda_getCurrentRawStream(t.get_device())
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -410,11 +415,12 @@ class DecodeAppendPlan:
         self._fn = _lib.load().pkv_paged_decode_append_attention
 
     def __call__(self, q, k_new, v_new, k_pool, v_pool, out) -> torch.Tensor:
+        # everything the validated arguments depend on besides the six pointers
         key = (q.dtype, k_new.dtype, v_new.dtype, k_pool.dtype, v_pool.dtype, out.dtype,
                q.shape, q.stride(), k_new.shape, k_new.stride(), v_new.shape, v_new.stride(),
-               k_pool.shape, v_pool.shape, out.shape, out.stride(), q.device,
-               torch.cuda.current_stream(q.device).cuda_stream)
-        if key != self._key or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+               k_pool.shape, k_pool.stride(), v_pool.shape, v_pool.stride(), out.shape, out.stride(),
+               q.get_device(), _raw_stream(q))
+        if key != self._key:
             tables, ctx, scale, ws, err = self._static
             args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, tables, ctx, scale, ws,
                                             out, err)
@@ -440,9 +446,9 @@ class DecodePlan(DecodeAppendPlan):
 
     def __call__(self, q, k_pool, v_pool, out) -> torch.Tensor:
         key = (q.dtype, k_pool.dtype, v_pool.dtype, out.dtype, q.shape, q.stride(), k_pool.shape,
-               v_pool.shape, out.shape, out.stride(), q.device,
-               torch.cuda.current_stream(q.device).cuda_stream)
-        if key != self._key or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+               k_pool.stride(), v_pool.shape, v_pool.stride(), out.shape, out.stride(),
+               q.get_device(), _raw_stream(q))
+        if key != self._key:
             tables, ctx, scale, ws, err = self._static
             args, out = _decode_args(q, k_pool, v_pool, tables, ctx, scale, ws, out, err)
             self._args, self._key = list(args), key
