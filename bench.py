@@ -64,10 +64,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
     ap.add_argument("--strong", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--e2e-packed", action="store_true",
-                    help="e2e: q, k, v of a layer staged as one [B, 18, 64] block (one copy per chunk)")
-    ap.add_argument("--e2e-chunks", type=int, default=4,
-                    help="e2e: layer chunks whose copies overlap the step's compute")
+    ap.add_argument("--e2e-chunks", default="2,4,6,6,4,2",
+                    help="e2e: layers per chunk (comma list summing to --layers); each chunk's copies "
+                         "overlap the other chunks' compute")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0,
@@ -347,34 +346,32 @@ def run_ours(args):
     kv = PagedKVCache(mgr)
     for i in range(B):
         kv.add_sequence(i, tabs_np[i, :nblk[i]].tolist(), int(ctx[i]) - 1)
-    if args.e2e_packed:
-        # one pinned [L, B, 18, 64] buffer: a layer's q, k, v are views of its rows
-        hqkv = torch.empty((L, B, 18, 64), dtype=dt).pin_memory()
-        hqkv[:, :, :14].copy_(q)
-        hqkv[:, :, 14:16].copy_(kn)
-        hqkv[:, :, 16:18].copy_(vn)
-        dqkv = torch.empty((L, B, 18, 64), device=dev, dtype=dt)
-        hs, ds = [hqkv], [dqkv]
-        dq, dk, dv = dqkv[:, :, :14], dqkv[:, :, 14:16], dqkv[:, :, 16:18]
-    else:
-        hq = torch.empty_like(q, device="cpu").pin_memory()
-        hk = torch.empty_like(kn, device="cpu").pin_memory()
-        hv = torch.empty_like(vn, device="cpu").pin_memory()
-        hq.copy_(q)
-        hk.copy_(kn)
-        hv.copy_(vn)
-        dq, dk, dv = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
-        hs, ds = [hq, hk, hv], [dq, dk, dv]
+    # the step's inputs in one pinned staging buffer, [L, B, 18, 64]: a
+    # layer's q, k and v are views of its rows (one copy per chunk)
+    hqkv = torch.empty((L, B, 18, 64), dtype=dt).pin_memory()
+    hqkv[:, :, :14].copy_(q)
+    hqkv[:, :, 14:16].copy_(kn)
+    hqkv[:, :, 16:18].copy_(vn)
+    dqkv = torch.empty((L, B, 18, 64), device=dev, dtype=dt)
+    lq = [dqkv[l, :, :14] for l in range(L)]
+    lk = [dqkv[l, :, 14:16] for l in range(L)]
+    lv = [dqkv[l, :, 16:18] for l in range(L)]
+    lo = [out[l] for l in range(L)]
     hout = torch.empty_like(out, device="cpu").pin_memory()
 
     # Each step is self-contained: its inputs go host -> device in chunks of
     # layers on a copy stream, each chunk's layers run as soon as it has
     # landed, and each chunk's outputs go back on a second copy stream; the
     # step ends when its last output is on the host.  The next step's copies
-    # start after this step's compute (no prefetch across steps).
+    # start after this step's compute (no prefetch across steps).  Small
+    # first and last chunks shorten the pipeline's fill (first copy in) and
+    # drain (last copy out).
+    sizes = [int(x) for x in args.e2e_chunks.split(",")]
+    if sum(sizes) != L:
+        sizes = [L]
+    bounds = [sum(sizes[:i]) for i in range(len(sizes) + 1)]
+    n_chunks = len(sizes)
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    n_chunks = args.e2e_chunks if L % args.e2e_chunks == 0 else 1
-    per = L // n_chunks
     ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
     ev_out = [torch.cuda.Event() for _ in range(n_chunks)]
     seqs_all = [(i, 1) for i in range(B)]
@@ -385,19 +382,18 @@ def run_ours(args):
         h2d_s.wait_stream(cur)
         with torch.cuda.stream(h2d_s):
             for c in range(n_chunks):
-                sl = slice(c * per, (c + 1) * per)
-                for d_, h_ in zip(ds, hs):
-                    d_[sl].copy_(h_[sl], non_blocking=True)
+                sl = slice(bounds[c], bounds[c + 1])
+                dqkv[sl].copy_(hqkv[sl], non_blocking=True)
                 ev_in[c].record(h2d_s)
         for c in range(n_chunks):
             cur.wait_event(ev_in[c])
-            for layer in range(c * per, (c + 1) * per):
-                kv.forward_layer(layer, dq[layer], dk[layer], dv[layer], meta, scale, out=out[layer],
+            for layer in range(bounds[c], bounds[c + 1]):
+                kv.forward_layer(layer, lq[layer], lk[layer], lv[layer], meta, scale, out=lo[layer],
                                  advance=False)
             ev_out[c].record(cur)
             d2h_s.wait_event(ev_out[c])
             with torch.cuda.stream(d2h_s):
-                sl = slice(c * per, (c + 1) * per)
+                sl = slice(bounds[c], bounds[c + 1])
                 hout[sl].copy_(out[sl], non_blocking=True)
         cur.wait_stream(d2h_s)
 
@@ -414,7 +410,7 @@ def run_ours(args):
     barrier()
     ops.check_flags(err, "bench e2e")
     e2e_ms = W.max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
-    h2d = sum(h_.numel() for h_ in hs) * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
+    h2d = hqkv.numel() * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
     d2h = hout.numel() * 2
 
     if world > 1:
@@ -454,10 +450,10 @@ def run_ours(args):
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4), "api": "PagedKVCache.prepare_step + forward_layer",
-                "copies": f"pinned host buffers; per step: metadata + q/k/v of 24 layers H2D in {n_chunks} "
-                          "chunks on a copy stream, outputs D2H per chunk on a second copy stream, "
-                          "overlapped with the step's own compute; the step ends when its outputs are on "
-                          "the host"},
+                "copies": f"pinned host buffers; per step: metadata, then q|k|v of 24 layers H2D in "
+                          f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
+                          "on a second copy stream, overlapped with the step's own compute; the step ends "
+                          "when its outputs are on the host"},
         "gpu_launches": 2 * L * args.steps,  # decode kernel + split-K merge per layer
         "clocks": clocks,
     }
