@@ -66,6 +66,10 @@ namespace pkv {
 #ifndef PKV_DEC_MIN_CTAS
 #define PKV_DEC_MIN_CTAS 3
 #endif
+// K/V tiles loaded with an L2 evict-first policy (read exactly once)
+#ifndef PKV_DEC_EVICT_FIRST
+#define PKV_DEC_EVICT_FIRST 1
+#endif
 // blocks of each CTA's range prefetched into L2 before griddepcontrol.wait
 #ifndef PKV_DEC_PREFETCH
 #define PKV_DEC_PREFETCH 3
@@ -312,6 +316,9 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       prefetch_tensormap(&vmap);
     }
     bool dead = false, waited = false;
+#if PKV_DEC_EVICT_FIRST
+    const uint64_t kv_policy = l2_evict_first_policy();
+#endif
     int i = 0;
     for (int b0 = r0; b0 < r1; b0 += 32) {
       const int gb = b0 + lane;
@@ -370,8 +377,14 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
             mbar_arrive_expect_tx(&full_bar[st], stage_bytes);
 #pragma unroll
             for (int hk = 0; hk < nkv; ++hk) {
+#if PKV_DEC_EVICT_FIRST
+              tma_load_3d_hint(stg + hk * tile_bytes, &kmap, &full_bar[st], 0, hk, blk * 16, kv_policy);
+              tma_load_3d_hint(stg + (nkv + hk) * tile_bytes, &vmap, &full_bar[st], 0, hk, blk * 16,
+                               kv_policy);
+#else
               tma_load_3d(stg + hk * tile_bytes, &kmap, &full_bar[st], 0, hk, blk * 16);
               tma_load_3d(stg + (nkv + hk) * tile_bytes, &vmap, &full_bar[st], 0, hk, blk * 16);
+#endif
             }
             if constexpr (FP8) {
               bulk_load(stg + 2 * nkv * tile_bytes, p.k_scale + static_cast<int64_t>(blk) * 16 * nkv,
@@ -712,6 +725,8 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
   const int per = max((total + decode_grid - 1) / decode_grid, kDecMinBlocksPerCta);
 
   pdl_wait();  // the decode grid's partials and outputs are complete and visible
+  // (triggering before the wait, so that the next layer's CTAs start in SMs
+  // the decode grid's tail frees, measured 2% slower)
   if (tid == 0) pdl_trigger();
   const int Hq = p.n_q_heads;
   T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
