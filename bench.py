@@ -277,9 +277,13 @@ def run_ours(args):
     ws = ops.new_decode_workspace(B, 14, 64, dev)
     err = ops.new_error_flags(dev)
 
-    # one call per layer: the decode kernel appends the new token itself
+    # per step: the decode schedule (once), then one call per layer, in which
+    # the decode kernel appends the new token itself
+    sched = ops.new_decode_schedule(B, tabs.shape[1], dev)
+    build_sched = ops.bind_decode_schedule(sched, tabs, ctx_d, nb, 14, 2, 64, dt, err=err)
     decodes = [ops.bind_paged_decode_append_attention(q[l], kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
-                                                      tabs, ctx_d, scale, ws, out[l], err)
+                                                      tabs, ctx_d, scale, ws, out[l], err,
+                                                      schedule=sched)
                for l in range(L)]
 
     dec_bytes = W.decode_bytes(ctx)
@@ -289,6 +293,7 @@ def run_ours(args):
     def step(ev=None):
         # ev brackets the whole layer loop: per-call events would break the
         # programmatic-dependent-launch overlap of consecutive calls
+        build_sched()
         if ev is not None:
             ev[0].record()
         for layer in range(L):
@@ -454,7 +459,7 @@ def run_ours(args):
                           f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
                           "on a second copy stream, overlapped with the step's own compute; the step ends "
                           "when its outputs are on the host"},
-        "gpu_launches": 2 * L * args.steps,  # decode kernel + split-K merge per layer
+        "gpu_launches": (2 * L + 1) * args.steps,  # schedule + (decode kernel + merge) per layer
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:
@@ -734,13 +739,14 @@ def run_decode_fp8(args):
     tabs = torch.from_numpy(tabs_np).to(dev)
     ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     ws = ops.new_decode_workspace(B, 14, 64, dev)
-    launches = []
+    sched = ops.new_decode_schedule(B, tabs.shape[1], dev)
+    launches = [ops.bind_decode_schedule(sched, tabs, ctx_d, nb, 14, 2, 64, dt, fp8=True, err=err)]
     for l in range(L):
         launches.append(ops.bind_reshape_and_cache_fp8(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
                                                        mgr.k_scale[l], mgr.v_scale[l], slots, err))
         launches.append(ops.bind_paged_decode_attention_fp8(q[l], mgr.k_pool[l], mgr.v_pool[l],
                                                             mgr.k_scale[l], mgr.v_scale[l], tabs, ctx_d,
-                                                            scale, ws, out[l], err))
+                                                            scale, ws, out[l], err, schedule=sched))
     tot = int(ctx.sum())
     dec_bytes = (tot * 2 * 64 * 2 + tot * 2 * 2 * 4 + B * 14 * 64 * 2 * 2 + int(nblk.sum()) * 4 + B * 4)
     app_bytes = B * (2 * 2 * 64 * 2 + 2 * 2 * 64 + 2 * 2 * 4 + 8)

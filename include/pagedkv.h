@@ -57,6 +57,7 @@ extern "C" {
 #define PKV_FLAG_PIPELINE_TIMEOUT 8
 #define PKV_FLAG_BAD_QUERY_LAYOUT 16
 #define PKV_FLAG_POSITION_OUT_OF_RANGE 32
+#define PKV_FLAG_BAD_SCHEDULE 64 /* a decode schedule built for another batch or grid */
 
 /* size of the device-resident scratch array behind
  * pkv_paged_decode_attention_noalloc (per GPU, held until the process exits) */
@@ -103,6 +104,55 @@ int pkv_reshape_and_cache(const void* k, const void* v, int64_t k_row_stride,
 int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,
                     const int32_t* block_pairs, int n_pairs, int num_blocks,
                     int64_t block_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
+ * Per-step decode schedule.  All layers of a decode step share the block
+ * tables and context lengths, so the stream-K partition of the step's blocks
+ * over the decode kernel's persistent CTAs is the same for every layer.
+ * pkv_decode_schedule computes it once per step (one small kernel: clamped
+ * lengths, block prefix, each CTA's block ids, with the bounds checks and
+ * their error flags), and the _scheduled decode calls read it instead of
+ * recomputing it in every layer's prologue.  The schedule buffer is
+ * caller-provided (pkv_decode_schedule_bytes, 16-byte aligned); n_q_heads,
+ * n_kv_heads, head_dim, block_size, dtype and fp8_pools (1 for the fp8
+ * decode) must be those of the decode calls that use it, and block_tables /
+ * context_lens must not change between building and using it.  A schedule
+ * for another batch size or grid sets PKV_FLAG_BAD_SCHEDULE and the decode
+ * call does nothing.  Shapes the tensor-core decode kernel does not serve
+ * build nothing and their _scheduled calls ignore the schedule.  The first
+ * decode launch after a build is stream-ordered behind it.
+ */
+size_t pkv_decode_schedule_bytes(int n_seqs, int max_blocks_per_seq);
+int pkv_decode_schedule(void* schedule, size_t schedule_bytes, const int32_t* block_tables,
+                        int64_t block_table_stride, int max_blocks_per_seq,
+                        const int32_t* context_lens, int n_seqs, int num_blocks, int n_q_heads,
+                        int n_kv_heads, int head_dim, int block_size, int dtype, int fp8_pools,
+                        int* err_flags, pkv_stream_t stream);
+/* pkv_paged_decode_attention / _fp8 / _append_attention with a schedule
+ * (the same arguments, then the schedule) */
+int pkv_paged_decode_attention_scheduled(void* out, int64_t out_row_stride, const void* q,
+                                         int64_t q_row_stride, const void* k_pool,
+                                         const void* v_pool, int num_blocks,
+                                         const int32_t* block_tables, int64_t block_table_stride,
+                                         int max_blocks_per_seq, const int32_t* context_lens,
+                                         int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                         int block_size, float scale, int dtype, void* workspace,
+                                         size_t workspace_bytes, int* err_flags,
+                                         pkv_stream_t stream, const void* schedule);
+int pkv_paged_decode_attention_fp8_scheduled(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_pool,
+    const void* v_pool, const float* k_scale, const float* v_scale, int num_blocks,
+    const int32_t* block_tables, int64_t block_table_stride, int max_blocks_per_seq,
+    const int32_t* context_lens, int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+    int block_size, float scale, int dtype, void* workspace, size_t workspace_bytes,
+    int* err_flags, pkv_stream_t stream, const void* schedule);
+int pkv_paged_decode_append_attention_scheduled(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, int num_blocks, const int32_t* block_tables, int64_t block_table_stride,
+    int max_blocks_per_seq, const int32_t* context_lens, int n_seqs, int n_q_heads,
+    int n_kv_heads, int head_dim, int block_size, float scale, int dtype, void* workspace,
+    size_t workspace_bytes, int* err_flags, pkv_stream_t stream, const void* schedule);
 
 /*
  * KV block migration between GPUs (one process per GPU).  Replaces the

@@ -369,18 +369,61 @@ int pkv_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride_byte
                                            static_cast<cudaStream_t>(stream)));
 }
 
+size_t pkv_decode_schedule_bytes(int n_seqs, int max_blocks_per_seq) {
+  if (n_seqs < 0 || max_blocks_per_seq < 0) return 0;
+  return decode_schedule_bytes(n_seqs, max_blocks_per_seq);
+}
+
+int pkv_decode_schedule(void* schedule, size_t schedule_bytes, const int32_t* block_tables,
+                        int64_t block_table_stride, int max_blocks_per_seq,
+                        const int32_t* context_lens, int n_seqs, int num_blocks, int n_q_heads,
+                        int n_kv_heads, int head_dim, int block_size, int dtype, int fp8_pools,
+                        int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0 || max_blocks_per_seq < 0) return PKV_ERR_BAD_SHAPE;
+  if (!schedule || !block_tables || !context_lens) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  if (schedule_bytes < decode_schedule_bytes(n_seqs, max_blocks_per_seq))
+    return PKV_ERR_WORKSPACE_TOO_SMALL;
+  if (n_seqs > 2048 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || num_blocks <= 0 ||
+      block_table_stride < max_blocks_per_seq)
+    return PKV_ERR_BAD_SHAPE;
+  if (dtype != PKV_DTYPE_F32 && dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16)
+    return PKV_ERR_BAD_DTYPE;
+  if (n_seqs == 0) return PKV_OK;
+  AttnArgs a{};
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.context_lens = context_lens;
+  a.n_seqs = n_seqs;
+  a.num_blocks = num_blocks;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.dtype = dtype;
+  a.err = err_flags;
+  static const float kOne = 1.f;  // marks fp8 pools for the grid choice only
+  if (fp8_pools) a.k_scale = a.v_scale = &kOne;
+  // the schedule serves the tensor-core kernel only; other shapes ignore it
+  if (!(decode_fast_supported_shape(a))) return PKV_OK;
+  return status_of(launch_decode_schedule(schedule, a, static_cast<cudaStream_t>(stream)));
+}
+
 size_t pkv_decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
   if (n_seqs < 0 || n_q_heads <= 0 || head_dim <= 0) return 0;
   return decode_workspace_bytes(n_seqs, n_q_heads, head_dim);
 }
 
-int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
-                               const void* k_pool, const void* v_pool, int num_blocks,
-                               const int32_t* block_tables, int64_t block_table_stride,
-                               int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
-                               int n_q_heads, int n_kv_heads, int head_dim, int block_size,
-                               float scale, int dtype, void* workspace, size_t workspace_bytes,
-                               int* err_flags, pkv_stream_t stream) {
+static int pkv_paged_decode_attention_impl(void* out, int64_t out_row_stride, const void* q,
+                                           int64_t q_row_stride, const void* k_pool,
+                                           const void* v_pool, int num_blocks,
+                                           const int32_t* block_tables, int64_t block_table_stride,
+                                           int max_blocks_per_seq, const int32_t* context_lens,
+                                           int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                           int block_size, float scale, int dtype, void* workspace,
+                                           size_t workspace_bytes, int* err_flags,
+                                           pkv_stream_t stream, const void* schedule) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -410,17 +453,22 @@ int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q,
   a.scale = scale;
   a.dtype = dtype;
   a.err = err_flags;
+  a.schedule = schedule;
   return decode_dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int pkv_paged_decode_attention_fp8(void* out, int64_t out_row_stride, const void* q,
-                                   int64_t q_row_stride, const void* k_pool, const void* v_pool,
-                                   const float* k_scale, const float* v_scale, int num_blocks,
-                                   const int32_t* block_tables, int64_t block_table_stride,
-                                   int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
-                                   int n_q_heads, int n_kv_heads, int head_dim, int block_size,
-                                   float scale, int dtype, void* workspace, size_t workspace_bytes,
-                                   int* err_flags, pkv_stream_t stream) {
+static int pkv_paged_decode_attention_fp8_impl(void* out, int64_t out_row_stride, const void* q,
+                                               int64_t q_row_stride, const void* k_pool,
+                                               const void* v_pool, const float* k_scale,
+                                               const float* v_scale, int num_blocks,
+                                               const int32_t* block_tables,
+                                               int64_t block_table_stride, int max_blocks_per_seq,
+                                               const int32_t* context_lens, int n_seqs,
+                                               int n_q_heads, int n_kv_heads, int head_dim,
+                                               int block_size, float scale, int dtype,
+                                               void* workspace, size_t workspace_bytes,
+                                               int* err_flags, pkv_stream_t stream,
+                                               const void* schedule) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -450,20 +498,26 @@ int pkv_paged_decode_attention_fp8(void* out, int64_t out_row_stride, const void
   a.scale = scale;
   a.dtype = dtype;
   a.err = err_flags;
+  a.schedule = schedule;
   a.k_scale = k_scale;
   a.v_scale = v_scale;
   return decode_dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const void* q,
-                                      int64_t q_row_stride, const void* k_new, const void* v_new,
-                                      int64_t k_new_row_stride, int64_t v_new_row_stride,
-                                      void* k_pool, void* v_pool, int num_blocks,
-                                      const int32_t* block_tables, int64_t block_table_stride,
-                                      int max_blocks_per_seq, const int32_t* context_lens,
-                                      int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
-                                      int block_size, float scale, int dtype, void* workspace,
-                                      size_t workspace_bytes, int* err_flags, pkv_stream_t stream) {
+static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_stride, const void* q,
+                                                  int64_t q_row_stride, const void* k_new,
+                                                  const void* v_new, int64_t k_new_row_stride,
+                                                  int64_t v_new_row_stride, void* k_pool,
+                                                  void* v_pool, int num_blocks,
+                                                  const int32_t* block_tables,
+                                                  int64_t block_table_stride,
+                                                  int max_blocks_per_seq,
+                                                  const int32_t* context_lens, int n_seqs,
+                                                  int n_q_heads, int n_kv_heads, int head_dim,
+                                                  int block_size, float scale, int dtype,
+                                                  void* workspace, size_t workspace_bytes,
+                                                  int* err_flags, pkv_stream_t stream,
+                                                  const void* schedule) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -495,6 +549,7 @@ int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const v
   a.scale = scale;
   a.dtype = dtype;
   a.err = err_flags;
+  a.schedule = schedule;
   a.k_new = k_new;
   a.v_new = v_new;
   a.k_new_stride = k_new_row_stride;
@@ -521,6 +576,117 @@ int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const v
   if (e != cudaSuccess) return status_of(e);
   a.k_new = a.v_new = nullptr;
   return status_of(launch_generic_attention(a, st));
+}
+
+int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                               const void* k_pool, const void* v_pool, int num_blocks,
+                               const int32_t* block_tables, int64_t block_table_stride,
+                               int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+                               int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                               float scale, int dtype, void* workspace, size_t workspace_bytes,
+                               int* err_flags, pkv_stream_t stream) {
+  return pkv_paged_decode_attention_impl(out, out_row_stride, q, q_row_stride, k_pool, v_pool,
+                                         num_blocks, block_tables, block_table_stride,
+                                         max_blocks_per_seq, context_lens, n_seqs, n_q_heads,
+                                         n_kv_heads, head_dim, block_size, scale, dtype, workspace,
+                                         workspace_bytes, err_flags, stream, nullptr);
+}
+
+int pkv_paged_decode_attention_scheduled(void* out, int64_t out_row_stride, const void* q,
+                                         int64_t q_row_stride, const void* k_pool,
+                                         const void* v_pool, int num_blocks,
+                                         const int32_t* block_tables, int64_t block_table_stride,
+                                         int max_blocks_per_seq, const int32_t* context_lens,
+                                         int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                         int block_size, float scale, int dtype, void* workspace,
+                                         size_t workspace_bytes, int* err_flags,
+                                         pkv_stream_t stream, const void* schedule) {
+  if (!schedule) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  return pkv_paged_decode_attention_impl(out, out_row_stride, q, q_row_stride, k_pool, v_pool,
+                                         num_blocks, block_tables, block_table_stride,
+                                         max_blocks_per_seq, context_lens, n_seqs, n_q_heads,
+                                         n_kv_heads, head_dim, block_size, scale, dtype, workspace,
+                                         workspace_bytes, err_flags, stream, schedule);
+}
+
+int pkv_paged_decode_attention_fp8(void* out, int64_t out_row_stride, const void* q,
+                                   int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                   const float* k_scale, const float* v_scale, int num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int block_size,
+                                   float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                   int* err_flags, pkv_stream_t stream) {
+  return pkv_paged_decode_attention_fp8_impl(out, out_row_stride, q, q_row_stride, k_pool, v_pool,
+                                             k_scale, v_scale, num_blocks, block_tables,
+                                             block_table_stride, max_blocks_per_seq, context_lens,
+                                             n_seqs, n_q_heads, n_kv_heads, head_dim, block_size,
+                                             scale, dtype, workspace, workspace_bytes, err_flags,
+                                             stream, nullptr);
+}
+
+int pkv_paged_decode_attention_fp8_scheduled(void* out, int64_t out_row_stride, const void* q,
+                                             int64_t q_row_stride, const void* k_pool,
+                                             const void* v_pool, const float* k_scale,
+                                             const float* v_scale, int num_blocks,
+                                             const int32_t* block_tables,
+                                             int64_t block_table_stride, int max_blocks_per_seq,
+                                             const int32_t* context_lens, int n_seqs, int n_q_heads,
+                                             int n_kv_heads, int head_dim, int block_size,
+                                             float scale, int dtype, void* workspace,
+                                             size_t workspace_bytes, int* err_flags,
+                                             pkv_stream_t stream, const void* schedule) {
+  if (!schedule) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  return pkv_paged_decode_attention_fp8_impl(out, out_row_stride, q, q_row_stride, k_pool, v_pool,
+                                             k_scale, v_scale, num_blocks, block_tables,
+                                             block_table_stride, max_blocks_per_seq, context_lens,
+                                             n_seqs, n_q_heads, n_kv_heads, head_dim, block_size,
+                                             scale, dtype, workspace, workspace_bytes, err_flags,
+                                             stream, schedule);
+}
+
+int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const void* q,
+                                      int64_t q_row_stride, const void* k_new, const void* v_new,
+                                      int64_t k_new_row_stride, int64_t v_new_row_stride,
+                                      void* k_pool, void* v_pool, int num_blocks,
+                                      const int32_t* block_tables, int64_t block_table_stride,
+                                      int max_blocks_per_seq, const int32_t* context_lens,
+                                      int n_seqs, int n_q_heads, int n_kv_heads, int head_dim,
+                                      int block_size, float scale, int dtype, void* workspace,
+                                      size_t workspace_bytes, int* err_flags, pkv_stream_t stream) {
+  return pkv_paged_decode_append_attention_impl(out, out_row_stride, q, q_row_stride, k_new, v_new,
+                                                k_new_row_stride, v_new_row_stride, k_pool, v_pool,
+                                                num_blocks, block_tables, block_table_stride,
+                                                max_blocks_per_seq, context_lens, n_seqs, n_q_heads,
+                                                n_kv_heads, head_dim, block_size, scale, dtype,
+                                                workspace, workspace_bytes, err_flags, stream,
+                                                nullptr);
+}
+
+int pkv_paged_decode_append_attention_scheduled(void* out, int64_t out_row_stride, const void* q,
+                                                int64_t q_row_stride, const void* k_new,
+                                                const void* v_new, int64_t k_new_row_stride,
+                                                int64_t v_new_row_stride, void* k_pool,
+                                                void* v_pool, int num_blocks,
+                                                const int32_t* block_tables,
+                                                int64_t block_table_stride, int max_blocks_per_seq,
+                                                const int32_t* context_lens, int n_seqs,
+                                                int n_q_heads, int n_kv_heads, int head_dim,
+                                                int block_size, float scale, int dtype,
+                                                void* workspace, size_t workspace_bytes,
+                                                int* err_flags, pkv_stream_t stream,
+                                                const void* schedule) {
+  if (!schedule) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  return pkv_paged_decode_append_attention_impl(out, out_row_stride, q, q_row_stride, k_new, v_new,
+                                                k_new_row_stride, v_new_row_stride, k_pool, v_pool,
+                                                num_blocks, block_tables, block_table_stride,
+                                                max_blocks_per_seq, context_lens, n_seqs, n_q_heads,
+                                                n_kv_heads, head_dim, block_size, scale, dtype,
+                                                workspace, workspace_bytes, err_flags, stream,
+                                                schedule);
 }
 
 int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,

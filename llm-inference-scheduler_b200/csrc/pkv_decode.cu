@@ -112,7 +112,31 @@ struct DecodeParams {
   // fp8 pools: fp32 scale per (slot, KV head)
   const float* k_scale;
   const float* v_scale;
+  // per-step schedule (NULL: derive it here): header, block prefix, clamped
+  // lengths and each CTA's block ids in rows of sched_rows
+  const int32_t* sched;
+  int sched_rows;
 };
+
+// Decode schedule (int32): kSchedHdr header words {n_seqs, total blocks,
+// blocks per CTA, grid, row length}, then the block prefix [n_seqs + 1], the
+// clamped context lengths [n_seqs], then (16-byte aligned) CTA c's block ids
+// at [c * rows, c * rows + per).
+constexpr int kSchedHdr = 8;
+__host__ __device__ inline int64_t sched_ids_offset(int n_seqs) {
+  return (kSchedHdr + 2 * static_cast<int64_t>(n_seqs) + 1 + 3) & ~static_cast<int64_t>(3);
+}
+// ids capacity: grid x rows <= n_seqs * max_blocks + grid * (1 + kDecMinBlocksPerCta)
+inline int64_t sched_ids_capacity(int n_seqs, int max_blocks) {
+  return static_cast<int64_t>(n_seqs) * max_blocks + static_cast<int64_t>(kDecMaxCtas) * 5;
+}
+size_t decode_schedule_bytes(int n_seqs, int max_blocks) {
+  return static_cast<size_t>(sched_ids_offset(n_seqs) + sched_ids_capacity(n_seqs, max_blocks)) * 4;
+}
+inline int sched_rows_for(int n_seqs, int max_blocks, int grid) {
+  const int64_t cap = static_cast<int64_t>(n_seqs) * max_blocks;
+  return static_cast<int>(std::max<int64_t>((cap + grid - 1) / grid, kDecMinBlocksPerCta));
+}
 
 // 16 fp8 e4m3 values -> 16 values of T (exact), low byte first
 template <typename T> __device__ __forceinline__ uint32_t fp8x2_to(uint32_t two);
@@ -158,6 +182,14 @@ size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim) {
   const size_t parts = static_cast<size_t>(2) * kDecMaxCtas *
                        (n_q_heads * head_dim + ((2 * n_q_heads + 3) & ~3)) * 4;
   return (parts + 255) & ~static_cast<size_t>(255);
+}
+
+// the shapes the tensor-core kernel serves (pointer alignment aside)
+bool decode_fast_supported_shape(const AttnArgs& a) {
+  const int G = a.n_q_heads / a.n_kv_heads;
+  return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
+         a.block_size == 16 && (a.n_kv_heads == 1 || a.n_kv_heads == 2 || a.n_kv_heads == 4) &&
+         G <= 8 && a.n_q_heads <= 32 && a.n_seqs <= kDecMaxSeqs;
 }
 
 bool decode_fast_supported(const AttnArgs& a) {
@@ -270,25 +302,46 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   int* prefix = misc + 40;                           // [B+1]
   int* ctxs = prefix + (B + 1);                      // [B]
 
-  // ---- prologue (reads only metadata): clamp contexts, prefix-sum block counts
-  const int cap_tokens = p.max_blocks * 16;
-  for (int s = tid; s < B; s += blockDim.x) {
-    int c = p.context_lens[s];
-    if (c < 0) c = 0;
-    if (c > cap_tokens) {
-      if (blockIdx.x == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
-      c = cap_tokens;
+  // ---- prologue (reads only metadata)
+  int total, per;
+  int sched_id0 = 0;  // producer lanes: this CTA's first 32 block ids (schedule)
+  if (p.sched != nullptr) {
+    // the step's schedule: one round trip, no scan; the producer's first
+    // block ids are loaded in the same round trip
+    const int32_t* sp = p.sched + kSchedHdr;
+    for (int s = tid; s <= B; s += blockDim.x) prefix[s] = __ldg(sp + s);
+    for (int s = tid; s < B; s += blockDim.x) ctxs[s] = __ldg(sp + B + 1 + s);
+    if (warp == nkv && lane < p.sched_rows)
+      sched_id0 = __ldg(p.sched + sched_ids_offset(B) + static_cast<int64_t>(blockIdx.x) * p.sched_rows + lane);
+    total = __ldg(p.sched + 1);
+    per = __ldg(p.sched + 2);
+    if (__ldg(p.sched) != B || __ldg(p.sched + 3) != static_cast<int>(gridDim.x)) {
+      // a schedule built for another batch or grid: do nothing
+      if (tid == 0 && blockIdx.x == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
+      if (tid == 0) pdl_trigger();
+      return;
     }
-    ctxs[s] = c;
-    prefix[s] = (c + 15) >> 4;
+    __syncthreads();
+  } else {
+    // clamp contexts, prefix-sum block counts
+    const int cap_tokens = p.max_blocks * 16;
+    for (int s = tid; s < B; s += blockDim.x) {
+      int c = p.context_lens[s];
+      if (c < 0) c = 0;
+      if (c > cap_tokens) {
+        if (blockIdx.x == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+        c = cap_tokens;
+      }
+      ctxs[s] = c;
+      prefix[s] = (c + 15) >> 4;
+    }
+    __syncthreads();
+    total = block_exclusive_scan(prefix, B, misc + 1);
+    if (tid == 0) prefix[B] = total;
+    __syncthreads();
+    per = max((total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x),
+              kDecMinBlocksPerCta);
   }
-  __syncthreads();
-  const int total = block_exclusive_scan(prefix, B, misc + 1);
-  if (tid == 0) prefix[B] = total;
-  __syncthreads();
-
-  const int per = max((total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x),
-                      kDecMinBlocksPerCta);
   const int n_active = (total + per - 1) / per;
   const bool active = static_cast<int>(blockIdx.x) < n_active;
 
@@ -327,9 +380,19 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       if (gb < r1) {
         const int s = find_seq(prefix, B, gb);
         const int jb = gb - prefix[s];
-        id = __ldg(p.block_tables + static_cast<int64_t>(s) * p.bt_stride + jb);
-        if (id < 0 || id >= p.num_blocks) {
-          raise_flag(p.err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+        if (p.sched != nullptr) {
+          // validated by the schedule builder (a bad id is stored as -1)
+          id = b0 == r0 ? sched_id0
+                        : __ldg(p.sched + sched_ids_offset(B) +
+                                static_cast<int64_t>(blockIdx.x) * p.sched_rows + (gb - r0));
+        } else {
+          id = __ldg(p.block_tables + static_cast<int64_t>(s) * p.bt_stride + jb);
+          if (id < 0 || id >= p.num_blocks) {
+            raise_flag(p.err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+            id = -1;
+          }
+        }
+        if (id < 0) {
           id = 0;  // read a valid block; never write through a bad id
         } else if (!FP8 && p.k_new != nullptr && gb == prefix[s + 1] - 1) {
           app_seq = s;
@@ -680,6 +743,62 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   }
 }
 
+// Schedule builder: what every layer's decode launch of a step would
+// otherwise recompute (clamped lengths, the block prefix, each CTA's
+// stream-K range of block ids), once per step.  CTA c scans the lengths and
+// writes the block ids of decode CTA c (one parallel round of table reads);
+// CTA 0 also writes the header, prefix and lengths.  Bounds problems are
+// flagged here, once per step; a bad block id is stored as -1.
+constexpr int kSchedThreads = 128;
+__global__ void __launch_bounds__(kSchedThreads) decode_schedule_kernel(
+    int32_t* __restrict__ sched, const int32_t* __restrict__ tables, int64_t bt_stride,
+    int max_blocks, const int32_t* __restrict__ context_lens, int B, int num_blocks, int grid,
+    int rows, int* err) {
+  extern __shared__ int sm_sched[];
+  int* misc = sm_sched;        // scan scratch
+  int* prefix = misc + 40;     // [B + 1]
+  const int tid = threadIdx.x;
+  const int cap_tokens = max_blocks * 16;
+  const bool lead = blockIdx.x == 0;
+  int32_t* ctx_out = sched + kSchedHdr + B + 1;
+  for (int s = tid; s < B; s += blockDim.x) {
+    int c = context_lens[s];
+    if (c < 0) c = 0;
+    if (c > cap_tokens) {
+      if (lead) raise_flag(err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+      c = cap_tokens;
+    }
+    if (lead) ctx_out[s] = c;
+    prefix[s] = (c + 15) >> 4;
+  }
+  __syncthreads();
+  const int total = block_exclusive_scan(prefix, B, misc + 1);
+  if (tid == 0) prefix[B] = total;
+  __syncthreads();
+  const int per = max((total + grid - 1) / grid, kDecMinBlocksPerCta);
+  if (lead) {
+    for (int s = tid; s <= B; s += blockDim.x) sched[kSchedHdr + s] = prefix[s];
+    if (tid == 0) {
+      sched[0] = B;
+      sched[1] = total;
+      sched[2] = per;
+      sched[3] = grid;
+      sched[4] = rows;
+    }
+  }
+  int32_t* row = sched + sched_ids_offset(B) + static_cast<int64_t>(blockIdx.x) * rows;
+  const int r0 = blockIdx.x * per, r1 = min(r0 + per, total);
+  for (int gb = r0 + tid; gb < r1; gb += blockDim.x) {
+    const int s = find_seq(prefix, B, gb);
+    int id = __ldg(tables + static_cast<int64_t>(s) * bt_stride + (gb - prefix[s]));
+    if (id < 0 || id >= num_blocks) {
+      raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+      id = -1;
+    }
+    row[gb - r0] = id;
+  }
+}
+
 // Split-K merge: CTA s finishes sequence s.  If the decode kernel split it
 // over CTAs c_first..c_last (stream-K ranges of `per` blocks), the partials
 // (m, l, O) are merged: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
@@ -852,18 +971,15 @@ DecodeKernel pick_kernel(int dtype, int nkv, bool fp8) {
 }
 }  // namespace
 
-cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
-                               void* workspace, cudaStream_t stream) {
-  if (a.n_seqs == 0) return cudaSuccess;
-  const int nkv = a.n_kv_heads;
+// the persistent grid of the decode kernel for this shape (cached occupancy)
+cudaError_t decode_grid(int dtype, int nkv, bool fp8, int n_seqs, int* grid_out) {
   const int threads = 32 * (nkv + 1);
-  const bool fp8 = a.k_scale != nullptr;
-  const size_t smem = decode_smem_bytes(nkv, a.n_seqs, fp8);
+  const size_t smem = decode_smem_bytes(nkv, n_seqs, fp8);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  DecodeKernel kern = pick_kernel(a.dtype, nkv, fp8);
-  const int kind = a.dtype * 8 + nkv + (fp8 ? 64 : 0);
+  DecodeKernel kern = pick_kernel(dtype, nkv, fp8);
+  const int kind = dtype * 8 + nkv + (fp8 ? 64 : 0);
   int grid = 0;
   {
     std::lock_guard<std::mutex> lk(g_occ_mu);
@@ -886,6 +1002,62 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
       it = g_occ.emplace(key, std::max(1, std::min(kDecMaxCtas, per_sm * sms))).first;
     }
     grid = it->second;
+  }
+  *grid_out = grid;
+  return cudaSuccess;
+}
+
+namespace {
+// schedules built on a stream and not yet read by a decode launch: that first
+// launch is stream-ordered (no programmatic overlap), because the kernel reads
+// the schedule before griddepcontrol.wait
+std::mutex g_fresh_mu;
+std::unordered_map<const void*, cudaStream_t> g_fresh;
+}  // namespace
+
+cudaError_t launch_decode_schedule(void* schedule, const AttnArgs& a, cudaStream_t stream) {
+  const bool fp8 = a.k_scale != nullptr;
+  int grid = 0;
+  cudaError_t e = decode_grid(a.dtype, a.n_kv_heads, fp8, a.n_seqs, &grid);
+  if (e != cudaSuccess) return e;
+  const int rows = sched_rows_for(a.n_seqs, a.max_blocks, grid);
+  const size_t smem = (40 + static_cast<size_t>(a.n_seqs) + 1) * sizeof(int);
+  if (smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(decode_schedule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  decode_schedule_kernel<<<grid, kSchedThreads, smem, stream>>>(
+      static_cast<int32_t*>(schedule), a.block_tables, a.bt_stride, a.max_blocks, a.context_lens,
+      a.n_seqs, a.num_blocks, grid, rows, a.err);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lk(g_fresh_mu);
+    if (g_fresh.size() > 4096) g_fresh.clear();  // schedules built and never used
+    g_fresh[schedule] = stream;
+  }
+  return e;
+}
+
+cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
+                               void* workspace, cudaStream_t stream) {
+  if (a.n_seqs == 0) return cudaSuccess;
+  const int nkv = a.n_kv_heads;
+  const int threads = 32 * (nkv + 1);
+  const bool fp8 = a.k_scale != nullptr;
+  const size_t smem = decode_smem_bytes(nkv, a.n_seqs, fp8);
+  DecodeKernel kern = pick_kernel(a.dtype, nkv, fp8);
+  int grid = 0;
+  cudaError_t e = decode_grid(a.dtype, nkv, fp8, a.n_seqs, &grid);
+  if (e != cudaSuccess) return e;
+  bool ordered = false;  // the schedule was just built: no programmatic overlap
+  if (a.schedule != nullptr) {
+    std::lock_guard<std::mutex> lk(g_fresh_mu);
+    auto it = g_fresh.find(a.schedule);
+    if (it != g_fresh.end()) {
+      ordered = true;
+      g_fresh.erase(it);
+    }
   }
   DecodeParams p;
   p.out = a.out;
@@ -916,6 +1088,8 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.v_pool = static_cast<uint8_t*>(const_cast<void*>(a.v_pool));
   p.k_scale = a.k_scale;
   p.v_scale = a.v_scale;
+  p.sched = static_cast<const int32_t*>(a.schedule);
+  p.sched_rows = a.schedule != nullptr ? sched_rows_for(a.n_seqs, a.max_blocks, grid) : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -926,11 +1100,12 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = ordered ? 0 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, *kmap, *vmap, p);
   if (e != cudaSuccess) return e;
 
   cudaLaunchConfig_t mcfg = cfg;
+  mcfg.numAttrs = 1;
   mcfg.gridDim = dim3(a.n_seqs);
   mcfg.blockDim = dim3(kMergeThreads);
   mcfg.dynamicSmemBytes = 0;

@@ -66,6 +66,8 @@ struct AttnArgs {
   // of `dtype` (q, out and the dequantised arithmetic stay in `dtype`)
   const float* k_scale = nullptr;
   const float* v_scale = nullptr;
+  // decode: the step's schedule built by pkv_decode_schedule (NULL = none)
+  const void* schedule = nullptr;
 };
 cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,
                                          int64_t v_stride, void* k_pool, void* v_pool,
@@ -87,6 +89,8 @@ cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k
                                          int block_size, int n_kv_heads, int head_dim, int esize,
                                          int* err, cudaStream_t stream);
 
+size_t decode_schedule_bytes(int n_seqs, int max_blocks);
+cudaError_t launch_decode_schedule(void* schedule, const AttnArgs& a, cudaStream_t stream);
 cudaError_t launch_copy_blocks_peer(void* dst_k, void* dst_v, int64_t dst_layer_stride,
                                     int dst_num_blocks, const void* src_k, const void* src_v,
                                     int64_t src_layer_stride, int src_num_blocks, int n_layers,
@@ -104,6 +108,7 @@ cudaError_t launch_generic_attention(const AttnArgs& a, cudaStream_t stream);
 // split with fused combine.  Requires fp16/bf16, head_dim 64, block 16,
 // n_kv_heads in {1,2,4}, q heads per kv head <= 8.
 bool decode_fast_supported(const AttnArgs& a);
+bool decode_fast_supported_shape(const AttnArgs& a);
 size_t decode_workspace_bytes(int n_seqs, int n_q_heads, int head_dim);
 cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
                                void* workspace, cudaStream_t stream);

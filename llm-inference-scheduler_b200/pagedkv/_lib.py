@@ -36,13 +36,14 @@ FLAG_CONTEXT_EXCEEDS_TABLE = 4
 FLAG_PIPELINE_TIMEOUT = 8
 FLAG_BAD_QUERY_LAYOUT = 16
 FLAG_POSITION_OUT_OF_RANGE = 32
+FLAG_BAD_SCHEDULE = 64
 
 DECODE_AUTO = 0
 DECODE_GENERIC = 1
 
 # every symbol include/pagedkv.h declares, with (restype, argtypes)
 _P, _I, _I64, _F, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
-SIGNATURES = {
+SIGNATURES: dict = {
     "pkv_abi_version": (_I, []),
     "pkv_status_string": (ctypes.c_char_p, [_I]),
     "pkv_reshape_and_cache": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -66,11 +67,19 @@ SIGNATURES = {
                                             _I, _I, _I, _I, _I, _F, _I, _P, _SZ, _P, _P]),
     "pkv_paged_prefill_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _I64, _I, _P,
                                              _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
+    "pkv_decode_schedule_bytes": (_SZ, [_I, _I]),
+    "pkv_decode_schedule": (_I, [_P, _SZ, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "pkv_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
     "pkv_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "pkv_ipc_close": (_I, [_P]),
     "pkv_copy_blocks_peer": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I, _P, _I, _I64, _P, _P]),
 }
+
+
+# decode entries with a per-step schedule: the same arguments plus the schedule
+for _n in ("pkv_paged_decode_attention", "pkv_paged_decode_attention_fp8",
+           "pkv_paged_decode_append_attention"):
+    SIGNATURES[_n + "_scheduled"] = (_I, SIGNATURES[_n][1] + [_P])
 
 
 class PagedKVUnavailable(RuntimeError):

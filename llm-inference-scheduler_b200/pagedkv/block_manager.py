@@ -193,6 +193,7 @@ class StepMetadata:
     num_prior_dev: torch.Tensor     # int32 [B]
     decode_plan: ops.DecodeAppendPlan | None = None  # built by the first forward_layer
     decode_plain_plan: ops.DecodePlan | None = None   # built by the first forward_layer_qkv
+    decode_schedule: torch.Tensor | None = None       # the step's decode schedule (first layer)
 
     @property
     def n_seqs(self) -> int:
@@ -272,6 +273,7 @@ class PagedKVCache:
         self.block_tables: dict[int, list[int]] = {}
         self._len: dict[int, int] = {}
         self._workspace: torch.Tensor | None = None
+        self._schedule_buf: torch.Tensor | None = None
         self._mirror = _TableMirror()
         self._stage_ring: list = [[None, None] for _ in range(4)]
         self._stage_next = 0
@@ -478,6 +480,21 @@ class PagedKVCache:
             num_prior_dev=ints_d[B * W + B: B * W + 2 * B],
             query_start_loc=ints_d[B * W + 2 * B:])
 
+    def _step_schedule(self, meta: StepMetadata, q: torch.Tensor) -> torch.Tensor:
+        """The step's decode schedule, built on its first decode layer into a
+        buffer this cache reuses from step to step (stream order keeps a
+        step's build behind the previous step's decode launches)."""
+        if meta.decode_schedule is None:
+            nd, W = meta.n_decode, meta.block_tables.shape[1]
+            need = ops.decode_schedule_bytes(nd, W)
+            if self._schedule_buf is None or self._schedule_buf.numel() < need:
+                self._schedule_buf = ops.new_decode_schedule(nd, W, self.mgr.device)
+            meta.decode_schedule = ops.build_decode_schedule(
+                self._schedule_buf, meta.block_tables[:nd], meta.context_lens[:nd],
+                self.mgr.num_blocks, q.shape[1], self.mgr.num_kv_heads, q.shape[2], q.dtype,
+                fp8=self.mgr.fp8, err=self.mgr.err)
+        return meta.decode_schedule
+
     def decode_workspace(self, n_seqs: int, n_q_heads: int, head_dim: int) -> torch.Tensor:
         need = ops.decode_workspace_bytes(n_seqs, n_q_heads, head_dim)
         if self._workspace is None or self._workspace.numel() < need:
@@ -513,7 +530,8 @@ class PagedKVCache:
             if plan is None or plan.scale != scale:
                 ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
                 plan = meta.decode_plan = ops.DecodeAppendPlan(
-                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err)
+                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err,
+                    schedule=self._step_schedule(meta, q))
             whole = nd == meta.n_tokens
             plan(q if whole else q[:nd], k_new if whole else k_new[:nd],
                  v_new if whole else v_new[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
@@ -547,7 +565,8 @@ class PagedKVCache:
             ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
             ops.paged_decode_attention_fp8(q[:nd], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
                                            meta.block_tables[:nd], meta.context_lens[:nd], scale,
-                                           workspace=ws, out=out[:nd], err=mgr.err)
+                                           workspace=ws, out=out[:nd], err=mgr.err,
+                                           schedule=self._step_schedule(meta, q))
         if nd < meta.n_seqs:
             ops.paged_prefill_attention_fp8(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
                                             meta.block_tables[nd:], meta.query_start_loc,
@@ -581,7 +600,8 @@ class PagedKVCache:
             if plan is None or plan.scale != scale:
                 ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
                 plan = meta.decode_plain_plan = ops.DecodePlan(
-                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err)
+                    meta.block_tables[:nd], meta.context_lens[:nd], scale, ws, mgr.err,
+                    schedule=self._step_schedule(meta, q))
             whole = nd == meta.n_tokens
             plan(q if whole else q[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
                  out if whole else out[:nd])

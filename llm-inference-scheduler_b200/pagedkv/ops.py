@@ -249,17 +249,58 @@ def _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace
     return args, out
 
 
+def decode_schedule_bytes(n_seqs: int, max_blocks_per_seq: int) -> int:
+    return int(_lib.load().pkv_decode_schedule_bytes(n_seqs, max_blocks_per_seq))
+
+
+def new_decode_schedule(n_seqs: int, max_blocks_per_seq: int, device) -> torch.Tensor:
+    """Buffer for a per-step decode schedule (any initial contents)."""
+    return torch.empty(max(16, decode_schedule_bytes(n_seqs, max_blocks_per_seq)), dtype=torch.uint8,
+                       device=device)
+
+
+def build_decode_schedule(schedule: torch.Tensor, block_tables: torch.Tensor,
+                          context_lens: torch.Tensor, num_blocks: int, n_q_heads: int,
+                          n_kv_heads: int, head_dim: int, dtype: torch.dtype, fp8: bool = False,
+                          err: torch.Tensor | None = None) -> torch.Tensor:
+    """The step's stream-K partition for the decode kernel, computed once and
+    read by every layer's `schedule=` decode call (pkv_decode_schedule).
+    dtype is the q / out dtype of those calls; fp8=True for the fp8 decode."""
+    _cuda(schedule, "schedule"), _cuda(context_lens, "context_lens")
+    _check_tables(block_tables)
+    if context_lens.dtype != torch.int32 or not context_lens.is_contiguous():
+        raise TypeError("pagedkv: context_lens must be a contiguous int32 tensor")
+    B = context_lens.shape[0]
+    rc = _lib.load().pkv_decode_schedule(
+        schedule.data_ptr(), schedule.numel() * schedule.element_size(), block_tables.data_ptr(),
+        block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(), B, num_blocks,
+        n_q_heads, n_kv_heads, head_dim, 16, dtype_code(dtype), int(bool(fp8)), _ptr(err),
+        _stream(context_lens))
+    _lib.check(rc, "pkv_decode_schedule")
+    return schedule
+
+
+def _sched_fn(name: str, schedule):
+    return getattr(_lib.load(), name + "_scheduled" if schedule is not None else name)
+
+
+def _sched_args(args: tuple, schedule) -> tuple:
+    return args + (schedule.data_ptr(),) if schedule is not None else args
+
+
 def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                            block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                            workspace: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                           err: torch.Tensor | None = None) -> torch.Tensor:
+                           err: torch.Tensor | None = None,
+                           schedule: torch.Tensor | None = None) -> torch.Tensor:
     """out[s] = softmax(scale * q[s] K_s^T) V_s over context_lens[s] tokens of
     sequence s, read in place through block_tables[s] (GQA: q head h uses kv
     head h // (Hq // Hkv)).  q: [B, Hq, D]; returns [B, Hq, D].
     Reference: block_manager.py:136-141 + qwen2.py:98-128 (num_new == 1).
     """
     args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err)
-    _lib.check(_lib.load().pkv_paged_decode_attention(*args), "pkv_paged_decode_attention")
+    _lib.check(_sched_fn("pkv_paged_decode_attention", schedule)(*_sched_args(args, schedule)),
+               "pkv_paged_decode_attention")
     return out
 
 
@@ -286,14 +327,15 @@ def paged_decode_append_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: t
                                   block_tables: torch.Tensor, context_lens: torch.Tensor,
                                   scale: float, workspace: torch.Tensor | None = None,
                                   out: torch.Tensor | None = None,
-                                  err: torch.Tensor | None = None) -> torch.Tensor:
+                                  err: torch.Tensor | None = None,
+                                  schedule: torch.Tensor | None = None) -> torch.Tensor:
     """One decode step of one layer: write k_new[s] / v_new[s] at position
     context_lens[s] - 1 of sequence s (slot from its block table), then the
     paged attention over context_lens[s] tokens.  Reference:
     PagedKVCache.append_and_fetch + Qwen2Model._attention (num_new == 1)."""
     args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
                                     scale, workspace, out, err)
-    _lib.check(_lib.load().pkv_paged_decode_append_attention(*args),
+    _lib.check(_sched_fn("pkv_paged_decode_append_attention", schedule)(*_sched_args(args, schedule)),
                "pkv_paged_decode_append_attention")
     return out
 
@@ -343,7 +385,8 @@ def reshape_and_cache_fp8(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor
 
 
 def paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
-                               scale, workspace=None, out=None, err=None) -> torch.Tensor:
+                               scale, workspace=None, out=None, err=None,
+                               schedule=None) -> torch.Tensor:
     """paged_decode_attention over fp8 e4m3 pools (value = e4m3(byte) *
     scale of its row); q / out in fp16, bf16 or fp32."""
     nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
@@ -360,12 +403,12 @@ def paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables
         workspace = new_decode_workspace(B, hq, d, q.device)
     if B == 0:
         return out
-    rc = _lib.load().pkv_paged_decode_attention_fp8(
-        out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
-        v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb, block_tables.data_ptr(),
-        block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(), B, hq, hkv, d, bs,
-        float(scale), dtype_code(q.dtype), workspace.data_ptr(),
-        workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            context_lens.data_ptr(), B, hq, hkv, d, bs, float(scale), dtype_code(q.dtype),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
+    rc = _sched_fn("pkv_paged_decode_attention_fp8", schedule)(*_sched_args(args, schedule))
     _lib.check(rc, "pkv_paged_decode_attention_fp8")
     return out
 
@@ -407,12 +450,13 @@ class DecodeAppendPlan:
 
     _PTRS = (0, 2, 4, 5, 8, 9)  # out, q, k_new, v_new, k_pool, v_pool in the C argument list
 
-    def __init__(self, block_tables, context_lens, scale, workspace, err=None):
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None, schedule=None):
         self._static = (block_tables, context_lens, scale, workspace, err)
         self.scale = scale
+        self.schedule = schedule  # the step's decode schedule (build_decode_schedule) or None
         self._key = None
         self._args: list = []
-        self._fn = _lib.load().pkv_paged_decode_append_attention
+        self._fn = _sched_fn("pkv_paged_decode_append_attention", schedule)
 
     def __call__(self, q, k_new, v_new, k_pool, v_pool, out) -> torch.Tensor:
         # everything the validated arguments depend on besides the six pointers
@@ -424,7 +468,7 @@ class DecodeAppendPlan:
             tables, ctx, scale, ws, err = self._static
             args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, tables, ctx, scale, ws,
                                             out, err)
-            self._args, self._key = list(args), key
+            self._args, self._key = list(_sched_args(args, self.schedule)), key
         else:
             a = self._args
             a[0], a[2], a[4], a[5], a[8], a[9] = (out.data_ptr(), q.data_ptr(), k_new.data_ptr(),
@@ -440,9 +484,9 @@ class DecodePlan(DecodeAppendPlan):
     the pools) for the layers of one step, with the same reuse of validated
     arguments as DecodeAppendPlan."""
 
-    def __init__(self, block_tables, context_lens, scale, workspace, err=None):
-        super().__init__(block_tables, context_lens, scale, workspace, err)
-        self._fn = _lib.load().pkv_paged_decode_attention
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None, schedule=None):
+        super().__init__(block_tables, context_lens, scale, workspace, err, schedule)
+        self._fn = _sched_fn("pkv_paged_decode_attention", schedule)
 
     def __call__(self, q, k_pool, v_pool, out) -> torch.Tensor:
         key = (q.dtype, k_pool.dtype, v_pool.dtype, out.dtype, q.shape, q.stride(), k_pool.shape,
@@ -451,7 +495,7 @@ class DecodePlan(DecodeAppendPlan):
         if key != self._key:
             tables, ctx, scale, ws, err = self._static
             args, out = _decode_args(q, k_pool, v_pool, tables, ctx, scale, ws, out, err)
-            self._args, self._key = list(args), key
+            self._args, self._key = list(_sched_args(args, self.schedule)), key
         else:
             a = self._args
             a[0], a[2], a[4], a[5] = out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
@@ -477,6 +521,18 @@ class BoundLaunch:
             _lib.check(rc, self._name)
 
 
+def bind_decode_schedule(schedule, block_tables, context_lens, num_blocks, n_q_heads, n_kv_heads,
+                         head_dim, dtype, fp8=False, err=None) -> BoundLaunch:
+    build_decode_schedule(schedule, block_tables, context_lens, num_blocks, n_q_heads, n_kv_heads,
+                          head_dim, dtype, fp8, err)  # validates (and runs once)
+    args = (schedule.data_ptr(), schedule.numel() * schedule.element_size(), block_tables.data_ptr(),
+            block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(),
+            context_lens.shape[0], num_blocks, n_q_heads, n_kv_heads, head_dim, 16, dtype_code(dtype),
+            int(bool(fp8)), _ptr(err), _stream(context_lens))
+    return BoundLaunch(_lib.load().pkv_decode_schedule, args, "pkv_decode_schedule",
+                       (schedule, block_tables, context_lens, err))
+
+
 def bind_reshape_and_cache(k, v, k_pool, v_pool, slot_mapping, err=None) -> BoundLaunch:
     args = _reshape_and_cache_args(k, v, k_pool, v_pool, slot_mapping, err)
     return BoundLaunch(_lib.load().pkv_reshape_and_cache, args, "pkv_reshape_and_cache",
@@ -484,20 +540,21 @@ def bind_reshape_and_cache(k, v, k_pool, v_pool, slot_mapping, err=None) -> Boun
 
 
 def bind_paged_decode_attention(q, k_pool, v_pool, block_tables, context_lens, scale, workspace,
-                                out, err=None) -> BoundLaunch:
+                                out, err=None, schedule=None) -> BoundLaunch:
     args, out = _decode_args(q, k_pool, v_pool, block_tables, context_lens, scale, workspace, out, err)
-    return BoundLaunch(_lib.load().pkv_paged_decode_attention, args, "pkv_paged_decode_attention",
-                       (q, k_pool, v_pool, block_tables, context_lens, workspace, out, err))
+    return BoundLaunch(_sched_fn("pkv_paged_decode_attention", schedule), _sched_args(args, schedule),
+                       "pkv_paged_decode_attention",
+                       (q, k_pool, v_pool, block_tables, context_lens, workspace, out, err, schedule))
 
 
 def bind_paged_decode_append_attention(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
-                                       scale, workspace, out, err=None) -> BoundLaunch:
+                                       scale, workspace, out, err=None, schedule=None) -> BoundLaunch:
     args, out = _decode_append_args(q, k_new, v_new, k_pool, v_pool, block_tables, context_lens,
                                     scale, workspace, out, err)
-    return BoundLaunch(_lib.load().pkv_paged_decode_append_attention, args,
-                       "pkv_paged_decode_append_attention",
+    return BoundLaunch(_sched_fn("pkv_paged_decode_append_attention", schedule),
+                       _sched_args(args, schedule), "pkv_paged_decode_append_attention",
                        (q, k_new, v_new, k_pool, v_pool, block_tables, context_lens, workspace, out,
-                        err))
+                        err, schedule))
 
 
 def _prefill_args(q, k_pool, v_pool, block_tables, query_start_loc, num_prior, max_query_len,
@@ -568,17 +625,17 @@ def bind_reshape_and_cache_fp8(k, v, k_pool, v_pool, k_scale, v_scale, slot_mapp
 
 
 def bind_paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
-                                    scale, workspace, out, err=None) -> BoundLaunch:
+                                    scale, workspace, out, err=None, schedule=None) -> BoundLaunch:
     nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
     paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens, scale,
-                               workspace, out, err)  # validates (and runs once)
+                               workspace, out, err, schedule)  # validates (and runs once)
     B, hq, _ = q.shape
     args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
             k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
             block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
             context_lens.data_ptr(), B, hq, hkv, d, bs, float(scale), dtype_code(q.dtype),
             workspace.data_ptr(), workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
-    return BoundLaunch(_lib.load().pkv_paged_decode_attention_fp8, args,
-                       "pkv_paged_decode_attention_fp8",
+    return BoundLaunch(_sched_fn("pkv_paged_decode_attention_fp8", schedule),
+                       _sched_args(args, schedule), "pkv_paged_decode_attention_fp8",
                        (q, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens, workspace,
-                        out, err))
+                        out, err, schedule))

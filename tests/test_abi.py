@@ -46,7 +46,7 @@ def test_header_constants_match_binding():
                  "UNSUPPORTED", "DRIVER"):
         assert d[f"PKV_ERR_{name}"] == getattr(_lib, f"ERR_{name}")
     for name in ("SLOT_OUT_OF_RANGE", "BLOCK_OUT_OF_RANGE", "CONTEXT_EXCEEDS_TABLE",
-                 "PIPELINE_TIMEOUT", "BAD_QUERY_LAYOUT", "POSITION_OUT_OF_RANGE"):
+                 "PIPELINE_TIMEOUT", "BAD_QUERY_LAYOUT", "POSITION_OUT_OF_RANGE", "BAD_SCHEDULE"):
         assert d[f"PKV_FLAG_{name}"] == getattr(_lib, f"FLAG_{name}")
 
 
@@ -99,6 +99,39 @@ def test_copy_blocks_peer_validation():
     assert call(L=70000) == _lib.ERR_UNSUPPORTED
     assert call(bb=4100, dls=8 * 4100, sls=8 * 4100) == _lib.ERR_MISALIGNED
     assert call(dk=ctypes.c_void_p(0x10008)) == _lib.ERR_MISALIGNED
+
+
+def test_decode_schedule_validation():
+    L = _lib.load()
+    nbytes = L.pkv_decode_schedule_bytes(256, 512)
+    assert nbytes >= 4 * (256 * 512 + 2 * 256 + 1)
+    assert L.pkv_decode_schedule_bytes(-1, 4) == 0
+    A = ctypes.c_void_p(0x10000)
+    ok = dict(s=A, sb=nbytes, tabs=A, bts=512, mb=512, ctx=A, B=256, nb=4096, hq=14, hkv=2, d=64,
+              bs=16, dt=1, fp8=0, err=None, stream=None)
+
+    def call(**kw):
+        a = dict(ok)
+        a.update(kw)
+        return L.pkv_decode_schedule(*a.values())
+
+    assert call(s=None) == _lib.ERR_NULL_POINTER
+    assert call(ctx=None) == _lib.ERR_NULL_POINTER
+    assert call(s=ctypes.c_void_p(0x10004)) == _lib.ERR_MISALIGNED
+    assert call(sb=nbytes - 4) == _lib.ERR_WORKSPACE_TOO_SMALL
+    assert call(B=-1) == _lib.ERR_BAD_SHAPE
+    assert call(hq=13) == _lib.ERR_BAD_SHAPE
+    assert call(bts=100) == _lib.ERR_BAD_SHAPE
+    assert call(dt=9) == _lib.ERR_BAD_DTYPE
+    assert call(B=0) == _lib.OK
+    # the scheduled decode entries check the schedule pointer before anything else
+    d = dict(out=FAKE, out_stride=896, q=FAKE, q_stride=896, k_pool=FAKE, v_pool=FAKE,
+             num_blocks=64, tables=FAKE, bt_stride=8, max_blocks=8, ctx=FAKE, n_seqs=4, hq=14,
+             hkv=2, d=64, bs=16, scale=0.125, dtype=1, ws=FAKE, ws_bytes=1 << 30, err=None,
+             stream=None)
+    f = L.pkv_paged_decode_attention_scheduled
+    assert f(*d.values(), None) == _lib.ERR_NULL_POINTER
+    assert f(*d.values(), ctypes.c_void_p(0x10008)) == _lib.ERR_MISALIGNED
 
 
 def test_ipc_validation():

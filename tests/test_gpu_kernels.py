@@ -687,3 +687,99 @@ def test_forward_layer_fp8_pools_and_cow(oracle_mod):
     assert src != dst
     assert torch.equal(m.k_cache[:, dst], m.k_cache[:, src])
     assert torch.equal(m.v_scale_cache[:, dst], m.v_scale_cache[:, src])
+
+
+# ---------------------------------------------------------------- per-step decode schedule
+
+def _sched_for(tabs, ctx, q, fp8=False, err=None):
+    s = ops.new_decode_schedule(ctx.shape[0], tabs.shape[1], "cuda")
+    s.random_(0, 255)  # the builder needs no initialised buffer
+    return ops.build_decode_schedule(s, tabs, ctx, NB_SCHED[0], q.shape[1], 2, q.shape[2], q.dtype,
+                                     fp8=fp8, err=err)
+
+
+NB_SCHED = [0]
+
+
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+@pytest.mark.parametrize("case", ("c3", "ragged", "edge"))
+def test_scheduled_decode_bit_identical(oracle_mod, dt, case):
+    """pkv_decode_schedule + the _scheduled decode calls (plain and fused
+    append) give the same bits as the unscheduled calls (the same stream-K
+    partition and arithmetic), and match the oracle."""
+    if case == "c3":
+        c = C.make_decode_case(3, 256, 16, 8192, 0, dt, lognormal_median=1024.0, pool_slack=1.1)
+    elif case == "ragged":
+        rng = np.random.default_rng(31)
+        ctx = rng.integers(1, 40, size=700).tolist()
+        ctx[5], ctx[300], ctx[699] = 8192, 5000, 4097
+        c = C.make_decode_case(31, len(ctx), 0, 0, sum((x + 15) // 16 for x in ctx) + 5, dt,
+                               ctx_list=ctx)
+    else:
+        c = C.make_decode_case(11, 9, 0, 0, 128, dt, ctx_list=[1, 2, 15, 16, 17, 31, 32, 33, 600])
+    NB_SCHED[0] = c["k_pool"].shape[0]
+    tabs, ctx = dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
+    q, kn, vn = dev(c["q"], dt), dev(c["k_new"], dt), dev(c["v_new"], dt)
+    err = ops.new_error_flags("cuda")
+    sched = _sched_for(tabs, ctx, q, err=err)
+    outs = {}
+    for mode in ("plain", "sched"):
+        kp, vp = dev(c["k_pool"], dt), dev(c["v_pool"], dt)
+        s = sched if mode == "sched" else None
+        o1 = ops.paged_decode_append_attention(q, kn, vn, kp, vp, tabs, ctx, 0.125, err=err,
+                                               schedule=s)
+        o2 = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err, schedule=s)
+        outs[mode] = (o1, o2, kp, vp)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for a, b in zip(outs["plain"], outs["sched"]):
+        assert torch.equal(a, b)
+    ref, ref_k, _ = oracle_mod.run_decode_case(c)
+    assert np.array_equal(host(outs["sched"][2], dt), ref_k)
+    assert max_abs_diff(host(outs["sched"][0], dt), ref, dt) <= PRODUCT_ATOL[dt]
+
+
+def test_scheduled_decode_reused_across_layers_and_fp8(oracle_mod):
+    """One schedule serves several layers' pools (the step's 24 calls), and
+    an fp8 schedule serves the fp8 decode bit-identically."""
+    c = C.make_decode_case(3, 256, 16, 8192, 0, "f16", lognormal_median=1024.0, pool_slack=1.1)
+    NB_SCHED[0] = c["k_pool"].shape[0]
+    tabs, ctx = dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
+    q = dev(c["q"], "f16")
+    err = ops.new_error_flags("cuda")
+    sched = _sched_for(tabs, ctx, q, err=err)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for _ in range(3):
+        kp = torch.randn(dev(c["k_pool"], "f16").shape, generator=g, device="cuda", dtype=torch.float16)
+        vp = torch.randn_like(kp)
+        a = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err)
+        b = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err, schedule=sched)
+        assert torch.equal(a, b)
+    k8 = torch.randint(0, 256, kp.shape, generator=g, device="cuda", dtype=torch.uint8)
+    k8[(k8 & 0x7f) == 0x7f] = 0  # no NaN encodings in live rows
+    v8 = torch.randint(0, 256, kp.shape, generator=g, device="cuda", dtype=torch.uint8)
+    v8[(v8 & 0x7f) == 0x7f] = 0
+    ks = torch.rand(kp.shape[:3], generator=g, device="cuda") + 0.5
+    vs = torch.rand(kp.shape[:3], generator=g, device="cuda") + 0.5
+    s8 = _sched_for(tabs, ctx, q, fp8=True, err=err)
+    a = ops.paged_decode_attention_fp8(q, k8, v8, ks, vs, tabs, ctx, 0.125, err=err)
+    b = ops.paged_decode_attention_fp8(q, k8, v8, ks, vs, tabs, ctx, 0.125, err=err, schedule=s8)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(a, b)
+
+
+def test_scheduled_decode_rejects_foreign_schedule():
+    """A schedule built for another batch size: the decode call sets
+    PKV_FLAG_BAD_SCHEDULE (its output rows are then unspecified)."""
+    c = C.make_decode_case(11, 9, 0, 0, 128, "f16", ctx_list=[1, 2, 15, 16, 17, 31, 32, 33, 600])
+    NB_SCHED[0] = c["k_pool"].shape[0]
+    tabs, ctx = dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
+    q = dev(c["q"], "f16")
+    kp, vp = dev(c["k_pool"], "f16"), dev(c["v_pool"], "f16")
+    sched = _sched_for(tabs[:5], ctx[:5], q[:5])
+    err = ops.new_error_flags("cuda")
+    out = torch.full_like(q, 7.0)
+    ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, out=out, err=err, schedule=sched)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_BAD_SCHEDULE
