@@ -6,9 +6,13 @@
 //
 // Design (HBM-bound: every KV byte is read exactly once):
 //  * Stream-K split.  The flattened list of all sequences' KV blocks is cut
-//    into gridDim.x equal ranges, one per persistent CTA (grid = SMs x
-//    resident CTAs), so lognormal context lengths cannot unbalance the GPU.
-//    A CTA walks its range as segments (one per sequence it touches).
+//    into equal ranges, one per pipeline (a "virtual CTA": a producer warp,
+//    one consumer warp per KV head and their own ring), so lognormal context
+//    lengths cannot unbalance the GPU.  A pipeline walks its range as
+//    segments (one per sequence it touches).  For two KV heads one CTA per
+//    SM holds 5 pipelines (the register limit of 5 one-pipeline CTAs), so a
+//    launch starts 148 CTAs instead of 740 and reads the step's metadata
+//    once per SM; other head counts run one pipeline per CTA.
 //  * Producer warp: TMA tensor loads (cp.async.bulk.tensor, 128-byte swizzle)
 //    of each 16-token block, one 16x64 tile per KV head for K and for V,
 //    into a kStages-deep shared-memory ring guarded by mbarriers
@@ -279,14 +283,23 @@ __device__ __forceinline__ int partial_slot(int c, int per, int blk_lo) {
   return (blk_lo > c * per) ? 2 * c + 1 : 2 * c;
 }
 
-template <typename T, int NKV, bool FP8>
-__global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
+template <typename T, int NKV, bool FP8, int PIPES>
+__global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DEC_MIN_CTAS)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int nkv = NKV;
   const int B = p.n_seqs;
+  // PIPES independent pipelines (a producer warp and nkv consumer warps each,
+  // with their own ring) per CTA, each serving one stream-K range (a
+  // "virtual CTA"): one CTA per SM starts all of them together and does the
+  // metadata prologue once
+  constexpr int kPw = NKV + 1;
+  const int pipe = warp / kPw;
+  const int pwarp = warp - pipe * kPw;
+  const int vcta = blockIdx.x * PIPES + pipe;
+  const int vgrid = gridDim.x * PIPES;
 
   // ---- shared memory carve-up (tiles 1024-byte aligned for the 128B swizzle)
   const uint32_t raw = smem_u32(smem_raw);
@@ -295,10 +308,11 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   constexpr int tile_bytes = FP8 ? kDecTile8 : kDecTile;
   constexpr int scale_bytes = FP8 ? 16 * nkv * 4 : 0;
   constexpr int stage_bytes = 2 * nkv * tile_bytes + 2 * scale_bytes;
-  uint8_t* tiles = base;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tiles + kDecStages * stage_bytes);
+  uint8_t* tiles = base + pipe * (kDecStages * stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + PIPES * (kDecStages * stage_bytes));
+  uint64_t* full_bar = bars + pipe * (2 * kDecStages);
   uint64_t* empty_bar = full_bar + kDecStages;
-  int* misc = reinterpret_cast<int*>(empty_bar + kDecStages);  // [1..9]: scan scratch
+  int* misc = reinterpret_cast<int*>(bars + PIPES * (2 * kDecStages));  // [1..33]: scan scratch
   int* prefix = misc + 40;                           // [B+1]
   int* ctxs = prefix + (B + 1);                      // [B]
 
@@ -311,13 +325,13 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     const int32_t* sp = p.sched + kSchedHdr;
     for (int s = tid; s <= B; s += blockDim.x) prefix[s] = __ldg(sp + s);
     for (int s = tid; s < B; s += blockDim.x) ctxs[s] = __ldg(sp + B + 1 + s);
-    if (warp == nkv && lane < p.sched_rows)
-      sched_id0 = __ldg(p.sched + sched_ids_offset(B) + static_cast<int64_t>(blockIdx.x) * p.sched_rows + lane);
+    if (pwarp == nkv && lane < p.sched_rows)
+      sched_id0 = __ldg(p.sched + sched_ids_offset(B) + static_cast<int64_t>(vcta) * p.sched_rows + lane);
     total = __ldg(p.sched + 1);
     per = __ldg(p.sched + 2);
-    if (__ldg(p.sched) != B || __ldg(p.sched + 3) != static_cast<int>(gridDim.x)) {
+    if (__ldg(p.sched) != B || __ldg(p.sched + 3) != vgrid) {
       // a schedule built for another batch or grid: do nothing
-      if (tid == 0 && blockIdx.x == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
+      if (tid == 0 && vcta == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
       if (tid == 0) pdl_trigger();
       return;
     }
@@ -329,7 +343,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
       int c = p.context_lens[s];
       if (c < 0) c = 0;
       if (c > cap_tokens) {
-        if (blockIdx.x == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+        if (vcta == 0) raise_flag(p.err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
         c = cap_tokens;
       }
       ctxs[s] = c;
@@ -339,30 +353,27 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
     total = block_exclusive_scan(prefix, B, misc + 1);
     if (tid == 0) prefix[B] = total;
     __syncthreads();
-    per = max((total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x),
-              kDecMinBlocksPerCta);
+    per = max((total + vgrid - 1) / vgrid, kDecMinBlocksPerCta);
   }
   const int n_active = (total + per - 1) / per;
-  const bool active = static_cast<int>(blockIdx.x) < n_active;
+  const bool active = vcta < n_active;
 
   // the merge kernel behind this one may be scheduled now: it waits for this
   // grid's completion before it reads anything this grid writes
   if (tid == 0) pdl_trigger();
-  if (!active) return;
-
-  const int r0 = blockIdx.x * per;
-  const int r1 = min(r0 + per, total);
 
   if (tid == 0) {
-    for (int i = 0; i < kDecStages; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], nkv);
-    }
+    for (int i = 0; i < PIPES * 2 * kDecStages; ++i)
+      mbar_init(&bars[i], (i % (2 * kDecStages)) < kDecStages ? 1 : nkv);
     fence_barrier_init();
   }
   __syncthreads();
+  if (!active) return;
 
-  if (warp == nkv) {
+  const int r0 = vcta * per;
+  const int r1 = min(r0 + per, total);
+
+  if (pwarp == nkv) {
     // ======================= producer warp =======================
     if (lane == 0) {
       prefetch_tensormap(&kmap);
@@ -384,7 +395,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
           // validated by the schedule builder (a bad id is stored as -1)
           id = b0 == r0 ? sched_id0
                         : __ldg(p.sched + sched_ids_offset(B) +
-                                static_cast<int64_t>(blockIdx.x) * p.sched_rows + (gb - r0));
+                                static_cast<int64_t>(vcta) * p.sched_rows + (gb - r0));
         } else {
           id = __ldg(p.block_tables + static_cast<int64_t>(s) * p.bt_stride + jb);
           if (id < 0 || id >= p.num_blocks) {
@@ -471,7 +482,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
   //                   16-dim tile, B = P^T from C via movmatrix.trans,
   //                   C holds dims {16mt+g, 16mt+g+8} x heads {2t, 2t+1}.
   pdl_wait();
-  const int h = warp;
+  const int h = pwarp;
   const int g = lane >> 2, t = lane & 3;
   // fp8 conversion on the integer pipes (fp16) or by cvt (bf16)
   constexpr bool kF16 = std::is_same<T, __half>::value;
@@ -699,7 +710,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1), PKV_DEC_MIN_CTAS)
         }
       }
     } else {
-      const int slot = partial_slot(blockIdx.x, per, prefix[s]);
+      const int slot = partial_slot(vcta, per, prefix[s]);
       float* po = p.part_o + (static_cast<int64_t>(slot) * p.n_q_heads + qh0) * 64;
       float* pml = p.part_ml + static_cast<int64_t>(slot) * p.ml_stride + qh0 * 2;
       if constexpr (FP8) {
@@ -933,11 +944,20 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
   }
 }
 
+// pipelines (virtual CTAs) per CTA: one CTA per SM holds as many as 5 CTAs
+// of one pipeline would (the register limit) for two KV heads; other head
+// counts keep one pipeline per CTA
+#ifndef PKV_DEC_PIPES
+#define PKV_DEC_PIPES 5
+#endif
+constexpr int pipes_for(int nkv) { return nkv == 2 ? PKV_DEC_PIPES : 1; }
+
 size_t decode_smem_bytes(int nkv, int n_seqs, bool fp8) {
   const size_t stage = fp8 ? 2 * nkv * kDecTile8 + 2 * 16 * nkv * 4 : 2 * nkv * kDecTile;
-  return 1024 + static_cast<size_t>(kDecStages) * stage +
-         2 * kDecStages * sizeof(uint64_t) + 40 * sizeof(int) +
-         (2 * static_cast<size_t>(n_seqs) + 1) * sizeof(int);
+  return 1024 +
+         static_cast<size_t>(pipes_for(nkv)) *
+             (static_cast<size_t>(kDecStages) * stage + 2 * kDecStages * sizeof(uint64_t)) +
+         40 * sizeof(int) + (2 * static_cast<size_t>(n_seqs) + 1) * sizeof(int);
 }
 
 namespace {
@@ -960,20 +980,23 @@ using DecodeKernel = void (*)(const CUtensorMap, const CUtensorMap, const Decode
 template <bool FP8>
 DecodeKernel pick_kernel_t(int dtype, int nkv) {
   if (dtype == PKV_DTYPE_F16)
-    return nkv == 1 ? paged_decode_kernel<__half, 1, FP8>
-         : nkv == 2 ? paged_decode_kernel<__half, 2, FP8> : paged_decode_kernel<__half, 4, FP8>;
-  return nkv == 1 ? paged_decode_kernel<__nv_bfloat16, 1, FP8>
-       : nkv == 2 ? paged_decode_kernel<__nv_bfloat16, 2, FP8>
-                  : paged_decode_kernel<__nv_bfloat16, 4, FP8>;
+    return nkv == 1   ? paged_decode_kernel<__half, 1, FP8, pipes_for(1)>
+           : nkv == 2 ? paged_decode_kernel<__half, 2, FP8, pipes_for(2)>
+                      : paged_decode_kernel<__half, 4, FP8, pipes_for(4)>;
+  return nkv == 1   ? paged_decode_kernel<__nv_bfloat16, 1, FP8, pipes_for(1)>
+         : nkv == 2 ? paged_decode_kernel<__nv_bfloat16, 2, FP8, pipes_for(2)>
+                    : paged_decode_kernel<__nv_bfloat16, 4, FP8, pipes_for(4)>;
 }
 DecodeKernel pick_kernel(int dtype, int nkv, bool fp8) {
   return fp8 ? pick_kernel_t<true>(dtype, nkv) : pick_kernel_t<false>(dtype, nkv);
 }
 }  // namespace
 
-// the persistent grid of the decode kernel for this shape (cached occupancy)
+// the persistent grid of the decode kernel for this shape, in virtual CTAs
+// (pipelines; cached occupancy); the launch has grid / pipes_for(nkv) CTAs
 cudaError_t decode_grid(int dtype, int nkv, bool fp8, int n_seqs, int* grid_out) {
-  const int threads = 32 * (nkv + 1);
+  const int pipes = pipes_for(nkv);
+  const int threads = 32 * (nkv + 1) * pipes;
   const size_t smem = decode_smem_bytes(nkv, n_seqs, fp8);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -999,7 +1022,7 @@ cudaError_t decode_grid(int dtype, int nkv, bool fp8, int n_seqs, int* grid_out)
       if (e != cudaSuccess) return e;
       e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       if (e != cudaSuccess) return e;
-      it = g_occ.emplace(key, std::max(1, std::min(kDecMaxCtas, per_sm * sms))).first;
+      it = g_occ.emplace(key, pipes * std::max(1, std::min(kDecMaxCtas / pipes, per_sm * sms))).first;
     }
     grid = it->second;
   }
@@ -1043,7 +1066,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
                                void* workspace, cudaStream_t stream) {
   if (a.n_seqs == 0) return cudaSuccess;
   const int nkv = a.n_kv_heads;
-  const int threads = 32 * (nkv + 1);
+  const int threads = 32 * (nkv + 1) * pipes_for(nkv);
   const bool fp8 = a.k_scale != nullptr;
   const size_t smem = decode_smem_bytes(nkv, a.n_seqs, fp8);
   DecodeKernel kern = pick_kernel(a.dtype, nkv, fp8);
@@ -1092,7 +1115,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.sched_rows = a.schedule != nullptr ? sched_rows_for(a.n_seqs, a.max_blocks, grid) : 0;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(grid / pipes_for(nkv));
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
