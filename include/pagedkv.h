@@ -215,6 +215,17 @@ int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void
                                int n_tokens, int num_blocks, int block_size, int n_q_heads,
                                int n_kv_heads, int head_dim, int dtype, int* err_flags,
                                pkv_stream_t stream);
+/* The same for fp8 e4m3 pools (uint8 k_pool / v_pool): the rotated k and the
+ * v rows are quantised as pkv_reshape_and_cache_fp8 quantises them (one fp32
+ * scale per (slot, KV head) into k_scale / v_scale), bit-identical to rotating
+ * in `dtype` and calling it.  q_out stays in `dtype`. */
+int pkv_rope_reshape_and_cache_fp8(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                                   int64_t qkv_row_stride, const int64_t* positions,
+                                   const void* cos_table, const void* sin_table, int max_position,
+                                   void* k_pool, void* v_pool, float* k_scale, float* v_scale,
+                                   const int64_t* slot_mapping, int n_tokens, int num_blocks,
+                                   int block_size, int n_q_heads, int n_kv_heads, int head_dim,
+                                   int dtype, int* err_flags, pkv_stream_t stream);
 
 /*
  * Bytes of device workspace pkv_paged_decode_attention needs for n_seqs

@@ -262,13 +262,12 @@ int pkv_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_row_stride
                                                 static_cast<cudaStream_t>(stream)));
 }
 
-int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void* qkv,
-                               int64_t qkv_row_stride, const int64_t* positions,
-                               const void* cos_table, const void* sin_table, int max_position,
-                               void* k_pool, void* v_pool, const int64_t* slot_mapping,
-                               int n_tokens, int num_blocks, int block_size, int n_q_heads,
-                               int n_kv_heads, int head_dim, int dtype, int* err_flags,
-                               pkv_stream_t stream) {
+static int rope_entry(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                      int64_t qkv_row_stride, const int64_t* positions, const void* cos_table,
+                      const void* sin_table, int max_position, void* k_pool, void* v_pool,
+                      float* k_scale, float* v_scale, const int64_t* slot_mapping, int n_tokens,
+                      int num_blocks, int block_size, int n_q_heads, int n_kv_heads, int head_dim,
+                      int dtype, int* err_flags, pkv_stream_t stream) {
   if (n_tokens < 0) return PKV_ERR_BAD_SHAPE;
   if (n_tokens == 0) return PKV_OK;
   if (!q_out || !qkv || !positions || !cos_table || !sin_table || !k_pool || !v_pool ||
@@ -301,7 +300,36 @@ int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void
   a.head_dim = head_dim;
   a.dtype = dtype;
   a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
   return status_of(launch_rope_reshape_and_cache(a, static_cast<cudaStream_t>(stream)));
+}
+
+int pkv_rope_reshape_and_cache(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                               int64_t qkv_row_stride, const int64_t* positions,
+                               const void* cos_table, const void* sin_table, int max_position,
+                               void* k_pool, void* v_pool, const int64_t* slot_mapping,
+                               int n_tokens, int num_blocks, int block_size, int n_q_heads,
+                               int n_kv_heads, int head_dim, int dtype, int* err_flags,
+                               pkv_stream_t stream) {
+  return rope_entry(q_out, q_out_row_stride, qkv, qkv_row_stride, positions, cos_table, sin_table,
+                    max_position, k_pool, v_pool, nullptr, nullptr, slot_mapping, n_tokens,
+                    num_blocks, block_size, n_q_heads, n_kv_heads, head_dim, dtype, err_flags,
+                    stream);
+}
+
+int pkv_rope_reshape_and_cache_fp8(void* q_out, int64_t q_out_row_stride, const void* qkv,
+                                   int64_t qkv_row_stride, const int64_t* positions,
+                                   const void* cos_table, const void* sin_table, int max_position,
+                                   void* k_pool, void* v_pool, float* k_scale, float* v_scale,
+                                   const int64_t* slot_mapping, int n_tokens, int num_blocks,
+                                   int block_size, int n_q_heads, int n_kv_heads, int head_dim,
+                                   int dtype, int* err_flags, pkv_stream_t stream) {
+  if (n_tokens > 0 && (!k_scale || !v_scale)) return PKV_ERR_NULL_POINTER;
+  return rope_entry(q_out, q_out_row_stride, qkv, qkv_row_stride, positions, cos_table, sin_table,
+                    max_position, k_pool, v_pool, k_scale, v_scale, slot_mapping, n_tokens,
+                    num_blocks, block_size, n_q_heads, n_kv_heads, head_dim, dtype, err_flags,
+                    stream);
 }
 
 int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, int n_layers,

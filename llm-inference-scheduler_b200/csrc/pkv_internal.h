@@ -27,6 +27,9 @@ struct RopeArgs {
   const int64_t* slots;
   int n_tokens, num_blocks, block_size, n_q_heads, n_kv_heads, head_dim, dtype;
   int* err;
+  // fp8 e4m3 pools: per-(slot, KV head) scales written with the bytes (NULL: 16/32-bit pools)
+  float* k_scale = nullptr;
+  float* v_scale = nullptr;
 };
 cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream);
 

@@ -99,6 +99,90 @@ __global__ void __launch_bounds__(256) rope_reshape_and_cache_kernel(
   }
 }
 
+// fp8 e4m3 pools: the same rotation, then the rotated k and the v rows are
+// quantised per (token, KV head) exactly as reshape_and_cache_fp8 quantises
+// its input (scale = absmax / 448, value = e4m3(x / scale), RNE, saturated):
+// bit-identical to rotating in the model dtype and calling that append.  A
+// head's values are produced twice by each lane (once for the warp absmax,
+// once to quantise), so any head_dim works.
+template <typename E>
+__global__ void __launch_bounds__(256) rope_reshape_and_cache_fp8_kernel(
+    E* __restrict__ q_out, int64_t q_out_stride, const E* __restrict__ qkv, int64_t qkv_stride,
+    const int64_t* __restrict__ positions, const E* __restrict__ cos_t,
+    const E* __restrict__ sin_t, int64_t max_pos, uint8_t* __restrict__ k_pool,
+    uint8_t* __restrict__ v_pool, float* __restrict__ k_scale, float* __restrict__ v_scale,
+    const int64_t* __restrict__ slots, int64_t n_slots, int n_tokens, int hq, int hkv, int d,
+    int* err) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const int64_t pos = __ldg(positions + t);
+  if (pos < 0 || pos >= max_pos) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t slot = __ldg(slots + t);
+  if (slot >= n_slots) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
+  }
+  const bool store_kv = slot >= 0 && slot < n_slots;  // slot -1: padding token
+  const E* row = qkv + static_cast<int64_t>(t) * qkv_stride;
+  const E* cr = cos_t + pos * d;
+  const E* sr = sin_t + pos * d;
+  const int half = d >> 1;
+  E* qrow = q_out + static_cast<int64_t>(t) * q_out_stride;
+  // rotated element pair (i, i + half) of head h of the projection row
+  auto rot = [&](int h, int i, E& o1, E& o2) {
+    const float c1 = tof<E>(__ldg(cr + i)), c2 = tof<E>(__ldg(cr + i + half));
+    const float s1 = tof<E>(__ldg(sr + i)), s2 = tof<E>(__ldg(sr + i + half));
+    const E* x = row + h * d;
+    const float x1 = tof<E>(__ldg(x + i)), x2 = tof<E>(__ldg(x + i + half));
+    o1 = rot_term<E>(x1, c1, -x2, s1);
+    o2 = rot_term<E>(x2, c2, x1, s2);
+  };
+  for (int h = 0; h < hq; ++h) {
+    for (int i = lane; i < half; i += 32) {
+      E o1, o2;
+      rot(h, i, o1, o2);
+      qrow[h * d + i] = o1;
+      qrow[h * d + i + half] = o2;
+    }
+  }
+  if (!store_kv) return;
+  for (int h = 0; h < hkv; ++h) {
+    // k: rotated
+    float amax = 0.f;
+    for (int i = lane; i < half; i += 32) {
+      E o1, o2;
+      rot(hq + h, i, o1, o2);
+      amax = fmaxf(amax, fmaxf(fabsf(tof<E>(o1)), fabsf(tof<E>(o2))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float sc = fp8_row_scale(amax);
+    uint8_t* kd = k_pool + (slot * hkv + h) * d;
+    for (int i = lane; i < half; i += 32) {
+      E o1, o2;
+      rot(hq + h, i, o1, o2);
+      kd[i] = fp8_quantize(tof<E>(o1), sc);
+      kd[i + half] = fp8_quantize(tof<E>(o2), sc);
+    }
+    if (lane == 0) k_scale[slot * hkv + h] = sc;
+    // v: as projected
+    const E* vsrc = row + (hq + hkv + h) * d;
+    amax = 0.f;
+    for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(tof<E>(__ldg(vsrc + i))));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    sc = fp8_row_scale(amax);
+    uint8_t* vd = v_pool + (slot * hkv + h) * d;
+    for (int i = lane; i < d; i += 32) vd[i] = fp8_quantize(tof<E>(__ldg(vsrc + i)), sc);
+    if (lane == 0) v_scale[slot * hkv + h] = sc;
+  }
+}
+
 cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream) {
   if (a.n_tokens == 0) return cudaSuccess;
   const int threads = 256;
@@ -115,6 +199,14 @@ cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream
   const int64_t n_slots = static_cast<int64_t>(a.num_blocks) * a.block_size;
   auto go = [&](auto tag) {
     using E = decltype(tag);
+    if (a.k_scale != nullptr)
+      return cudaLaunchKernelEx(&cfg, rope_reshape_and_cache_fp8_kernel<E>, static_cast<E*>(a.q_out),
+                                a.q_out_stride, static_cast<const E*>(a.qkv), a.qkv_stride,
+                                a.positions, static_cast<const E*>(a.cos_t),
+                                static_cast<const E*>(a.sin_t), static_cast<int64_t>(a.max_pos),
+                                static_cast<uint8_t*>(a.k_pool), static_cast<uint8_t*>(a.v_pool),
+                                a.k_scale, a.v_scale, a.slots, n_slots, a.n_tokens, a.n_q_heads,
+                                a.n_kv_heads, a.head_dim, a.err);
     return cudaLaunchKernelEx(&cfg, rope_reshape_and_cache_kernel<E>, static_cast<E*>(a.q_out),
                               a.q_out_stride, static_cast<const E*>(a.qkv), a.qkv_stride,
                               a.positions, static_cast<const E*>(a.cos_t),

@@ -557,9 +557,15 @@ class PagedKVCache:
         """forward_layer over fp8 pools: the quantising append of every token,
         then decode and chunked prefill over the fp8 pools."""
         mgr = self.mgr
+        ops.reshape_and_cache_fp8(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer],
+                                  mgr.k_scale[layer], mgr.v_scale[layer], meta.slot_mapping, mgr.err)
+        return self._attend_fp8(layer, q, meta, scale, out, advance)
+
+    def _attend_fp8(self, layer, q, meta, scale, out, advance):
+        """The step's attention launches over fp8 pools whose rows are already
+        appended: decode (with the step's schedule) and chunked prefill."""
+        mgr = self.mgr
         ks, vs = mgr.k_scale[layer], mgr.v_scale[layer]
-        ops.reshape_and_cache_fp8(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
-                                  meta.slot_mapping, mgr.err)
         nd = meta.n_decode
         if nd:
             ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
@@ -586,10 +592,13 @@ class PagedKVCache:
         prefill).  Returns out [T, Hq, D].  Same results as rotating q and k
         with Rope.rotate and calling forward_layer."""
         mgr = self.mgr
-        if mgr.fp8:
-            raise NotImplementedError("pagedkv: forward_layer_qkv writes 16-bit pools; with fp8 "
-                                      "pools rotate q and k and call forward_layer")
         mgr.flush_copies()
+        if mgr.fp8:  # rotated k and v quantised into the fp8 pools in the same launch
+            q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer],
+                                           mgr.v_pool[layer], meta.slot_mapping, err=mgr.err,
+                                           k_scale=mgr.k_scale[layer], v_scale=mgr.v_scale[layer])
+            return self._attend_fp8(layer, q, meta, scale, torch.empty_like(q) if out is None else out,
+                                    advance)
         q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer], mgr.v_pool[layer],
                                        meta.slot_mapping, err=mgr.err)
         if out is None:

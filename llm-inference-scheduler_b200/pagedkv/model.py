@@ -166,7 +166,7 @@ class PagedQwen2Model:
         pos_np = np.concatenate([s.positions for s in seq_infos]).astype(np.int64)
         positions = torch.from_numpy(pos_np).pin_memory().to(self.device, non_blocking=True)
         cos_t, sin_t = self.rope.tables(int(pos_np.max()) + 1)
-        fused = self.fused_rope and not kv_cache.mgr.fp8  # the fused kernel writes 16-bit pools
+        fused = self.fused_rope
         if not fused:
             cos, sin = cos_t[positions].unsqueeze(1), sin_t[positions].unsqueeze(1)
         timing = self.timing

@@ -173,7 +173,8 @@ def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device) -> 
 def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor,
                            sin: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                            slot_mapping: torch.Tensor, q_out: torch.Tensor | None = None,
-                           err: torch.Tensor | None = None) -> torch.Tensor:
+                           err: torch.Tensor | None = None, k_scale: torch.Tensor | None = None,
+                           v_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Rotary embedding of q and k fused with the append.
 
     qkv: [T, (Hq + 2 Hkv) * D] rows of the fused q/k/v projection (unit inner
@@ -184,6 +185,10 @@ def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torc
     elementwise multiply/add operations (pagedkv.model.Rope.rotate) followed
     by reshape_and_cache.  Reference: qwen2.py:152-158 (RoPE before the
     append, K cached post-RoPE) + block_manager.py:121-131.
+
+    fp8 e4m3 pools (uint8 k_pool / v_pool, fp32 k_scale / v_scale [NB, bs,
+    Hkv]): the rotated k and the v rows are quantised as reshape_and_cache_fp8
+    quantises them, bit-identical to rotating and calling it.
     """
     for t, n in ((qkv, "qkv"), (positions, "positions"), (cos, "cos"), (sin, "sin"),
                  (k_pool, "k_pool"), (v_pool, "v_pool"), (slot_mapping, "slot_mapping")):
@@ -196,7 +201,12 @@ def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torc
     if not (k_pool.is_contiguous() and v_pool.is_contiguous() and cos.is_contiguous() and sin.is_contiguous()):
         raise ValueError("pagedkv: pools and rope tables must be contiguous")
     dt = qkv.dtype
-    if any(t.dtype != dt for t in (cos, sin, k_pool, v_pool)):
+    fp8 = k_scale is not None or v_scale is not None
+    if fp8:
+        _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+        if cos.dtype != dt or sin.dtype != dt:
+            raise TypeError("pagedkv: the rope tables must have the qkv dtype")
+    elif any(t.dtype != dt for t in (cos, sin, k_pool, v_pool)):
         raise TypeError("pagedkv: qkv, the rope tables and the pools must share one dtype")
     nb, bs, hkv, d = k_pool.shape
     T, W = qkv.shape
@@ -209,6 +219,14 @@ def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torc
     elif q_out.dtype != dt or tuple(q_out.shape) != (T, hq, d):
         raise ValueError("pagedkv: q_out must be [tokens, n_q_heads, head_dim] in the qkv dtype")
     if T == 0:
+        return q_out
+    if fp8:
+        rc = _lib.load().pkv_rope_reshape_and_cache_fp8(
+            q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),
+            positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], k_pool.data_ptr(),
+            v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), slot_mapping.data_ptr(), T,
+            nb, bs, hq, hkv, d, dtype_code(dt), _ptr(err), _stream(qkv))
+        _lib.check(rc, "pkv_rope_reshape_and_cache_fp8")
         return q_out
     rc = _lib.load().pkv_rope_reshape_and_cache(
         q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),

@@ -783,3 +783,89 @@ def test_scheduled_decode_rejects_foreign_schedule():
     ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, out=out, err=err, schedule=sched)
     torch.cuda.synchronize()
     assert int(err.item()) & _lib.FLAG_BAD_SCHEDULE
+
+
+# ---------------------------------------------------------------- fused RoPE + fp8 append
+
+@pytest.mark.parametrize("dt", DTS)
+def test_rope_reshape_and_cache_fp8_bit_identical(dt):
+    """pkv_rope_reshape_and_cache_fp8 against the unfused path: Rope.rotate in
+    the model dtype, then reshape_and_cache_fp8.  Rotated q, the e4m3 bytes
+    and the scales must be identical bit for bit; a padding slot (-1) writes
+    q only."""
+    from pagedkv.model import Rope
+
+    tdt = TORCH_DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(64)
+    T, hq, hkv, d, nb = 200, 14, 2, 64, 64
+    rope = Rope(d, 1e6, "cuda", tdt)
+    cos, sin = rope.tables(5000)
+    qkv = (3 * torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda")).to(tdt)
+    pos = torch.randint(0, 5000, (T,), generator=g, device="cuda")
+    slots = torch.randperm(nb * 16, generator=g, device="cuda")[:T]
+    slots[7] = -1
+    kp = torch.randint(0, 255, (nb, 16, hkv, d), generator=g, device="cuda", dtype=torch.uint8)
+    vp = torch.randint(0, 255, (nb, 16, hkv, d), generator=g, device="cuda", dtype=torch.uint8)
+    ks = torch.rand((nb, 16, hkv), generator=g, device="cuda")
+    vs = torch.rand((nb, 16, hkv), generator=g, device="cuda")
+    ref = [t.clone() for t in (kp, vp, ks, vs)]
+    err = ops.new_error_flags("cuda")
+    q = ops.rope_reshape_and_cache(qkv, pos, cos, sin, kp, vp, slots, err=err, k_scale=ks, v_scale=vs)
+    c, s = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+    q_ref = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), c, s)
+    k_ref = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), c, s)
+    v_ref = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+    ops.reshape_and_cache_fp8(k_ref.contiguous(), v_ref.contiguous(), *ref, slots)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(q, q_ref)
+    for a, b in zip((kp, vp, ks, vs), ref):
+        assert torch.equal(a, b)
+
+
+def test_forward_layer_qkv_fp8_equals_forward_layer_fp8():
+    """Over fp8 pools, forward_layer_qkv (fused RoPE + quantising append, then
+    the fp8 decode and prefill) equals rotating in torch and calling
+    forward_layer, bit for bit (pools, scales and outputs)."""
+    from pagedkv.model import Rope
+
+    tdt = torch.float16
+    g = torch.Generator(device="cuda").manual_seed(65)
+    L, nb, hq, hkv, d = 2, 256, 14, 2, 64
+    plan = [(0, 100, 1), (1, 17, 1), (2, 0, 1), (3, 48, 30), (4, 5, 64), (5, 31, 1)]
+    caches = []
+    for _ in range(2):
+        m = BlockManager(nb, 16, L, hkv, d, device="cuda", dtype=torch.float8_e4m3fn)
+        kv = PagedKVCache(m)
+        o = 0
+        for s, prior, n in plan:
+            nblk = (prior + n + 15) // 16
+            kv.add_sequence(s, list(range(o, o + nblk)), prior)
+            o += nblk
+        caches.append((m, kv))
+    src = torch.randn((L, nb * 16, hkv, d), generator=g, device="cuda").to(tdt)
+    allslots = torch.arange(nb * 16, device="cuda")
+    for m, _ in caches:
+        for layer in range(L):
+            ops.reshape_and_cache_fp8(src[layer], src[layer], m.k_pool[layer], m.v_pool[layer],
+                                      m.k_scale[layer], m.v_scale[layer], allslots)
+    metas = [kv.prepare_step([(s, n) for s, _, n in plan]) for _, kv in caches]
+    T = metas[0].n_tokens
+    pos = torch.from_numpy(np.concatenate([np.arange(p, p + n) for _, p, n in plan])).cuda()
+    cos, sin = Rope(d, 1e6, "cuda", tdt).tables(4096)
+    for layer in range(L):
+        qkv = torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda").to(tdt)
+        out_a = caches[0][1].forward_layer_qkv(layer, qkv, pos, cos, sin, metas[0], 0.125)
+        c, s_ = cos[pos].unsqueeze(1), sin[pos].unsqueeze(1)
+        q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), c, s_)
+        k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), c, s_)
+        v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+        out_b = caches[1][1].forward_layer(layer, q, k.contiguous(), v.contiguous(), metas[1], 0.125)
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, out_b)
+    for a, b in ((caches[0][0].k_cache, caches[1][0].k_cache), (caches[0][0].v_cache, caches[1][0].v_cache),
+                 (caches[0][0].k_scale_cache, caches[1][0].k_scale_cache),
+                 (caches[0][0].v_scale_cache, caches[1][0].v_scale_cache)):
+        assert torch.equal(a, b)
+    for m, _ in caches:
+        m.check_errors()
