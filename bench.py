@@ -63,7 +63,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
     ap.add_argument("--strong", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--e2e-steps", type=int, default=50, help="e2e: steps per timing window")
+    ap.add_argument("--e2e-windows", type=int, default=5, help="e2e: timing windows (median reported)")
     ap.add_argument("--e2e-chunks", default="2,4,6,6,4,2",
                     help="e2e: layers per chunk (comma list summing to --layers); each chunk's copies "
                          "overlap the other chunks' compute")
@@ -402,19 +403,25 @@ def run_ours(args):
                 hout[sl].copy_(out[sl], non_blocking=True)
         cur.wait_stream(d2h_s)
 
-    for _ in range(3):
+    for _ in range(10):
         e2e_step()
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.e2e_steps):
-        e2e_step()
-    e1.record()
+    # the step is host-bound (Python enqueues every copy and launch), so host
+    # hiccups on a shared machine move its mean: time it in windows of steps
+    # back to back and report the median window (all windows in the line)
+    n_win = max(1, args.e2e_windows)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_win + 1)]
+    evs[0].record()
+    for w in range(n_win):
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        evs[w + 1].record()
     torch.cuda.synchronize()
     barrier()
     ops.check_flags(err, "bench e2e")
-    e2e_ms = W.max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    win_ms = [evs[w].elapsed_time(evs[w + 1]) / args.e2e_steps for w in range(n_win)]
+    e2e_ms = W.max_over_ranks(statistics.median(win_ms))
     h2d = hqkv.numel() * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
     d2h = hout.numel() * 2
 
@@ -455,6 +462,8 @@ def run_ours(args):
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4), "api": "PagedKVCache.prepare_step + forward_layer",
+                "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back",
+                "windows_ms_per_step": [round(x, 4) for x in win_ms],
                 "copies": f"pinned host buffers; per step: metadata, then q|k|v of 24 layers H2D in "
                           f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
                           "on a second copy stream, overlapped with the step's own compute; the step ends "
