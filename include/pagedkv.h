@@ -106,6 +106,31 @@ int pkv_copy_blocks(void* k_pools, void* v_pools, int64_t layer_stride_bytes, in
                     int64_t block_bytes, int* err_flags, pkv_stream_t stream);
 
 /*
+ * The fp8 decode step of one layer in one launch: each sequence's new K/V
+ * token (k_new / v_new rows in `dtype`) is quantised into the fp8 pools at
+ * position context_lens[s] - 1 (as pkv_reshape_and_cache_fp8 quantises it,
+ * with its scales) by the decode kernel itself, then the fp8 decode
+ * attention runs (pkv_paged_decode_attention_fp8 semantics).  Replaces, for
+ * fp8 pools, the scatter of PagedKVCache.append_and_fetch
+ * (mini_engine/paged/block_manager.py:121-131) plus the decode attention.
+ */
+int pkv_paged_decode_append_attention_fp8(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, float* k_scale, float* v_scale, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream);
+int pkv_paged_decode_append_attention_fp8_scheduled(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, float* k_scale, float* v_scale, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule);
+
+/*
  * Per-step decode schedule.  All layers of a decode step share the block
  * tables and context lengths, so the stream-K partition of the step's blocks
  * over the decode kernel's persistent CTAs is the same for every layer.

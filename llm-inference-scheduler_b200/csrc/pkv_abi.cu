@@ -606,6 +606,96 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
   return status_of(launch_generic_attention(a, st));
 }
 
+static int pkv_paged_decode_append_attention_fp8_impl(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, float* k_scale, float* v_scale, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule) {
+  if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!context_lens || !k_new || !v_new || !k_scale || !v_scale) return PKV_ERR_NULL_POINTER;
+  const int64_t kv_row = static_cast<int64_t>(n_kv_heads) * head_dim;
+  if (k_new_row_stride < kv_row || v_new_row_stride < kv_row) return PKV_ERR_BAD_SHAPE;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.context_lens = context_lens;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_seqs;
+  a.max_query_len = 1;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.schedule = schedule;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.k_new_stride = k_new_row_stride;
+  a.v_new_stride = v_new_row_stride;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a))
+    return decode_dispatch(a, workspace, workspace_bytes, st);
+  // separate quantising append (slot from the block table) + CUDA-core attention
+  cudaError_t e = launch_append_at_context_end_fp8(
+      k_new, v_new, k_new_row_stride, v_new_row_stride, k_pool, v_pool, k_scale, v_scale,
+      block_tables, block_table_stride, max_blocks_per_seq, context_lens, n_seqs, num_blocks,
+      block_size, n_kv_heads, head_dim, dtype, err_flags, st);
+  if (e != cudaSuccess) return status_of(e);
+  a.k_new = a.v_new = nullptr;
+  return decode_dispatch(a, workspace, workspace_bytes, st);
+}
+
+int pkv_paged_decode_append_attention_fp8(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, float* k_scale, float* v_scale, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream) {
+  return pkv_paged_decode_append_attention_fp8_impl(
+      out, out_row_stride, q, q_row_stride, k_new, v_new, k_new_row_stride, v_new_row_stride,
+      k_pool, v_pool, k_scale, v_scale, num_blocks, block_tables, block_table_stride,
+      max_blocks_per_seq, context_lens, n_seqs, n_q_heads, n_kv_heads, head_dim, block_size, scale,
+      dtype, workspace, workspace_bytes, err_flags, stream, nullptr);
+}
+
+int pkv_paged_decode_append_attention_fp8_scheduled(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_new,
+    const void* v_new, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pool,
+    void* v_pool, float* k_scale, float* v_scale, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule) {
+  if (!schedule) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  return pkv_paged_decode_append_attention_fp8_impl(
+      out, out_row_stride, q, q_row_stride, k_new, v_new, k_new_row_stride, v_new_row_stride,
+      k_pool, v_pool, k_scale, v_scale, num_blocks, block_tables, block_table_stride,
+      max_blocks_per_seq, context_lens, n_seqs, n_q_heads, n_kv_heads, head_dim, block_size, scale,
+      dtype, workspace, workspace_bytes, err_flags, stream, schedule);
+}
+
 int pkv_paged_decode_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                                const void* k_pool, const void* v_pool, int num_blocks,
                                const int32_t* block_tables, int64_t block_table_stride,

@@ -159,20 +159,60 @@ __global__ void __launch_bounds__(256) reshape_and_cache_fp8_kernel(
     if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
     return;
   }
-  for (int which = 0; which < 2; ++which) {
-    const E* src = which ? v + t * v_stride : k + t * k_stride;
-    uint8_t* dst = (which ? v_pool : k_pool) + slot * hkv * d;
-    float* sc = (which ? v_scale : k_scale) + slot * hkv;
-    for (int h = 0; h < hkv; ++h) {
-      float amax = 0.f;
-      for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(Elem<E>::to_f(src[h * d + i])));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float s = fp8_row_scale(amax);
-      for (int i = lane; i < d; i += 32) dst[h * d + i] = fp8_quantize(Elem<E>::to_f(src[h * d + i]), s);
-      if (lane == 0) sc[h] = s;
-    }
+  fp8_store_token<E>(k + t * k_stride, k_pool + slot * hkv * d, k_scale + slot * hkv, hkv, d, lane);
+  fp8_store_token<E>(v + t * v_stride, v_pool + slot * hkv * d, v_scale + slot * hkv, hkv, d, lane);
+}
+
+// append_at_context_end into fp8 pools: the quantising append of
+// reshape_and_cache_fp8 at the slot of each sequence's newest token.
+template <typename E>
+__global__ void __launch_bounds__(256) append_at_context_end_fp8(
+    const E* __restrict__ k, const E* __restrict__ v, int64_t k_stride, int64_t v_stride,
+    uint8_t* __restrict__ k_pool, uint8_t* __restrict__ v_pool, float* __restrict__ k_scale,
+    float* __restrict__ v_scale, const int32_t* __restrict__ tables, int64_t bt_stride,
+    int max_blocks, const int32_t* __restrict__ context_lens, int n_seqs, int num_blocks,
+    int block_size, int hkv, int d, int* err) {
+  const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= n_seqs) return;
+  const int ctx = context_lens[s];
+  if (ctx <= 0) return;
+  if (ctx > max_blocks * block_size) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_CONTEXT_EXCEEDS_TABLE);
+    return;
   }
+  const int blk = tables[static_cast<int64_t>(s) * bt_stride + (ctx - 1) / block_size];
+  if (blk < 0 || blk >= num_blocks) {
+    if (lane == 0) raise_flag(err, PKV_FLAG_BLOCK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t slot = static_cast<int64_t>(blk) * block_size + (ctx - 1) % block_size;
+  fp8_store_token<E>(k + s * k_stride, k_pool + slot * hkv * d, k_scale + slot * hkv, hkv, d, lane);
+  fp8_store_token<E>(v + s * v_stride, v_pool + slot * hkv * d, v_scale + slot * hkv, hkv, d, lane);
+}
+
+cudaError_t launch_append_at_context_end_fp8(const void* k, const void* v, int64_t k_stride,
+                                             int64_t v_stride, void* k_pool, void* v_pool,
+                                             float* k_scale, float* v_scale, const int32_t* tables,
+                                             int64_t bt_stride, int max_blocks,
+                                             const int32_t* context_lens, int n_seqs,
+                                             int num_blocks, int block_size, int n_kv_heads,
+                                             int head_dim, int src_dtype, int* err,
+                                             cudaStream_t stream) {
+  if (n_seqs == 0) return cudaSuccess;
+  const int grid = (n_seqs + 7) / 8;
+  auto go = [&](auto tag) {
+    using E = decltype(tag);
+    append_at_context_end_fp8<E><<<grid, 256, 0, stream>>>(
+        static_cast<const E*>(k), static_cast<const E*>(v), k_stride, v_stride,
+        static_cast<uint8_t*>(k_pool), static_cast<uint8_t*>(v_pool), k_scale, v_scale, tables,
+        bt_stride, max_blocks, context_lens, n_seqs, num_blocks, block_size, n_kv_heads, head_dim,
+        err);
+    return cudaGetLastError();
+  };
+  if (src_dtype == PKV_DTYPE_F32) return go(float{});
+  if (src_dtype == PKV_DTYPE_F16) return go(__half{});
+  return go(__nv_bfloat16{});
 }
 
 cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,

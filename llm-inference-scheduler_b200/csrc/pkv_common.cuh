@@ -392,6 +392,24 @@ __device__ __forceinline__ float fp8_row_scale(float absmax) {
 __device__ __forceinline__ uint8_t fp8_quantize(float x, float scale) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(__fdiv_rn(x, scale), __NV_SATFINITE, __NV_E4M3));
 }
+// Warp-collective fp8 append of one token: its n_heads rows of d values of
+// type E (src, row h at src + h * d) quantised per row (scale = absmax / 448,
+// e4m3 bytes, RNE, saturated) into dst (bytes, row h at dst + h * d) with the
+// scales in sc[h].  Every lane of the warp must call it.
+template <typename E>
+__device__ __forceinline__ void fp8_store_token(const E* __restrict__ src, uint8_t* __restrict__ dst,
+                                                float* __restrict__ sc, int n_heads, int d, int lane) {
+  for (int h = 0; h < n_heads; ++h) {
+    float amax = 0.f;
+    for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(Elem<E>::to_f(src[h * d + i])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = fp8_row_scale(amax);
+    for (int i = lane; i < d; i += 32) dst[h * d + i] = fp8_quantize(Elem<E>::to_f(src[h * d + i]), s);
+    if (lane == 0) sc[h] = s;
+  }
+}
+
 // exact: every e4m3 value is representable in fp16
 __device__ __forceinline__ float fp8_to_float(uint8_t b) {
   return __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E4M3)));

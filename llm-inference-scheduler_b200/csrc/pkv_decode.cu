@@ -48,6 +48,11 @@
 //    epilogue writes them back in natural order).  Scales are applied
 //    outside the MMAs: K's to the token's scores, V's folded into P after
 //    the softmax sums.
+//  * Fused append (k_new != NULL): before loading the block that holds a
+//    sequence's newest token, the producer warp writes that token's K and V
+//    rows into the pool (fp8: quantised per row with their scales, exactly
+//    as the separate fp8 append does), then fences the generic-proxy writes
+//    against its TMA read.
 //  * Programmatic dependent launch chains append -> decode -> merge: each
 //    kernel's prologue (context scan, block-table reads) runs before
 //    griddepcontrol.wait and overlaps its predecessor; pool, q, out and
@@ -202,9 +207,8 @@ bool decode_fast_supported(const AttnArgs& a) {
   if (a.k_new != nullptr &&
       (!al(a.k_new, 16) || !al(a.v_new, 16) || (a.k_new_stride * 2) % 16 || (a.v_new_stride * 2) % 16))
     return false;
-  // fp8 pools: no fused append; the scale rows are bulk-copied (16-byte aligned)
-  if (a.k_scale != nullptr && (a.k_new != nullptr || !al(a.k_scale, 16) || !al(a.v_scale, 16)))
-    return false;
+  // fp8 pools: the scale rows are bulk-copied (16-byte aligned)
+  if (a.k_scale != nullptr && (!al(a.k_scale, 16) || !al(a.v_scale, 16))) return false;
   return (a.dtype == PKV_DTYPE_F16 || a.dtype == PKV_DTYPE_BF16) && a.head_dim == 64 &&
          a.block_size == 16 && (a.n_kv_heads == 1 || a.n_kv_heads == 2 || a.n_kv_heads == 4) &&
          G <= 8 && a.n_q_heads <= 32 && a.n_seqs <= kDecMaxSeqs && (a.q_stride % 2) == 0 &&
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         }
         if (id < 0) {
           id = 0;  // read a valid block; never write through a bad id
-        } else if (!FP8 && p.k_new != nullptr && gb == prefix[s + 1] - 1) {
+        } else if (p.k_new != nullptr && gb == prefix[s + 1] - 1) {
           app_seq = s;
           app_row = id * 16 + ((ctxs[s] - 1) & 15);
         }
@@ -423,19 +427,31 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
         const int a_seq = __shfl_sync(0xffffffffu, app_seq, k);
-        if (!FP8 && a_seq >= 0) {
-          // append before the block is loaded: the warp copies the K and V
-          // rows (nkv*128 bytes each) into the pool, then orders those
-          // generic-proxy writes before lane 0's TMA read of the block
+        if (a_seq >= 0) {
+          // append before the block is loaded: the warp writes the K and V
+          // rows into the pool (fp8: quantised, with their scales), then
+          // orders those generic-proxy writes before lane 0's TMA read of
+          // the block
           const int row = __shfl_sync(0xffffffffu, app_row, k);
-          constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
-          for (int v = lane; v < 2 * row_vecs; v += 32) {
-            const bool is_v = v >= row_vecs;
-            const int vi = is_v ? v - row_vecs : v;
-            const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
-                                       : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
-            uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
-            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
+          if constexpr (FP8) {
+            fp8_store_token<T>(reinterpret_cast<const T*>(p.k_new + a_seq * p.k_new_stride_b),
+                               p.k_pool + static_cast<int64_t>(row) * (nkv * 64),
+                               const_cast<float*>(p.k_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                               lane);
+            fp8_store_token<T>(reinterpret_cast<const T*>(p.v_new + a_seq * p.v_new_stride_b),
+                               p.v_pool + static_cast<int64_t>(row) * (nkv * 64),
+                               const_cast<float*>(p.v_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                               lane);
+          } else {
+            constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
+            for (int v = lane; v < 2 * row_vecs; v += 32) {
+              const bool is_v = v >= row_vecs;
+              const int vi = is_v ? v - row_vecs : v;
+              const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
+                                         : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
+              uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
+              *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
+            }
           }
           fence_proxy_async_global();
           __syncwarp();

@@ -85,6 +85,14 @@ cudaError_t launch_reshape_and_cache(const void* k, const void* v, int64_t k_str
                                      int block_size, int n_kv_heads, int head_dim, int esize,
                                      int* err, cudaStream_t stream);
 
+cudaError_t launch_append_at_context_end_fp8(const void* k, const void* v, int64_t k_stride,
+                                             int64_t v_stride, void* k_pool, void* v_pool,
+                                             float* k_scale, float* v_scale, const int32_t* tables,
+                                             int64_t bt_stride, int max_blocks,
+                                             const int32_t* context_lens, int n_seqs,
+                                             int num_blocks, int block_size, int n_kv_heads,
+                                             int head_dim, int src_dtype, int* err,
+                                             cudaStream_t stream);
 cudaError_t launch_append_at_context_end(const void* k, const void* v, int64_t k_stride,
                                          int64_t v_stride, void* k_pool, void* v_pool,
                                          const int32_t* tables, int64_t bt_stride, int max_blocks,

@@ -69,6 +69,9 @@ SIGNATURES: dict = {
                                              _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "pkv_rope_reshape_and_cache_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _I, _P, _P, _P, _P, _P,
                                             _I, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "pkv_paged_decode_append_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P,
+                                                   _P, _I, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _F,
+                                                   _I, _P, _SZ, _P, _P]),
     "pkv_decode_schedule_bytes": (_SZ, [_I, _I]),
     "pkv_decode_schedule": (_I, [_P, _SZ, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "pkv_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
@@ -80,7 +83,7 @@ SIGNATURES: dict = {
 
 # decode entries with a per-step schedule: the same arguments plus the schedule
 for _n in ("pkv_paged_decode_attention", "pkv_paged_decode_attention_fp8",
-           "pkv_paged_decode_append_attention"):
+           "pkv_paged_decode_append_attention", "pkv_paged_decode_append_attention_fp8"):
     SIGNATURES[_n + "_scheduled"] = (_I, SIGNATURES[_n][1] + [_P])
 
 

@@ -554,12 +554,28 @@ class PagedKVCache:
             self._len[s] = p + n
 
     def _forward_layer_fp8(self, layer, q, k_new, v_new, meta, scale, out, advance):
-        """forward_layer over fp8 pools: the quantising append of every token,
-        then decode and chunked prefill over the fp8 pools."""
+        """forward_layer over fp8 pools: the decode kernel quantises the decode
+        tokens itself; the chunk tokens take the quantising append; then the
+        chunked prefill over the fp8 pools."""
         mgr = self.mgr
-        ops.reshape_and_cache_fp8(k_new, v_new, mgr.k_pool[layer], mgr.v_pool[layer],
-                                  mgr.k_scale[layer], mgr.v_scale[layer], meta.slot_mapping, mgr.err)
-        return self._attend_fp8(layer, q, meta, scale, out, advance)
+        ks, vs = mgr.k_scale[layer], mgr.v_scale[layer]
+        nd = meta.n_decode
+        if nd:
+            ws = self.decode_workspace(nd, q.shape[1], q.shape[2])
+            ops.paged_decode_append_attention_fp8(
+                q[:nd], k_new[:nd], v_new[:nd], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
+                meta.block_tables[:nd], meta.context_lens[:nd], scale, workspace=ws, out=out[:nd],
+                err=mgr.err, schedule=self._step_schedule(meta, q))
+        if nd < meta.n_seqs:
+            ops.reshape_and_cache_fp8(k_new[nd:], v_new[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
+                                      ks, vs, meta.slot_mapping[nd:], mgr.err)
+            ops.paged_prefill_attention_fp8(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
+                                            meta.block_tables[nd:], meta.query_start_loc,
+                                            meta.num_prior_dev[nd:], meta.max_query_len, scale,
+                                            out=out[nd:], err=mgr.err)
+        if advance and layer == mgr.num_layers - 1:
+            self._advance(meta)
+        return out
 
     def _attend_fp8(self, layer, q, meta, scale, out, advance):
         """The step's attention launches over fp8 pools whose rows are already

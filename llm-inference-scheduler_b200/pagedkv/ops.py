@@ -431,6 +431,51 @@ def paged_decode_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables
     return out
 
 
+def _decode_append_fp8_args(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale, block_tables,
+                            context_lens, scale, workspace, out, err):
+    nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
+    for t, n in ((q, "q"), (k_new, "k_new"), (v_new, "v_new"), (context_lens, "context_lens")):
+        _cuda(t, n)
+    _check_tables(block_tables)
+    if context_lens.dtype != torch.int32 or not context_lens.is_contiguous():
+        raise TypeError("pagedkv: context_lens must be a contiguous int32 tensor")
+    B, hq, dq = q.shape
+    if dq != d or block_tables.shape[0] < B or context_lens.shape[0] < B:
+        raise ValueError("pagedkv: q / block_tables / context_lens shapes disagree")
+    if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+        raise TypeError("pagedkv: k_new / v_new must have the q dtype")
+    if k_new.shape[0] < B or v_new.shape[0] < B or tuple(k_new.shape[1:]) != (hkv, d) \
+            or tuple(v_new.shape[1:]) != (hkv, d):
+        raise ValueError("pagedkv: k_new / v_new must be [n_seqs, n_kv_heads, head_dim]")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if workspace is None:
+        workspace = new_decode_workspace(B, hq, d, q.device)
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_new.data_ptr(), v_new.data_ptr(), _row_stride(k_new, "k_new"), _row_stride(v_new, "v_new"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            context_lens.data_ptr(), B, hq, hkv, d, bs, float(scale), dtype_code(q.dtype),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), _ptr(err), _stream(q))
+    return args, out
+
+
+def paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale,
+                                      block_tables, context_lens, scale, workspace=None, out=None,
+                                      err=None, schedule=None) -> torch.Tensor:
+    """One fp8 decode step of one layer: the decode kernel quantises
+    k_new[s] / v_new[s] into the fp8 pools at position context_lens[s] - 1
+    (reshape_and_cache_fp8's quantisation, scales included), then attends
+    (paged_decode_attention_fp8)."""
+    args, out = _decode_append_fp8_args(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale,
+                                        block_tables, context_lens, scale, workspace, out, err)
+    if q.shape[0] == 0:
+        return out
+    rc = _sched_fn("pkv_paged_decode_append_attention_fp8", schedule)(*_sched_args(args, schedule))
+    _lib.check(rc, "pkv_paged_decode_append_attention_fp8")
+    return out
+
+
 def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
                                 num_prior, max_query_len, scale, out=None, err=None) -> torch.Tensor:
     """paged_prefill_attention over fp8 e4m3 pools (CUDA-core kernel)."""
@@ -537,6 +582,17 @@ class BoundLaunch:
         rc = self._fn(*self._args)
         if rc:
             _lib.check(rc, self._name)
+
+
+def bind_paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale,
+                                           block_tables, context_lens, scale, workspace, out, err=None,
+                                           schedule=None) -> BoundLaunch:
+    args, out = _decode_append_fp8_args(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale,
+                                        block_tables, context_lens, scale, workspace, out, err)
+    return BoundLaunch(_sched_fn("pkv_paged_decode_append_attention_fp8", schedule),
+                       _sched_args(args, schedule), "pkv_paged_decode_append_attention_fp8",
+                       (q, k_new, v_new, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
+                        workspace, out, err, schedule))
 
 
 def bind_decode_schedule(schedule, block_tables, context_lens, num_blocks, n_q_heads, n_kv_heads,

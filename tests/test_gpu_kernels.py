@@ -869,3 +869,46 @@ def test_forward_layer_qkv_fp8_equals_forward_layer_fp8():
         assert torch.equal(a, b)
     for m, _ in caches:
         m.check_errors()
+
+
+@pytest.mark.parametrize("q_dt", ("f16", "bf16"))
+@pytest.mark.parametrize("impl", ("auto", "generic"))
+def test_decode_append_fp8_fused_equals_unfused(q_dt, impl):
+    """pkv_paged_decode_append_attention_fp8 (the tensor-core decode kernel
+    quantises the new token itself; the CUDA-core path appends with a
+    separate kernel) gives the same pool bytes, scales and outputs, bit for
+    bit, as reshape_and_cache_fp8 at the newest slot followed by
+    paged_decode_attention_fp8, with and without a schedule."""
+    ops.set_decode_impl(_lib.DECODE_AUTO if impl == "auto" else _lib.DECODE_GENERIC)
+    try:
+        ctx = [1, 15, 16, 17, 33, 600, 1000, 2047, 64, 5000, 3, 250]
+        c = _fp8_case(73, ctx, "f16")
+        B = len(ctx)
+        tdt = TORCH_DT[q_dt]
+        g = torch.Generator(device="cuda").manual_seed(9)
+        q = torch.randn((B, 14, 64), generator=g, device="cuda").to(tdt)
+        kn = (2 * torch.randn((B, 2, 64), generator=g, device="cuda")).to(tdt)
+        vn = torch.randn((B, 2, 64), generator=g, device="cuda").to(tdt)
+        tabs_np = C.pad_tables(c["tables"])
+        tabs, ctx_d = dev(tabs_np), dev(c["ctx"].astype(np.int32))
+        pos = c["ctx"] - 1
+        slots = torch.from_numpy(tabs_np[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16).cuda()
+        err = ops.new_error_flags("cuda")
+        ref = [t.clone() for t in (c["kp"], c["vp"], c["ks"], c["vs"])]
+        ops.reshape_and_cache_fp8(kn, vn, *ref, slots, err)
+        out_ref = ops.paged_decode_attention_fp8(q, *ref, tabs, ctx_d, 0.125, err=err)
+        for use_sched in (False, True):
+            pools = [t.clone() for t in (c["kp"], c["vp"], c["ks"], c["vs"])]
+            sched = None
+            if use_sched:
+                NB_SCHED[0] = pools[0].shape[0]
+                sched = _sched_for(tabs, ctx_d, q, fp8=True, err=err)
+            out = ops.paged_decode_append_attention_fp8(q, kn, vn, *pools, tabs, ctx_d, 0.125, err=err,
+                                                        schedule=sched)
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            for a, b in zip(pools, ref):
+                assert torch.equal(a, b)
+            assert torch.equal(out, out_ref)
+    finally:
+        ops.set_decode_impl(_lib.DECODE_AUTO)
