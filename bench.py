@@ -53,6 +53,8 @@ def parse():
                          "migrate = KV block migration between rank pairs over NVLink (2+ ranks)")
     ap.add_argument("--migrate-blocks", type=int, default=1024,
                     help="migrate: blocks per copy launch (x 24 layers, K and V)")
+    ap.add_argument("--kv-fp8", action="store_true",
+                    help="prefill: fp8 e4m3 pools (quantising append, tensor-core fp8 prefill)")
     ap.add_argument("--append-tokens", type=int, nargs="+", default=[8192, 65536],
                     help="cache_ops: tokens appended per reshape_and_cache launch")
     ap.add_argument("--copy-pairs", type=int, default=4096, help="cache_ops: (src, dst) block pairs")
@@ -515,10 +517,20 @@ def run_prefill(args):
     tabs_np = W.prefill_tables(prior, chunk, 48, nb, seed=200 + rank)
     g = torch.Generator(device=dev)
     g.manual_seed(4321 + rank)
-    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=dt)
-    for layer in range(L):
-        mgr.k_pool[layer].normal_(generator=g)
-        mgr.v_pool[layer].normal_(generator=g)
+    fp8 = args.kv_fp8
+    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=torch.float8_e4m3fn if fp8 else dt)
+    if fp8:  # every slot quantised from N(0,1) rows
+        fill = torch.empty((nb * 16, 2, 64), device=dev, dtype=dt)
+        all_slots = torch.arange(nb * 16, device=dev, dtype=torch.int64)
+        for layer in range(L):
+            fill.normal_(generator=g)
+            ops.reshape_and_cache_fp8(fill, fill, mgr.k_pool[layer], mgr.v_pool[layer],
+                                      mgr.k_scale[layer], mgr.v_scale[layer], all_slots)
+        del fill
+    else:
+        for layer in range(L):
+            mgr.k_pool[layer].normal_(generator=g)
+            mgr.v_pool[layer].normal_(generator=g)
     q = torch.randn((L, T, 14, 64), generator=g, device=dev, dtype=dt)
     kn = torch.randn((L, T, 2, 64), generator=g, device=dev, dtype=dt)
     vn = torch.randn((L, T, 2, 64), generator=g, device=dev, dtype=dt)
@@ -532,11 +544,25 @@ def run_prefill(args):
     qsl = torch.from_numpy(np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)).to(dev)
     prior_d = torch.from_numpy(prior.astype(np.int32)).to(dev)
     err = ops.new_error_flags(dev)
-    appends = [ops.bind_reshape_and_cache(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], slots, err)
-               for l in range(L)]
-    prefills = [ops.bind_paged_prefill_attention(q[l], mgr.k_pool[l], mgr.v_pool[l], tabs, qsl,
-                                                 prior_d, int(chunk.max()), scale, out[l], err)
-                for l in range(L)]
+    if fp8:
+        # quantising append, then the tensor-core fp8 prefill: the pass that
+        # writes the visible blocks into the 16-bit scratch is timed with it
+        scratch = torch.empty(ops.prefill_fp8_scratch_bytes(B, tabs.shape[1], 2, 64),
+                              dtype=torch.uint8, device=dev)
+        appends = [ops.bind_reshape_and_cache_fp8(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
+                                                  mgr.k_scale[l], mgr.v_scale[l], slots, err)
+                   for l in range(L)]
+        prefills = [ops.bind_paged_prefill_attention_fp8(q[l], mgr.k_pool[l], mgr.v_pool[l],
+                                                         mgr.k_scale[l], mgr.v_scale[l], tabs, qsl,
+                                                         prior_d, int(chunk.max()), scale, out[l],
+                                                         scratch, err)
+                    for l in range(L)]
+    else:
+        appends = [ops.bind_reshape_and_cache(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], slots, err)
+                   for l in range(L)]
+        prefills = [ops.bind_paged_prefill_attention(q[l], mgr.k_pool[l], mgr.v_pool[l], tabs, qsl,
+                                                     prior_d, int(chunk.max()), scale, out[l], err)
+                    for l in range(L)]
     flops = W.prefill_flops(prior, chunk)
 
     def step(ev=None):
@@ -593,7 +619,7 @@ def run_prefill(args):
     peak, kind = peaks_tflops()
     achieved = flops / (ker_ms * 1e-3) / 1e12
     line = {
-        "metric": "paged chunked-prefill attention TFLOP/s (config 4)",
+        "metric": "paged chunked-prefill attention TFLOP/s (config 4)" + (" over fp8 e4m3 KV" if fp8 else ""),
         "value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
@@ -601,11 +627,12 @@ def run_prefill(args):
         "config": {"workload": "config4: 16 seqs x 512-token chunk over 48-token shared prefix + "
                                "private prior U[0,4096], 24 layers x (append + prefill), 14q/2kv, d64",
                    "sum_prior": int(prior.sum()), "flops_per_layer": flops, "layers": L},
-        "roofline": {"kernel": "paged_prefill_tc_kernel<half>", "bound": "tensor",
+        "roofline": {"kernel": "paged_prefill_tc_kernel<half>" + (" + fp8 scratch pass" if fp8 else ""),
+                     "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": kind,
                      "avg_launch_ms": round(ker_ms, 5)},
-        "gpu_launches": 2 * L * args.steps,
+        "gpu_launches": (3 if fp8 else 2) * L * args.steps,
         "clocks": sampler.summary(t0, t1) if sampler else None,
     }
     print(json.dumps(line), flush=True)

@@ -131,6 +131,29 @@ int pkv_paged_decode_append_attention_fp8_scheduled(
     const void* schedule);
 
 /*
+ * Chunked prefill over fp8 e4m3 pools on the tensor cores.  Same arguments
+ * and semantics as pkv_paged_prefill_attention_fp8, plus a caller-provided
+ * scratch buffer (pkv_prefill_fp8_scratch_bytes(n_seqs, max_blocks_per_seq,
+ * n_kv_heads, head_dim) bytes, 256-byte aligned, any contents): one pass
+ * writes the blocks the step can see there as 16-bit rows (e4m3 x scale,
+ * rounded once to `dtype`), then the tcgen05 prefill kernel runs over them.
+ * The results differ from the CUDA-core fp8 prefill by that one rounding.
+ * Shapes the tensor-core kernel does not serve fall back to the CUDA-core
+ * kernel (the scratch is then unused).  Replaces, for fp8 pools, the gather
+ * and _attention with num_new > 1 (mini_engine/paged/block_manager.py:136-141,
+ * mini_engine/model/qwen2.py:98-128).
+ */
+size_t pkv_prefill_fp8_scratch_bytes(int n_seqs, int max_blocks_per_seq, int n_kv_heads,
+                                     int head_dim);
+int pkv_paged_prefill_attention_fp8_scratch(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_pool,
+    const void* v_pool, const float* k_scale, const float* v_scale, int num_blocks,
+    const int32_t* block_tables, int64_t block_table_stride, int max_blocks_per_seq,
+    const int32_t* query_start_loc, const int32_t* num_prior, int n_seqs, int n_tokens,
+    int max_query_len, int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale,
+    int dtype, void* scratch, size_t scratch_bytes, int* err_flags, pkv_stream_t stream);
+
+/*
  * Per-step decode schedule.  All layers of a decode step share the block
  * tables and context lengths, so the stream-K partition of the step's blocks
  * over the decode kernel's persistent CTAs is the same for every layer.

@@ -807,6 +807,81 @@ int pkv_paged_decode_append_attention_scheduled(void* out, int64_t out_row_strid
                                                 schedule);
 }
 
+size_t pkv_prefill_fp8_scratch_bytes(int n_seqs, int max_blocks_per_seq, int n_kv_heads,
+                                     int head_dim) {
+  if (n_seqs < 0 || max_blocks_per_seq < 0 || n_kv_heads <= 0 || head_dim <= 0) return 0;
+  return prefill_fp8_scratch_bytes(n_seqs, max_blocks_per_seq, n_kv_heads, head_dim);
+}
+
+int pkv_paged_prefill_attention_fp8_scratch(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, const void* k_pool,
+    const void* v_pool, const float* k_scale, const float* v_scale, int num_blocks,
+    const int32_t* block_tables, int64_t block_table_stride, int max_blocks_per_seq,
+    const int32_t* query_start_loc, const int32_t* num_prior, int n_seqs, int n_tokens,
+    int max_query_len, int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale,
+    int dtype, void* scratch, size_t scratch_bytes, int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0 || n_tokens < 0 || max_query_len < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0 || n_tokens == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!query_start_loc || !num_prior || !k_scale || !v_scale || !scratch) return PKV_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(scratch) & 255) != 0) return PKV_ERR_MISALIGNED;
+  if (scratch_bytes < prefill_fp8_scratch_bytes(n_seqs, max_blocks_per_seq, n_kv_heads, head_dim))
+    return PKV_ERR_WORKSPACE_TOO_SMALL;
+  if (n_seqs > 65535) return PKV_ERR_UNSUPPORTED;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.query_start_loc = query_start_loc;
+  a.num_prior = num_prior;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_tokens;
+  a.max_query_len = max_query_len;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  AttnArgs t = a;  // the tensor-core prefill over the 16-bit scratch pool
+  t.k_scale = t.v_scale = nullptr;
+  t.k_pool = t.v_pool = scratch;  // alignment stand-ins until the pass sets them
+  if (g_decode_impl.load() != PKV_DECODE_AUTO || !prefill_fast_supported(t))
+    return status_of(launch_generic_attention(a, st));
+  void *kq = nullptr, *vq = nullptr;
+  int32_t* tab = nullptr;
+  cudaError_t e = launch_dequant_blocks(a, scratch, st, &kq, &vq, &tab);
+  if (e != cudaSuccess) return status_of(e);
+  t.k_pool = kq;
+  t.v_pool = vq;
+  t.num_blocks = n_seqs * max_blocks_per_seq;
+  t.block_tables = tab;
+  t.bt_stride = max_blocks_per_seq;
+  CUtensorMap qm, km, vm;
+  rc = encode_q_tensormap(&qm, q, q_row_stride, n_tokens, n_q_heads, head_dim, dtype);
+  if (rc != 0) return rc;
+  // the scratch pool's maps are encoded per call (its block count follows the step)
+  rc = encode_pool_tensormap(&km, kq, t.num_blocks, block_size, n_kv_heads, head_dim, dtype);
+  if (rc != 0) return rc;
+  rc = encode_pool_tensormap(&vm, vq, t.num_blocks, block_size, n_kv_heads, head_dim, dtype);
+  if (rc != 0) return rc;
+  return status_of(launch_prefill_fast(t, &qm, &km, &vm, st));
+}
+
 int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                                 const void* k_pool, const void* v_pool, int num_blocks,
                                 const int32_t* block_tables, int64_t block_table_stride,

@@ -133,6 +133,9 @@ int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, in
 // Chunked prefill on tcgen05 tensor cores: fp16/bf16, head_dim 64, block 16,
 // 16-byte aligned q / out rows.
 bool prefill_fast_supported(const AttnArgs& a);
+size_t prefill_fp8_scratch_bytes(int n_seqs, int max_blocks, int n_kv_heads, int head_dim);
+cudaError_t launch_dequant_blocks(const AttnArgs& a, void* scratch, cudaStream_t stream,
+                                  void** k_out, void** v_out, int32_t** table_out);
 cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, const CUtensorMap* kmap,
                                 const CUtensorMap* vmap, cudaStream_t stream);
 // TMA descriptor for q viewed as [n_tokens][n_q_heads][head_dim] (row stride

@@ -72,6 +72,10 @@ SIGNATURES: dict = {
     "pkv_paged_decode_append_attention_fp8": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P,
                                                    _P, _I, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _F,
                                                    _I, _P, _SZ, _P, _P]),
+    "pkv_prefill_fp8_scratch_bytes": (_SZ, [_I, _I, _I, _I]),
+    "pkv_paged_prefill_attention_fp8_scratch": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P,
+                                                     _I64, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                                     _F, _I, _P, _SZ, _P, _P]),
     "pkv_decode_schedule_bytes": (_SZ, [_I, _I]),
     "pkv_decode_schedule": (_I, [_P, _SZ, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "pkv_ipc_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),

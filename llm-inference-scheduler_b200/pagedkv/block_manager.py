@@ -274,6 +274,7 @@ class PagedKVCache:
         self._len: dict[int, int] = {}
         self._workspace: torch.Tensor | None = None
         self._schedule_buf: torch.Tensor | None = None
+        self._fp8_scratch: torch.Tensor | None = None
         self._mirror = _TableMirror()
         self._stage_ring: list = [[None, None] for _ in range(4)]
         self._stage_next = 0
@@ -495,6 +496,16 @@ class PagedKVCache:
                 fp8=self.mgr.fp8, err=self.mgr.err)
         return meta.decode_schedule
 
+    def _prefill_scratch(self, meta: StepMetadata, q: torch.Tensor) -> torch.Tensor:
+        """16-bit scratch pool of the fp8 tensor-core prefill, reused across
+        layers and steps (stream order keeps each use behind the previous)."""
+        n_pre = meta.n_seqs - meta.n_decode
+        need = ops.prefill_fp8_scratch_bytes(n_pre, meta.block_tables.shape[1], self.mgr.num_kv_heads,
+                                             q.shape[2])
+        if self._fp8_scratch is None or self._fp8_scratch.numel() < need:
+            self._fp8_scratch = torch.empty(need, dtype=torch.uint8, device=self.mgr.device)
+        return self._fp8_scratch
+
     def decode_workspace(self, n_seqs: int, n_q_heads: int, head_dim: int) -> torch.Tensor:
         need = ops.decode_workspace_bytes(n_seqs, n_q_heads, head_dim)
         if self._workspace is None or self._workspace.numel() < need:
@@ -572,7 +583,8 @@ class PagedKVCache:
             ops.paged_prefill_attention_fp8(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
                                             meta.block_tables[nd:], meta.query_start_loc,
                                             meta.num_prior_dev[nd:], meta.max_query_len, scale,
-                                            out=out[nd:], err=mgr.err)
+                                            out=out[nd:], err=mgr.err,
+                                            scratch=self._prefill_scratch(meta, q))
         if advance and layer == mgr.num_layers - 1:
             self._advance(meta)
         return out
@@ -593,7 +605,8 @@ class PagedKVCache:
             ops.paged_prefill_attention_fp8(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], ks, vs,
                                             meta.block_tables[nd:], meta.query_start_loc,
                                             meta.num_prior_dev[nd:], meta.max_query_len, scale,
-                                            out=out[nd:], err=mgr.err)
+                                            out=out[nd:], err=mgr.err,
+                                            scratch=self._prefill_scratch(meta, q))
         if advance and layer == mgr.num_layers - 1:
             self._advance(meta)
         return out

@@ -476,9 +476,20 @@ def paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_scale, 
     return out
 
 
+def prefill_fp8_scratch_bytes(n_seqs: int, max_blocks_per_seq: int, n_kv_heads: int,
+                              head_dim: int) -> int:
+    return int(_lib.load().pkv_prefill_fp8_scratch_bytes(n_seqs, max_blocks_per_seq, n_kv_heads,
+                                                          head_dim))
+
+
 def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
-                                num_prior, max_query_len, scale, out=None, err=None) -> torch.Tensor:
-    """paged_prefill_attention over fp8 e4m3 pools (CUDA-core kernel)."""
+                                num_prior, max_query_len, scale, out=None, err=None,
+                                tensor_cores: bool = True, scratch=None) -> torch.Tensor:
+    """paged_prefill_attention over fp8 e4m3 pools.  tensor_cores=True: the
+    blocks the step sees are written as 16-bit rows (e4m3 x scale, rounded
+    once to q's dtype) into `scratch` (prefill_fp8_scratch_bytes; allocated
+    here when None) and the tcgen05 prefill runs over them; False: the
+    CUDA-core kernel dequantises on load (no scratch, no extra rounding)."""
     nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
     for t, n in ((q, "q"), (query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
         _cuda(t, n)
@@ -490,6 +501,20 @@ def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_table
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     if T == 0 or n_seqs == 0:
+        return out
+    if tensor_cores and q.dtype in (torch.float16, torch.bfloat16):
+        need = prefill_fp8_scratch_bytes(n_seqs, block_tables.shape[1], hkv, d)
+        if scratch is None:
+            scratch = torch.empty(need, dtype=torch.uint8, device=q.device)
+        _cuda(scratch, "scratch")
+        rc = _lib.load().pkv_paged_prefill_attention_fp8_scratch(
+            out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            query_start_loc.data_ptr(), num_prior.data_ptr(), n_seqs, T, int(max_query_len), hq, hkv,
+            d, bs, float(scale), dtype_code(q.dtype), scratch.data_ptr(),
+            scratch.numel() * scratch.element_size(), _ptr(err), _stream(q))
+        _lib.check(rc, "pkv_paged_prefill_attention_fp8_scratch")
         return out
     rc = _lib.load().pkv_paged_prefill_attention_fp8(
         out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"), k_pool.data_ptr(),
@@ -593,6 +618,26 @@ def bind_paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_sc
                        _sched_args(args, schedule), "pkv_paged_decode_append_attention_fp8",
                        (q, k_new, v_new, k_pool, v_pool, k_scale, v_scale, block_tables, context_lens,
                         workspace, out, err, schedule))
+
+
+def bind_paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables,
+                                     query_start_loc, num_prior, max_query_len, scale, out, scratch,
+                                     err=None) -> BoundLaunch:
+    """The tensor-core fp8 prefill (scratch pass + tcgen05 kernel) bound to fixed tensors."""
+    paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
+                                num_prior, max_query_len, scale, out=out, err=err, scratch=scratch)
+    nb, bs, hkv, d = k_pool.shape
+    T, hq, _ = q.shape
+    args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            query_start_loc.data_ptr(), num_prior.data_ptr(), query_start_loc.shape[0] - 1, T,
+            int(max_query_len), hq, hkv, d, bs, float(scale), dtype_code(q.dtype), scratch.data_ptr(),
+            scratch.numel() * scratch.element_size(), _ptr(err), _stream(q))
+    return BoundLaunch(_lib.load().pkv_paged_prefill_attention_fp8_scratch, args,
+                       "pkv_paged_prefill_attention_fp8_scratch",
+                       (q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc, num_prior,
+                        out, scratch, err))
 
 
 def bind_decode_schedule(schedule, block_tables, context_lens, num_blocks, n_q_heads, n_kv_heads,

@@ -618,25 +618,59 @@ def test_decode_fp8_matches_oracle(oracle_mod, decode_impl, q_dt):
     assert np.abs(got - ref).max() <= fp8_atol(q_dt, ref)
 
 
-def test_prefill_fp8_matches_oracle(oracle_mod):
-    """Chunked prefill over fp8 pools (CUDA-core kernel): chunks over a prior."""
-    prior = np.array([48, 0, 300, 17], dtype=np.int64)
-    chunk = np.array([64, 130, 1, 40], dtype=np.int64)
+@pytest.mark.parametrize("q_dt", ("f16", "bf16"))
+@pytest.mark.parametrize("tensor_cores", (True, False))
+def test_prefill_fp8_matches_oracle(oracle_mod, q_dt, tensor_cores):
+    """Chunked prefill over fp8 pools, chunks over a prior: the tensor-core
+    path (16-bit scratch pool + tcgen05 kernel) and the CUDA-core kernel."""
+    prior = np.array([48, 0, 300, 17, 1000], dtype=np.int64)
+    chunk = np.array([64, 130, 1, 40, 300], dtype=np.int64)
     c = _fp8_case(73, prior + chunk, "f16")
     T = int(chunk.sum())
-    q = C.to_dtype(c["rng"].standard_normal((T, 14, 64), dtype=np.float32), "f16")
+    q = C.to_dtype(c["rng"].standard_normal((T, 14, 64), dtype=np.float32), q_dt)
     tabs = C.pad_tables(c["tables"])
     qsl = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
     err = ops.new_error_flags("cuda")
-    out = ops.paged_prefill_attention_fp8(dev(q, "f16"), c["kp"], c["vp"], c["ks"], c["vs"], dev(tabs),
+    out = ops.paged_prefill_attention_fp8(dev(q, q_dt), c["kp"], c["vp"], c["ks"], c["vs"], dev(tabs),
                                           dev(qsl), dev(prior.astype(np.int32)), int(chunk.max()), 0.125,
-                                          err=err)
+                                          err=err, tensor_cores=tensor_cores)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ref = oracle_mod.paged_attention_fp8(q.astype(np.float32), c["kp"].cpu().numpy(),
+    ref = oracle_mod.paged_attention_fp8(as_f32(q, q_dt), c["kp"].cpu().numpy(),
                                          c["vp"].cpu().numpy(), c["ks"].cpu().numpy(),
                                          c["vs"].cpu().numpy(), tabs, qsl, prior.astype(np.int32))
-    assert np.abs(host(out, "f16").astype(np.float32) - ref).max() <= fp8_atol("f16", ref)
+    got = as_f32(host(out, q_dt), q_dt)
+    assert np.abs(got - ref).max() <= fp8_atol(q_dt, ref)
+
+
+def test_prefill_fp8_tensor_cores_config4_shape():
+    """Config-4 shape over fp8 pools (16 chunks of 512 over a 48-token shared
+    prefix plus private priors): the tensor-core path against the CUDA-core
+    kernel, within the fp16 fp8 tolerance; the scratch is reused across two
+    calls with different pools (no state carried)."""
+    rng = np.random.default_rng(74)
+    prior = 48 + rng.integers(0, 4096, size=16)
+    chunk = np.full(16, 512)
+    c = _fp8_case(74, prior + chunk, "f16")
+    T = int(chunk.sum())
+    tabs = dev(C.pad_tables(c["tables"]))
+    qsl = dev(np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32))
+    pr = dev(prior.astype(np.int32))
+    err = ops.new_error_flags("cuda")
+    scratch = torch.full((ops.prefill_fp8_scratch_bytes(16, tabs.shape[1], 2, 64),), 255,
+                         dtype=torch.uint8, device="cuda")
+    for seed in (1, 2):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        q = torch.randn((T, 14, 64), generator=g, device="cuda").half()
+        kp = c["kp"] if seed == 1 else torch.roll(c["kp"], 1, dims=0)
+        a = ops.paged_prefill_attention_fp8(q, kp, c["vp"], c["ks"], c["vs"], tabs, qsl, pr, 512, 0.125,
+                                            err=err, scratch=scratch)
+        b = ops.paged_prefill_attention_fp8(q, kp, c["vp"], c["ks"], c["vs"], tabs, qsl, pr, 512, 0.125,
+                                            err=err, tensor_cores=False)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        ref = b.float().cpu().numpy()
+        assert np.abs(a.float().cpu().numpy() - ref).max() <= 2 * fp8_atol("f16", ref)
 
 
 def test_forward_layer_fp8_pools_and_cow(oracle_mod):
