@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--conversations", type=int, default=64, help="config 5: conversations")
     ap.add_argument("--rate", type=float, default=40.0, help="config 5: Poisson arrivals per second")
     ap.add_argument("--max-num-seqs", type=int, default=128)
+    ap.add_argument("--no-cuda-graphs", action="store_true",
+                    help="config 5: run decode-only steps eagerly instead of replaying CUDA graphs")
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
@@ -669,7 +671,11 @@ def run_e2e(args):
     mgr = BlockManager(num_blocks, 16, cfg.num_hidden_layers, 2, 64, device="cuda", dtype=torch.float16)
     sched = Scheduler(model, mgr, max_num_seqs=args.max_num_seqs,
                       max_batched_tokens=args.max_batched_tokens, enable_prefix_cache=True,
-                      eos_ids=set())
+                      eos_ids=set(), cuda_graphs=not args.no_cuda_graphs)
+    t_cap = time.perf_counter()
+    if sched.cuda_graphs:  # every padded batch size, before the timed run
+        sched.decode_graphs().capture_all()
+    t_cap = time.perf_counter() - t_cap
 
     def drive(n_conv, arr):
         pending = list(range(n_conv))
@@ -697,7 +703,9 @@ def run_e2e(args):
     sched.radix.evict(num_blocks)   # forget the warm-up prefixes
     for k in list(sched.metrics):
         sched.metrics[k] = 0
+    replays0 = sched.graphs.replays if sched.graphs is not None else 0
     wall, done = drive(n, arrivals)
+    replays = (sched.graphs.replays if sched.graphs is not None else 0) - replays0
     mgr.check_errors()
     steps_timed = sched.metrics["steps"]
     sched_metrics = dict(sched.metrics)
@@ -724,7 +732,11 @@ def run_e2e(args):
         "config": {"workload": "config5: Poisson arrivals of 2-turn conversations, prompts 64-512 "
                                "tokens with a shared 48-token prefix, 128 greedy output tokens/turn",
                    "conversations": n, "rate_per_s": args.rate, "max_num_seqs": args.max_num_seqs,
-                   "max_batched_tokens": args.max_batched_tokens, "num_blocks": num_blocks},
+                   "max_batched_tokens": args.max_batched_tokens, "num_blocks": num_blocks,
+                   "cuda_graphs": sched.cuda_graphs},
+        "cuda_graphs": {"decode_steps_replayed": replays, "steps": steps_timed,
+                        "buckets": sched.graphs.buckets if sched.graphs is not None else None,
+                        "capture_s": round(t_cap, 3)},
         "generated_tokens": gen, "wall_s": round(wall, 3),
         "ttft_ms": {"p50": pct(ttft, 50), "p99": pct(ttft, 99)},
         "itl_ms": {"p50": pct(itl, 50), "p99": pct(itl, 99)},

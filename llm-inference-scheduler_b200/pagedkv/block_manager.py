@@ -194,6 +194,8 @@ class StepMetadata:
     decode_plan: ops.DecodeAppendPlan | None = None  # built by the first forward_layer
     decode_plain_plan: ops.DecodePlan | None = None   # built by the first forward_layer_qkv
     decode_schedule: torch.Tensor | None = None       # the step's decode schedule (first layer)
+    rope_plan: ops.RopePlan | None = None             # built by the first forward_layer_qkv
+    prefill_plan: ops.PrefillPlan | None = None       # built by the first prefill layer
 
     @property
     def n_seqs(self) -> int:
@@ -350,7 +352,8 @@ class PagedKVCache:
 
     # ---- batched hot path ---------------------------------------------------
 
-    def step_arrays(self, seqs: list[tuple[int, int]], out=None) -> dict:
+    def step_arrays(self, seqs: list[tuple[int, int]], out=None, width: int | None = None,
+                    pad_to: int | None = None) -> dict:
         """Host half of prepare_step (no device work): numpy arrays of the step.
 
         Returns dict(ints=int32 [B*W + 2B + n_prefill + 1] = block tables (B x W;
@@ -360,6 +363,11 @@ class PagedKVCache:
         out(n_ints, n_slots) -> (int32 array, int64 array), the two arrays are
         written into the buffers it returns (prepare_step: its pinned staging
         buffer) instead of fresh ones.
+
+        width fixes W (AssertionError if a sequence needs more blocks).
+        pad_to (decode-only steps) lays the arrays out for pad_to >= B rows:
+        the rows past B are padding, context length 0, slot -1 and an all-zero
+        table row, which the kernels skip (a CUDA-graph step of fixed shape).
         """
         bs = self.mgr.block_size
         B = len(seqs)
@@ -390,26 +398,36 @@ class PagedKVCache:
                               f"{n_blocks[bad[0]]} blocks allocated")
         used = (totals + bs - 1) // bs
         W = max(1, int(used.max(initial=1)))
+        if width is not None:
+            assert W <= width, f"a sequence needs {W} blocks, more than the fixed width {width}"
+            W = width
         ones = num_new == 1
         n_dec = B if ones.all() else int(np.argmin(ones))
         pre_new = num_new[n_dec:]
         n_pre = B - n_dec
         T = int(num_new.sum())
-        n_ints = B * W + 2 * B + n_pre + 1
+        R = B if pad_to is None else pad_to  # rows of the layout
+        assert R >= B and (R == B or n_pre == 0), "pad_to is for decode-only steps of <= pad_to rows"
+        n_ints = R * W + 2 * R + n_pre + 1
         if out is None:
-            ints, slots = np.empty(n_ints, dtype=np.int32), np.empty(T, dtype=np.int64)
+            ints, slots = np.empty(n_ints, dtype=np.int32), np.empty(T + R - B, dtype=np.int64)
         else:
-            ints, slots = out(n_ints, T)
-        tabs = ints[: B * W].reshape(B, W)
+            ints, slots = out(n_ints, T + R - B)
+        tabs = ints[: R * W].reshape(R, W)
         mirror._fit(1, W)
         # entries past a sequence's used blocks are left as the mirror holds
         # them (allocated-ahead block ids or zeros): no kernel reads them
-        np.take(mirror.buf[:, :W], rows, axis=0, out=tabs)
-        ints[B * W: B * W + B] = totals
-        ints[B * W + B: B * W + 2 * B] = num_prior
-        ints[B * W + 2 * B] = 0
+        np.take(mirror.buf[:, :W], rows, axis=0, out=tabs[:B])
+        ints[R * W: R * W + B] = totals
+        ints[R * W + R: R * W + R + B] = num_prior
+        if R > B:
+            tabs[B:] = 0
+            ints[R * W + B: R * W + R] = 0
+            ints[R * W + R + B: R * W + 2 * R] = 0
+            slots[T:] = -1
+        ints[R * W + 2 * R] = 0
         if n_pre:
-            ints[B * W + 2 * B + 1:] = np.cumsum(pre_new)
+            ints[R * W + 2 * R + 1:] = np.cumsum(pre_new)
         # decode sequences: one slot each, gathered in one step
         pos = num_prior[:n_dec]
         slots[:n_dec] = mirror.buf[rows[:n_dec], pos // bs].astype(np.int64) * bs + pos % bs
@@ -421,7 +439,7 @@ class PagedKVCache:
             o += n
         return dict(ints=ints, slots=slots, seq_ids=seq_ids, num_new=num_new.tolist(),
                     num_prior=num_prior.tolist(), n_tokens=T, n_decode=n_dec,
-                    max_query_len=int(pre_new.max(initial=0)), B=B, W=W)
+                    max_query_len=int(pre_new.max(initial=0)), B=B, W=W, R=R)
 
     def _staging(self, nbytes: int) -> torch.Tensor:
         """A pinned host buffer of >= nbytes from a small ring; waits (normally
@@ -550,13 +568,22 @@ class PagedKVCache:
         if nd < meta.n_seqs:
             ops.reshape_and_cache(k_new[nd:], v_new[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
                                   meta.slot_mapping[nd:], mgr.err)
-            ops.paged_prefill_attention(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
-                                        meta.block_tables[nd:], meta.query_start_loc,
-                                        meta.num_prior_dev[nd:], meta.max_query_len, scale,
-                                        out=out[nd:], err=mgr.err)
+            self._prefill(layer, q, meta, scale, out)
         if advance and layer == mgr.num_layers - 1:
             self._advance(meta)
         return out
+
+    def _prefill(self, layer: int, q: torch.Tensor, meta: StepMetadata, scale: float,
+                 out: torch.Tensor) -> None:
+        """The step's chunked-prefill launch over the 16-bit pools for the rows
+        after the decode sequences (arguments validated on the first layer)."""
+        nd, mgr = meta.n_decode, self.mgr
+        plan = meta.prefill_plan
+        if plan is None or plan.scale != scale:
+            plan = meta.prefill_plan = ops.PrefillPlan(
+                meta.block_tables[nd:], meta.query_start_loc, meta.num_prior_dev[nd:],
+                meta.max_query_len, scale, mgr.err)
+        plan(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer], out[nd:])
 
     def _advance(self, meta: StepMetadata):
         """After the last layer: the step's tokens count as cached
@@ -621,15 +648,16 @@ class PagedKVCache:
         prefill).  Returns out [T, Hq, D].  Same results as rotating q and k
         with Rope.rotate and calling forward_layer."""
         mgr = self.mgr
-        mgr.flush_copies()
+        if mgr._pending:
+            mgr.flush_copies()
+        rope = meta.rope_plan
+        if rope is None or not rope.uses(positions, cos, sin):
+            rope = meta.rope_plan = ops.RopePlan(positions, cos, sin, meta.slot_mapping, mgr.err)
         if mgr.fp8:  # rotated k and v quantised into the fp8 pools in the same launch
-            q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer],
-                                           mgr.v_pool[layer], meta.slot_mapping, err=mgr.err,
-                                           k_scale=mgr.k_scale[layer], v_scale=mgr.v_scale[layer])
+            q = rope(qkv, mgr.k_pool[layer], mgr.v_pool[layer], mgr.k_scale[layer], mgr.v_scale[layer])
             return self._attend_fp8(layer, q, meta, scale, torch.empty_like(q) if out is None else out,
                                     advance)
-        q = ops.rope_reshape_and_cache(qkv, positions, cos, sin, mgr.k_pool[layer], mgr.v_pool[layer],
-                                       meta.slot_mapping, err=mgr.err)
+        q = rope(qkv, mgr.k_pool[layer], mgr.v_pool[layer])
         if out is None:
             out = torch.empty_like(q)
         nd = meta.n_decode
@@ -644,10 +672,7 @@ class PagedKVCache:
             plan(q if whole else q[:nd], mgr.k_pool[layer], mgr.v_pool[layer],
                  out if whole else out[:nd])
         if nd < meta.n_seqs:
-            ops.paged_prefill_attention(q[nd:], mgr.k_pool[layer], mgr.v_pool[layer],
-                                        meta.block_tables[nd:], meta.query_start_loc,
-                                        meta.num_prior_dev[nd:], meta.max_query_len, scale,
-                                        out=out[nd:], err=mgr.err)
+            self._prefill(layer, q, meta, scale, out)
         if advance and layer == mgr.num_layers - 1:
             self._advance(meta)
         return out

@@ -93,6 +93,9 @@ def random_weights(cfg: Qwen2Config, seed: int = 0, std: float = 0.02,
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """The reference's RMSNorm as written (qwen2.py:32-35): fp32 math, the
+    weight applied in fp32, one rounding to x's dtype.  The model's forward
+    uses torch's fused F.rms_norm, the same formula in one kernel."""
     dt = x.dtype
     xf = x.float()
     xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
@@ -150,7 +153,8 @@ class PagedQwen2Model:
                                 w[f"{p}.self_attn.v_proj.bias"]]),
                 wo=w[f"{p}.self_attn.o_proj.weight"],
                 ln2=w[f"{p}.post_attention_layernorm.weight"],
-                wgate=w[f"{p}.mlp.gate_proj.weight"], wup=w[f"{p}.mlp.up_proj.weight"],
+                # gate and up projections as one [2 I, H] GEMM operand
+                wgu=torch.cat([w[f"{p}.mlp.gate_proj.weight"], w[f"{p}.mlp.up_proj.weight"]]),
                 wdown=w[f"{p}.mlp.down_proj.weight"]))
         self.rope = Rope(cfg.head_dim, cfg.rope_theta, dev, dtype)
         self.scale = cfg.head_dim ** -0.5
@@ -175,32 +179,50 @@ class PagedQwen2Model:
             t_step = (ev(), ev())
             t_attn = [(ev(), ev()) for _ in self.layers]
             t_step[0].record()
-        h = self.embed[input_ids]
-        T = h.shape[0]
-        for li, lw in enumerate(self.layers):
-            residual = h
-            x = rms_norm(h, lw["ln1"], cfg.rms_norm_eps)
-            qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
-            if timing is not None:
-                t_attn[li][0].record()
-            if fused:
-                attn = kv_cache.forward_layer_qkv(li, qkv, positions, cos_t, sin_t, meta, self.scale)
-            else:
-                q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), cos, sin)
-                k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), cos, sin)
-                v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
-                attn = kv_cache.forward_layer(li, q, k, v, meta, self.scale)
-            if timing is not None:
-                t_attn[li][1].record()
-            h = residual + F.linear(attn.view(T, hq * d), lw["wo"])
-            residual = h
-            x = rms_norm(h, lw["ln2"], cfg.rms_norm_eps)
-            h = residual + F.linear(F.silu(F.linear(x, lw["wgate"])) * F.linear(x, lw["wup"]),
-                                    lw["wdown"])
-        h = rms_norm(h, self.final_norm, cfg.rms_norm_eps)
+        h = self._layers(self.embed[input_ids], positions, cos_t, sin_t,
+                         None if fused else (cos, sin), meta, kv_cache,
+                         t_attn if timing is not None else None)
+        h = F.rms_norm(h, (cfg.hidden_size,), self.final_norm, cfg.rms_norm_eps)
         last = torch.tensor([s.flat_start + s.num_tokens - 1 for s in seq_infos], device=self.device)
         logits = F.linear(h[last], self.embed)
         if timing is not None:
             t_step[1].record()
             timing.append((t_step, t_attn))
         return logits
+
+    def _layers(self, h, positions, cos_t, sin_t, rot, meta, kv_cache, t_attn=None, advance=True):
+        """The 24 decoder layers over the flat batch h [T, hidden] (the step's
+        metadata in `meta`); rot = (cos, sin) per token for the unfused RoPE,
+        None for the fused RoPE + append launch.
+
+        The reference's layer math (qwen2.py:143-176) in fewer launches, all
+        torch operations outside the attention: fused F.rms_norm; the residual
+        adds folded into the o_proj and down_proj GEMMs (addmm: the sum is
+        rounded once); gate and up as one GEMM."""
+        cfg = self.cfg
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        H, I, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
+        T = h.shape[0]
+        for li, lw in enumerate(self.layers):
+            residual = h
+            x = F.rms_norm(h, (H,), lw["ln1"], eps)
+            qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
+            if t_attn is not None:
+                t_attn[li][0].record()
+            if rot is None:
+                attn = kv_cache.forward_layer_qkv(li, qkv, positions, cos_t, sin_t, meta, self.scale,
+                                                  advance=advance)
+            else:
+                cos, sin = rot
+                q = Rope.rotate(qkv[:, : hq * d].view(T, hq, d), cos, sin)
+                k = Rope.rotate(qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d), cos, sin)
+                v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+                attn = kv_cache.forward_layer(li, q, k, v, meta, self.scale, advance=advance)
+            if t_attn is not None:
+                t_attn[li][1].record()
+            h = torch.addmm(residual, attn.view(T, hq * d), lw["wo"].t())
+            residual = h
+            x = F.rms_norm(h, (H,), lw["ln2"], eps)
+            gu = torch.mm(x, lw["wgu"].t())
+            h = torch.addmm(residual, F.silu(gu[:, :I]) * gu[:, I:], lw["wdown"].t())
+        return h

@@ -220,21 +220,68 @@ def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torc
         raise ValueError("pagedkv: q_out must be [tokens, n_q_heads, head_dim] in the qkv dtype")
     if T == 0:
         return q_out
-    if fp8:
-        rc = _lib.load().pkv_rope_reshape_and_cache_fp8(
-            q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),
-            positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], k_pool.data_ptr(),
-            v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), slot_mapping.data_ptr(), T,
-            nb, bs, hq, hkv, d, dtype_code(dt), _ptr(err), _stream(qkv))
-        _lib.check(rc, "pkv_rope_reshape_and_cache_fp8")
-        return q_out
-    rc = _lib.load().pkv_rope_reshape_and_cache(
-        q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),
-        positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], k_pool.data_ptr(),
-        v_pool.data_ptr(), slot_mapping.data_ptr(), T, nb, bs, hq, hkv, d, dtype_code(dt), _ptr(err),
-        _stream(qkv))
-    _lib.check(rc, "pkv_rope_reshape_and_cache")
+    name, args = _rope_args(qkv, positions, cos, sin, k_pool, v_pool, slot_mapping, q_out, err,
+                            k_scale, v_scale, hq)
+    _lib.check(getattr(_lib.load(), name)(*args), name)
     return q_out
+
+
+def _rope_args(qkv, positions, cos, sin, k_pool, v_pool, slot_mapping, q_out, err, k_scale, v_scale,
+               hq):
+    """C arguments of pkv_rope_reshape_and_cache(_fp8) for validated tensors:
+    (entry point name, argument tuple)."""
+    nb, bs, hkv, d = k_pool.shape
+    T = qkv.shape[0]
+    head = (q_out.data_ptr(), _row_stride(q_out, "q_out"), qkv.data_ptr(), qkv.stride(0),
+            positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], k_pool.data_ptr(),
+            v_pool.data_ptr())
+    tail = (slot_mapping.data_ptr(), T, nb, bs, hq, hkv, d, dtype_code(qkv.dtype), _ptr(err),
+            _stream(qkv))
+    if k_scale is not None:
+        return "pkv_rope_reshape_and_cache_fp8", head + (k_scale.data_ptr(), v_scale.data_ptr()) + tail
+    return "pkv_rope_reshape_and_cache", head + tail
+
+
+class RopePlan:
+    """rope_reshape_and_cache for the layers of one step, which share
+    positions, RoPE tables, slot mapping and error word.  The first call (and
+    any call whose tensors differ in dtype, shape, stride or stream from the
+    previous one) validates through rope_reshape_and_cache; the others only
+    fill in the layer's pointers (q_out, qkv, pools, fp8 scales)."""
+
+    def __init__(self, positions, cos, sin, slot_mapping, err=None):
+        self._static = (positions, cos, sin, slot_mapping, err)
+        self._key = None
+        self._args: list = []
+
+    def uses(self, positions, cos, sin) -> bool:
+        """Whether this plan was made for these positions and tables."""
+        st = self._static
+        return st[0] is positions and st[1] is cos and st[2] is sin
+
+    def __call__(self, qkv, k_pool, v_pool, k_scale=None, v_scale=None) -> torch.Tensor:
+        key = (qkv.dtype, qkv.shape, qkv.stride(), k_pool.dtype, k_pool.shape, k_pool.stride(),
+               v_pool.shape, v_pool.stride(), k_scale is None, v_scale is None, qkv.get_device(),
+               _raw_stream(qkv))
+        if key != self._key:
+            positions, cos, sin, slots, err = self._static
+            q_out = rope_reshape_and_cache(qkv, positions, cos, sin, k_pool, v_pool, slots, err=err,
+                                           k_scale=k_scale, v_scale=v_scale)
+            if qkv.shape[0] and (k_scale is None) == (v_scale is None):
+                name, args = _rope_args(qkv, positions, cos, sin, k_pool, v_pool, slots, q_out, err,
+                                        k_scale, v_scale, q_out.shape[1])
+                self._fn, self._name, self._args = getattr(_lib.load(), name), name, list(args)
+                self._qshape, self._key = tuple(q_out.shape), key
+            return q_out
+        q_out = torch.empty(self._qshape, dtype=qkv.dtype, device=qkv.device)
+        a = self._args
+        a[0], a[2], a[8], a[9] = q_out.data_ptr(), qkv.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
+        if k_scale is not None:
+            a[10], a[11] = k_scale.data_ptr(), v_scale.data_ptr()
+        rc = self._fn(*a)
+        if rc:
+            _lib.check(rc, self._name)
+        return q_out
 
 
 def _check_tables(block_tables: torch.Tensor) -> None:
@@ -718,6 +765,37 @@ def paged_prefill_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch
         return out
     _lib.check(_lib.load().pkv_paged_prefill_attention(*args), "pkv_paged_prefill_attention")
     return out
+
+
+class PrefillPlan:
+    """paged_prefill_attention for the layers of one step, which share block
+    tables, query_start_loc, num_prior, max_query_len, scale and error word,
+    with the same reuse of validated arguments as DecodePlan (pointers
+    swapped: out, q, pools)."""
+
+    def __init__(self, block_tables, query_start_loc, num_prior, max_query_len, scale, err=None):
+        self._static = (block_tables, query_start_loc, num_prior, max_query_len, scale, err)
+        self.scale = scale
+        self._key = None
+        self._args: list = []
+
+    def __call__(self, q, k_pool, v_pool, out) -> torch.Tensor:
+        key = (q.dtype, k_pool.dtype, v_pool.dtype, out.dtype, q.shape, q.stride(), k_pool.shape,
+               k_pool.stride(), v_pool.shape, v_pool.stride(), out.shape, out.stride(),
+               q.get_device(), _raw_stream(q))
+        if key != self._key:
+            tables, qsl, prior, mql, scale, err = self._static
+            args, out = _prefill_args(q, k_pool, v_pool, tables, qsl, prior, mql, scale, out, err)
+            self._args, self._key = list(args), key
+        else:
+            a = self._args
+            a[0], a[2], a[4], a[5] = out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
+        if self._args[13] == 0:
+            return out
+        rc = _lib.load().pkv_paged_prefill_attention(*self._args)
+        if rc:
+            _lib.check(rc, "pkv_paged_prefill_attention")
+        return out
 
 
 def bind_paged_prefill_attention(q, k_pool, v_pool, block_tables, query_start_loc, num_prior,

@@ -19,7 +19,10 @@ restated so that a run here makes the same decisions, token for token:
 What differs is the execution of a step: the device metadata is built once
 (PagedKVCache.prepare_step), every layer runs one append + at most two
 attention launches, and the greedy argmax of the whole batch comes back to
-the host in one copy.
+the host in one copy.  With cuda_graphs=True a decode-only step (every
+scheduled sequence adds one token) replays a captured CUDA graph of the
+model step (pagedkv.graphs.DecodeGraphs); mixed and prefill steps run
+eagerly.  The decisions are the same either way.
 """
 
 from __future__ import annotations
@@ -71,7 +74,8 @@ class Request:
 class Scheduler:
     def __init__(self, model: PagedQwen2Model, block_manager: BlockManager, max_num_seqs: int = 8,
                  max_batched_tokens: int = 256, enable_prefix_cache: bool = True,
-                 eos_ids: set[int] | None = None):
+                 eos_ids: set[int] | None = None, cuda_graphs: bool = False,
+                 graph_max_blocks: int = 64):
         self.model = model
         self.mgr = block_manager
         self.kv = PagedKVCache(block_manager)
@@ -83,6 +87,17 @@ class Scheduler:
         self.running: list[Request] = []
         self.metrics = dict(requests_finished=0, requests_cancelled=0, preemptions=0, steps=0,
                             tokens_generated=0, prefill_tokens_computed=0, prefix_cache_hit_tokens=0)
+        self.cuda_graphs = cuda_graphs and model.device.type == "cuda"
+        self.graph_max_blocks = graph_max_blocks
+        self.graphs = None  # DecodeGraphs, made at the first decode-only step
+
+    def decode_graphs(self):
+        """The CUDA-graph runner of decode-only steps (cuda_graphs=True)."""
+        if self.graphs is None:
+            from .graphs import DecodeGraphs
+            self.graphs = DecodeGraphs(self.model, self.kv, self.max_num_seqs,
+                                       max_blocks_per_seq=self.graph_max_blocks)
+        return self.graphs
 
     # ---- memory ----------------------------------------------------------
 
@@ -222,7 +237,10 @@ class Scheduler:
         ids = torch.tensor(flat, dtype=torch.long)
         if self.model.device.type == "cuda":
             ids = ids.pin_memory().to(self.model.device, non_blocking=True)
-        logits = self.model.forward(ids, infos, self.kv)
+        if self.cuda_graphs and self.model.timing is None and self.decode_graphs().supports(infos):
+            logits = self.graphs.forward(ids, infos)
+        else:
+            logits = self.model.forward(ids, infos, self.kv)
         tokens = logits.float().argmax(dim=-1).tolist()  # greedy, one D2H per step
 
         now = time.monotonic()

@@ -51,11 +51,11 @@ def weights():
     return random_weights(Qwen2Config(), seed=C.E2E_SEED, final_norm_scale=C.E2E_FINAL_NORM_SCALE)
 
 
-def run_engine(model, sc, dtype):
+def run_engine(model, sc, dtype, **sched_kw):
     mgr = BlockManager(sc["num_blocks"], 16, 24, 2, 64, device="cuda", dtype=dtype)
     sched = Scheduler(model, mgr, max_num_seqs=sc["max_num_seqs"],
                       max_batched_tokens=sc["max_batched_tokens"],
-                      enable_prefix_cache=sc["prefix_cache"], eos_ids={-1})
+                      enable_prefix_cache=sc["prefix_cache"], eos_ids={-1}, **sched_kw)
     reqs = []
     for i, p in enumerate(sc["prompts"]):
         r = Request(i, list(p), max_new_tokens=sc["max_new_tokens"])
@@ -84,12 +84,17 @@ def first_divergence(a, b):
     return None if len(a) == len(b) else min(len(a), len(b))
 
 
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graphs"])
 @pytest.mark.parametrize("scenario", ["prefix", "preempt"])
-def test_fp32_greedy_streams_identical_to_reference(golden_e2e, weights, scenario):
+def test_fp32_greedy_streams_identical_to_reference(golden_e2e, weights, scenario, graphs):
+    """graphs: decode-only steps replay CUDA graphs (pagedkv.graphs); the
+    table width starts at 2 blocks so the runner also regrows and recaptures."""
     sc = C.e2e_scenarios()[scenario]
     g = golden_e2e[scenario]
     model = PagedQwen2Model(Qwen2Config(), weights, device="cuda", dtype=torch.float32)
-    reqs, sched = run_engine(model, sc, torch.float32)
+    reqs, sched = run_engine(model, sc, torch.float32, cuda_graphs=graphs, graph_max_blocks=2)
+    if graphs:
+        assert sched.graphs.replays > 0 and sched.graphs.W > 2
     for r, ref in zip(reqs, g["outputs"]):
         assert r.output_ids == ref, (
             f"req {r.req_id}: first divergence at token {first_divergence(r.output_ids, ref)}")
@@ -100,25 +105,29 @@ def test_fp32_greedy_streams_identical_to_reference(golden_e2e, weights, scenari
     assert [r.preemptions for r in reqs] == g["preemptions"]
 
 
-def test_fp32_unfused_rope_path_identical_to_reference(golden_e2e, weights):
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graphs"])
+def test_fp32_unfused_rope_path_identical_to_reference(golden_e2e, weights, graphs):
     """The same fp32 parity through the unfused path (torch RoPE +
     forward_layer with the decode kernel's own append)."""
     sc = C.e2e_scenarios()["prefix"]
     g = golden_e2e["prefix"]
     model = PagedQwen2Model(Qwen2Config(), weights, device="cuda", dtype=torch.float32,
                             fused_rope=False)
-    reqs, _ = run_engine(model, sc, torch.float32)
+    reqs, sched = run_engine(model, sc, torch.float32, cuda_graphs=graphs)
+    assert not graphs or sched.graphs.replays > 0
     for r, ref in zip(reqs, g["outputs"]):
         assert r.output_ids == ref, (
             f"req {r.req_id}: first divergence at token {first_divergence(r.output_ids, ref)}")
 
 
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graphs"])
 @pytest.mark.parametrize("scenario", ["prefix", "preempt"])
-def test_fp16_greedy_streams_match_reference(golden_e2e, margins, weights, scenario):
+def test_fp16_greedy_streams_match_reference(golden_e2e, margins, weights, scenario, graphs):
     sc = C.e2e_scenarios()[scenario]
     g = golden_e2e[scenario]
     model = PagedQwen2Model(Qwen2Config(), weights, device="cuda", dtype=torch.float16)
-    reqs, sched = run_engine(model, sc, torch.float16)
+    reqs, sched = run_engine(model, sc, torch.float16, cuda_graphs=graphs)
+    assert not graphs or sched.graphs.replays > 0
     for r, ref, marg in zip(reqs, g["outputs"], margins[scenario]):
         d = first_divergence(r.output_ids, ref)
         if d is None:

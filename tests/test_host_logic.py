@@ -156,6 +156,47 @@ def test_step_arrays_capacity_assert():
         kv.step_arrays([(0, 1)])
 
 
+def test_step_arrays_padded_fixed_width_layout():
+    """step_arrays(width=W, pad_to=R) (the CUDA-graph decode step): the real
+    rows as in the unpadded arrays, re-laid for R rows of W blocks; padding
+    rows have a zero table row, context length 0, num_prior 0 and slot -1."""
+    m = mgr(num_blocks=64, block_size=16)
+    kv = PagedKVCache(m)
+    kv.add_sequence(10, [m.allocate() for _ in range(3)], 33)
+    kv.add_sequence(11, [m.allocate() for _ in range(2)], 15)
+    kv.add_sequence(12, [m.allocate() for _ in range(1)], 0)
+    seqs = [(10, 1), (11, 1), (12, 1)]
+    base = kv.step_arrays(seqs)
+    B, W0 = base["B"], base["W"]
+    bt0 = base["ints"][:B * W0].reshape(B, W0)
+    R, W = 8, 5
+    a = kv.step_arrays(seqs, width=W, pad_to=R)
+    assert a["W"] == W and a["R"] == R and a["B"] == B and a["n_decode"] == B
+    ints = a["ints"]
+    assert ints.size == R * W + 2 * R + 1
+    tabs = ints[:R * W].reshape(R, W)
+    for i, (s, _) in enumerate(seqs):
+        u = (kv.seq_len(s) + 1 + 15) // 16
+        assert tabs[i, :u].tolist() == bt0[i, :u].tolist() == kv.block_tables[s][:u]
+    assert not tabs[B:].any()
+    assert ints[R * W:R * W + R].tolist() == [34, 16, 1] + [0] * (R - B)
+    assert ints[R * W + R:R * W + 2 * R].tolist() == [33, 15, 0] + [0] * (R - B)
+    assert ints[R * W + 2 * R:].tolist() == [0]
+    assert a["slots"].tolist() == base["slots"].tolist() + [-1] * (R - B)
+    with pytest.raises(AssertionError):  # a sequence needs 3 blocks
+        kv.step_arrays(seqs, width=2, pad_to=R)
+    with pytest.raises(AssertionError):  # padding is for decode-only steps
+        kv.step_arrays([(10, 1), (12, 4)], pad_to=R)
+
+
+def test_graph_buckets():
+    from pagedkv.graphs import default_buckets
+    assert default_buckets(1) == [1]
+    assert default_buckets(6) == [1, 2, 4, 6]
+    assert default_buckets(128) == [1, 2, 4, 8, 16, 32, 48, 64, 80, 96, 112, 128]
+    assert default_buckets(200) == [1, 2, 4, 8, 16, 32, 48, 64, 80, 96, 112, 128, 160, 192, 200]
+
+
 def test_no_cpu_pools():
     with pytest.raises(RuntimeError):
         BlockManager(8, 16, 1, 2, 64, device="cpu")
