@@ -16,8 +16,11 @@
 // (multiply in fp32, round; add in fp32, round; no fused multiply-add), so
 // the result is bit-identical to that path for fp32, fp16 and bf16.
 //
-// One warp per token; lane l owns the pairs (i, i + D/2) for i = l, l + 32,
-// ... of every head, so each head's loads and stores are coalesced.
+// One warp per (token, head) of the projection row: Hq query heads, Hkv key
+// heads, Hkv value heads.  Lane l owns the pairs (i, i + D/2) for i = l,
+// l + 32, ..., so a head's loads and stores are coalesced, and a decode step
+// of B tokens runs B x (Hq + 2 Hkv) independent warps (one warp per token
+// looping over the heads left a 64-token step latency-bound on 8 SMs).
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
 
@@ -56,46 +59,38 @@ __global__ void __launch_bounds__(256) rope_reshape_and_cache_kernel(
   // prologue start
   pdl_wait();
   pdl_trigger();
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int heads = hq + 2 * hkv;
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (t >= n_tokens) return;
+  if (w >= static_cast<int64_t>(n_tokens) * heads) return;
+  const int t = static_cast<int>(w / heads);
+  const int h = static_cast<int>(w - static_cast<int64_t>(t) * heads);
   const int64_t pos = __ldg(positions + t);
   if (pos < 0 || pos >= max_pos) {
-    if (lane == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
+    if (lane == 0 && h == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
     return;
   }
   const int64_t slot = __ldg(slots + t);
-  if (slot >= n_slots) {
-    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
-  }
+  if (slot >= n_slots && lane == 0 && h == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
   const bool store_kv = slot >= 0 && slot < n_slots;  // slot -1: padding token
-  const E* row = qkv + static_cast<int64_t>(t) * qkv_stride;
+  if (h >= hq && !store_kv) return;
+  const E* x = qkv + static_cast<int64_t>(t) * qkv_stride + static_cast<int64_t>(h) * d;
+  if (h >= hq + hkv) {  // v: as projected
+    E* vdst = v_pool + slot * (static_cast<int64_t>(hkv) * d) + static_cast<int64_t>(h - hq - hkv) * d;
+    for (int i = lane; i < d; i += 32) vdst[i] = __ldg(x + i);
+    return;
+  }
   const E* cr = cos_t + pos * d;
   const E* sr = sin_t + pos * d;
   const int half = d >> 1;
-  E* qrow = q_out + static_cast<int64_t>(t) * q_out_stride;
-  E* krow = store_kv ? k_pool + slot * (static_cast<int64_t>(hkv) * d) : nullptr;
+  E* dst = h < hq ? q_out + static_cast<int64_t>(t) * q_out_stride + static_cast<int64_t>(h) * d
+                  : k_pool + slot * (static_cast<int64_t>(hkv) * d) + static_cast<int64_t>(h - hq) * d;
   for (int i = lane; i < half; i += 32) {
     const float c1 = tof<E>(__ldg(cr + i)), c2 = tof<E>(__ldg(cr + i + half));
     const float s1 = tof<E>(__ldg(sr + i)), s2 = tof<E>(__ldg(sr + i + half));
-    for (int h = 0; h < hq + hkv; ++h) {
-      const E* x = row + h * d;
-      const float x1 = tof<E>(__ldg(x + i)), x2 = tof<E>(__ldg(x + i + half));
-      const E o1 = rot_term<E>(x1, c1, -x2, s1);
-      const E o2 = rot_term<E>(x2, c2, x1, s2);
-      if (h < hq) {
-        qrow[h * d + i] = o1;
-        qrow[h * d + i + half] = o2;
-      } else if (store_kv) {
-        krow[(h - hq) * d + i] = o1;
-        krow[(h - hq) * d + i + half] = o2;
-      }
-    }
-  }
-  if (store_kv) {
-    const E* vsrc = row + (hq + hkv) * d;
-    E* vdst = v_pool + slot * (static_cast<int64_t>(hkv) * d);
-    for (int i = lane; i < hkv * d; i += 32) vdst[i] = __ldg(vsrc + i);
+    const float x1 = tof<E>(__ldg(x + i)), x2 = tof<E>(__ldg(x + i + half));
+    dst[i] = rot_term<E>(x1, c1, -x2, s1);
+    dst[i + half] = rot_term<E>(x2, c2, x1, s2);
   }
 }
 
@@ -115,78 +110,80 @@ __global__ void __launch_bounds__(256) rope_reshape_and_cache_fp8_kernel(
     int* err) {
   pdl_wait();
   pdl_trigger();
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int heads = hq + 2 * hkv;
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (t >= n_tokens) return;
+  if (w >= static_cast<int64_t>(n_tokens) * heads) return;  // warp-uniform
+  const int t = static_cast<int>(w / heads);
+  const int h = static_cast<int>(w - static_cast<int64_t>(t) * heads);
   const int64_t pos = __ldg(positions + t);
   if (pos < 0 || pos >= max_pos) {
-    if (lane == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
+    if (lane == 0 && h == 0) raise_flag(err, PKV_FLAG_POSITION_OUT_OF_RANGE);
     return;
   }
   const int64_t slot = __ldg(slots + t);
-  if (slot >= n_slots) {
-    if (lane == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
-  }
+  if (slot >= n_slots && lane == 0 && h == 0) raise_flag(err, PKV_FLAG_SLOT_OUT_OF_RANGE);
   const bool store_kv = slot >= 0 && slot < n_slots;  // slot -1: padding token
-  const E* row = qkv + static_cast<int64_t>(t) * qkv_stride;
+  if (h >= hq && !store_kv) return;
+  const E* x = qkv + static_cast<int64_t>(t) * qkv_stride + static_cast<int64_t>(h) * d;
   const E* cr = cos_t + pos * d;
   const E* sr = sin_t + pos * d;
   const int half = d >> 1;
-  E* qrow = q_out + static_cast<int64_t>(t) * q_out_stride;
-  // rotated element pair (i, i + half) of head h of the projection row
-  auto rot = [&](int h, int i, E& o1, E& o2) {
+  // rotated element pair (i, i + half) of this head
+  auto rot = [&](int i, E& o1, E& o2) {
     const float c1 = tof<E>(__ldg(cr + i)), c2 = tof<E>(__ldg(cr + i + half));
     const float s1 = tof<E>(__ldg(sr + i)), s2 = tof<E>(__ldg(sr + i + half));
-    const E* x = row + h * d;
     const float x1 = tof<E>(__ldg(x + i)), x2 = tof<E>(__ldg(x + i + half));
     o1 = rot_term<E>(x1, c1, -x2, s1);
     o2 = rot_term<E>(x2, c2, x1, s2);
   };
-  for (int h = 0; h < hq; ++h) {
+  if (h < hq) {
+    E* qrow = q_out + static_cast<int64_t>(t) * q_out_stride + static_cast<int64_t>(h) * d;
     for (int i = lane; i < half; i += 32) {
       E o1, o2;
-      rot(h, i, o1, o2);
-      qrow[h * d + i] = o1;
-      qrow[h * d + i + half] = o2;
+      rot(i, o1, o2);
+      qrow[i] = o1;
+      qrow[i + half] = o2;
     }
+    return;
   }
-  if (!store_kv) return;
-  for (int h = 0; h < hkv; ++h) {
-    // k: rotated
-    float amax = 0.f;
+  float amax = 0.f;
+  if (h < hq + hkv) {  // k: rotated
+    const int kh = h - hq;
     for (int i = lane; i < half; i += 32) {
       E o1, o2;
-      rot(hq + h, i, o1, o2);
+      rot(i, o1, o2);
       amax = fmaxf(amax, fmaxf(fabsf(tof<E>(o1)), fabsf(tof<E>(o2))));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    float sc = fp8_row_scale(amax);
-    uint8_t* kd = k_pool + (slot * hkv + h) * d;
+    const float sc = fp8_row_scale(amax);
+    uint8_t* kd = k_pool + (slot * hkv + kh) * d;
     for (int i = lane; i < half; i += 32) {
       E o1, o2;
-      rot(hq + h, i, o1, o2);
+      rot(i, o1, o2);
       kd[i] = fp8_quantize(tof<E>(o1), sc);
       kd[i + half] = fp8_quantize(tof<E>(o2), sc);
     }
-    if (lane == 0) k_scale[slot * hkv + h] = sc;
-    // v: as projected
-    const E* vsrc = row + (hq + hkv + h) * d;
-    amax = 0.f;
-    for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(tof<E>(__ldg(vsrc + i))));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    sc = fp8_row_scale(amax);
-    uint8_t* vd = v_pool + (slot * hkv + h) * d;
-    for (int i = lane; i < d; i += 32) vd[i] = fp8_quantize(tof<E>(__ldg(vsrc + i)), sc);
-    if (lane == 0) v_scale[slot * hkv + h] = sc;
+    if (lane == 0) k_scale[slot * hkv + kh] = sc;
+    return;
   }
+  const int vh = h - hq - hkv;  // v: as projected
+  for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(tof<E>(__ldg(x + i))));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float sc = fp8_row_scale(amax);
+  uint8_t* vd = v_pool + (slot * hkv + vh) * d;
+  for (int i = lane; i < d; i += 32) vd[i] = fp8_quantize(tof<E>(__ldg(x + i)), sc);
+  if (lane == 0) v_scale[slot * hkv + vh] = sc;
 }
 
 cudaError_t launch_rope_reshape_and_cache(const RopeArgs& a, cudaStream_t stream) {
   if (a.n_tokens == 0) return cudaSuccess;
   const int threads = 256;
-  const int grid = (a.n_tokens + 7) / 8;
+  const int64_t warps = static_cast<int64_t>(a.n_tokens) * (a.n_q_heads + 2 * a.n_kv_heads);
+  if ((warps + 7) / 8 > 0x7fffffff) return cudaErrorInvalidValue;
+  const int grid = static_cast<int>((warps + 7) / 8);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
