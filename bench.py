@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--rate", type=float, default=40.0, help="config 5: Poisson arrivals per second")
     ap.add_argument("--max-num-seqs", type=int, default=128)
     ap.add_argument("--no-cuda-graphs", action="store_true",
-                    help="config 5: run decode-only steps eagerly instead of replaying CUDA graphs")
+                    help="config 5: run every step eagerly instead of replaying CUDA graphs")
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
@@ -673,8 +673,8 @@ def run_e2e(args):
                       max_batched_tokens=args.max_batched_tokens, enable_prefix_cache=True,
                       eos_ids=set(), cuda_graphs=not args.no_cuda_graphs)
     t_cap = time.perf_counter()
-    if sched.cuda_graphs:  # every padded batch size, before the timed run
-        sched.decode_graphs().capture_all()
+    if sched.cuda_graphs:  # every padded step shape, before the timed run
+        sched.step_graphs().capture_all()
     t_cap = time.perf_counter() - t_cap
 
     def drive(n_conv, arr):
@@ -734,8 +734,8 @@ def run_e2e(args):
                    "conversations": n, "rate_per_s": args.rate, "max_num_seqs": args.max_num_seqs,
                    "max_batched_tokens": args.max_batched_tokens, "num_blocks": num_blocks,
                    "cuda_graphs": sched.cuda_graphs},
-        "cuda_graphs": {"decode_steps_replayed": replays, "steps": steps_timed,
-                        "buckets": sched.graphs.buckets if sched.graphs is not None else None,
+        "cuda_graphs": {"steps_replayed": replays, "steps": steps_timed,
+                        "shapes": len(sched.graphs.graphs) if sched.graphs is not None else 0,
                         "capture_s": round(t_cap, 3)},
         "generated_tokens": gen, "wall_s": round(wall, 3),
         "ttft_ms": {"p50": pct(ttft, 50), "p99": pct(ttft, 99)},

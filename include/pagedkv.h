@@ -363,7 +363,10 @@ int pkv_paged_decode_attention_noalloc(void* out, int64_t out_row_stride, const 
  * attends to keys 0 .. num_prior[s] + i of the sequence (causal with the
  * reference's num_prior offset; the chunk's own K/V must already be in the
  * pool).  Shared radix-prefix blocks are read in place.  max_query_len bounds
- * query_start_loc[s+1] - query_start_loc[s]; n_tokens = query_start_loc[n_seqs].
+ * query_start_loc[s+1] - query_start_loc[s]; n_tokens >= query_start_loc[n_seqs]:
+ * rows from query_start_loc[n_seqs] to n_tokens are padding (a fixed-shape
+ * step, e.g. a captured CUDA graph, with fewer real tokens), neither read nor
+ * written; a sequence with no rows is skipped.
  */
 int pkv_paged_prefill_attention(void* out, int64_t out_row_stride, const void* q,
                                 int64_t q_row_stride, const void* k_pool, const void* v_pool,

@@ -55,6 +55,10 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(A
     total = max(a.context_lens[s], 0);
     limit = total;
   } else {
+    // rows at or past the last query start are padding (a fixed-shape step
+    // with fewer real tokens): no sequence owns them, their output rows stay
+    // as they are, as in the tensor-core prefill
+    if (t >= a.query_start_loc[a.n_seqs]) return;
     int lo = 0, hi = a.n_seqs - 1;  // last s with query_start_loc[s] <= t
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;

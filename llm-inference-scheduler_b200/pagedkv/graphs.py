@@ -1,42 +1,56 @@
-"""CUDA graphs of the decode-only model step.
+"""CUDA graphs of the model step (decode-only and mixed decode + prefill).
 
-A decode-only step (every scheduled sequence adds one token) of the 24-layer
-model is about 11 launches per layer, some 270 in all.  Issued from Python
-one by one they cost more host time than the GPU spends on them.  `DecodeGraphs` captures
-the whole step (embedding gather, 24 layers with the fused RoPE + append and
-the scheduled decode attention, final norm, LM head) once per padded batch
-size and replays it: a step then costs one host-to-device copy of its
-metadata and one graph launch.
+A step of the 24-layer model is about 11 launches per layer, some 270 in
+all.  Issued from Python one by one they cost more host time than the GPU
+spends on them (about 4 ms of host time for a step of 96 decodes and a
+128-token chunk, against under 2 ms of kernels).  `StepGraphs` captures the
+whole step once per padded shape and replays it: a step then costs one
+host-to-device copy of its metadata, one or two small device copies of the
+token ids, and one graph launch.
 
-Fixed shapes make the replay valid for any decode step of up to R
-sequences:
-* the step's metadata lives in one device buffer, laid out for R rows and a
-  block-table width of W blocks: tables [R, W] | context lens [R] |
-  num_prior [R] | query_start_loc [1] (int32), then slots [R] and positions
-  [R] (int64).  `PagedKVCache.step_arrays(width=W, pad_to=R)` writes it into a
-  pinned staging buffer; one copy moves it;
-* rows past the step's B sequences are padding: context length 0 (the
-  decode kernel gives them no blocks and the merge writes zero rows), slot
-  -1 (the RoPE + append launch stores nothing), positions 0;
+Shapes.  A graph is keyed (R, P):
+* P = 0: a decode-only step of up to R sequences (R in `buckets`);
+* P > 0: a mixed step of up to R decode sequences (R in `mixed_rows`) and up
+  to `prefill_seqs` prefill sequences with up to P new tokens in all (P in
+  `prefill_tokens`).  The flat batch is R decode rows, then P prefill rows.
+
+Fixed shapes make a replay valid for any step that fits:
+* the step's metadata lives in one device buffer laid out for S = R +
+  prefill_seqs sequence rows and a block-table width of W blocks: tables
+  [S, W] | context lens [S] | num_prior [S] | query_start_loc [prefill_seqs
+  + 1] (int32), then slots [R + P], positions [R + P] and the LM-head rows
+  [R + prefill_seqs] (int64).  The host fills a pinned staging copy; one copy
+  moves it;
+* padding decode rows have context length 0 (the decode kernel gives them no
+  blocks, the merge writes zero rows) and slot -1 (the RoPE + append launch
+  stores nothing); padding prefill sequences have no query rows (their
+  prefill CTAs return at once); padding prefill rows belong to no sequence
+  and have slot -1;
 * the decode schedule is built inside the graph from that metadata, so the
-  stream-K partition follows the step's real lengths;
+  stream-K partition follows the step's real lengths; the chunked-prefill
+  launch is sized for P query rows and prefill_seqs sequences, and its CTAs
+  past a sequence's rows return;
+* the LM head runs on the rows listed in the metadata: the decode rows, then
+  each prefill sequence's last row, so the first B logits rows are the
+  step's sequences in order;
 * the runner owns the decode schedule, the RoPE tables (sized for W * 16
-  positions) and the logits buffer; the split-K workspace is the cache's,
-  sized for R rows before the first capture and held here so a later
-  reallocation by an eager step cannot free it under a graph.
+  positions) and the logits buffer; the cache's split-K workspace and fp8
+  prefill scratch are sized for the largest graph before the first capture
+  and held here, so a later reallocation by an eager step cannot free them
+  under a graph.
 
-Padding rows do not change the real rows: the schedule gives them no
-blocks, and every other operation of the step (GEMMs, RMSNorm, SwiGLU, the
-LM head) is row-independent.  The GEMMs see M = R instead of B, so the
-library may pick another algorithm: logits agree with the eager step to
-rounding, not bit for bit.
+Padding does not change the real rows: the attention kernels give padding
+rows no keys and no output, and every other operation of the step (GEMMs,
+RMSNorm, SwiGLU, the LM head) is row-independent.  The GEMMs see padded M,
+so the library may pick another algorithm: logits agree with the eager step
+to rounding, not bit for bit.
 
 Graphs are captured lazily (or all at once by `capture_all`) into one
-memory pool, largest first.  A step whose sequences need more than W
-blocks doubles W and drops the graphs.  Replays and eager steps share the
-current stream.
+memory pool, largest first.  A step whose sequences need more than W blocks
+doubles W and drops the graphs.  Replays and eager steps share the current
+stream.
 
-Reference: the decode path of mini_engine/scheduler.py step() +
+Reference: the step of mini_engine/scheduler.py step() +
 mini_engine/model/qwen2.py forward (one Python call per sequence and layer
 there).
 """
@@ -52,8 +66,8 @@ from .model import PagedQwen2Model, SequenceForwardInfo
 
 
 def default_buckets(max_batch: int) -> list[int]:
-    """Padded batch sizes: 1, 2, 4, 8, then steps of 16 up to 128 and of 32
-    beyond, and max_batch itself."""
+    """Padded batch sizes of decode-only steps: 1, 2, 4, 8, then steps of 16
+    up to 128 and of 32 beyond, and max_batch itself."""
     out = [b for b in (1, 2, 4, 8) if b < max_batch]
     b = 16
     while b < max_batch:
@@ -63,170 +77,316 @@ def default_buckets(max_batch: int) -> list[int]:
     return sorted(set(out))
 
 
+def mixed_row_buckets(max_batch: int) -> list[int]:
+    """Padded decode-row counts of mixed steps: 16, 32, then steps of 32, and
+    max_batch (padding decode rows cost little: no keys, and GEMM rows)."""
+    out = [b for b in (16, 32) if b < max_batch]
+    b = 64
+    while b < max_batch:
+        out.append(b)
+        b += 32
+    out.append(max_batch)
+    return sorted(set(out))
+
+
+def prefill_token_buckets(max_tokens: int) -> list[int]:
+    """Padded prefill-token counts of mixed steps: 32, 64, then steps of 64,
+    and max_tokens (padding rows cost GEMM work, so the steps are finer)."""
+    out = [b for b in (32, 64) if b < max_tokens]
+    b = 128
+    while b < max_tokens:
+        out.append(b)
+        b += 64
+    out.append(max_tokens)
+    return sorted(set(out))
+
+
+def graph_keys(buckets: list[int], mixed_rows: list[int], prefill_tokens: list[int],
+               max_tokens: int) -> list[tuple[int, int]]:
+    """Every (R, P) shape to capture: (R, 0) for the decode-only buckets, and
+    (R, P) for the mixed ones that the token budget can reach (the smallest
+    step of the shape, one more decode row than the bucket below and one
+    more prefill token than the bucket below, fits max_tokens)."""
+    out = [(R, 0) for R in buckets]
+    for i, R in enumerate(mixed_rows):
+        r_lo = mixed_rows[i - 1] + 1 if i else 0
+        for j, P in enumerate(prefill_tokens):
+            p_lo = prefill_tokens[j - 1] + 1 if j else 1
+            if r_lo + p_lo <= max_tokens:
+                out.append((R, P))
+    return out
+
+
 def _align16(n: int) -> int:
     return (n + 15) // 16 * 16
 
 
-class DecodeGraphs:
-    """Captured decode-only steps of `model` over `kv_cache`, one CUDA graph
-    per padded batch size (buckets), for steps of up to max(buckets)
-    sequences whose contexts fit max_blocks_per_seq blocks (grown by doubling
-    when a step needs more)."""
+def _bucket(buckets: list[int], n: int) -> int | None:
+    for b in buckets:
+        if b >= n:
+            return b
+    return None
+
+
+class StepGraphs:
+    """Captured steps of `model` over `kv_cache`: decode-only steps of up to
+    max_batch sequences, and (max_tokens given: the scheduler's token budget)
+    mixed steps of up to max_batch decodes plus up to prefill_seqs prefill
+    sequences of up to max_tokens new tokens, for contexts that fit
+    max_blocks_per_seq blocks (grown by doubling when a step needs more)."""
 
     def __init__(self, model: PagedQwen2Model, kv_cache: PagedKVCache, max_batch: int,
-                 max_blocks_per_seq: int = 64, buckets: list[int] | None = None):
+                 max_tokens: int | None = None, max_blocks_per_seq: int = 64,
+                 buckets: list[int] | None = None, prefill_seqs: int = 4):
         if model.device.type != "cuda":
             raise RuntimeError("pagedkv: CUDA graphs need the model on a CUDA device")
         self.model, self.kv = model, kv_cache
         self.buckets = sorted(buckets or default_buckets(max_batch))
         self.max_batch = self.buckets[-1]
+        self.prefill_seqs = prefill_seqs if max_tokens else 0
+        self.mixed_rows = mixed_row_buckets(self.max_batch) if max_tokens else []
+        self.prefill_tokens = prefill_token_buckets(max_tokens) if max_tokens else []
+        self.max_tokens = max_tokens or 0
         self.W = max(1, int(max_blocks_per_seq))
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
         self.replays = 0
+        self._key_set = set(self.keys())
         self._alloc()
 
-    # ---- buffers ----------------------------------------------------------
+    # ---- shapes and buffers ---------------------------------------------------
 
-    def _layout(self, R: int) -> tuple[int, int, int]:
-        """(int32 count, byte offset of the slots, total bytes) of an R-row step."""
-        n_ints = R * self.W + 2 * R + 1
-        s_off = _align16(4 * n_ints)
-        return n_ints, s_off, s_off + 16 * R
+    def keys(self) -> list[tuple[int, int]]:
+        return graph_keys(self.buckets, self.mixed_rows, self.prefill_tokens, self.max_tokens)
+
+    def _layout(self, R: int, P: int) -> dict:
+        """Byte offsets of an (R, P) step's metadata."""
+        NP = self.prefill_seqs if P else 0
+        S = R + NP
+        n_ints = S * self.W + 2 * S + NP + 1
+        o64 = _align16(4 * n_ints)
+        T = R + P
+        return dict(NP=NP, S=S, T=T, n_ints=n_ints, slots=o64, pos=o64 + 8 * T,
+                    last=o64 + 16 * T, end=o64 + 16 * T + 8 * (R + NP))
 
     def _alloc(self) -> None:
-        m, mgr = self.model, self.kv.mgr
-        cfg, dev = m.cfg, m.device
-        Rm = self.max_batch
-        nbytes = self._layout(Rm)[2]
+        m, kv = self.model, self.kv
+        mgr, cfg, dev = kv.mgr, m.cfg, m.device
+        keys = self.keys()
+        nbytes = max(self._layout(R, P)["end"] for R, P in keys)
+        rows = max(R + P for R, P in keys)
+        heads = max(R + self._layout(R, P)["NP"] for R, P in keys)
         self.graphs = {}
         self.pool = torch.cuda.graph_pool_handle()
         self.meta_dev = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         self.stage = [[torch.empty(nbytes, dtype=torch.uint8).pin_memory(), None] for _ in range(2)]
         self._stage_next = 0
-        self.ids = torch.zeros(Rm, dtype=torch.long, device=dev)
-        self.logits = torch.empty((Rm, cfg.vocab_size), dtype=m.dtype, device=dev)
+        self.ids = torch.zeros(rows, dtype=torch.long, device=dev)
+        self.logits = torch.empty((heads, cfg.vocab_size), dtype=m.dtype, device=dev)
+        Rm = max(R for R, _ in keys)
         self.schedule = ops.new_decode_schedule(Rm, self.W, dev)
-        self.workspace = self.kv.decode_workspace(Rm, cfg.num_attention_heads, cfg.head_dim)
+        self.workspace = kv.decode_workspace(Rm, cfg.num_attention_heads, cfg.head_dim)
+        self.scratch = None
+        if mgr.fp8 and self.prefill_seqs:
+            need = ops.prefill_fp8_scratch_bytes(self.prefill_seqs, self.W, mgr.num_kv_heads,
+                                                 cfg.head_dim)
+            if kv._fp8_scratch is None or kv._fp8_scratch.numel() < need:
+                kv._fp8_scratch = torch.empty(need, dtype=torch.uint8, device=dev)
+            self.scratch = kv._fp8_scratch
         cos, sin = m.rope.tables(self.W * mgr.block_size)
         self.cos, self.sin = cos, sin  # held: an eager step that grows the tables drops them
 
-    def _views(self, R: int) -> dict:
-        n_ints, s_off, _ = self._layout(R)
-        W, buf = self.W, self.meta_dev
-        ints = buf[: 4 * n_ints].view(torch.int32)
-        return dict(tables=ints[: R * W].view(R, W), ctx=ints[R * W: R * W + R],
-                    prior=ints[R * W + R: R * W + 2 * R], qsl=ints[R * W + 2 * R:],
-                    slots=buf[s_off: s_off + 8 * R].view(torch.int64),
-                    positions=buf[s_off + 8 * R: s_off + 16 * R].view(torch.int64))
+    def _views(self, R: int, P: int) -> dict:
+        L, W, buf = self._layout(R, P), self.W, self.meta_dev
+        S, NP, T = L["S"], L["NP"], L["T"]
+        ints = buf[: 4 * L["n_ints"]].view(torch.int32)
+        return dict(tables=ints[: S * W].view(S, W), ctx=ints[S * W: S * W + S],
+                    prior=ints[S * W + S: S * W + 2 * S], qsl=ints[S * W + 2 * S:],
+                    slots=buf[L["slots"]: L["slots"] + 8 * T].view(torch.int64),
+                    positions=buf[L["pos"]: L["pos"] + 8 * T].view(torch.int64),
+                    last=buf[L["last"]: L["last"] + 8 * (R + NP)].view(torch.int64))
 
-    def _meta(self, R: int) -> StepMetadata:
-        v = self._views(R)
-        return StepMetadata(seq_ids=list(range(R)), num_new=[1] * R, num_prior=[0] * R, n_tokens=R,
-                            n_decode=R, max_query_len=0, slot_mapping=v["slots"],
+    def _meta(self, R: int, P: int) -> StepMetadata:
+        v, S = self._views(R, P), self._layout(R, P)["S"]
+        return StepMetadata(seq_ids=list(range(S)), num_new=[1] * S, num_prior=[0] * S,
+                            n_tokens=R + P, n_decode=R, max_query_len=P, slot_mapping=v["slots"],
                             block_tables=v["tables"], context_lens=v["ctx"],
                             query_start_loc=v["qsl"], num_prior_dev=v["prior"])
 
     # ---- the captured step -------------------------------------------------
 
-    def _step(self, R: int) -> None:
-        """The decode-only step over the R-row metadata (what a graph holds)."""
+    def _step(self, R: int, P: int) -> None:
+        """The step over the (R, P) metadata (what a graph holds)."""
         m, kv = self.model, self.kv
         mgr, cfg = kv.mgr, m.cfg
-        meta = self._meta(R)
-        pos = self._views(R)["positions"]
+        meta = self._meta(R, P)
+        v = self._views(R, P)
+        pos = v["positions"]
         meta.decode_schedule = ops.build_decode_schedule(
-            self.schedule, meta.block_tables, meta.context_lens, mgr.num_blocks,
+            self.schedule, meta.block_tables[:R], meta.context_lens[:R], mgr.num_blocks,
             cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, m.dtype,
             fp8=mgr.fp8, err=mgr.err)
         rot = None
         if not m.fused_rope:
             rot = (self.cos[pos].unsqueeze(1), self.sin[pos].unsqueeze(1))
-        h = m._layers(m.embed[self.ids[:R]], pos, self.cos, self.sin, rot, meta, kv, advance=False)
+        h = m._layers(m.embed[self.ids[:R + P]], pos, self.cos, self.sin, rot, meta, kv, advance=False)
+        if P:
+            h = h[v["last"]]
         h = torch.nn.functional.rms_norm(h, (cfg.hidden_size,), m.final_norm, cfg.rms_norm_eps)
-        torch.mm(h, m.embed.t(), out=self.logits[:R])
+        torch.mm(h, m.embed.t(), out=self.logits[:h.shape[0]])
 
-    def capture(self, R: int) -> None:
-        """Capture the R-row step (R a bucket).  Runs it once uncaptured
-        first, on all-padding metadata, which reads and writes no KV."""
-        if R not in self.buckets:
-            raise ValueError(f"pagedkv: {R} is not one of the buckets {self.buckets}")
+    def capture(self, R: int, P: int = 0) -> None:
+        """Capture the (R, P) step.  Runs it once uncaptured first, on
+        all-padding metadata, which reads and writes no KV."""
+        if (R, P) not in self._key_set:
+            raise ValueError(f"pagedkv: ({R}, {P}) is not a captured shape of this runner")
         self.kv.mgr.flush_copies()
-        v = self._views(R)
+        v = self._views(R, P)
         cur = torch.cuda.current_stream(self.model.device)
-        # all rows padding: zero tables / lengths / positions, slots -1
+        # all rows padding: zero tables / lengths / positions / query starts /
+        # LM-head rows, slots -1
         self.meta_dev.zero_()
         v["slots"].fill_(-1)
         side = torch.cuda.Stream(self.model.device)
         side.wait_stream(cur)
         with torch.cuda.stream(side):
-            self._step(R)  # library handles, kernel attributes, argument caches
+            self._step(R, P)  # library handles, kernel attributes, argument caches
         cur.wait_stream(side)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=self.pool):
-            self._step(R)
-        self.graphs[R] = g
+            self._step(R, P)
+        self.graphs[(R, P)] = g
 
     def capture_all(self) -> None:
-        for R in reversed(self.buckets):
-            if R not in self.graphs:
-                self.capture(R)
+        for key in sorted(self._key_set, key=lambda k: -(k[0] + k[1])):
+            if key not in self.graphs:
+                self.capture(*key)
 
     # ---- a step -------------------------------------------------------------
 
-    def bucket(self, B: int) -> int:
-        for R in self.buckets:
-            if R >= B:
-                return R
-        raise ValueError(f"pagedkv: {B} sequences, more than the largest bucket {self.max_batch}")
+    def shape_of(self, seq_infos: list[SequenceForwardInfo]) -> tuple[int, int] | None:
+        """The (R, P) graph that serves this step (decode sequences first, as
+        the scheduler orders them), or None if none does."""
+        B = len(seq_infos)
+        nd = 0
+        while nd < B and seq_infos[nd].num_tokens == 1:
+            nd += 1
+        if nd == B:
+            R = _bucket(self.buckets, B)
+            return None if R is None or B == 0 else (R, 0)
+        if B - nd > self.prefill_seqs:
+            return None
+        R = _bucket(self.mixed_rows, nd)
+        P = _bucket(self.prefill_tokens, sum(s.num_tokens for s in seq_infos[nd:]))
+        if R is None or P is None or (R, P) not in self._key_set:
+            return None
+        return R, P
 
     def supports(self, seq_infos: list[SequenceForwardInfo]) -> bool:
-        """A decode-only step of at most max_batch sequences."""
-        return 0 < len(seq_infos) <= self.max_batch and all(s.num_tokens == 1 for s in seq_infos)
+        return self.shape_of(seq_infos) is not None
 
     def forward(self, input_ids: torch.Tensor, seq_infos: list[SequenceForwardInfo]) -> torch.Tensor:
-        """PagedQwen2Model.forward for a decode-only step, by graph replay.
+        """PagedQwen2Model.forward by graph replay, for a step that `supports`.
 
-        input_ids [B] on the device, one token per sequence.  Returns the
-        logits [B, vocab] as a view of the runner's buffer, valid until the
-        next replay.  The sequences' lengths advance as after an eager step."""
+        input_ids [T] on the device (flat: the decode tokens, then each
+        prefill sequence's chunk).  Returns the logits [B, vocab] of each
+        sequence's last new token as a view of the runner's buffer, valid
+        until the next replay.  The sequences' lengths advance as after an
+        eager step."""
         kv, bs = self.kv, self.kv.mgr.block_size
-        B = len(seq_infos)
-        if not self.supports(seq_infos):
-            raise ValueError("pagedkv: DecodeGraphs.forward takes decode-only steps of <= "
-                             f"{self.max_batch} sequences")
-        need = (max(kv._len[s.seq_id] for s in seq_infos) + bs) // bs  # blocks incl. the new token
+        shape = self.shape_of(seq_infos)
+        if shape is None:
+            raise ValueError("pagedkv: StepGraphs.forward: no captured shape serves this step")
+        need = max((kv._len[s.seq_id] + s.num_tokens + bs - 1) // bs for s in seq_infos)
         if need > self.W:
             w = self.W
             while w < need:
                 w *= 2
             self.W = w
             self._alloc()
-        R = self.bucket(B)
-        if R not in self.graphs:
-            self.capture(R)
+        R, P = shape
+        if shape not in self.graphs:
+            self.capture(R, P)
         kv.mgr.flush_copies()
         i = self._stage_next = (self._stage_next + 1) % len(self.stage)
         host, ev = self.stage[i]
         if ev is not None:
             ev.synchronize()
         hnp = host.numpy()
-        _, s_off, nbytes = self._layout(R)
+        L = self._layout(R, P)
+        B = len(seq_infos)
+        seqs = [(s.seq_id, s.num_tokens) for s in seq_infos]
+        if P == 0:
+            def into(n_ints: int, n_slots: int):
+                return (hnp[: 4 * n_ints].view(np.int32),
+                        hnp[L["slots"]: L["slots"] + 8 * n_slots].view(np.int64))
 
-        def into(n_ints: int, n_slots: int):
-            return hnp[: 4 * n_ints].view(np.int32), hnp[s_off: s_off + 8 * n_slots].view(np.int64)
-
-        a = kv.step_arrays([(s.seq_id, 1) for s in seq_infos], out=into, width=self.W, pad_to=R)
-        pos = hnp[s_off + 8 * R: s_off + 16 * R].view(np.int64)
-        pos[:B] = [int(s.positions[0]) for s in seq_infos]
-        pos[B:] = 0
-        self.meta_dev[:nbytes].copy_(host[:nbytes], non_blocking=True)
+            a = kv.step_arrays(seqs, out=into, width=self.W, pad_to=R)
+            pos = hnp[L["pos"]: L["pos"] + 8 * R].view(np.int64)
+            pos[:B] = [int(s.positions[0]) for s in seq_infos]
+            pos[B:] = 0
+        else:
+            a = kv.step_arrays(seqs, width=self.W)
+            self._lay_mixed(hnp, L, R, a, seq_infos)
+        self.meta_dev[: L["end"]].copy_(host[: L["end"]], non_blocking=True)
         cur = torch.cuda.current_stream(self.model.device)
         ev = torch.cuda.Event()
         ev.record(cur)
         self.stage[i][1] = ev
-        self.ids[:B].copy_(input_ids, non_blocking=True)
-        self.graphs[R].replay()
+        nd = a["n_decode"]
+        if P == 0:
+            self.ids[:B].copy_(input_ids, non_blocking=True)
+        else:
+            if nd:
+                self.ids[:nd].copy_(input_ids[:nd], non_blocking=True)
+            self.ids[R: R + input_ids.shape[0] - nd].copy_(input_ids[nd:], non_blocking=True)
+        self.graphs[shape].replay()
         self.replays += 1
-        for s_id, p in zip(a["seq_ids"], a["num_prior"]):
-            kv._len[s_id] = p + 1
+        for s_id, p, n in zip(a["seq_ids"], a["num_prior"], a["num_new"]):
+            kv._len[s_id] = p + n
         return self.logits[:B]
+
+    def _lay_mixed(self, hnp, L, R, a, seq_infos) -> None:
+        """Write step_arrays' unpadded arrays into the staging buffer in the
+        (R, P) layout: decode rows 0..nd-1 then padding up to R, prefill
+        sequences R..R+n_pre-1 then empty ones; tokens likewise."""
+        W, S, NP = self.W, L["S"], L["NP"]
+        B, nd = a["B"], a["n_decode"]
+        n_pre = B - nd
+        src = a["ints"]
+        ints = hnp[: 4 * L["n_ints"]].view(np.int32)
+        tabs = ints[: S * W].reshape(S, W)
+        stabs = src[: B * W].reshape(B, W)
+        tabs[:nd] = stabs[:nd]
+        tabs[nd:R] = 0
+        tabs[R: R + n_pre] = stabs[nd:]
+        tabs[R + n_pre:] = 0
+        for k, off in ((0, S * W), (1, S * W + S)):  # context lens, num_prior
+            col = src[B * W + k * B: B * W + (k + 1) * B]
+            dst = ints[off: off + S]
+            dst[:nd] = col[:nd]
+            dst[nd:R] = 0
+            dst[R: R + n_pre] = col[nd:]
+            dst[R + n_pre:] = 0
+        qsl = src[B * W + 2 * B:]  # n_pre + 1 entries, qsl[0] = 0
+        dq = ints[S * W + 2 * S: S * W + 2 * S + NP + 1]
+        dq[: n_pre + 1] = qsl
+        dq[n_pre + 1:] = qsl[-1]
+        t_pre = int(qsl[-1])
+        sl = a["slots"]
+        slots = hnp[L["slots"]: L["slots"] + 8 * L["T"]].view(np.int64)
+        slots[:nd] = sl[:nd]
+        slots[nd:R] = -1
+        slots[R: R + t_pre] = sl[nd:]
+        slots[R + t_pre:] = -1
+        pos = hnp[L["pos"]: L["pos"] + 8 * L["T"]].view(np.int64)
+        pos[:nd] = [int(s.positions[0]) for s in seq_infos[:nd]]
+        pos[nd:R] = 0
+        pos[R: R + t_pre] = np.concatenate([s.positions for s in seq_infos[nd:]])
+        pos[R + t_pre:] = 0
+        last = hnp[L["last"]: L["last"] + 8 * (R + NP)].view(np.int64)
+        last[:nd] = np.arange(nd)
+        last[nd: nd + n_pre] = R + qsl[1:] - 1
+        last[nd + n_pre:] = 0
+
+
+DecodeGraphs = StepGraphs  # decode-only use: StepGraphs(model, kv, max_batch)

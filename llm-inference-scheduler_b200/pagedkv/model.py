@@ -183,7 +183,9 @@ class PagedQwen2Model:
                          None if fused else (cos, sin), meta, kv_cache,
                          t_attn if timing is not None else None)
         h = F.rms_norm(h, (cfg.hidden_size,), self.final_norm, cfg.rms_norm_eps)
-        last = torch.tensor([s.flat_start + s.num_tokens - 1 for s in seq_infos], device=self.device)
+        last = torch.tensor([s.flat_start + s.num_tokens - 1 for s in seq_infos])
+        if self.device.type == "cuda":  # a pageable copy would wait for the whole step
+            last = last.pin_memory().to(self.device, non_blocking=True)
         logits = F.linear(h[last], self.embed)
         if timing is not None:
             t_step[1].record()

@@ -19,10 +19,10 @@ restated so that a run here makes the same decisions, token for token:
 What differs is the execution of a step: the device metadata is built once
 (PagedKVCache.prepare_step), every layer runs one append + at most two
 attention launches, and the greedy argmax of the whole batch comes back to
-the host in one copy.  With cuda_graphs=True a decode-only step (every
-scheduled sequence adds one token) replays a captured CUDA graph of the
-model step (pagedkv.graphs.DecodeGraphs); mixed and prefill steps run
-eagerly.  The decisions are the same either way.
+the host in one copy.  With cuda_graphs=True a step replays a captured CUDA
+graph of the model step (pagedkv.graphs.StepGraphs) when one of its padded
+shapes fits: decode-only steps, and mixed steps of up to 4 prefill
+sequences; other steps run eagerly.  The decisions are the same either way.
 """
 
 from __future__ import annotations
@@ -89,14 +89,15 @@ class Scheduler:
                             tokens_generated=0, prefill_tokens_computed=0, prefix_cache_hit_tokens=0)
         self.cuda_graphs = cuda_graphs and model.device.type == "cuda"
         self.graph_max_blocks = graph_max_blocks
-        self.graphs = None  # DecodeGraphs, made at the first decode-only step
+        self.graphs = None  # StepGraphs, made at the first step
 
-    def decode_graphs(self):
-        """The CUDA-graph runner of decode-only steps (cuda_graphs=True)."""
+    def step_graphs(self):
+        """The CUDA-graph runner of the model step (cuda_graphs=True)."""
         if self.graphs is None:
-            from .graphs import DecodeGraphs
-            self.graphs = DecodeGraphs(self.model, self.kv, self.max_num_seqs,
-                                       max_blocks_per_seq=self.graph_max_blocks)
+            from .graphs import StepGraphs
+            self.graphs = StepGraphs(self.model, self.kv, self.max_num_seqs,
+                                     max_tokens=self.max_batched_tokens,
+                                     max_blocks_per_seq=self.graph_max_blocks)
         return self.graphs
 
     # ---- memory ----------------------------------------------------------
@@ -237,7 +238,7 @@ class Scheduler:
         ids = torch.tensor(flat, dtype=torch.long)
         if self.model.device.type == "cuda":
             ids = ids.pin_memory().to(self.model.device, non_blocking=True)
-        if self.cuda_graphs and self.model.timing is None and self.decode_graphs().supports(infos):
+        if self.cuda_graphs and self.model.timing is None and self.step_graphs().supports(infos):
             logits = self.graphs.forward(ids, infos)
         else:
             logits = self.model.forward(ids, infos, self.kv)

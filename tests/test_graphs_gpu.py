@@ -1,15 +1,20 @@
-"""CUDA-graph decode steps (pagedkv.graphs.DecodeGraphs) against the eager step.
+"""CUDA-graph steps (pagedkv.graphs.StepGraphs) against the eager step.
 
-One decode-only step of a random-init Qwen2.5-0.5B-shaped model over pools
-of random K/V, run twice from the same state: eagerly (PagedQwen2Model.forward)
-and by graph replay, with a batch that is not a bucket size so padding rows
-are in the graph.  Checks:
-* the logits agree to rounding (the GEMMs see M = padded rows, so the
-  library may pick another algorithm) and the greedy tokens are equal;
-* the pools differ from the eager step's only at the step's appended slots,
-  and there to rounding: padding rows write nothing;
-* the lengths advance as after the eager step, and a second replay after
-  that advance agrees with a second eager step.
+Steps of a random-init Qwen2.5-0.5B-shaped model over pools of random K/V,
+run twice from the same state: eagerly (PagedQwen2Model.forward) and by graph
+replay, with batches that are not bucket sizes so padding is in the graph:
+* decode-only: 13 sequences (bucket 16), two steps;
+* mixed: 13 decodes and two prefill chunks (40 tokens after a 37-token
+  prior context, 100 tokens of a fresh prompt) in the (16, 192) graph, then
+  a decode-only step of all 15 sequences.
+Checks:
+* the logits agree to rounding (the GEMMs see padded M, so the library may
+  pick another algorithm) and the greedy tokens are equal where the top two
+  logits are apart;
+* each run changes the pools only at the steps' appended slots (padding rows
+  and padding sequences write nothing), and both runs write every one of
+  them, to rounding (16-bit pools) or to the fp8 scale tolerance;
+* the lengths advance as after the eager steps.
 """
 
 import numpy as np
@@ -17,10 +22,12 @@ import pytest
 import torch
 
 from pagedkv import BlockManager, PagedKVCache
-from pagedkv.graphs import DecodeGraphs
+from pagedkv.graphs import StepGraphs
 from pagedkv.model import PagedQwen2Model, Qwen2Config, SequenceForwardInfo, random_weights
 
 pytestmark = pytest.mark.gpu
+
+V = Qwen2Config().vocab_size
 
 
 @pytest.fixture(scope="module")
@@ -30,10 +37,9 @@ def model():
                            dtype=torch.float16)
 
 
-def _state(kv_dtype, B, seed):
-    """Pools of random K/V, B sequences of random lengths whose tables already
-    hold blocks for the two decode steps (no allocation during the runs)."""
-    rng = np.random.default_rng(seed)
+def _state(kv_dtype, lens, extra, seed):
+    """Pools of random K/V and tables that already hold blocks for
+    lens[s] + extra[s] tokens (no allocation during the runs)."""
     mgr = BlockManager(1200, 16, 24, 2, 64, device="cuda", dtype=kv_dtype)
     g = torch.Generator(device="cuda").manual_seed(seed)
     if kv_dtype == torch.float8_e4m3fn:
@@ -44,10 +50,8 @@ def _state(kv_dtype, B, seed):
     else:
         mgr.k_cache.normal_(generator=g)
         mgr.v_cache.normal_(generator=g)
-    lens = rng.integers(1, 400, size=B).tolist()
-    tables = [[mgr.allocate() for _ in range((n + 2 + 15) // 16)] for n in lens]
-    ids = rng.integers(0, Qwen2Config().vocab_size, size=(2, B))
-    return mgr, lens, tables, ids
+    tables = [[mgr.allocate() for _ in range((n + e + 15) // 16)] for n, e in zip(lens, extra)]
+    return mgr, tables
 
 
 def _pools(mgr):
@@ -63,50 +67,82 @@ def _rows(mask):
     return {(int(b), int(r)) for b, r in torch.nonzero(m).tolist()}
 
 
-def _run(model, mgr, lens, tables, ids, graphs: bool):
+def _run(model, mgr, lens, tables, steps, graphs: bool, seed: int):
+    """steps: per step, [(sequence index, new tokens)] in flat order."""
+    rng = np.random.default_rng(seed)
     kv = PagedKVCache(mgr)
     for s, (n, t) in enumerate(zip(lens, tables)):
         kv.add_sequence(100 + s, list(t), n)
-    runner = DecodeGraphs(model, kv, max_batch=32) if graphs else None
+    runner = StepGraphs(model, kv, max_batch=32, max_tokens=256) if graphs else None
     logits = []
-    for step in range(2):
-        infos = [SequenceForwardInfo(100 + s, s, 1, np.array([kv.seq_len(100 + s)]))
-                 for s in range(len(lens))]
-        x = torch.tensor(ids[step], dtype=torch.long, device="cuda")
-        out = runner.forward(x, infos) if graphs else model.forward(x, infos, kv)
+    for step in steps:
+        infos, flat = [], 0
+        for s, n in step:
+            p = kv.seq_len(100 + s)
+            infos.append(SequenceForwardInfo(100 + s, flat, n, np.arange(p, p + n)))
+            flat += n
+        x = torch.tensor(rng.integers(0, V, size=flat), dtype=torch.long, device="cuda")
+        if graphs:
+            assert runner.supports(infos)
+            out = runner.forward(x, infos)
+        else:
+            out = model.forward(x, infos, kv)
         logits.append(out.float().clone())
     torch.cuda.synchronize()
     mgr.check_errors()
     return logits, [p.clone() for p in _pools(mgr)], [kv.seq_len(100 + s) for s in range(len(lens))], runner
 
 
-@pytest.mark.parametrize("kv_dtype", [torch.float16, torch.float8_e4m3fn], ids=["f16", "fp8"])
-def test_graph_decode_step_matches_eager(model, kv_dtype):
-    B = 13  # padded to the bucket of 16
-    mgr, lens, tables, ids = _state(kv_dtype, B, seed=11)
+def _compare(model, kv_dtype, lens, steps, seed):
+    extra = [0] * len(lens)
+    for step in steps:
+        for s, n in step:
+            extra[s] += n
+    mgr, tables = _state(kv_dtype, lens, extra, seed)
     before = [p.clone() for p in _pools(mgr)]
-    le, pe, len_e, _ = _run(model, mgr, lens, tables, ids, graphs=False)
+    le, pe, len_e, _ = _run(model, mgr, lens, tables, steps, graphs=False, seed=seed)
     for p, b in zip(_pools(mgr), before):
         p.copy_(b)
-    lg, pg, len_g, runner = _run(model, mgr, lens, tables, ids, graphs=True)
-    assert runner.replays == 2 and set(runner.graphs) == {16}
-    assert len_g == len_e == [n + 2 for n in lens]
+    lg, pg, len_g, runner = _run(model, mgr, lens, tables, steps, graphs=True, seed=seed)
+    assert runner.replays == len(steps)
+    assert len_g == len_e == [n + e for n, e in zip(lens, extra)]
     for a, b in zip(le, lg):
         # fp16 rounding through 24 layers of GEMMs that may run another
-        # algorithm (M = 16 padded rows instead of 13): measured max 0.037 on
-        # logits of magnitude ~5; a systematic error would move the mean
+        # algorithm (padded M): measured max 0.037 on logits of magnitude ~5;
+        # a systematic error would move the mean
         torch.testing.assert_close(b, a, atol=8e-2, rtol=2e-2)
         assert (b - a).abs().mean().item() < 5e-3
         top2 = a.topk(2, dim=-1).values
         clear = (top2[:, 0] - top2[:, 1]) > 0.1
         assert torch.equal(a.argmax(-1)[clear], b.argmax(-1)[clear])
-    appended = {(t[p // 16], p % 16) for t, n in zip(tables, lens) for p in (n, n + 1)}
+    appended = {(t[p // 16], p % 16) for t, n, e in zip(tables, lens, extra) for p in range(n, n + e)}
+    u8 = lambda x: x.view(torch.uint8)  # noqa: E731
     for i, (a, b, b0) in enumerate(zip(pe, pg, before)):
-        u8 = lambda x: x.view(torch.uint8)  # noqa: E731
-        assert _rows(u8(a) != u8(b0)) <= appended, f"pool {i}: the eager step wrote elsewhere"
-        assert _rows(u8(b) != u8(b0)) <= appended, f"pool {i}: the graph step wrote elsewhere"
+        assert _rows(u8(a) != u8(b0)) <= appended, f"pool {i}: the eager steps wrote elsewhere"
+        assert _rows(u8(b) != u8(b0)) <= appended, f"pool {i}: the graph steps wrote elsewhere"
         if a.dtype == torch.float16:
-            assert _rows(a != b0) == appended  # every appended row was written
+            assert _rows(a != b0) == appended == _rows(b != b0)  # every appended row was written
             torch.testing.assert_close(b.float(), a.float(), atol=2e-2, rtol=1e-2)
         elif a.dtype == torch.float32:  # fp8 scales
             torch.testing.assert_close(b, a, atol=1e-4, rtol=2e-2)
+    return runner
+
+
+KV_DTYPES = pytest.mark.parametrize("kv_dtype", [torch.float16, torch.float8_e4m3fn], ids=["f16", "fp8"])
+
+
+@KV_DTYPES
+def test_graph_decode_steps_match_eager(model, kv_dtype):
+    lens = np.random.default_rng(11).integers(1, 400, size=13).tolist()
+    steps = [[(s, 1) for s in range(13)]] * 2
+    runner = _compare(model, kv_dtype, lens, steps, seed=11)
+    assert set(runner.graphs) == {(16, 0)}
+
+
+@KV_DTYPES
+def test_graph_mixed_step_matches_eager(model, kv_dtype):
+    lens = np.random.default_rng(12).integers(1, 400, size=13).tolist() + [37, 0]
+    steps = [[(s, 1) for s in range(13)] + [(13, 40), (14, 100)],
+             [(s, 1) for s in range(15)]]
+    runner = _compare(model, kv_dtype, lens, steps, seed=12)
+    assert set(runner.graphs) == {(16, 192), (16, 0)}

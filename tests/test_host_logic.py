@@ -190,11 +190,72 @@ def test_step_arrays_padded_fixed_width_layout():
 
 
 def test_graph_buckets():
-    from pagedkv.graphs import default_buckets
+    from pagedkv.graphs import default_buckets, graph_keys, mixed_row_buckets, prefill_token_buckets
     assert default_buckets(1) == [1]
     assert default_buckets(6) == [1, 2, 4, 6]
     assert default_buckets(128) == [1, 2, 4, 8, 16, 32, 48, 64, 80, 96, 112, 128]
     assert default_buckets(200) == [1, 2, 4, 8, 16, 32, 48, 64, 80, 96, 112, 128, 160, 192, 200]
+    assert mixed_row_buckets(3) == [3]
+    assert mixed_row_buckets(128) == [16, 32, 64, 96, 128]
+    assert prefill_token_buckets(48) == [32, 48]
+    assert prefill_token_buckets(512) == [32, 64, 128, 192, 256, 320, 384, 448, 512]
+    rows, toks = mixed_row_buckets(128), prefill_token_buckets(512)
+    keys = graph_keys(default_buckets(128), rows, toks, 512)
+    assert keys[:12] == [(b, 0) for b in default_buckets(128)]
+    mixed = set(keys[12:])
+    # a shape is kept iff its smallest step (one more than the buckets below) fits 512 tokens
+    for i, R in enumerate(rows):
+        for j, P in enumerate(toks):
+            lo = (rows[i - 1] + 1 if i else 0) + (toks[j - 1] + 1 if j else 1)
+            assert ((R, P) in mixed) == (lo <= 512), (R, P)
+    assert (128, 448) in mixed and (128, 512) not in mixed and (16, 512) in mixed
+
+
+def test_graph_mixed_layout():
+    """StepGraphs._lay_mixed: the unpadded step arrays re-laid for an (R, P)
+    graph: decode rows, padding to R, prefill sequences, empty ones; token
+    rows likewise; LM-head rows = the decode rows then each chunk's last row."""
+    from pagedkv.graphs import StepGraphs
+    from pagedkv.model import SequenceForwardInfo
+    m = mgr(num_blocks=64, block_size=16)
+    kv = PagedKVCache(m)
+    kv.add_sequence(1, [m.allocate() for _ in range(3)], 33)   # decode
+    kv.add_sequence(2, [m.allocate() for _ in range(2)], 15)   # decode
+    kv.add_sequence(3, [m.allocate() for _ in range(2)], 5)    # 20-token chunk
+    kv.add_sequence(4, [m.allocate()], 0)                      # 3-token prompt
+    seqs = [(1, 1), (2, 1), (3, 20), (4, 3)]
+    infos, flat = [], 0
+    for s, n in seqs:
+        p = kv.seq_len(s)
+        infos.append(SequenceForwardInfo(s, flat, n, np.arange(p, p + n)))
+        flat += n
+    g = StepGraphs.__new__(StepGraphs)  # layout only: no device state
+    g.W, g.prefill_seqs = 4, 4
+    R, P = 16, 32
+    L = g._layout(R, P)
+    a = kv.step_arrays(seqs, width=g.W)
+    hnp = np.full(L["end"], 0x5A, dtype=np.uint8)  # stale bytes everywhere
+    g._lay_mixed(hnp, L, R, a, infos)
+    S, W = L["S"], g.W
+    assert S == 20 and L["T"] == 48
+    ints = hnp[:4 * L["n_ints"]].view(np.int32)
+    tabs = ints[:S * W].reshape(S, W)
+    assert tabs[0, :3].tolist() == kv.block_tables[1] and tabs[1, :2].tolist() == kv.block_tables[2]
+    assert tabs[R, :2].tolist() == kv.block_tables[3] and tabs[R + 1, :1].tolist() == kv.block_tables[4]
+    assert not tabs[2:R].any() and not tabs[R + 2:].any()
+    ctx, prior = ints[S * W:S * W + S], ints[S * W + S:S * W + 2 * S]
+    assert ctx.tolist() == [34, 16] + [0] * 14 + [25, 3, 0, 0]
+    assert prior.tolist() == [33, 15] + [0] * 14 + [5, 0, 0, 0]
+    assert ints[S * W + 2 * S:].tolist() == [0, 20, 23, 23, 23]
+    slots = hnp[L["slots"]:L["slots"] + 8 * 48].view(np.int64)
+    assert slots[:2].tolist() == a["slots"][:2].tolist()
+    assert (slots[2:R] == -1).all() and (slots[R + 23:] == -1).all()
+    assert slots[R:R + 23].tolist() == a["slots"][2:].tolist()
+    pos = hnp[L["pos"]:L["pos"] + 8 * 48].view(np.int64)
+    assert pos[:2].tolist() == [33, 15] and not pos[2:R].any()
+    assert pos[R:R + 23].tolist() == list(range(5, 25)) + [0, 1, 2] and not pos[R + 23:].any()
+    last = hnp[L["last"]:L["last"] + 8 * (R + 4)].view(np.int64)
+    assert last.tolist() == [0, 1, R + 19, R + 22] + [0] * (R + 4 - 4)
 
 
 def test_no_cpu_pools():
