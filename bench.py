@@ -46,11 +46,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("decode", "prefill", "e2e", "cache_ops", "decode_fp8",
-                                           "migrate"),
+                                           "migrate", "model_step"),
                     default="decode",
                     help="decode = BASELINE config 3 (headline); prefill = config 4; e2e = config 5; "
                          "cache_ops = reshape_and_cache and copy_blocks at bandwidth-sized batches; "
-                         "migrate = KV block migration between rank pairs over NVLink (2+ ranks)")
+                         "migrate = KV block migration between rank pairs over NVLink (2+ ranks); "
+                         "model_step = config 5's model step replayed from its CUDA graphs")
     ap.add_argument("--migrate-blocks", type=int, default=1024,
                     help="migrate: blocks per copy launch (x 24 layers, K and V)")
     ap.add_argument("--kv-fp8", action="store_true",
@@ -1035,8 +1036,88 @@ def run_migrate(args):
     dist.destroy_process_group()
 
 
+def run_model_step(args):
+    """GPU time of config 5's model step as the engine replays it: the
+    random-init Qwen2.5-0.5B-shaped fp16 model's CUDA graphs
+    (pagedkv.graphs.StepGraphs) for a decode-only step of 64 sequences
+    (contexts uniform in [300, 900)) and for a mixed step of those 64 decodes
+    plus a 128-token chunk after a 300-token prior context.  CUDA events
+    around `--steps` replays each; the step's inputs are already on the
+    device (the metadata copy of a real step is not in the timed region).
+    With --profile-steps N, N replays of the decode-only graph run inside an
+    NVTX range "model_step" (for ncu --nvtx-include) and nothing is timed."""
+    import numpy as np
+    import torch
+
+    from pagedkv import BlockManager, PagedKVCache
+    from pagedkv.graphs import StepGraphs
+    from pagedkv.model import PagedQwen2Model, Qwen2Config, SequenceForwardInfo, random_weights
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    cfg = Qwen2Config()
+    model = PagedQwen2Model(cfg, random_weights(cfg, seed=5, final_norm_scale=4.0), device="cuda",
+                            dtype=torch.float16)
+    mgr = BlockManager(8000, 16, cfg.num_hidden_layers, 2, 64, device="cuda", dtype=torch.float16)
+    kv = PagedKVCache(mgr)
+    rng = np.random.default_rng(0)
+    B, chunk = 64, 128
+    lens = rng.integers(300, 900, size=B).tolist() + [300]
+    for s, n in enumerate(lens):
+        kv.add_sequence(s, [mgr.allocate() for _ in range((n + chunk + 16) // 16 + 1)], n)
+    runner = StepGraphs(model, kv, max_batch=B, max_tokens=512)
+
+    def infos(mixed):
+        out = [SequenceForwardInfo(s, s, 1, np.array([lens[s]])) for s in range(B)]
+        if mixed:
+            out.append(SequenceForwardInfo(B, B, chunk, np.arange(lens[B], lens[B] + chunk)))
+        return out
+
+    res = {}
+    for mixed in (False, True):
+        inf = infos(mixed)
+        ids = torch.tensor(rng.integers(0, cfg.vocab_size, size=B + (chunk if mixed else 0)),
+                           device="cuda")
+        runner.forward(ids, inf)  # captures the shape and stages the step's metadata
+        for s in range(B + 1):    # forward advanced the lengths: restore them
+            kv._len[s] = lens[s]
+        g = runner.graphs[runner.shape_of(inf)]
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        if args.profile_steps and not mixed:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("model_step")
+            for _ in range(args.profile_steps):
+                g.replay()
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
+        if args.profile_steps:
+            continue
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res["mixed" if mixed else "decode"] = {
+            "shape": list(runner.shape_of(inf)), "ms_per_step": round(e0.elapsed_time(e1) / args.steps, 4)}
+    mgr.check_errors()
+    if args.profile_steps:
+        return
+    print(json.dumps({
+        "metric": "config-5 model step GPU time (CUDA-graph replay)", "unit": "ms",
+        "value": res["decode"]["ms_per_step"], "higher_is_better": False, "steps": args.steps,
+        "data": "synthetic: random-init Qwen2.5-0.5B-shaped weights, random token ids", "dtype": "f16",
+        "config": {"workload": "decode-only step of 64 sequences (contexts uniform [300, 900)); "
+                               "mixed: + one 128-token chunk after 300 cached tokens"},
+        "steps_by_shape": res}), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "model_step":
+        run_model_step(args)
+        return
     if args.workload == "migrate":
         run_migrate(args)
         return
