@@ -72,6 +72,11 @@ namespace pkv {
 #ifndef PKV_DEC_STAGES
 #define PKV_DEC_STAGES 3
 #endif
+// fp8 stages carry half the bytes: a deeper ring keeps as many bytes in
+// flight per SM as the 16-bit ring
+#ifndef PKV_DEC_STAGES_FP8
+#define PKV_DEC_STAGES_FP8 6
+#endif
 #ifndef PKV_DEC_MIN_CTAS
 #define PKV_DEC_MIN_CTAS 3
 #endif
@@ -83,7 +88,7 @@ namespace pkv {
 #ifndef PKV_DEC_PREFETCH
 #define PKV_DEC_PREFETCH 3
 #endif
-constexpr int kDecStages = PKV_DEC_STAGES;
+template <bool FP8> __host__ __device__ constexpr int dec_stages() { return FP8 ? PKV_DEC_STAGES_FP8 : PKV_DEC_STAGES; }
 constexpr int kDecMaxCtas = 1024;
 constexpr int kDecMaxSeqs = 2048;
 constexpr int kDecMinBlocksPerCta = 4;
@@ -309,6 +314,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   // stage: K tiles, V tiles (fp8: then the K and V scale rows of the block)
+  constexpr int kDecStages = dec_stages<FP8>();
   constexpr int tile_bytes = FP8 ? kDecTile8 : kDecTile;
   constexpr int scale_bytes = FP8 ? 16 * nkv * 4 : 0;
   constexpr int stage_bytes = 2 * nkv * tile_bytes + 2 * scale_bytes;
@@ -540,65 +546,67 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-    for (int jb = jb0; jb < jb0 + (seg_end - pos); ++jb, ++i) {
-      const int st = i % kDecStages;
-      if (!dead && !mbar_wait(&full_bar[st], (i / kDecStages) & 1)) {
-        if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
-        dead = true;
-      }
-      // tokens of this block inside the context; only a sequence's last
-      // block has fewer than 16 (warp-uniform)
-      const int valid = min(16, ctx - jb * 16);
-      uint32_t kt = 0, vt = 0;                           // 16-bit tiles: ldmatrix bases
-      float ks0 = 1.f, ks1 = 1.f, vs0 = 1.f, vs1 = 1.f;  // fp8 scales of tokens g, g + 8
-      uint4 kr0, kr1;  // fp8: K rows g and g + 8, bytes 16t .. 16t + 15
-      uint2 vr[4];     // fp8: V rows 2t + sw, 2t + 1 - sw, 2t + 8 + sw, 2t + 9 - sw
-      if constexpr (FP8) {
+    const int jb_end = jb0 + (seg_end - pos);
+    if constexpr (FP8) {
+      // Two ring blocks per iteration (32 tokens): two independent QK^T
+      // chains, one max reduction / vote / rescale for both, and the PV
+      // products of both interleaved.  An odd last block is paired with a
+      // phantom block (no wait, zero fragments, every token masked: P = 0).
+      struct Frag {
+        uint4 kr0, kr1;  // K rows g and g + 8, bytes 16t .. 16t + 15
+        uint2 vr[4];     // V rows 2t + sw, 2t + 1 - sw, 2t + 8 + sw, 2t + 9 - sw
+        float ks0, ks1, vs0, vs1;  // scales of tokens g, g + 8
+        int valid;       // tokens of the block inside the context
+      };
+      auto load = [&](int ii, int jbb, Frag& f) {
+        const int st = ii % kDecStages;
+        if (!dead && !mbar_wait(&full_bar[st], (ii / kDecStages) & 1)) {
+          if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+          dead = true;
+        }
+        // only a sequence's last block has fewer than 16 tokens (warp-uniform)
+        f.valid = min(16, ctx - jbb * 16);
         const uint8_t* stg = tiles + st * stage_bytes;
         const uint8_t* k8 = stg + h * kDecTile8;
         const uint8_t* v8 = stg + (nkv + h) * kDecTile8;
         const float* ksc = reinterpret_cast<const float*>(stg + 2 * nkv * kDecTile8);
         const float* vsc = ksc + 16 * nkv;
-        kr0 = *reinterpret_cast<const uint4*>(k8 + g * 64 + t * 16);
-        kr1 = *reinterpret_cast<const uint4*>(k8 + (g + 8) * 64 + t * 16);
+        f.kr0 = *reinterpret_cast<const uint4*>(k8 + g * 64 + t * 16);
+        f.kr1 = *reinterpret_cast<const uint4*>(k8 + (g + 8) * 64 + t * 16);
         // lanes with odd t (sw = 1) take their row pair in the other order, so
         // that each 8-byte load's 32 lanes fill all 32 banks (two wavefronts);
         // the byte permutes below swap their operands back (sel ^ 0x4444)
-        vr[0] = *reinterpret_cast<const uint2*>(v8 + (2 * t + sw) * 64 + 8 * g);
-        vr[1] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 1 - sw) * 64 + 8 * g);
-        vr[2] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 8 + sw) * 64 + 8 * g);
-        vr[3] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 9 - sw) * 64 + 8 * g);
-        ks0 = ksc[g * nkv + h];
-        ks1 = ksc[(g + 8) * nkv + h];
-        vs0 = vsc[g * nkv + h];
-        vs1 = vsc[(g + 8) * nkv + h];
+        f.vr[0] = *reinterpret_cast<const uint2*>(v8 + (2 * t + sw) * 64 + 8 * g);
+        f.vr[1] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 1 - sw) * 64 + 8 * g);
+        f.vr[2] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 8 + sw) * 64 + 8 * g);
+        f.vr[3] = *reinterpret_cast<const uint2*>(v8 + (2 * t + 9 - sw) * 64 + 8 * g);
+        f.ks0 = ksc[g * nkv + h];
+        f.ks1 = ksc[(g + 8) * nkv + h];
+        f.vs0 = vsc[g * nkv + h];
+        f.vs1 = vsc[(g + 8) * nkv + h];
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[st]);  // the stage is free once in registers
-        if (valid < 16) {
+        if (f.valid < 16) {
           // rows past the context: scales 0, V bytes 0 (an unused slot may hold
           // any bytes, and 0 x NaN would reach O); their scores are masked below
-          if (g >= valid) ks0 = vs0 = 0.f;
-          if (g + 8 >= valid) ks1 = vs1 = 0.f;
+          if (g >= f.valid) f.ks0 = f.vs0 = 0.f;
+          if (g + 8 >= f.valid) f.ks1 = f.vs1 = 0.f;
           const uint2 z = make_uint2(0u, 0u);
-          if (2 * t + sw >= valid) vr[0] = z;
-          if (2 * t + 1 - sw >= valid) vr[1] = z;
-          if (2 * t + 8 + sw >= valid) vr[2] = z;
-          if (2 * t + 9 - sw >= valid) vr[3] = z;
+          if (2 * t + sw >= f.valid) f.vr[0] = z;
+          if (2 * t + 1 - sw >= f.valid) f.vr[1] = z;
+          if (2 * t + 8 + sw >= f.valid) f.vr[2] = z;
+          if (2 * t + 9 - sw >= f.valid) f.vr[3] = z;
         }
-      } else {
-        kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
-        vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
-      }
-      // ---- S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int mi = lane >> 3;
+      };
+      // S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
+      auto qk = [&](const Frag& f, float (&sc)[4]) {
+        sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t a[4];
-        if constexpr (FP8) {
+        for (int kk = 0; kk < 4; ++kk) {
           // k-step kk: bytes 4kk .. 4kk + 3 of rows g and g + 8
-          const uint32_t w0 = kk == 0 ? kr0.x : kk == 1 ? kr0.y : kk == 2 ? kr0.z : kr0.w;
-          const uint32_t w1 = kk == 0 ? kr1.x : kk == 1 ? kr1.y : kk == 2 ? kr1.z : kr1.w;
+          const uint32_t w0 = kk == 0 ? f.kr0.x : kk == 1 ? f.kr0.y : kk == 2 ? f.kr0.z : f.kr0.w;
+          const uint32_t w1 = kk == 0 ? f.kr1.x : kk == 1 ? f.kr1.y : kk == 2 ? f.kr1.z : f.kr1.w;
+          uint32_t a[4];
           if constexpr (kAluK) {
             a[0] = e4m3_even_h2(w0);
             a[1] = e4m3_even_h2(w1);
@@ -610,18 +618,124 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
             a[2] = fp8x2_to<T>(w0 >> 16);
             a[3] = fp8x2_to<T>(w1 >> 16);
           }
-        } else {
-          const int row = (lane & 7) + ((mi & 1) << 3);
-          const int chunk = 2 * kk + (mi >> 1);
-          ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+          mma16816<T>(sc, a, qa[kk][0], qa[kk][1]);
         }
+      };
+      // O^T += V^T P^T, 4 tiles of 16 dims (O rows g, g + 8 of tile mt are
+      // dims 8g + 2mt and 8g + 2mt + 1)
+      auto pv_a = [&](const Frag& f, int mt, uint32_t (&a)[4]) {
+        // interleave tokens (2t, 2t + 1) and (2t + 8, 2t + 9) byte by byte
+        const uint32_t sel = (mt & 1) ? sel_hi : sel_lo;
+        const uint32_t x01 = __byte_perm(mt < 2 ? f.vr[0].x : f.vr[0].y, mt < 2 ? f.vr[1].x : f.vr[1].y, sel);
+        const uint32_t x23 = __byte_perm(mt < 2 ? f.vr[2].x : f.vr[2].y, mt < 2 ? f.vr[3].x : f.vr[3].y, sel);
+        if constexpr (kAluV) {
+          a[0] = e4m3_even_h2(x01);
+          a[1] = e4m3_odd_h2(x01);
+          a[2] = e4m3_even_h2(x23);
+          a[3] = e4m3_odd_h2(x23);
+        } else {
+          a[0] = fp8x2_to<T>(x01 & 0xffffu);
+          a[1] = fp8x2_to<T>(x01 >> 16);
+          a[2] = fp8x2_to<T>(x23 & 0xffffu);
+          a[3] = fp8x2_to<T>(x23 >> 16);
+        }
+      };
+      for (int jb = jb0; jb < jb_end; jb += 2) {
+        const bool two = jb + 1 < jb_end;
+        Frag fa, fb;
+        load(i, jb, fa);
+        if (two) {
+          load(i + 1, jb + 1, fb);
+        } else {
+          fb.kr0 = fb.kr1 = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) fb.vr[r] = make_uint2(0u, 0u);
+          fb.ks0 = fb.ks1 = fb.vs0 = fb.vs1 = 0.f;
+          fb.valid = 0;
+        }
+        i += two ? 2 : 1;
+        float sa_[4], sb_[4];
+        qk(fa, sa_);
+        qk(fb, sb_);
+        // ---- online softmax per head over the 32 tokens (exp2 domain)
+        float xa0 = sa_[0] * (sl2 * fa.ks0), xa1 = sa_[1] * (sl2 * fa.ks0);  // block a, token g
+        float xa2 = sa_[2] * (sl2 * fa.ks1), xa3 = sa_[3] * (sl2 * fa.ks1);  // block a, token g + 8
+        float xb0 = sb_[0] * (sl2 * fb.ks0), xb1 = sb_[1] * (sl2 * fb.ks0);
+        float xb2 = sb_[2] * (sl2 * fb.ks1), xb3 = sb_[3] * (sl2 * fb.ks1);
+        if (fa.valid < 16) {
+          if (g >= fa.valid) xa0 = xa1 = -INFINITY;
+          if (g + 8 >= fa.valid) xa2 = xa3 = -INFINITY;
+        }
+        if (fb.valid < 16) {
+          if (g >= fb.valid) xb0 = xb1 = -INFINITY;
+          if (g + 8 >= fb.valid) xb2 = xb3 = -INFINITY;
+        }
+        float ma = fmaxf(fmaxf(xa0, xa2), fmaxf(xb0, xb2));
+        float mb = fmaxf(fmaxf(xa1, xa3), fmaxf(xb1, xb3));
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
+          mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        }
+        // lazy rescale: the reference max moves only when some head's max
+        // exceeds it by more than kRescaleSlack, so P stays <= 2^kRescaleSlack
+        // and the (m, l, O) triple stays exact relative to its own m
+        if (__any_sync(0xffffffffu, ma > m0 + kRescaleSlack || mb > m1 + kRescaleSlack)) {
+          const float mna = fmaxf(m0, ma), mnb = fmaxf(m1, mb);
+          const float ca = ex2_approx(m0 - mna), cb = ex2_approx(m1 - mnb);
+          l0 *= ca;
+          l1 *= cb;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) { o[j][0] *= ca; o[j][1] *= cb; o[j][2] *= ca; o[j][3] *= cb; }
+          m0 = mna;
+          m1 = mnb;
+        }
+        const float pa0 = ex2_approx(xa0 - m0), pa2 = ex2_approx(xa2 - m0);
+        const float pa1 = ex2_approx(xa1 - m1), pa3 = ex2_approx(xa3 - m1);
+        const float pb0 = ex2_approx(xb0 - m0), pb2 = ex2_approx(xb2 - m0);
+        const float pb1 = ex2_approx(xb1 - m1), pb3 = ex2_approx(xb3 - m1);
+        l0 += (pa0 + pa2) + (pb0 + pb2);
+        l1 += (pa1 + pa3) + (pb1 + pb3);
+        // P^T fragments with V's per-token scale folded in (l sums the unscaled P)
+        const uint32_t ba0 = movmatrix_t(pack2<T>(pa0 * fa.vs0, pa1 * fa.vs0));  // tokens 0-7
+        const uint32_t ba1 = movmatrix_t(pack2<T>(pa2 * fa.vs1, pa3 * fa.vs1));  // tokens 8-15
+        const uint32_t bb0 = movmatrix_t(pack2<T>(pb0 * fb.vs0, pb1 * fb.vs0));
+        const uint32_t bb1 = movmatrix_t(pack2<T>(pb2 * fb.vs1, pb3 * fb.vs1));
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t aa[4], ab[4];
+          pv_a(fa, mt, aa);
+          pv_a(fb, mt, ab);
+          mma16816<T>(o[mt], aa, ba0, ba1);
+          mma16816<T>(o[mt], ab, bb0, bb1);
+        }
+      }
+    } else {
+    for (int jb = jb0; jb < jb_end; ++jb, ++i) {
+      const int st = i % kDecStages;
+      if (!dead && !mbar_wait(&full_bar[st], (i / kDecStages) & 1)) {
+        if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+        dead = true;
+      }
+      // tokens of this block inside the context; only a sequence's last
+      // block has fewer than 16 (warp-uniform)
+      const int valid = min(16, ctx - jb * 16);
+      const uint32_t kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
+      const uint32_t vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
+      // ---- S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int mi = lane >> 3;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a[4];
+        const int row = (lane & 7) + ((mi & 1) << 3);
+        const int chunk = 2 * kk + (mi >> 1);
+        ldsm_x4(kt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
         mma16816<T>(sc, a, qa[kk][0], qa[kk][1]);
       }
       // ---- online softmax per head (exp2 domain)
-      const float sa = FP8 ? sl2 * ks0 : sl2;
-      const float sb = FP8 ? sl2 * ks1 : sl2;
-      float x0 = sc[0] * sa, x1 = sc[1] * sa;  // token g
-      float x2 = sc[2] * sb, x3 = sc[3] * sb;  // token g + 8
+      float x0 = sc[0] * sl2, x1 = sc[1] * sl2;  // token g
+      float x2 = sc[2] * sl2, x3 = sc[3] * sl2;  // token g + 8
       if (valid < 16) {
         if (g >= valid) x0 = x1 = -INFINITY;
         if (g + 8 >= valid) x2 = x3 = -INFINITY;
@@ -650,41 +764,20 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       l0 += p0 + p2;
       l1 += p1 + p3;
       // ---- P^T fragments: transpose (token x head) 8x8 tiles to (head x token)
-      // (fp8: V's per-token scale folded into P; l above sums the unscaled P)
-      const uint32_t b0 = movmatrix_t(FP8 ? pack2<T>(p0 * vs0, p1 * vs0) : pack2<T>(p0, p1));  // tokens 0-7
-      const uint32_t b1 = movmatrix_t(FP8 ? pack2<T>(p2 * vs1, p3 * vs1) : pack2<T>(p2, p3));  // tokens 8-15
-      // ---- O^T += V^T P^T, 4 tiles of 16 dims (fp8: O rows g, g + 8 of tile
-      // mt are dims 8g + 2mt and 8g + 2mt + 1)
+      const uint32_t b0 = movmatrix_t(pack2<T>(p0, p1));  // tokens 0-7
+      const uint32_t b1 = movmatrix_t(pack2<T>(p2, p3));  // tokens 8-15
+      // ---- O^T += V^T P^T, 4 tiles of 16 dims
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
         uint32_t a[4];
-        if constexpr (FP8) {
-          // interleave tokens (2t, 2t + 1) and (2t + 8, 2t + 9) byte by byte
-          const uint32_t sel = (mt & 1) ? sel_hi : sel_lo;
-          const uint32_t x01 = __byte_perm(mt < 2 ? vr[0].x : vr[0].y, mt < 2 ? vr[1].x : vr[1].y, sel);
-          const uint32_t x23 = __byte_perm(mt < 2 ? vr[2].x : vr[2].y, mt < 2 ? vr[3].x : vr[3].y, sel);
-          if constexpr (kAluV) {
-            a[0] = e4m3_even_h2(x01);
-            a[1] = e4m3_odd_h2(x01);
-            a[2] = e4m3_even_h2(x23);
-            a[3] = e4m3_odd_h2(x23);
-          } else {
-            a[0] = fp8x2_to<T>(x01 & 0xffffu);
-            a[1] = fp8x2_to<T>(x01 >> 16);
-            a[2] = fp8x2_to<T>(x23 & 0xffffu);
-            a[3] = fp8x2_to<T>(x23 >> 16);
-          }
-        } else {
-          const int row = (lane & 7) + ((mi >> 1) << 3);
-          const int chunk = 2 * mt + (mi & 1);
-          ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
-        }
+        const int row = (lane & 7) + ((mi >> 1) << 3);
+        const int chunk = 2 * mt + (mi & 1);
+        ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
         mma16816<T>(o[mt], a, b0, b1);
       }
-      if constexpr (!FP8) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[st]);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[st]);
+    }
     }
 
     // ---- segment epilogue: per-head sums over the 8 token groups
@@ -970,9 +1063,10 @@ constexpr int pipes_for(int nkv) { return nkv == 2 ? PKV_DEC_PIPES : 1; }
 
 size_t decode_smem_bytes(int nkv, int n_seqs, bool fp8) {
   const size_t stage = fp8 ? 2 * nkv * kDecTile8 + 2 * 16 * nkv * 4 : 2 * nkv * kDecTile;
+  const int stages = fp8 ? dec_stages<true>() : dec_stages<false>();
   return 1024 +
          static_cast<size_t>(pipes_for(nkv)) *
-             (static_cast<size_t>(kDecStages) * stage + 2 * kDecStages * sizeof(uint64_t)) +
+             (static_cast<size_t>(stages) * stage + 2 * stages * sizeof(uint64_t)) +
          40 * sizeof(int) + (2 * static_cast<size_t>(n_seqs) + 1) * sizeof(int);
 }
 
