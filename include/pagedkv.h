@@ -57,7 +57,7 @@ extern "C" {
 #define PKV_FLAG_PIPELINE_TIMEOUT 8
 #define PKV_FLAG_BAD_QUERY_LAYOUT 16
 #define PKV_FLAG_POSITION_OUT_OF_RANGE 32
-#define PKV_FLAG_BAD_SCHEDULE 64 /* a decode schedule built for another batch or grid */
+#define PKV_FLAG_BAD_SCHEDULE 64 /* a decode schedule built for another batch, grid or table width */
 
 /* size of the device-resident scratch array behind
  * pkv_paged_decode_attention_noalloc (per GPU, held until the process exits) */
@@ -165,8 +165,9 @@ int pkv_paged_prefill_attention_fp8_scratch(
  * n_kv_heads, head_dim, block_size, dtype and fp8_pools (1 for the fp8
  * decode) must be those of the decode calls that use it, and block_tables /
  * context_lens must not change between building and using it.  A schedule
- * for another batch size or grid sets PKV_FLAG_BAD_SCHEDULE and the decode
- * call does nothing.  Shapes the tensor-core decode kernel does not serve
+ * built for another batch size, grid or max_blocks_per_seq (table width)
+ * sets PKV_FLAG_BAD_SCHEDULE and the decode call reads nothing of it and
+ * does nothing.  Shapes the tensor-core decode kernel does not serve
  * build nothing and their _scheduled calls ignore the schedule.  The first
  * decode launch after a build is stream-ordered behind it.
  */

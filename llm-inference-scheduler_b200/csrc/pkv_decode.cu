@@ -133,7 +133,7 @@ struct DecodeParams {
 };
 
 // Decode schedule (int32): kSchedHdr header words {n_seqs, total blocks,
-// blocks per CTA, grid, row length}, then the block prefix [n_seqs + 1], the
+// blocks per CTA, grid, row length, table width}, then the block prefix [n_seqs + 1], the
 // clamped context lengths [n_seqs], then (16-byte aligned) CTA c's block ids
 // at [c * rows, c * rows + per).
 constexpr int kSchedHdr = 8;
@@ -339,7 +339,10 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       sched_id0 = __ldg(p.sched + sched_ids_offset(B) + static_cast<int64_t>(vcta) * p.sched_rows + lane);
     total = __ldg(p.sched + 1);
     per = __ldg(p.sched + 2);
-    if (__ldg(p.sched) != B || __ldg(p.sched + 3) != vgrid) {
+    // a schedule built for another batch, grid or table width (its row
+    // length and size follow from the width) is not read
+    if (__ldg(p.sched) != B || __ldg(p.sched + 3) != vgrid || __ldg(p.sched + 4) != p.sched_rows ||
+        __ldg(p.sched + 5) != p.max_blocks) {
       // a schedule built for another batch or grid: do nothing
       if (tid == 0 && vcta == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
       if (tid == 0) pdl_trigger();
@@ -904,6 +907,7 @@ __global__ void __launch_bounds__(kSchedThreads) decode_schedule_kernel(
       sched[2] = per;
       sched[3] = grid;
       sched[4] = rows;
+      sched[5] = max_blocks;
     }
   }
   int32_t* row = sched + sched_ids_offset(B) + static_cast<int64_t>(blockIdx.x) * rows;

@@ -819,6 +819,31 @@ def test_scheduled_decode_rejects_foreign_schedule():
     assert int(err.item()) & _lib.FLAG_BAD_SCHEDULE
 
 
+def test_scheduled_decode_rejects_schedule_of_another_table_width():
+    """A schedule built over block tables of another width (so another row
+    length and buffer size) is not read: PKV_FLAG_BAD_SCHEDULE, and the
+    decode call with the matching width still gives the unscheduled bits."""
+    c = C.make_decode_case(12, 9, 0, 0, 128, "f16", ctx_list=[1, 2, 15, 16, 17, 31, 32, 33, 600])
+    NB_SCHED[0] = c["k_pool"].shape[0]
+    tabs, ctx = dev(C.pad_tables(c["tables"])), dev(c["ctx"].astype(np.int32))
+    wide = torch.zeros((tabs.shape[0], tabs.shape[1] + 64), dtype=torch.int32, device="cuda")
+    wide[:, :tabs.shape[1]] = tabs
+    q = dev(c["q"], "f16")
+    kp, vp = dev(c["k_pool"], "f16"), dev(c["v_pool"], "f16")
+    sched = _sched_for(tabs, ctx, q)
+    err = ops.new_error_flags("cuda")
+    out = torch.full_like(q, 7.0)
+    ops.paged_decode_attention(q, kp, vp, wide, ctx, 0.125, out=out, err=err, schedule=sched)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.FLAG_BAD_SCHEDULE
+    err2 = ops.new_error_flags("cuda")
+    got = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err2, schedule=sched)
+    want = ops.paged_decode_attention(q, kp, vp, tabs, ctx, 0.125, err=err2)
+    torch.cuda.synchronize()
+    assert int(err2.item()) == 0
+    assert torch.equal(got, want)
+
+
 # ---------------------------------------------------------------- fused RoPE + fp8 append
 
 @pytest.mark.parametrize("dt", DTS)
