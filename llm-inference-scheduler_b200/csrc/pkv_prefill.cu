@@ -64,7 +64,10 @@ namespace pkv {
 constexpr int kPfM = 128;                 // query rows per tile
 constexpr int kPfPair = 2 * kPfM;         // query rows per CTA (tiles A and B)
 constexpr int kPfN = 128;                 // keys per tile (8 blocks of 16)
-constexpr int kPfStages = 4;              // K/V ring depth
+#ifndef PKV_PF_STAGES
+#define PKV_PF_STAGES 4
+#endif
+constexpr int kPfStages = PKV_PF_STAGES;  // K/V ring depth
 constexpr int kPfTile = 128 * 64 * 2;     // 16 KB: 128 rows x 64 dims x 2 bytes
 constexpr int kPfThreads = 384;
 constexpr int kPfRegsSoftmax = 224;       // per thread, warpgroups 0 and 1
@@ -92,6 +95,7 @@ constexpr int kNumBars = 1 + 2 * kPfStages + 4 * 2;
 constexpr int kOffSched = kOffBar + kNumBars * 8;      // tmem slot, work item, length keys
 constexpr int kSchedInts = 4 + kPfOrderMaxSeqs;
 constexpr int kPfSmemBytes = 1024 + kOffSched + kSchedInts * 4;
+static_assert(kPfSmemBytes <= 232448, "prefill ring does not fit the 227 KB of shared memory per CTA");
 
 struct PrefillParams {
   void* out;
