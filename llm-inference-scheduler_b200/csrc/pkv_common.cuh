@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/pagedkv.h"
 
 namespace pkv {
@@ -396,9 +398,59 @@ __device__ __forceinline__ uint8_t fp8_quantize(float x, float scale) {
 // type E (src, row h at src + h * d) quantised per row (scale = absmax / 448,
 // e4m3 bytes, RNE, saturated) into dst (bytes, row h at dst + h * d) with the
 // scales in sc[h].  Every lane of the warp must call it.
+// two values as e4m3 bytes (lo in bits 0-7), rounded to nearest even and
+// saturated at +-448: the rounding and saturation fp8_quantize asks of CUDA's
+// conversion, two values per PTX cvt
+__device__ __forceinline__ uint32_t e4m3x2_rn_sat(float lo, float hi) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// four consecutive values of type E as floats (p aligned to 4 * sizeof(E))
+template <typename E>
+__device__ __forceinline__ void load4_f(const E* __restrict__ p, float* v) {
+  if constexpr (sizeof(E) == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    const uint32_t w[2] = {t.x, t.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const unsigned short b = static_cast<unsigned short>(w[i >> 1] >> (16 * (i & 1)));
+      if constexpr (std::is_same<E, __half>::value) v[i] = __half2float(__ushort_as_half(b));
+      else v[i] = __bfloat162float(__ushort_as_bfloat16(b));
+    }
+  }
+}
 template <typename E>
 __device__ __forceinline__ void fp8_store_token(const E* __restrict__ src, uint8_t* __restrict__ dst,
                                                 float* __restrict__ sc, int n_heads, int d, int lane) {
+  // Rows of 64 values (the pools' head_dim), aligned: two rows per pass, a
+  // half-warp per row and four values per lane (one 8- or 16-byte load, one
+  // 4-byte store, a 16-lane max).  Same per-value arithmetic as the general
+  // loop below, so the same bytes and scales.
+  if (d == 64 && (reinterpret_cast<uintptr_t>(src) & (4 * sizeof(E) - 1)) == 0 &&
+      (reinterpret_cast<uintptr_t>(dst) & 3) == 0) {
+    const int half = lane >> 4, l16 = lane & 15;
+    for (int h0 = 0; h0 < n_heads; h0 += 2) {
+      const int h = h0 + half;
+      const bool on = h < n_heads;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (on) load4_f<E>(src + h * 64 + l16 * 4, v);
+      float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (on) {
+        const float s = fp8_row_scale(amax);
+        const uint32_t q = e4m3x2_rn_sat(__fdiv_rn(v[0], s), __fdiv_rn(v[1], s)) |
+                           (e4m3x2_rn_sat(__fdiv_rn(v[2], s), __fdiv_rn(v[3], s)) << 16);
+        *reinterpret_cast<uint32_t*>(dst + h * 64 + l16 * 4) = q;
+        if (l16 == 0) sc[h] = s;
+      }
+    }
+    return;
+  }
   for (int h = 0; h < n_heads; ++h) {
     float amax = 0.f;
     for (int i = lane; i < d; i += 32) amax = fmaxf(amax, fabsf(Elem<E>::to_f(src[h * d + i])));
