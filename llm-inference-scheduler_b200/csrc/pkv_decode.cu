@@ -433,38 +433,47 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         waited = true;
       }
       const int n = min(32, r1 - b0);
+      // fused append: the warp writes the K and V rows of the sequence whose
+      // newest token lies in batch block kk (fp8: quantised, with their
+      // scales); fence_appends() then orders those generic-proxy writes
+      // before lane 0's TMA reads
+      auto append_rows = [&](int kk) {
+        const int a_seq = __shfl_sync(0xffffffffu, app_seq, kk);
+        const int row = __shfl_sync(0xffffffffu, app_row, kk);
+        if constexpr (FP8) {
+          fp8_store_token<T>(reinterpret_cast<const T*>(p.k_new + a_seq * p.k_new_stride_b),
+                             p.k_pool + static_cast<int64_t>(row) * (nkv * 64),
+                             const_cast<float*>(p.k_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                             lane);
+          fp8_store_token<T>(reinterpret_cast<const T*>(p.v_new + a_seq * p.v_new_stride_b),
+                             p.v_pool + static_cast<int64_t>(row) * (nkv * 64),
+                             const_cast<float*>(p.v_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                             lane);
+        } else {
+          constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
+          for (int v = lane; v < 2 * row_vecs; v += 32) {
+            const bool is_v = v >= row_vecs;
+            const int vi = is_v ? v - row_vecs : v;
+            const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
+                                       : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
+            uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
+            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
+          }
+        }
+      };
+      auto fence_appends = [&]() {
+        fence_proxy_async_global();
+        __syncwarp();
+        if (lane == 0) fence_proxy_async_global();
+      };
+      // batch blocks that hold a sequence's newest token and are not yet written
+      uint32_t pending = __ballot_sync(0xffffffffu, app_seq >= 0);
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
-        const int a_seq = __shfl_sync(0xffffffffu, app_seq, k);
-        if (a_seq >= 0) {
-          // append before the block is loaded: the warp writes the K and V
-          // rows into the pool (fp8: quantised, with their scales), then
-          // orders those generic-proxy writes before lane 0's TMA read of
-          // the block
-          const int row = __shfl_sync(0xffffffffu, app_row, k);
-          if constexpr (FP8) {
-            fp8_store_token<T>(reinterpret_cast<const T*>(p.k_new + a_seq * p.k_new_stride_b),
-                               p.k_pool + static_cast<int64_t>(row) * (nkv * 64),
-                               const_cast<float*>(p.k_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
-                               lane);
-            fp8_store_token<T>(reinterpret_cast<const T*>(p.v_new + a_seq * p.v_new_stride_b),
-                               p.v_pool + static_cast<int64_t>(row) * (nkv * 64),
-                               const_cast<float*>(p.v_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
-                               lane);
-          } else {
-            constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
-            for (int v = lane; v < 2 * row_vecs; v += 32) {
-              const bool is_v = v >= row_vecs;
-              const int vi = is_v ? v - row_vecs : v;
-              const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
-                                         : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
-              uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
-              *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
-            }
-          }
-          fence_proxy_async_global();
-          __syncwarp();
-          if (lane == 0) fence_proxy_async_global();
+        if ((pending >> k) & 1u) {  // append before the block is loaded
+          append_rows(k);
+          fence_appends();
+          pending &= ~(1u << k);
         }
         if (lane == 0 && !dead) {
           const int st = i % kDecStages;
@@ -492,6 +501,19 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
                         p.v_scale + static_cast<int64_t>(blk) * 16 * nkv, scale_bytes, &full_bar[st]);
             }
           }
+        }
+        // 16-bit pools: the ring is full from here on, so the next load waits
+        // for a consumer to free a stage; write the batch's later appends
+        // now, while the tiles in flight arrive, instead of stalling the
+        // 3-stage ring at their blocks (each is still written and fenced
+        // before its block's load).  The fp8 appends (quantisation) stay at
+        // their blocks: done early they delay the next load once a stage
+        // frees, and the 6-stage fp8 ring hides them where they are.
+        if (!FP8 && i + 1 >= kDecStages && k + 1 < n && (pending >> (k + 1)) != 0u) {
+          for (uint32_t rest = pending >> (k + 1), kk = k + 1; rest != 0u; rest >>= 1, ++kk)
+            if (rest & 1u) append_rows(static_cast<int>(kk));
+          fence_appends();
+          pending &= (2u << k) - 1u;
         }
       }
     }
