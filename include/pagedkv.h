@@ -337,9 +337,11 @@ int pkv_paged_decode_append_attention(void* out, int64_t out_row_stride, const v
  * split-K partials in a fixed array of PKV_NOALLOC_SCRATCH_BYTES (8 MiB) that
  * is part of the library's device image: every GPU that loads the library
  * holds it until the process exits.  Nothing is allocated per call.
- *  - The first call on each device looks up that array's device address
- *    (cudaGetSymbolAddress, with that device current); make this first call
- *    before any stream capture.
+ *  - The first call in each CUDA context looks up that array's device
+ *    address (cudaGetSymbolAddress, with that device current) and caches it
+ *    under the context's unique id; a context made again after
+ *    cudaDeviceReset looks it up again.  Make the first call on a device
+ *    (and the first after a reset) before any stream capture.
  *  - Problems whose partials exceed the array (pkv_decode_workspace_bytes >
  *    PKV_NOALLOC_SCRATCH_BYTES, e.g. more than 15 query heads at head_dim 64)
  *    are rejected with PKV_ERR_SCRATCH_LIMIT before anything is launched.

@@ -209,8 +209,8 @@ const char* pkv_status_string(int status) {
     case PKV_ERR_MISALIGNED: return "pointer or stride misaligned for this kernel";
     case PKV_ERR_UNSUPPORTED: return "combination of arguments not supported";
     case PKV_ERR_DRIVER:
-      return "a CUDA driver entry point (cuTensorMapEncodeTiled, cuMemGetAddressRange) is "
-             "unavailable or failed";
+      return "a CUDA driver entry point (cuTensorMapEncodeTiled, cuMemGetAddressRange, "
+             "cuCtxGetCurrent, cuCtxGetId) is unavailable or failed";
     case PKV_ERR_SCRATCH_LIMIT:
       return "problem needs more split-K scratch than the allocation-free decode entry point's "
              "fixed PKV_NOALLOC_SCRATCH_BYTES array holds; use pkv_paged_decode_attention";

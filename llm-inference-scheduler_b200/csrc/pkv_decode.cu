@@ -1167,11 +1167,23 @@ cudaError_t decode_grid(int dtype, int nkv, bool fp8, int n_seqs, int* grid_out)
 }
 
 namespace {
-// schedules built on a stream and not yet read by a decode launch: that first
-// launch is stream-ordered (no programmatic overlap), because the kernel reads
-// the schedule before griddepcontrol.wait
-std::mutex g_fresh_mu;
-std::unordered_map<const void*, cudaStream_t> g_fresh;
+// The decode kernel reads its schedule before griddepcontrol.wait, so a decode
+// launch may overlap its predecessor only if the schedule is known to be
+// complete: a decode launch has already read it since its last build.  This
+// table maps a schedule to that fact.  A schedule that was just built, or one
+// the table does not know (never seen, or forgotten when the table was
+// cleared), gets a stream-ordered launch; clearing the table therefore costs
+// at most one overlap per schedule and never lets a launch read a schedule
+// that is still being written.
+constexpr size_t kSchedTableMax = 4096;
+std::mutex g_sched_mu;
+std::unordered_map<const void*, bool> g_sched_read;
+
+void sched_table_set(const void* schedule, bool read) {
+  if (g_sched_read.size() >= kSchedTableMax && g_sched_read.find(schedule) == g_sched_read.end())
+    g_sched_read.clear();
+  g_sched_read[schedule] = read;
+}
 }  // namespace
 
 cudaError_t launch_decode_schedule(void* schedule, const AttnArgs& a, cudaStream_t stream) {
@@ -1191,9 +1203,8 @@ cudaError_t launch_decode_schedule(void* schedule, const AttnArgs& a, cudaStream
       a.n_seqs, a.num_blocks, grid, rows, a.err);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
-    std::lock_guard<std::mutex> lk(g_fresh_mu);
-    if (g_fresh.size() > 4096) g_fresh.clear();  // schedules built and never used
-    g_fresh[schedule] = stream;
+    std::lock_guard<std::mutex> lk(g_sched_mu);
+    sched_table_set(schedule, false);
   }
   return e;
 }
@@ -1209,14 +1220,11 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   int grid = 0;
   cudaError_t e = decode_grid(a.dtype, nkv, fp8, a.n_seqs, &grid);
   if (e != cudaSuccess) return e;
-  bool ordered = false;  // the schedule was just built: no programmatic overlap
+  bool ordered = false;  // no programmatic overlap unless the schedule is known complete
   if (a.schedule != nullptr) {
-    std::lock_guard<std::mutex> lk(g_fresh_mu);
-    auto it = g_fresh.find(a.schedule);
-    if (it != g_fresh.end()) {
-      ordered = true;
-      g_fresh.erase(it);
-    }
+    std::lock_guard<std::mutex> lk(g_sched_mu);
+    auto it = g_sched_read.find(a.schedule);
+    ordered = it == g_sched_read.end() || !it->second;
   }
   DecodeParams p;
   p.out = a.out;
@@ -1262,6 +1270,10 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   cfg.numAttrs = ordered ? 0 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, *kmap, *vmap, p);
   if (e != cudaSuccess) return e;
+  if (a.schedule != nullptr) {  // read by a launch that is now queued behind its build
+    std::lock_guard<std::mutex> lk(g_sched_mu);
+    sched_table_set(a.schedule, true);
+  }
 
   cudaLaunchConfig_t mcfg = cfg;
   mcfg.numAttrs = 1;

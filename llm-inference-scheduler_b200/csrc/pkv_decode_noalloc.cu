@@ -10,10 +10,15 @@
 // until the process exits).  Nothing is allocated per call.
 //
 // The array's host-side name is only a handle: its device address is looked
-// up with cudaGetSymbolAddress once per device, with that device current, on
-// the first call made on it.  All calls on a device share the array; it keeps
-// the last call's partials, none of which need to start at zero, and calls
-// that overlap on the GPU race on it.
+// up with cudaGetSymbolAddress, with the device current, on the first call in
+// each CUDA context, and cached under that context's unique id.  A context
+// that is destroyed and made again (cudaDeviceReset, or the primary context
+// released and retained again) reloads the module, so the array may move; the
+// new context has a new id and the address is looked up again.  All calls on
+// a device share the array; it keeps the last call's partials, none of which
+// need to start at zero, and calls that overlap on the GPU race on it.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "pkv_common.cuh"
@@ -26,23 +31,61 @@ constexpr size_t kScratchBytes = PKV_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
+struct ScratchSlot {
+  unsigned long long ctx_id = 0;  // unique id of the context the address belongs to (0: none)
+  void* addr = nullptr;
+};
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of g_decode_scratch on the current device (looked up once).
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_fns_once;
+
+// Unique id of the calling thread's current context (0 when none is current).
+int current_context_id(unsigned long long* id) {
+  std::call_once(g_ctx_fns_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 4000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  if (!g_ctx_current || !g_ctx_id) return PKV_ERR_DRIVER;
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS) return PKV_ERR_DRIVER;
+  *id = 0;
+  if (ctx && g_ctx_id(ctx, id) != CUDA_SUCCESS) return PKV_ERR_DRIVER;
+  return PKV_OK;
+}
+
+// Device address of g_decode_scratch in the current device's current context.
 int scratch_on_current_device(void** addr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return PKV_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  unsigned long long id = 0;
+  int rc = current_context_id(&id);
+  if (rc != PKV_OK) return rc;
+  ScratchSlot& slot = g_scratch[dev];
+  if (id == 0 || slot.addr == nullptr || slot.ctx_id != id) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);  // makes the primary context current if needed
     if (e != cudaSuccess) return static_cast<int>(e);
-    g_scratch_addr[dev] = p;
+    rc = current_context_id(&id);
+    if (rc != PKV_OK) return rc;
+    slot.ctx_id = id;
+    slot.addr = p;
   }
-  *addr = g_scratch_addr[dev];
+  *addr = slot.addr;
   return PKV_OK;
 }
 

@@ -230,6 +230,15 @@ def migrate_blocks(peers: PeerPools, src: int, dst: int, blocks: list[int] | Non
             mgr.decref(b)
         peers._send([1] + [0] * n, src)
         raise
+    # A fresh block may have been freed just now by a sequence whose work on
+    # it is not done: a copy-on-write pair that reads it, still queued in the
+    # manager, or kernels on this rank's stream that read or write it.  The
+    # queued copies are launched first, so stream order puts them before a
+    # pull copy.  A push copy is the source's kernel, outside this rank's
+    # stream order, so the stream is also drained before the ids leave.
+    mgr.flush_copies()
+    if push:
+        peers._sync()
     peers._send([0] + ids, src)
     failure: Exception | None = None
     if push:

@@ -8,6 +8,9 @@ sync methods.  The checks:
 * a destination that cannot allocate raises OutOfBlocks on both ranks and
   keeps nothing;
 * a failed copy raises on both ranks and frees the destination's blocks;
+* a fresh destination block that a queued copy-on-write pair still reads is
+  not handed to the source before that pair is launched (and, in push mode,
+  before the destination's stream has drained);
 * migrate_sequence registers the sequence on the destination with its
   length and a table of ceil(len / 16) blocks.
 
@@ -66,7 +69,15 @@ def _fake_peer_pools_cls():
             dist.barrier(group=self.host_group)
 
         def _sync(self):
-            pass
+            self.syncs = getattr(self, "syncs", 0) + 1
+
+        def _send(self, values, peer):
+            # the destination's reply with fresh ids: record what was still
+            # queued and whether its stream had been drained
+            if self.rank == 1 and len(values) > 1 and values[0] == 0:
+                self.replies = getattr(self, "replies", []) + [
+                    (len(self.mgr.pending_copies), getattr(self, "syncs", 0))]
+            super()._send(values, peer)
 
         def _launch_copy(self, dst, src, pairs):
             if self.fail_copy:
@@ -126,6 +137,25 @@ def _cpu_rank(rank, world, port, pools, out_dir):
             res[f"fail_freed_{mode}"] = np.array(int(mgr.num_free == free_before))
             fpeers.close()
         Fake.fail_copy = False
+        # the destination recycles a block that a queued copy-on-write pair
+        # still reads: the pair must be launched (and, for push, the stream
+        # drained) before the fresh ids reach the source
+        for mode in ("push", "pull"):
+            rpeers = Fake(mgr, mode=mode)
+            if rank == 1:
+                a = mgr.allocate()
+                mgr.incref(a)
+                d = mgr.copy_block(a)   # queued (a, d)
+                mgr.decref(a)
+                mgr.decref(a)           # a is free again, first in the LIFO list
+            ids = migrate_blocks(rpeers, 0, 1, [2] if rank == 0 else None)
+            if rank == 1:
+                pend, syncs = rpeers.replies[-1]
+                res[f"recycled_{mode}"] = np.array([int(ids[0] == a), pend, int(syncs > 0)])
+                res[f"recycled_ids_{mode}"] = np.array(ids)
+                mgr.decref(d)
+                mgr.decref(ids[0])
+            rpeers.close()
         # a whole sequence: 37 tokens in a 4-block table -> 3 blocks move
         cache = PagedKVCache(mgr)
         if rank == 0:
@@ -160,11 +190,15 @@ def test_migration_protocol_two_gloo_ranks(tmp_path):
             for a, b in zip(before[0], pools[1]):
                 assert torch.equal(a[:, s], b[:, d]), (mode, s, d)
     touched = set(r1["push_ids"].tolist()) | set(r1["pull_ids"].tolist()) | set(r1["seq_table"].tolist())
+    touched |= set(r1["recycled_ids_push"].tolist()) | set(r1["recycled_ids_pull"].tolist())
     for d in range(nb1):
         if d not in touched:
             for a, b in zip(before[1], pools[1]):
                 assert torch.equal(a[:, d], b[:, d]), d
     assert r0["oob"] == 1 and r1["oob"] == 1 and r1["free_kept"] == 1
+    # recycled block: nothing queued at the reply; push drained the stream
+    assert r1["recycled_push"].tolist() == [1, 0, 1]
+    assert r1["recycled_pull"].tolist()[:2] == [1, 0]
     for mode in ("push", "pull"):
         assert r0[f"fail_{mode}"] == 1 and r1[f"fail_{mode}"] == 1, mode
         assert r1[f"fail_freed_{mode}"] == 1, mode

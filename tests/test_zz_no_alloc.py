@@ -8,7 +8,8 @@ scratch in a fixed 8 MiB device array inside the library instead.
 
 These tests call it through the C ABI (ctypes, raw pointers) and check:
 * two calls in a row each match the regular entry point (which gets its own
-  workspace) within the fp16/bf16 tolerances the other parity tests use;
+  workspace) and the CPU oracle within the fp16/bf16 tolerances the other
+  parity tests use;
 * a problem whose partials would not fit the fixed array is refused with
   PKV_ERR_SCRATCH_LIMIT before anything runs, leaving the output untouched.
 
@@ -55,8 +56,9 @@ def _call_noalloc(out, q, k_pool, v_pool, tables, ctx, err, scale=0.125):
                                                  lognormal_median=1024.0, pool_slack=1.1)),
     ("config1", "bf16", lambda: C.make_decode_case(1, 8, 32, 600, 512, "bf16")),
 ])
-def test_noalloc_matches_regular_entry_point_on_two_calls(name, dt, make):
+def test_noalloc_matches_regular_entry_point_on_two_calls(name, dt, make, oracle_mod):
     c = make()
+    want, _, _ = oracle_mod.run_decode_case(c)
     kp, vp = _dev(c["k_pool"], dt), _dev(c["v_pool"], dt)
     ops.reshape_and_cache(_dev(c["k_new"], dt), _dev(c["v_new"], dt), kp, vp,
                           torch.from_numpy(C.decode_slots(c)).cuda())
@@ -72,6 +74,8 @@ def test_noalloc_matches_regular_entry_point_on_two_calls(name, dt, make):
         torch.cuda.synchronize()
         d = max_abs_diff(_host(out, dt), _host(ref, dt), dt)
         assert d <= PRODUCT_ATOL[dt], f"{name} call {call}: max |noalloc - regular| = {d}"
+        d = max_abs_diff(_host(out, dt), want, dt)
+        assert d <= PRODUCT_ATOL[dt], f"{name} call {call}: max |noalloc - oracle| = {d}"
     assert int(err.item()) == 0
 
 
