@@ -241,17 +241,106 @@ def run_reference(args):
 
 # --------------------------------------------------------------- GPU arm
 
+def pin_rank_cpus(local: int, local_world: int) -> list[int]:
+    """Pin this process to its disjoint share of the host cores (torchrun
+    ranks of one node would otherwise contend for the same cores while they
+    enqueue launches and copies).  Returns the cores now allowed."""
+    from pagedkv import workloads as W
+
+    cpus = sorted(os.sched_getaffinity(0))
+    mine = W.rank_cpus(cpus, local, local_world)
+    if mine and local_world > 1:
+        os.sched_setaffinity(0, mine)
+    return sorted(os.sched_getaffinity(0))
+
+
+class DecodeRun:
+    """One rank's config-3 decode workload on its GPU: pools of 1.1x the
+    needed blocks per layer (random N(0,1) contents), scattered tables, the
+    step's q / new K / new V per layer, and the bound launches of one step
+    (schedule build, then one fused append + decode call per layer)."""
+
+    def __init__(self, batch: int, strong: bool, rank: int, world: int, L: int, dev):
+        import numpy as np
+        import torch
+
+        from pagedkv import BlockManager, ops
+        from pagedkv import workloads as W
+
+        self.L, self.scale, self.dt = L, 0.125, torch.float16
+        dt = self.dt
+        self.ctx = ctx = W.shard_contexts(batch, rank, world, strong=strong)
+        self.B = B = len(ctx)
+        self.nblk = nblk = (ctx + 15) // 16
+        self.nb = nb = int(math.ceil(1.1 * nblk.sum()))
+        self.tabs_np = W.make_tables(ctx, nb, seed=100 + rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(1234 + rank)
+        self.mgr = mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=dt)
+        for layer in range(L):
+            mgr.k_pool[layer].normal_(generator=g)
+            mgr.v_pool[layer].normal_(generator=g)
+        self.q = torch.randn((L, B, 14, 64), generator=g, device=dev, dtype=dt)
+        self.kn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+        self.vn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
+        self.out = torch.empty_like(self.q)
+        self.tabs = torch.from_numpy(self.tabs_np).to(dev)
+        self.ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+        self.ws = ops.new_decode_workspace(B, 14, 64, dev)
+        self.err = ops.new_error_flags(dev)
+        self.sched = ops.new_decode_schedule(B, self.tabs.shape[1], dev)
+        self.build_sched = ops.bind_decode_schedule(self.sched, self.tabs, self.ctx_d, nb, 14, 2, 64, dt,
+                                                    err=self.err)
+        self.decodes = [ops.bind_paged_decode_append_attention(
+            self.q[l], self.kn[l], self.vn[l], mgr.k_pool[l], mgr.v_pool[l], self.tabs, self.ctx_d,
+            self.scale, self.ws, self.out[l], self.err, schedule=self.sched) for l in range(L)]
+        self.dec_bytes = W.decode_bytes(ctx)
+        self.app_bytes = W.append_bytes(B)
+        self.step_bytes = L * (self.dec_bytes + self.app_bytes)
+
+    def step(self):
+        """One decode step: the schedule, then one call per layer (the decode
+        kernel appends the step's token itself, then its merge)."""
+        self.build_sched()
+        for f in self.decodes:
+            f()
+
+    def calls(self):
+        """The step's 24 calls without the schedule build (it stays valid:
+        the lengths and tables do not change)."""
+        for f in self.decodes:
+            f()
+
+    def timed(self, fn, steps: int, barrier) -> float:
+        """Device ms per call of `fn`, `steps` calls back to back bracketed by
+        a barrier and a device synchronisation on both sides."""
+        import torch
+
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+        return start.elapsed_time(end) / steps
+
+
 def run_ours(args):
     import numpy as np
     import torch
     import torch.distributed as dist
 
-    from pagedkv import BlockManager, PagedKVCache, ops
+    from pagedkv import PagedKVCache, ops
     from pagedkv import workloads as W
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    cpus = pin_rank_cpus(local, local_world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -259,129 +348,77 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    L, scale, dt = args.layers, 0.125, torch.float16
-    ctx = W.shard_contexts(args.batch, rank, world, strong=args.strong)
-    B = len(ctx)
-    nblk = (ctx + 15) // 16
-    nb = int(math.ceil(1.1 * nblk.sum()))
-    tabs_np = W.make_tables(ctx, nb, seed=100 + rank)
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-
-    mgr = BlockManager(nb, 16, L, 2, 64, device=dev, dtype=dt)
-    for layer in range(L):
-        mgr.k_pool[layer].normal_(generator=g)
-        mgr.v_pool[layer].normal_(generator=g)
-    q = torch.randn((L, B, 14, 64), generator=g, device=dev, dtype=dt)
-    kn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
-    vn = torch.randn((L, B, 2, 64), generator=g, device=dev, dtype=dt)
-    out = torch.empty_like(q)
-    pos = ctx - 1
-    slots = torch.from_numpy(tabs_np[np.arange(B), pos // 16].astype(np.int64) * 16 + pos % 16).to(dev)
-    tabs = torch.from_numpy(tabs_np).to(dev)
-    ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
-    ws = ops.new_decode_workspace(B, 14, 64, dev)
-    err = ops.new_error_flags(dev)
-
-    # per step: the decode schedule (once), then one call per layer, in which
-    # the decode kernel appends the new token itself
-    sched = ops.new_decode_schedule(B, tabs.shape[1], dev)
-    build_sched = ops.bind_decode_schedule(sched, tabs, ctx_d, nb, 14, 2, 64, dt, err=err)
-    decodes = [ops.bind_paged_decode_append_attention(q[l], kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
-                                                      tabs, ctx_d, scale, ws, out[l], err,
-                                                      schedule=sched)
-               for l in range(L)]
-
-    dec_bytes = W.decode_bytes(ctx)
-    app_bytes = W.append_bytes(B)
-    step_bytes = L * (dec_bytes + app_bytes)
-
-    def step(ev=None):
-        # ev brackets the whole layer loop: per-call events would break the
-        # programmatic-dependent-launch overlap of consecutive calls
-        build_sched()
-        if ev is not None:
-            ev[0].record()
-        for layer in range(L):
-            decodes[layer]()
-        if ev is not None:
-            ev[1].record()
-
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    L = args.layers
+    R = DecodeRun(args.batch, args.strong, rank, world, L, dev)
+    B, ctx, nblk, mgr, scale, dt = R.B, R.ctx, R.nblk, R.mgr, R.scale, R.dt
+
     for _ in range(args.warmup):
-        step()
+        R.step()
     torch.cuda.synchronize()
-    ops.check_flags(err, "bench warm-up")
+    ops.check_flags(R.err, "bench warm-up")
 
     if args.profile_steps:
         for _ in range(args.profile_steps):
-            step()
+            R.step()
         torch.cuda.synchronize()
         if world > 1:
             dist.destroy_process_group()
         return
 
-    # events around the L back-to-back decode calls of every 10th timed step
-    # (decode kernel roofline: one call = decode kernel + its split-K merge)
-    every = 10
-    ev_steps = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                for _ in range((args.steps + every - 1) // every)]
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     time.sleep(0.3 if sampler else 0)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
     t_wall0 = time.time()
-    start.record()
-    for i in range(args.steps):
-        step(ev_steps[i // every] if i % every == 0 else None)
-    end.record()
-    torch.cuda.synchronize()
+    # (1) the step: schedule build + 24 calls, the headline value
+    ms_local = R.timed(R.step, args.steps, barrier)
+    # (2) the roofline: the same 24 calls without the build, so that 24 x the
+    # call time is part of the step time by construction
+    dec_ms_local = R.timed(R.calls, args.steps, barrier) / L
     t_wall1 = time.time()
-    barrier()
     if sampler:
         sampler.stop()
-    ops.check_flags(err, "bench timed region")
-    ms_local = start.elapsed_time(end) / args.steps
-    dec_ms_samples = [a.elapsed_time(b) / L for (a, b) in ev_steps]
-    dec_ms_local = sum(dec_ms_samples) / len(dec_ms_samples)
+    ops.check_flags(R.err, "bench timed region")
     ms = W.max_over_ranks(ms_local)
     dec_ms = W.max_over_ranks(dec_ms_local)
-    total_bytes = W.sum_over_ranks(step_bytes)
+    total_bytes = W.sum_over_ranks(R.step_bytes)
     total_seqs = W.sum_over_ranks(B)
+    per_rank = {"sum_ctx": [int(x) for x in W.gather_over_ranks(int(ctx.sum()))],
+                "seqs": [int(x) for x in W.gather_over_ranks(B)],
+                "ms_local": [round(x, 5) for x in W.gather_over_ranks(ms_local)],
+                "decode_call_ms_local": [round(x, 6) for x in W.gather_over_ranks(dec_ms_local)],
+                "host_cpus": [int(x) for x in W.gather_over_ranks(len(cpus))]}
 
     # ---- end to end through the public API: pinned host inputs in, outputs back
     kv = PagedKVCache(mgr)
     for i in range(B):
-        kv.add_sequence(i, tabs_np[i, :nblk[i]].tolist(), int(ctx[i]) - 1)
-    # the step's inputs in one pinned staging buffer, [L, B, 18, 64]: a
-    # layer's q, k and v are views of its rows (one copy per chunk)
+        kv.add_sequence(i, R.tabs_np[i, :nblk[i]].tolist(), int(ctx[i]) - 1)
+    # the step's inputs in one pinned staging buffer, [L, B, 18, 64]: a run
+    # of layers' q, k and v are views of its rows (one copy per chunk)
     hqkv = torch.empty((L, B, 18, 64), dtype=dt).pin_memory()
-    hqkv[:, :, :14].copy_(q)
-    hqkv[:, :, 14:16].copy_(kn)
-    hqkv[:, :, 16:18].copy_(vn)
+    hqkv[:, :, :14].copy_(R.q)
+    hqkv[:, :, 14:16].copy_(R.kn)
+    hqkv[:, :, 16:18].copy_(R.vn)
     dqkv = torch.empty((L, B, 18, 64), device=dev, dtype=dt)
-    lq = [dqkv[l, :, :14] for l in range(L)]
-    lk = [dqkv[l, :, 14:16] for l in range(L)]
-    lv = [dqkv[l, :, 16:18] for l in range(L)]
-    lo = [out[l] for l in range(L)]
+    out = R.out
     hout = torch.empty_like(out, device="cpu").pin_memory()
 
     # Each step is self-contained: its inputs go host -> device in chunks of
     # layers on a copy stream, each chunk's layers run as soon as it has
-    # landed, and each chunk's outputs go back on a second copy stream; the
-    # step ends when its last output is on the host.  The next step's copies
-    # start after this step's compute (no prefetch across steps).  Small
-    # first and last chunks shorten the pipeline's fill (first copy in) and
-    # drain (last copy out).
+    # landed (one PagedKVCache.forward_layers call per chunk), and each
+    # chunk's outputs go back on a second copy stream; the step ends when its
+    # last output is on the host.  The next step's copies start after this
+    # step's compute (no prefetch across steps).  Small first and last chunks
+    # shorten the pipeline's fill (first copy in) and drain (last copy out).
     sizes = [int(x) for x in args.e2e_chunks.split(",")]
     if sum(sizes) != L:
         sizes = [L]
     bounds = [sum(sizes[:i]) for i in range(len(sizes) + 1)]
     n_chunks = len(sizes)
+    chunks = [(bounds[c], bounds[c + 1]) for c in range(n_chunks)]
+    views = [(dqkv[a:b, :, :14], dqkv[a:b, :, 14:16], dqkv[a:b, :, 16:18], out[a:b]) for a, b in chunks]
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
     ev_out = [torch.cuda.Event() for _ in range(n_chunks)]
@@ -392,43 +429,83 @@ def run_ours(args):
         meta = kv.prepare_step(seqs_all)
         h2d_s.wait_stream(cur)
         with torch.cuda.stream(h2d_s):
-            for c in range(n_chunks):
-                sl = slice(bounds[c], bounds[c + 1])
-                dqkv[sl].copy_(hqkv[sl], non_blocking=True)
+            for c, (a, b) in enumerate(chunks):
+                dqkv[a:b].copy_(hqkv[a:b], non_blocking=True)
                 ev_in[c].record(h2d_s)
-        for c in range(n_chunks):
+        for c, (a, b) in enumerate(chunks):
             cur.wait_event(ev_in[c])
-            for layer in range(bounds[c], bounds[c + 1]):
-                kv.forward_layer(layer, lq[layer], lk[layer], lv[layer], meta, scale, out=lo[layer],
-                                 advance=False)
+            q_, k_, v_, o_ = views[c]
+            kv.forward_layers(a, q_, k_, v_, meta, scale, out=o_, advance=False)
             ev_out[c].record(cur)
             d2h_s.wait_event(ev_out[c])
             with torch.cuda.stream(d2h_s):
-                sl = slice(bounds[c], bounds[c + 1])
-                hout[sl].copy_(out[sl], non_blocking=True)
+                hout[a:b].copy_(out[a:b], non_blocking=True)
         cur.wait_stream(d2h_s)
 
     for _ in range(10):
         e2e_step()
     torch.cuda.synchronize()
     barrier()
-    # the step is host-bound (Python enqueues every copy and launch), so host
-    # hiccups on a shared machine move its mean: time it in windows of steps
-    # back to back and report the median window (all windows in the line)
+    # host hiccups on a shared machine move the mean of a host-driven step:
+    # time it in windows of steps back to back and report the median window
+    # (all windows in the line)
     n_win = max(1, args.e2e_windows)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_win + 1)]
+    host_s = []
     evs[0].record()
     for w in range(n_win):
+        h0 = time.perf_counter()
         for _ in range(args.e2e_steps):
             e2e_step()
+        host_s.append(time.perf_counter() - h0)
         evs[w + 1].record()
     torch.cuda.synchronize()
     barrier()
-    ops.check_flags(err, "bench e2e")
+    ops.check_flags(R.err, "bench e2e")
     win_ms = [evs[w].elapsed_time(evs[w + 1]) / args.e2e_steps for w in range(n_win)]
-    e2e_ms = W.max_over_ranks(statistics.median(win_ms))
+    e2e_ms_local = statistics.median(win_ms)
+    e2e_ms = W.max_over_ranks(e2e_ms_local)
+    host_ms_local = 1e3 * statistics.median(host_s) / args.e2e_steps
+    per_rank["e2e_ms_local"] = [round(x, 5) for x in W.gather_over_ranks(e2e_ms_local)]
+    per_rank["e2e_host_enqueue_ms_local"] = [round(x, 5) for x in W.gather_over_ranks(host_ms_local)]
     h2d = hqkv.numel() * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
     d2h = hout.numel() * 2
+    del kv, dqkv, hqkv, hout
+
+    # ---- the same job under strong scaling (BASELINE config 3's wording:
+    # 256 sequences in total, dealt over the N GPUs), same process
+    strong = None
+    if not args.strong:
+        if world == 1:
+            strong = {"same_as_weak": True}
+        else:
+            S = DecodeRun(args.batch, True, rank, world, L, dev)
+            for _ in range(args.warmup):
+                S.step()
+            torch.cuda.synchronize()
+            s_ms_local = S.timed(S.step, args.steps, barrier)
+            s_dec_local = S.timed(S.calls, args.steps, barrier) / L
+            ops.check_flags(S.err, "bench strong pass")
+            s_ms = W.max_over_ranks(s_ms_local)
+            s_dec = W.max_over_ranks(s_dec_local)
+            s_bytes = W.sum_over_ranks(S.step_bytes)
+            s_seqs = W.sum_over_ranks(S.B)
+            s_call_bytes = W.gather_over_ranks(S.dec_bytes + S.app_bytes)
+            s_dec_list = W.gather_over_ranks(s_dec_local)
+            peak_s, _ = peaks()
+            strong = {
+                "global_batch": int(s_seqs), "ms_per_step": round(s_ms, 4),
+                "value": round(s_bytes / (s_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+                "decode_tok_s": round(s_seqs / (s_ms * 1e-3), 1),
+                "decode_call_ms": round(s_dec, 5),
+                "decode_call_frac_per_rank": [round(b / (t * 1e-3) / 1e9 / peak_s, 4)
+                                              for b, t in zip(s_call_bytes, s_dec_list)],
+                "per_rank": {"sum_ctx": [int(x) for x in W.gather_over_ranks(int(S.ctx.sum()))],
+                             "seqs": [int(x) for x in W.gather_over_ranks(S.B)],
+                             "ms_local": [round(x, 5) for x in W.gather_over_ranks(s_ms_local)],
+                             "decode_call_ms_local": [round(x, 6) for x in s_dec_list]},
+            }
+            del S
 
     if world > 1:
         dist.destroy_process_group()
@@ -436,8 +513,12 @@ def run_ours(args):
         return
 
     peak, peak_kind = peaks()
-    achieved = (dec_bytes + app_bytes) / (dec_ms * 1e-3) / 1e9
+    ctx0 = W.shard_contexts(args.batch, 0, world, strong=args.strong)
+    call_bytes = W.decode_bytes(ctx0) + W.append_bytes(len(ctx0))
+    dec_ms0 = per_rank["decode_call_ms_local"][0]
+    achieved = call_bytes / (dec_ms0 * 1e-3) / 1e9
     clocks = sampler.summary(t_wall0, t_wall1) if sampler else None
+    mean_ms = statistics.mean(per_rank["ms_local"])
     line = {
         "metric": METRIC,
         "value": round(total_bytes / (ms * 1e-3) / 1e9, 2),
@@ -452,28 +533,34 @@ def run_ours(args):
         "dtype": "f16",
         "data": "synthetic (seeded normal K/V/Q; lognormal contexts); no weights involved",
         "config": {"workload": WORKLOAD, "global_batch": int(total_seqs), "layers": L,
-                   "sum_ctx_rank0": int(ctx.sum()), "pool_blocks_rank0": nb,
+                   "sum_ctx_rank0": int(ctx.sum()), "pool_blocks_rank0": rank0_pool_blocks(args, world),
                    "parallelism": f"sequence-sharded x{world}, no collective on the data path",
                    "l2": "inputs larger than L2: ~155 MB of KV per layer, 24 distinct layer pools per step"},
         "decode_tok_s": round(total_seqs / (ms * 1e-3), 1),
         "hbm_frac_step": round(total_bytes / world / (ms * 1e-3) / 1e9 / peak, 4),
+        "per_rank": per_rank,
+        "max_over_ranks_vs_mean": round(ms / mean_ms, 4),
         "roofline": {"kernel": "paged_decode_kernel<half>", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic_from_profiles(), "bytes_per_launch": dec_bytes + app_bytes,
-                     "avg_launch_ms": round(dec_ms, 5),
-                     "timing": "CUDA events around the 24 back-to-back fused append+decode calls of every "
-                               "10th timed step, / 24; a call is the decode kernel plus its split-K merge"},
+                     "traffic": traffic_from_profiles(), "bytes_per_launch": call_bytes,
+                     "avg_launch_ms": round(dec_ms0, 5),
+                     "timing": "rank 0; CUDA events around --steps rounds of the 24 fused append+decode "
+                               "calls back to back (the step without its schedule build), / (steps x 24); "
+                               "a call is the decode kernel plus its split-K merge"},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "ms_per_step": round(e2e_ms, 4), "api": "PagedKVCache.prepare_step + forward_layer",
-                "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back",
+                "ms_per_step": round(e2e_ms, 4),
+                "api": "PagedKVCache.prepare_step + forward_layers (one C call per chunk of layers)",
+                "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back, max over ranks",
                 "windows_ms_per_step": [round(x, 4) for x in win_ms],
                 "copies": f"pinned host buffers; per step: metadata, then q|k|v of 24 layers H2D in "
                           f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
                           "on a second copy stream, overlapped with the step's own compute; the step ends "
-                          "when its outputs are on the host"},
-        "gpu_launches": (2 * L + 1) * args.steps,  # schedule + (decode kernel + merge) per layer
+                          "when its outputs are on the host",
+                "host_cpus_per_rank": len(cpus)},
+        "strong": strong,
+        "gpu_launches": (2 * L + 1) * args.steps,  # per timed step: schedule + (decode, merge) x 24
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:
@@ -481,6 +568,14 @@ def run_ours(args):
         line["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": cores,
                                 "kind": "port", "sample": sample}
     print(json.dumps(line), flush=True)
+
+
+def rank0_pool_blocks(args, world: int) -> int:
+    """Pool blocks of rank 0 (1.1x its needed blocks)."""
+    from pagedkv import workloads as W
+
+    ctx0 = W.shard_contexts(args.batch, 0, world, strong=args.strong)
+    return int(math.ceil(1.1 * ((ctx0 + 15) // 16).sum()))
 
 
 def peaks_tflops():

@@ -204,6 +204,35 @@ int pkv_paged_decode_append_attention_scheduled(
     size_t workspace_bytes, int* err_flags, pkv_stream_t stream, const void* schedule);
 
 /*
+ * A decode step over a run of consecutive layers in one call: for layer
+ * l = 0 .. n_layers-1 exactly pkv_paged_decode_append_attention(_scheduled)
+ * with every per-layer pointer advanced by l times its layer stride.  Replaces
+ * the per-layer loop of Qwen2Model.forward (mini_engine/model/qwen2.py:
+ * 159-166) over PagedKVCache.append_and_fetch (block_manager.py:111-141) +
+ * _attention, for a step whose sequences all decode one token and whose
+ * layers' q / k / v are ready together (e.g. copied in from the host at
+ * once): one host call issues 2 x n_layers launches instead of n_layers
+ * calls, each with its own argument checks.
+ *   q, out       : layer l at + l * q_layer_stride / out_layer_stride elements;
+ *   k_new, v_new : layer l at + l * new_layer_stride elements;
+ *   k_pools, v_pools : layer l's pool at + l * pool_layer_stride_bytes bytes
+ *                  (the [num_layers][num_blocks][block_size][Hkv][D] caches).
+ * Tables, lengths, scale, workspace and schedule are shared by the layers
+ * (a schedule built for the step serves them all; NULL: none).  Arguments
+ * are checked for the first and the last layer before anything launches; on
+ * a launch error the call returns it and the later layers are not issued.
+ */
+int pkv_paged_decode_append_attention_layers(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule);
+
+/*
  * KV block migration between GPUs (one process per GPU).  Replaces the
  * reference's recompute preemption (mini_engine/scheduler.py:143-156 frees a
  * preempted sequence's blocks and recomputes its KV later): a rank copies a

@@ -807,6 +807,67 @@ int pkv_paged_decode_append_attention_scheduled(void* out, int64_t out_row_strid
                                                 schedule);
 }
 
+int pkv_paged_decode_append_attention_layers(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule) {
+  if (n_layers < 0 || n_seqs < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_layers == 0 || n_seqs == 0) return PKV_OK;
+  if (!out || !q || !k_new || !v_new || !k_pools || !v_pools) return PKV_ERR_NULL_POINTER;
+  if (schedule && (reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  if (dtype != PKV_DTYPE_F32 && dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16)
+    return PKV_ERR_BAD_DTYPE;
+  const int64_t es = esize_of(dtype);
+  // consecutive layers' pools must not overlap
+  const int64_t pool_bytes = static_cast<int64_t>(num_blocks) * block_size * n_kv_heads *
+                             head_dim * es;
+  if (n_layers > 1 && (pool_layer_stride_bytes < pool_bytes || out_layer_stride <= 0 ||
+                       q_layer_stride <= 0 || new_layer_stride <= 0))
+    return PKV_ERR_BAD_SHAPE;
+  if ((pool_layer_stride_bytes & 15) != 0) return PKV_ERR_MISALIGNED;
+  auto at = [](const void* base, int64_t off_bytes) {
+    return static_cast<const void*>(static_cast<const uint8_t*>(base) + off_bytes);
+  };
+  auto layer_call = [&](int l) -> int {
+    void* o = const_cast<void*>(at(out, l * out_layer_stride * es));
+    const void* ql = at(q, l * q_layer_stride * es);
+    const void* kn = at(k_new, l * new_layer_stride * es);
+    const void* vn = at(v_new, l * new_layer_stride * es);
+    void* kp = const_cast<void*>(at(k_pools, l * pool_layer_stride_bytes));
+    void* vp = const_cast<void*>(at(v_pools, l * pool_layer_stride_bytes));
+    return pkv_paged_decode_append_attention_impl(
+        o, out_row_stride, ql, q_row_stride, kn, vn, k_new_row_stride, v_new_row_stride, kp, vp,
+        num_blocks, block_tables, block_table_stride, max_blocks_per_seq, context_lens, n_seqs,
+        n_q_heads, n_kv_heads, head_dim, block_size, scale, dtype, workspace, workspace_bytes,
+        err_flags, stream, schedule);
+  };
+  // the shared arguments and the last layer's pointers are checked before
+  // the first launch, so a bad call issues nothing
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pools, v_pools, num_blocks,
+                      block_tables, block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads,
+                      head_dim, block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  const int last = n_layers - 1;
+  rc = check_attn(at(out, last * out_layer_stride * es), out_row_stride,
+                  at(q, last * q_layer_stride * es), q_row_stride,
+                  at(k_pools, last * pool_layer_stride_bytes),
+                  at(v_pools, last * pool_layer_stride_bytes), num_blocks, block_tables,
+                  block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                  block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!context_lens) return PKV_ERR_NULL_POINTER;
+  for (int l = 0; l < n_layers; ++l) {
+    rc = layer_call(l);
+    if (rc != PKV_OK) return rc;
+  }
+  return PKV_OK;
+}
+
 size_t pkv_prefill_fp8_scratch_bytes(int n_seqs, int max_blocks_per_seq, int n_kv_heads,
                                      int head_dim) {
   if (n_seqs < 0 || max_blocks_per_seq < 0 || n_kv_heads <= 0 || head_dim <= 0) return 0;

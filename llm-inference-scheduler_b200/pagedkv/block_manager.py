@@ -192,6 +192,7 @@ class StepMetadata:
     query_start_loc: torch.Tensor   # int32 [B - n_decode + 1], relative to the prefill rows
     num_prior_dev: torch.Tensor     # int32 [B]
     decode_plan: ops.DecodeAppendPlan | None = None  # built by the first forward_layer
+    layers_plan: ops.DecodeAppendLayersPlan | None = None  # built by the first forward_layers
     decode_plain_plan: ops.DecodePlan | None = None   # built by the first forward_layer_qkv
     decode_schedule: torch.Tensor | None = None       # the step's decode schedule (first layer)
     rope_plan: ops.RopePlan | None = None             # built by the first forward_layer_qkv
@@ -571,6 +572,41 @@ class PagedKVCache:
             self._prefill(layer, q, meta, scale, out)
         if advance and layer == mgr.num_layers - 1:
             self._advance(meta)
+        return out
+
+    def forward_layers(self, first_layer: int, q: torch.Tensor, k_new: torch.Tensor,
+                       v_new: torch.Tensor, meta: StepMetadata, scale: float,
+                       out: torch.Tensor | None = None, advance: bool = True) -> torch.Tensor:
+        """forward_layer for the n consecutive layers first_layer ..
+        first_layer + n - 1 at once, with layer-major inputs: q [n, T, Hq, D],
+        k_new / v_new [n, T, Hkv, D] -> out [n, T, Hq, D].  A decode-only step
+        over 16-bit pools is one C call for the whole run
+        (pkv_paged_decode_append_attention_layers: the fused append + decode
+        and the merge of every layer); other steps run forward_layer layer by
+        layer.  The results are those of forward_layer either way."""
+        mgr = self.mgr
+        n = q.shape[0]
+        last = first_layer + n
+        assert 0 <= first_layer and last <= mgr.num_layers, "layers outside the pools"
+        if out is None:
+            out = torch.empty((n, meta.n_tokens) + tuple(q.shape[2:]), dtype=q.dtype, device=q.device)
+        if mgr._pending:
+            mgr.flush_copies()
+        nd = meta.n_decode
+        if not mgr.fp8 and 0 < nd == meta.n_tokens:
+            plan = meta.layers_plan
+            if plan is None or plan.scale != scale:
+                ws = self.decode_workspace(nd, q.shape[2], q.shape[3])
+                plan = meta.layers_plan = ops.DecodeAppendLayersPlan(
+                    meta.block_tables, meta.context_lens, scale, ws, mgr.err,
+                    schedule=self._step_schedule(meta, q[0]))
+            plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out)
+            if advance and last == mgr.num_layers:
+                self._advance(meta)
+            return out
+        for i in range(n):
+            self.forward_layer(first_layer + i, q[i], k_new[i], v_new[i], meta, scale, out=out[i],
+                               advance=advance)
         return out
 
     def _prefill(self, layer: int, q: torch.Tensor, meta: StepMetadata, scale: float,

@@ -614,6 +614,67 @@ class DecodeAppendPlan:
         return out
 
 
+class DecodeAppendLayersPlan:
+    """pkv_paged_decode_append_attention_layers for runs of consecutive layers
+    of one decode-only step: one C call per run issues every layer's decode
+    (with the fused append) and merge.  Layer-major inputs: q and out
+    [n, B, Hq, D], k_new and v_new [n, B, Hkv, D] (dense [heads, dims]), the
+    pools the layer slices [n, NB, bs, Hkv, D] of the step's contiguous
+    [L, NB, bs, Hkv, D] caches.  Validated arguments are reused as
+    DecodeAppendPlan reuses them, with the run's pointers and length swapped
+    in."""
+
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None, schedule=None):
+        self._static = (block_tables, context_lens, scale, workspace, err)
+        self.scale = scale
+        self.schedule = schedule
+        self._key = None
+        self._args: list = []
+        self._fn = _lib.load().pkv_paged_decode_append_attention_layers
+
+    @staticmethod
+    def _layer_stride(t: torch.Tensor, name: str) -> int:
+        if t.dim() != 4:
+            raise ValueError(f"pagedkv: `{name}` must be [layers, rows, heads, head_dim]")
+        return t.stride(0)
+
+    def __call__(self, q, k_new, v_new, k_pools, v_pools, out) -> torch.Tensor:
+        n = q.shape[0]
+        if k_new.shape[0] != n or v_new.shape[0] != n or out.shape[0] != n or \
+                k_pools.shape[0] != n or v_pools.shape[0] != n:
+            raise ValueError("pagedkv: q, k_new, v_new, out and the pools must cover the same layers")
+        if n == 0:
+            return out
+        key = (q.dtype, k_new.dtype, v_new.dtype, k_pools.dtype, out.dtype, q.shape[1:], q.stride(),
+               k_new.shape[1:], k_new.stride(), v_new.stride(), k_pools.shape[1:], k_pools.stride(),
+               v_pools.stride(), out.shape[1:], out.stride(), q.get_device(), _raw_stream(q))
+        if key != self._key:
+            if k_new.stride(0) != v_new.stride(0):
+                raise ValueError("pagedkv: k_new and v_new must share one layer stride")
+            if k_pools.stride() != v_pools.stride() or not k_pools[0].is_contiguous():
+                raise ValueError("pagedkv: the K and V pools must be equally strided, layers dense")
+            tables, ctx, scale, ws, err = self._static
+            # the per-layer checks of the single-layer call, on layer 0
+            args, _ = _decode_append_args(q[0], k_new[0], v_new[0], k_pools[0], v_pools[0], tables,
+                                          ctx, scale, ws, out[0], err)
+            (o, o_rs, qp, q_rs, kn, vn, kn_rs, vn_rs, kp, vp, nb, bt, bt_s, mb, cl, B, hq, hkv, d, bs,
+             sc, dt, wsp, wsb, errp, st) = args
+            self._args = [n, o, self._layer_stride(out, "out"), o_rs, qp, self._layer_stride(q, "q"),
+                          q_rs, kn, vn, self._layer_stride(k_new, "k_new"), kn_rs, vn_rs, kp, vp,
+                          k_pools.stride(0) * k_pools.element_size(), nb, bt, bt_s, mb, cl, B, hq,
+                          hkv, d, bs, sc, dt, wsp, wsb, errp, st,
+                          None if self.schedule is None else self.schedule.data_ptr()]
+            self._key = key
+        a = self._args
+        a[0], a[1], a[4], a[7], a[8], a[12], a[13] = (n, out.data_ptr(), q.data_ptr(), k_new.data_ptr(),
+                                                      v_new.data_ptr(), k_pools.data_ptr(),
+                                                      v_pools.data_ptr())
+        rc = self._fn(*a)
+        if rc:
+            _lib.check(rc, "pkv_paged_decode_append_attention_layers")
+        return out
+
+
 class DecodePlan(DecodeAppendPlan):
     """pkv_paged_decode_attention (no append: the step's K/V are already in
     the pools) for the layers of one step, with the same reuse of validated

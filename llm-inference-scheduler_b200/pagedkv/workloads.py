@@ -106,6 +106,40 @@ def sum_over_ranks(value: float, group=None) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(value: float, group=None) -> list[float]:
+    """[value of rank 0, value of rank 1, ...] over the default process group
+    ([value] when torch.distributed is not initialised)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return [float(value)]
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(out, t, group=group)
+    return [float(x.item()) for x in out]
+
+
+def rank_cpus(cpus, local_rank: int, local_world: int) -> list[int]:
+    """This rank's share of the host cores: the sorted core list cut into
+    local_world contiguous, disjoint slices (the last ones one core shorter
+    when the count does not divide), so that the ranks of one node do not
+    contend for the same cores when they enqueue work.  Every rank gets at
+    least one core; with fewer cores than ranks, ranks share them round-robin."""
+    cpus = sorted(int(c) for c in cpus)
+    if not cpus:
+        return []
+    if local_world <= 1:
+        return cpus
+    if len(cpus) < local_world:
+        return [cpus[local_rank % len(cpus)]]
+    base, extra = divmod(len(cpus), local_world)
+    start = local_rank * base + min(local_rank, extra)
+    return cpus[start:start + base + (1 if local_rank < extra else 0)]
+
+
 def config4_layout(seed: int = 4, n_seqs: int = 16, chunk: int = 512, prior_hi: int = 4096,
                    shared: int = 48):
     """Config 4: n_seqs chunks of `chunk` queries over a `shared`-token radix

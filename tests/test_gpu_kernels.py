@@ -440,6 +440,105 @@ def test_forward_layer_mixed_batch(oracle_mod, dt):
     m.check_errors()
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_forward_layers_equals_forward_layer_and_oracle(oracle_mod, dt):
+    """PagedKVCache.forward_layers (one pkv_paged_decode_append_attention_layers
+    call per run of layers) against forward_layer layer by layer on a copy of
+    the same pools: outputs and pools bit-identical; outputs within the
+    product tolerance of the oracle.  Layer-major inputs are strided views of
+    one [L, B, Hq + 2 Hkv, D] buffer, as the end-to-end bench stages them.  A
+    mixed step (not decode-only) takes the per-layer path and still matches."""
+    rng = np.random.default_rng(43)
+    L, nb, tdt = 5, 512, TORCH_DT[dt]
+    ctx = rng.integers(1, 700, size=37)
+    ctx[:3] = [1, 16, 17]
+    pools_k = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
+    pools_v = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
+    managers = []
+    for _ in range(2):
+        m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=tdt)
+        m.k_cache.copy_(dev(pools_k, dt))
+        m.v_cache.copy_(dev(pools_v, dt))
+        kv = PagedKVCache(m)
+        perm = np.random.default_rng(7).permutation(nb)
+        o = 0
+        for s, c in enumerate(ctx):
+            n = (int(c) + 15) // 16
+            kv.add_sequence(s, perm[o:o + n].tolist(), int(c) - 1)
+            o += n
+        managers.append((m, kv))
+    B = len(ctx)
+    qkv = C.to_dtype(rng.standard_normal((L, B, 18, 64), dtype=np.float32), dt)
+    dqkv = dev(qkv, dt)
+    (m1, kv1), (m2, kv2) = managers
+    meta1 = kv1.prepare_step([(s, 1) for s in range(B)])
+    meta2 = kv2.prepare_step([(s, 1) for s in range(B)])
+    out1 = torch.empty((L, B, 14, 64), dtype=tdt, device="cuda")
+    out2 = torch.empty_like(out1)
+    # runs of 2 and 3 layers
+    for a, b in ((0, 2), (2, 5)):
+        kv1.forward_layers(a, dqkv[a:b, :, :14], dqkv[a:b, :, 14:16], dqkv[a:b, :, 16:18], meta1,
+                           0.125, out=out1[a:b])
+    for layer in range(L):
+        kv2.forward_layer(layer, dqkv[layer, :, :14], dqkv[layer, :, 14:16], dqkv[layer, :, 16:18],
+                          meta2, 0.125, out=out2[layer])
+    torch.cuda.synchronize()
+    m1.check_errors()
+    assert torch.equal(out1, out2)
+    assert torch.equal(m1.k_cache, m2.k_cache) and torch.equal(m1.v_cache, m2.v_cache)
+    assert [kv1.seq_len(s) for s in range(B)] == [int(c) for c in ctx]
+    tabs = C.pad_tables([kv1.block_tables[s] for s in range(B)])
+    for layer in (0, L - 1):
+        slots = np.array([kv1._slots(kv1.block_tables[s], int(c) - 1, 1)[0] for s, c in enumerate(ctx)])
+        kp, vp = pools_k[layer].copy(), pools_v[layer].copy()
+        kn_l, vn_l = (np.ascontiguousarray(qkv[layer, :, a:b]) for a, b in ((14, 16), (16, 18)))
+        assert oracle_mod.reshape_and_cache(kp, vp, kn_l, vn_l, slots, dt) == 0
+        ref = oracle_mod.paged_attention(np.ascontiguousarray(qkv[layer, :, :14]), kp, vp, tabs,
+                                         np.arange(B + 1, dtype=np.int32),
+                                         (ctx - 1).astype(np.int32), dt)
+        assert max_abs_diff(host(out1[layer], dt), ref, dt) <= PRODUCT_ATOL[dt]
+        assert np.array_equal(host(m1.k_cache[layer], dt), kp)
+    # a mixed step goes layer by layer and equals forward_layer
+    kv1.add_sequence(B, [m1.allocate() for _ in range(3)], 5)
+    kv2.add_sequence(B, [m2.allocate() for _ in range(3)], 5)
+    seqs = [(s, 1) for s in range(B)] + [(B, 20)]
+    meta1, meta2 = kv1.prepare_step(seqs), kv2.prepare_step(seqs)
+    T = meta1.n_tokens
+    x = dev(C.to_dtype(rng.standard_normal((2, T, 18, 64), dtype=np.float32), dt), dt)
+    o1 = kv1.forward_layers(0, x[:, :, :14], x[:, :, 14:16], x[:, :, 16:18], meta1, 0.125)
+    o2 = torch.stack([kv2.forward_layer(layer, x[layer, :, :14], x[layer, :, 14:16],
+                                        x[layer, :, 16:18], meta2, 0.125) for layer in range(2)])
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+
+
+def test_decode_layers_abi_rejects_overlapping_pools():
+    """pkv_paged_decode_append_attention_layers refuses a pool layer stride
+    smaller than one layer's pool (the layers would overlap) before any launch."""
+    from pagedkv import _lib
+
+    nb, B, L = 8, 2, 2
+    kc = torch.zeros((L, nb, 16, 2, 64), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q = torch.zeros((L, B, 14, 64), dtype=torch.float16, device="cuda")
+    kn = torch.zeros((L, B, 2, 64), dtype=torch.float16, device="cuda")
+    out = torch.full_like(q, 7.0)
+    tabs = torch.zeros((B, 1), dtype=torch.int32, device="cuda")
+    ctx = torch.ones(B, dtype=torch.int32, device="cuda")
+    ws = ops.new_decode_workspace(B, 14, 64, "cuda")
+    lib = _lib.load()
+    pool_bytes = nb * 16 * 2 * 64 * 2
+    for stride, want in ((pool_bytes - 16, _lib.ERR_BAD_SHAPE), (pool_bytes + 8, _lib.ERR_MISALIGNED)):
+        rc = lib.pkv_paged_decode_append_attention_layers(
+            L, out.data_ptr(), q.stride(0), 14 * 64, q.data_ptr(), q.stride(0), 14 * 64,
+            kn.data_ptr(), kn.data_ptr(), kn.stride(0), 128, 128, kc.data_ptr(), vc.data_ptr(), stride,
+            nb, tabs.data_ptr(), 1, 1, ctx.data_ptr(), B, 14, 2, 64, 16, 0.125, _lib.F16,
+            ws.data_ptr(), ws.numel(), None, torch.cuda.current_stream().cuda_stream, None)
+        assert rc == want, (stride, rc)
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all()) and not kc.any()
+
+
 # ---------------------------------------------------------------- fused RoPE + append
 
 @pytest.mark.parametrize("dt", DTS)

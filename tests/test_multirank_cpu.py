@@ -4,7 +4,10 @@ The checks:
 * the sequences are dealt to the ranks disjointly and completely (weak scaling:
   256 per rank; strong: 256 in total);
 * each rank's pool and scattered block tables are private;
-* the max-over-ranks timing and the sum-over-ranks bytes are right.
+* the max-over-ranks timing, the sum-over-ranks bytes and the per-rank lists
+  (gather over ranks) are right;
+* each rank's share of the host cores (the bench pins a rank to it) is
+  disjoint from the others' and together they cover the node's cores.
 
 No collective touches the data path, so the gloo process group carries only
 these scalars.
@@ -50,8 +53,9 @@ def _rank_main(rank, world, port, out_dir, strong):
         a = kv.step_arrays([(i, 1) for i in range(len(ctx))])
         t = W.max_over_ranks(1.0 + rank)               # rank-dependent "time"
         b = W.sum_over_ranks(float(W.decode_bytes(ctx)))
+        g = W.gather_over_ranks(10.0 * rank + 0.5)
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), ctx=ctx, idx=idx, slots=a["slots"],
-                 tmax=t, bsum=b, mine=float(W.decode_bytes(ctx)))
+                 tmax=t, bsum=b, mine=float(W.decode_bytes(ctx)), gathered=np.array(g))
     finally:
         dist.destroy_process_group()
 
@@ -76,5 +80,26 @@ def test_two_gloo_ranks_shard_by_sequence(tmp_path, strong):
         assert float(x["tmax"]) == world                         # max over ranks
         assert float(x["bsum"]) == sum(float(y["mine"]) for y in r)
         assert len(set(x["slots"].tolist())) == len(x["slots"])  # private slots per rank
+        assert x["gathered"].tolist() == [10.0 * k + 0.5 for k in range(world)]
     if not strong:
         assert np.array_equal(r[0]["ctx"][:1], all_ctx[:1])
+
+
+@pytest.mark.parametrize("n_cpus,world", [(32, 8), (30, 8), (7, 2), (3, 4), (1, 1), (16, 1)])
+def test_rank_cpu_shares_are_disjoint_and_cover_the_node(n_cpus, world):
+    import sys
+
+    sys.path.insert(0, PKG_ROOT)
+    from pagedkv import workloads as W
+
+    cpus = list(range(100, 100 + n_cpus))[::-1]   # any order, any ids
+    shares = [W.rank_cpus(cpus, r, world) for r in range(world)]
+    assert all(shares), "every rank gets at least one core"
+    if n_cpus >= world:
+        flat = [c for s in shares for c in s]
+        assert sorted(flat) == sorted(cpus)                   # cover, no overlap
+        assert max(map(len, shares)) - min(map(len, shares)) <= 1
+        for s in shares:                                      # contiguous slices
+            assert s == list(range(s[0], s[0] + len(s)))
+    else:
+        assert all(len(s) == 1 for s in shares)
