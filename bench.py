@@ -747,7 +747,7 @@ def run_e2e(args):
 
     from pagedkv import BlockManager
     from pagedkv.model import PagedQwen2Model, Qwen2Config, random_weights
-    from pagedkv.scheduler import Request, Scheduler
+    from pagedkv.engine import Engine, Seq
 
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     rank = int(os.environ.get("RANK", "0"))
@@ -765,59 +765,55 @@ def run_e2e(args):
     out_len = 128
     num_blocks = 24000  # 4.7 GB of fp16 KV for 24 layers
     mgr = BlockManager(num_blocks, 16, cfg.num_hidden_layers, 2, 64, device="cuda", dtype=torch.float16)
-    sched = Scheduler(model, mgr, max_num_seqs=args.max_num_seqs,
-                      max_batched_tokens=args.max_batched_tokens, enable_prefix_cache=True,
-                      eos_ids=set(), cuda_graphs=not args.no_cuda_graphs)
+    eng = Engine(model, mgr, max_seqs=args.max_num_seqs, token_budget=args.max_batched_tokens,
+                 prefix_reuse=True, eos_ids=(), cuda_graphs=not args.no_cuda_graphs)
     t_cap = time.perf_counter()
-    if sched.cuda_graphs:  # every padded step shape, before the timed run
-        sched.step_graphs().capture_all()
+    if eng.run_step.cuda_graphs:  # every padded step shape, before the timed run
+        eng.run_step.step_graphs().capture_all()
     t_cap = time.perf_counter() - t_cap
 
     def drive(n_conv, arr):
         pending = list(range(n_conv))
         reqs, turn2 = {}, {}
         t0 = time.perf_counter()
-        while pending or sched.has_work:
+        while pending or eng.busy:
             now = time.perf_counter() - t0
             while pending and arr[pending[0]] <= now:
                 i = pending.pop(0)
-                reqs[i] = Request(i, list(prompts[i]), max_new_tokens=out_len)
-                sched.add_request(reqs[i])
-            if not sched.has_work:
+                reqs[i] = eng.submit(Seq(i, list(prompts[i]), limit=out_len))
+            if not eng.busy:
                 time.sleep(min(1e-3, max(0.0, arr[pending[0]] - now)))
                 continue
-            sched.step()
+            eng.step()
             for i, r in list(reqs.items()):
-                if r.finish_reason and i not in turn2:
-                    turn2[i] = Request(n_conv + i, r.prompt_ids + r.output_ids + extra[i],
-                                       max_new_tokens=out_len)
-                    sched.add_request(turn2[i])
+                if r.finish and i not in turn2:
+                    turn2[i] = eng.submit(Seq(n_conv + i, r.tokens + extra[i], limit=out_len))
         torch.cuda.synchronize()
         return time.perf_counter() - t0, list(reqs.values()) + list(turn2.values())
 
     drive(min(4, n), np.zeros(n))  # warm-up: rope tables, TMA descriptors, allocator
-    sched.radix.evict(num_blocks)   # forget the warm-up prefixes
-    for k in list(sched.metrics):
-        sched.metrics[k] = 0
-    replays0 = sched.graphs.replays if sched.graphs is not None else 0
+    eng.index.clear()   # forget the warm-up prefixes
+    for k in list(eng.counts):
+        eng.counts[k] = 0
+    replays0 = eng.graphs.replays if eng.graphs is not None else 0
     wall, done = drive(n, arrivals)
-    replays = (sched.graphs.replays if sched.graphs is not None else 0) - replays0
+    replays = (eng.graphs.replays if eng.graphs is not None else 0) - replays0
     mgr.check_errors()
-    steps_timed = sched.metrics["steps"]
-    sched_metrics = dict(sched.metrics)
+    steps_timed = eng.counts["steps"]
+    sched_metrics = dict(eng.counts)
     # attention share, in a separate short run (events around the attention
     # part of every layer would perturb the timed run): fused RoPE + append +
     # attention launches over the whole model step, GPU time
-    sched.radix.evict(num_blocks)
+    eng.index.clear()
     model.timing = []
     drive(min(16, n), np.zeros(n))
     torch.cuda.synchronize()
     step_ms = sum(a.elapsed_time(b) for (a, b), _ in model.timing)
     attn_ms = sum(a.elapsed_time(b) for _, layers in model.timing for a, b in layers)
     model.timing = None
-    gen = sum(len(r.output_ids) for r in done)
-    ttft = [r.first_token_at - r.arrived_at for r in done]
-    itl = [(r.finished_at - r.first_token_at) / max(1, len(r.output_ids) - 1) for r in done]
+    gen = sum(len(r.generated) for r in done)
+    ttft = [r.t_first - r.t_arrive for r in done]
+    itl = [(r.t_done - r.t_first) / max(1, len(r.generated) - 1) for r in done]
     pct = lambda xs, q: round(1e3 * float(np.percentile(xs, q)), 2)  # noqa: E731
     line = {
         "metric": "end-to-end continuous-batching decode tok/s (config 5)",
@@ -829,14 +825,14 @@ def run_e2e(args):
                                "tokens with a shared 48-token prefix, 128 greedy output tokens/turn",
                    "conversations": n, "rate_per_s": args.rate, "max_num_seqs": args.max_num_seqs,
                    "max_batched_tokens": args.max_batched_tokens, "num_blocks": num_blocks,
-                   "cuda_graphs": sched.cuda_graphs},
+                   "cuda_graphs": eng.run_step.cuda_graphs},
         "cuda_graphs": {"steps_replayed": replays, "steps": steps_timed,
-                        "shapes": len(sched.graphs.graphs) if sched.graphs is not None else 0,
+                        "shapes": len(eng.graphs.graphs) if eng.graphs is not None else 0,
                         "capture_s": round(t_cap, 3)},
         "generated_tokens": gen, "wall_s": round(wall, 3),
         "ttft_ms": {"p50": pct(ttft, 50), "p99": pct(ttft, 99)},
         "itl_ms": {"p50": pct(itl, 50), "p99": pct(itl, 99)},
-        "scheduler": sched_metrics,
+        "engine": sched_metrics,
         "attention_share": {"value": round(attn_ms / step_ms, 4) if step_ms else None,
                             "what": "GPU time of fused RoPE+append and the attention launches / GPU time "
                                     "of the model step, CUDA events, separate run of 16 conversations"},

@@ -449,9 +449,10 @@ def test_forward_layers_equals_forward_layer_and_oracle(oracle_mod, dt):
     one [L, B, Hq + 2 Hkv, D] buffer, as the end-to-end bench stages them.  A
     mixed step (not decode-only) takes the per-layer path and still matches."""
     rng = np.random.default_rng(43)
-    L, nb, tdt = 5, 512, TORCH_DT[dt]
+    L, nb, tdt = 5, 1024, TORCH_DT[dt]
     ctx = rng.integers(1, 700, size=37)
     ctx[:3] = [1, 16, 17]
+    assert int(((ctx + 15) // 16).sum()) <= nb - 8  # the last 8 blocks stay for the mixed step
     pools_k = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
     pools_v = C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt)
     managers = []
@@ -460,7 +461,7 @@ def test_forward_layers_equals_forward_layer_and_oracle(oracle_mod, dt):
         m.k_cache.copy_(dev(pools_k, dt))
         m.v_cache.copy_(dev(pools_v, dt))
         kv = PagedKVCache(m)
-        perm = np.random.default_rng(7).permutation(nb)
+        perm = np.random.default_rng(7).permutation(nb - 8)
         o = 0
         for s, c in enumerate(ctx):
             n = (int(c) + 15) // 16
@@ -499,9 +500,10 @@ def test_forward_layers_equals_forward_layer_and_oracle(oracle_mod, dt):
         assert max_abs_diff(host(out1[layer], dt), ref, dt) <= PRODUCT_ATOL[dt]
         assert np.array_equal(host(m1.k_cache[layer], dt), kp)
     # a mixed step goes layer by layer and equals forward_layer
-    kv1.add_sequence(B, [m1.allocate() for _ in range(3)], 5)
-    kv2.add_sequence(B, [m2.allocate() for _ in range(3)], 5)
-    seqs = [(s, 1) for s in range(B)] + [(B, 20)]
+    kv1.add_sequence(B, [nb - 8, nb - 7, nb - 6], 5)
+    kv2.add_sequence(B, [nb - 8, nb - 7, nb - 6], 5)
+    # decode sequences whose last block has room for one more token
+    seqs = [(s, 1) for s in range(B) if ctx[s] % 16] + [(B, 20)]
     meta1, meta2 = kv1.prepare_step(seqs), kv2.prepare_step(seqs)
     T = meta1.n_tokens
     x = dev(C.to_dtype(rng.standard_normal((2, T, 18, 64), dtype=np.float32), dt), dt)
