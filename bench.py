@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--strong", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50, help="e2e: steps per timing window")
     ap.add_argument("--e2e-windows", type=int, default=5, help="e2e: timing windows (median reported)")
-    ap.add_argument("--e2e-chunks", default="2,4,6,6,4,2",
+    ap.add_argument("--e2e-chunks", default="1,2,4,5,5,4,2,1",
                     help="e2e: layers per chunk (comma list summing to --layers); each chunk's copies "
                          "overlap the other chunks' compute")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
@@ -407,24 +407,34 @@ def run_ours(args):
 
     # Each step is self-contained: its inputs go host -> device in chunks of
     # layers on a copy stream, each chunk's layers run as soon as it has
-    # landed (one PagedKVCache.forward_layers call per chunk), and each
-    # chunk's outputs go back on a second copy stream; the step ends when its
-    # last output is on the host.  The next step's copies start after this
-    # step's compute (no prefetch across steps).  Small first and last chunks
-    # shorten the pipeline's fill (first copy in) and drain (last copy out).
+    # landed (one pkv_paged_decode_append_attention_layers call per chunk),
+    # and each chunk's outputs go back on a second copy stream; the step ends
+    # when its last output is on the host.  The next step's copies start after
+    # this step's compute (no prefetch across steps).  Small first and last
+    # chunks shorten the pipeline's fill (first copy in) and drain (last copy
+    # out).  Headline: pagedkv.graphs.DecodeStepGraph, which holds all of that
+    # in one CUDA graph (per step: the host metadata, one copy, one replay).
+    # Beside it, the same pipeline issued from Python
+    # (PagedKVCache.prepare_step + forward_layers per chunk).
+    from pagedkv.graphs import DecodeStepGraph
+
     sizes = [int(x) for x in args.e2e_chunks.split(",")]
     if sum(sizes) != L:
         sizes = [L]
-    bounds = [sum(sizes[:i]) for i in range(len(sizes) + 1)]
-    n_chunks = len(sizes)
-    chunks = [(bounds[c], bounds[c + 1]) for c in range(n_chunks)]
-    views = [(dqkv[a:b, :, :14], dqkv[a:b, :, 14:16], dqkv[a:b, :, 16:18], out[a:b]) for a, b in chunks]
-    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
-    ev_out = [torch.cuda.Event() for _ in range(n_chunks)]
     seqs_all = [(i, 1) for i in range(B)]
+    runner = DecodeStepGraph(kv, hqkv, hout, scale, chunks=sizes, max_blocks_per_seq=int(nblk.max()))
 
     def e2e_step():
+        runner.run(seqs_all)
+
+    bounds = [sum(sizes[:i]) for i in range(len(sizes) + 1)]
+    chunks = [(bounds[c], bounds[c + 1]) for c in range(len(sizes))]
+    views = [(dqkv[a:b, :, :14], dqkv[a:b, :, 14:16], dqkv[a:b, :, 16:18], out[a:b]) for a, b in chunks]
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in chunks]
+    ev_out = [torch.cuda.Event() for _ in chunks]
+
+    def e2e_step_eager():
         cur = torch.cuda.current_stream(dev)
         meta = kv.prepare_step(seqs_all)
         h2d_s.wait_stream(cur)
@@ -442,35 +452,43 @@ def run_ours(args):
                 hout[a:b].copy_(out[a:b], non_blocking=True)
         cur.wait_stream(d2h_s)
 
-    for _ in range(10):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    # host hiccups on a shared machine move the mean of a host-driven step:
-    # time it in windows of steps back to back and report the median window
-    # (all windows in the line)
-    n_win = max(1, args.e2e_windows)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_win + 1)]
-    host_s = []
-    evs[0].record()
-    for w in range(n_win):
-        h0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        host_s.append(time.perf_counter() - h0)
-        evs[w + 1].record()
-    torch.cuda.synchronize()
-    barrier()
+    def time_windows(fn):
+        """Host-driven steps move with host hiccups on a shared machine: time
+        them in windows of steps back to back (device events), median window;
+        also the host's own time per step."""
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        n_win = max(1, args.e2e_windows)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_win + 1)]
+        host_s = []
+        evs[0].record()
+        for w in range(n_win):
+            h0 = time.perf_counter()
+            for _ in range(args.e2e_steps):
+                fn()
+            host_s.append(time.perf_counter() - h0)
+            evs[w + 1].record()
+        torch.cuda.synchronize()
+        barrier()
+        win = [evs[w].elapsed_time(evs[w + 1]) / args.e2e_steps for w in range(n_win)]
+        return win, 1e3 * statistics.median(host_s) / args.e2e_steps
+
+    win_ms, host_ms_local = time_windows(e2e_step)
+    eager_win, eager_host = time_windows(e2e_step_eager)
     ops.check_flags(R.err, "bench e2e")
-    win_ms = [evs[w].elapsed_time(evs[w + 1]) / args.e2e_steps for w in range(n_win)]
+    n_win = len(win_ms)
     e2e_ms_local = statistics.median(win_ms)
     e2e_ms = W.max_over_ranks(e2e_ms_local)
-    host_ms_local = 1e3 * statistics.median(host_s) / args.e2e_steps
+    eager_ms = W.max_over_ranks(statistics.median(eager_win))
     per_rank["e2e_ms_local"] = [round(x, 5) for x in W.gather_over_ranks(e2e_ms_local)]
     per_rank["e2e_host_enqueue_ms_local"] = [round(x, 5) for x in W.gather_over_ranks(host_ms_local)]
-    h2d = hqkv.numel() * 2 + B * (int(nblk.max()) + 2) * 4 + B * 8
+    per_rank["e2e_eager_host_enqueue_ms_local"] = [round(x, 5) for x in W.gather_over_ranks(eager_host)]
+    meta_bytes = 4 * (B * runner.W + 2 * B + 1) + 8 * B
+    h2d = hqkv.numel() * 2 + meta_bytes
     d2h = hout.numel() * 2
-    del kv, dqkv, hqkv, hout
+    del kv, dqkv, hqkv, hout, runner
 
     # ---- the same job under strong scaling (BASELINE config 3's wording:
     # 256 sequences in total, dealt over the N GPUs), same process
@@ -551,13 +569,19 @@ def run_ours(args):
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4),
-                "api": "PagedKVCache.prepare_step + forward_layers (one C call per chunk of layers)",
+                "api": "pagedkv.graphs.DecodeStepGraph.run: PagedKVCache.step_arrays into pinned staging, "
+                       "one metadata copy, one CUDA-graph replay (per-chunk H2D of q|k|v, the decode "
+                       "schedule, one pkv_paged_decode_append_attention_layers call per chunk, per-chunk D2H)",
                 "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back, max over ranks",
                 "windows_ms_per_step": [round(x, 4) for x in win_ms],
                 "copies": f"pinned host buffers; per step: metadata, then q|k|v of 24 layers H2D in "
                           f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
                           "on a second copy stream, overlapped with the step's own compute; the step ends "
                           "when its outputs are on the host",
+                "eager": {"ms_per_step": round(eager_ms, 4),
+                          "value": round(total_bytes / (eager_ms * 1e-3) / 1e9, 2),
+                          "api": "the same pipeline issued from Python: PagedKVCache.prepare_step + "
+                                 "forward_layers per chunk (host-bound)"},
                 "host_cpus_per_rank": len(cpus)},
         "strong": strong,
         "gpu_launches": (2 * L + 1) * args.steps,  # per timed step: schedule + (decode, merge) x 24

@@ -390,3 +390,202 @@ class StepGraphs:
 
 
 DecodeGraphs = StepGraphs  # decode-only use: StepGraphs(model, kv, max_batch)
+
+
+class DecodeStepGraph:
+    """A decode-only step over every layer of a cache's pools, fed from and
+    returned to caller-owned pinned host buffers, captured as one CUDA graph.
+
+    For hosts that hold one step's q / new K / new V of every layer together,
+    as layer-major rows host_qkv [L, R, Hq + 2 Hkv, D] (pinned), and want every
+    layer's attention output back in host_out [L, R, Hq, D] (pinned).  Issued
+    from Python one by one, such a step is about 100 launches, copies and
+    event operations, which cost more host time than the GPU spends on them.
+    Here the host builds the step's metadata (PagedKVCache.step_arrays into a
+    pinned staging buffer, padded to R rows), copies it with one H2D copy and
+    launches one graph holding:
+    * the decode schedule build;
+    * per chunk of layers, on a copy stream, the H2D copy of the chunk's rows;
+    * per chunk, once its rows have landed, one
+      pkv_paged_decode_append_attention_layers call (the fused append + decode
+      and the merge of each of its layers);
+    * per chunk, on a second copy stream, the D2H copy of the chunk's outputs.
+    Small first and last chunks shorten the pipeline's fill and drain.
+
+    A step of B <= R sequences (one new token each, host rows 0 .. B-1) pads
+    rows B .. R-1: context length 0, slot -1, so they read and write no KV
+    and their outputs are zeros.  The block-table width W is fixed at capture
+    and doubled (with a new capture) when a step needs more.  With
+    advance=True the sequences' lengths advance as after forward_layer's last
+    layer (block_manager.py:133-134 semantics).  Results equal
+    PagedKVCache.forward_layers over the same rows bit for bit.
+    Reference: the per-layer loop of Qwen2Model.forward (qwen2.py:159-166)
+    over PagedKVCache.append_and_fetch + _attention, for decode steps.
+    """
+
+    def __init__(self, kv_cache: PagedKVCache, host_qkv: torch.Tensor, host_out: torch.Tensor,
+                 scale: float, chunks: tuple[int, ...] | None = None, max_blocks_per_seq: int = 64):
+        mgr = kv_cache.mgr
+        if mgr.fp8 or mgr.device is None or mgr.device.type != "cuda":
+            raise RuntimeError("pagedkv: DecodeStepGraph serves 16-bit pools on a CUDA device")
+        L, R, width, D = host_qkv.shape
+        hkv = mgr.num_kv_heads
+        hq = width - 2 * hkv
+        if L != mgr.num_layers or D != mgr.head_dim or hq <= 0 or host_qkv.dtype != mgr.dtype:
+            raise ValueError("pagedkv: host_qkv must be [num_layers, rows, Hq + 2 Hkv, head_dim] "
+                             "in the pool dtype")
+        if tuple(host_out.shape) != (L, R, hq, D) or host_out.dtype != mgr.dtype:
+            raise ValueError("pagedkv: host_out must be [num_layers, rows, Hq, head_dim]")
+        if not (host_qkv.is_pinned() and host_out.is_pinned() and host_qkv.is_contiguous()
+                and host_out.is_contiguous()):
+            raise ValueError("pagedkv: host_qkv / host_out must be contiguous pinned host tensors")
+        chunks = tuple(chunks or _default_chunks(L))
+        if sum(chunks) != L or min(chunks) <= 0:
+            raise ValueError(f"pagedkv: chunks {chunks} must be positive and sum to {L}")
+        self.kv, self.scale = kv_cache, float(scale)
+        self.host_qkv, self.host_out = host_qkv, host_out
+        self.R, self.hq, self.L = R, hq, L
+        self.bounds = [(sum(chunks[:i]), sum(chunks[:i + 1])) for i in range(len(chunks))]
+        self.W = max(1, int(max_blocks_per_seq))
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.replays = 0
+        dev = mgr.device
+        self.dev_qkv = torch.empty((L, R, width, D), dtype=mgr.dtype, device=dev)
+        self.dev_out = torch.empty((L, R, hq, D), dtype=mgr.dtype, device=dev)
+        self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        self.workspace = kv_cache.decode_workspace(R, hq, D)
+        self._alloc()
+
+    def _layout(self) -> dict:
+        R, W = self.R, self.W
+        n_ints = R * W + 2 * R + 1
+        o64 = _align16(4 * n_ints)
+        return dict(n_ints=n_ints, slots=o64, end=o64 + 8 * R)
+
+    def _alloc(self) -> None:
+        dev = self.kv.mgr.device
+        end = self._layout()["end"]
+        self.meta_dev = torch.zeros(end, dtype=torch.uint8, device=dev)
+        self.stage = [[torch.empty(end, dtype=torch.uint8).pin_memory(), None] for _ in range(2)]
+        self._stage_next = 0
+        self.schedule = ops.new_decode_schedule(self.R, self.W, dev)
+        self.graph = None
+
+    def _meta(self) -> StepMetadata:
+        R, W, lay = self.R, self.W, self._layout()
+        ints = self.meta_dev[: 4 * lay["n_ints"]].view(torch.int32)
+        return StepMetadata(seq_ids=list(range(R)), num_new=[1] * R, num_prior=[0] * R,
+                            n_tokens=R, n_decode=R, max_query_len=0,
+                            slot_mapping=self.meta_dev[lay["slots"]: lay["end"]].view(torch.int64),
+                            block_tables=ints[: R * W].view(R, W), context_lens=ints[R * W: R * W + R],
+                            query_start_loc=ints[R * W + 2 * R:],
+                            num_prior_dev=ints[R * W + R: R * W + 2 * R])
+
+    def _step(self) -> None:
+        """What the graph holds (on the current stream, forking to the copy streams)."""
+        kv, mgr = self.kv, self.kv.mgr
+        meta = self._meta()
+        cur = torch.cuda.current_stream(mgr.device)
+        hkv, q = mgr.num_kv_heads, self.dev_qkv
+        # the input copies first: they depend on nothing in the step and run
+        # beside the schedule build
+        self.h2d.wait_stream(cur)
+        ev_in = [torch.cuda.Event() for _ in self.bounds]
+        with torch.cuda.stream(self.h2d):
+            for (a, b), ev in zip(self.bounds, ev_in):
+                q[a:b].copy_(self.host_qkv[a:b], non_blocking=True)
+                ev.record(self.h2d)
+        meta.decode_schedule = ops.build_decode_schedule(
+            self.schedule, meta.block_tables, meta.context_lens, mgr.num_blocks, self.hq,
+            mgr.num_kv_heads, mgr.head_dim, mgr.dtype, err=mgr.err)
+        meta.layers_plan = ops.DecodeAppendLayersPlan(meta.block_tables, meta.context_lens, self.scale,
+                                                      self.workspace, mgr.err,
+                                                      schedule=meta.decode_schedule)
+        for (a, b), ev in zip(self.bounds, ev_in):
+            cur.wait_event(ev)
+            kv.forward_layers(a, q[a:b, :, :self.hq], q[a:b, :, self.hq:self.hq + hkv],
+                              q[a:b, :, self.hq + hkv:], meta, self.scale, out=self.dev_out[a:b],
+                              advance=False)
+            done = torch.cuda.Event()
+            done.record(cur)
+            self.d2h.wait_event(done)
+            with torch.cuda.stream(self.d2h):
+                self.host_out[a:b].copy_(self.dev_out[a:b], non_blocking=True)
+        cur.wait_stream(self.d2h)
+
+    def capture(self) -> None:
+        """Capture the step.  Runs it once uncaptured first, on all-padding
+        metadata (no KV read or written), so every library handle, kernel
+        attribute and argument cache exists before the capture."""
+        mgr = self.kv.mgr
+        mgr.flush_copies()
+        lay = self._layout()
+        self.meta_dev.zero_()
+        self.meta_dev[lay["slots"]: lay["end"]].view(torch.int64).fill_(-1)
+        cur = torch.cuda.current_stream(mgr.device)
+        side = torch.cuda.Stream(mgr.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            self._step()
+        cur.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step()
+        self.graph = g
+
+    def run(self, seqs: list[tuple[int, int]], advance: bool = False) -> None:
+        """One decode step for seqs = [(seq_id, 1)] * B (B <= R, in the host
+        rows' order): host_out receives every layer's output when the
+        current stream reaches the end of the step."""
+        kv, bs = self.kv, self.kv.mgr.block_size
+        B = len(seqs)
+        if B > self.R or any(n != 1 for _, n in seqs):
+            raise ValueError(f"pagedkv: DecodeStepGraph serves up to {self.R} one-token sequences")
+        need = max(((kv._len[s] + 1 + bs - 1) // bs for s, _ in seqs), default=1)
+        if need > self.W:
+            while self.W < need:
+                self.W *= 2
+            self._alloc()
+        if self.graph is None:
+            self.capture()
+        kv.mgr.flush_copies()
+        i = self._stage_next = (self._stage_next + 1) % len(self.stage)
+        host, ev = self.stage[i]
+        if ev is not None:
+            ev.synchronize()
+        hnp = host.numpy()
+        lay = self._layout()
+
+        def into(n_ints: int, n_slots: int):
+            return (hnp[: 4 * n_ints].view(np.int32),
+                    hnp[lay["slots"]: lay["slots"] + 8 * n_slots].view(np.int64))
+
+        a = kv.step_arrays(seqs, out=into, width=self.W, pad_to=self.R)
+        cur = torch.cuda.current_stream(kv.mgr.device)
+        self.meta_dev.copy_(host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.stage[i][1] = ev
+        self.graph.replay()
+        self.replays += 1
+        if advance:
+            for s_id, p in zip(a["seq_ids"], a["num_prior"]):
+                kv._len[s_id] = p + 1
+
+
+def _default_chunks(n_layers: int) -> list[int]:
+    """Chunks of layers for the copy pipeline (24 layers: 1, 2, 4, 5, 5, 4, 2,
+    1).  Small first and last chunks shorten the fill (first copy in) and the
+    drain (last copy out).  Every chunk boundary costs the first decode of the
+    chunk its overlap with the kernel before it (it waits on a copy event), so
+    finer chunks that would track the host-to-device rate more closely (1, 1,
+    2, 3, 4, 5, 5, 2, 1) measured slower: 0.826 against 0.810 ms per step."""
+    head, tail = [1, 2, 4], [4, 2, 1]
+    mid = n_layers - sum(head) - sum(tail)
+    if mid < 0:
+        return [n_layers]
+    out = list(head)
+    while mid > 0:
+        out.append(min(5, mid))
+        mid -= out[-1]
+    return out + tail

@@ -146,3 +146,63 @@ def test_graph_mixed_step_matches_eager(model, kv_dtype):
              [(s, 1) for s in range(15)]]
     runner = _compare(model, kv_dtype, lens, steps, seed=12)
     assert set(runner.graphs) == {(16, 192), (16, 0)}
+
+
+# ---------------------------------------------------------------- DecodeStepGraph
+
+def _decode_state(dt, ctx, nb, seed):
+    """Two identical caches of one-layer-per-pool random K/V and scattered tables."""
+    from pagedkv.graphs import DecodeStepGraph  # noqa: F401  (import check)
+
+    L = 5
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kp = torch.randn((L, nb, 16, 2, 64), generator=g, device="cuda").to(dt)
+    vp = torch.randn((L, nb, 16, 2, 64), generator=g, device="cuda").to(dt)
+    perm = np.random.default_rng(seed).permutation(nb)
+    out = []
+    for _ in range(2):
+        m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=dt)
+        m.k_cache.copy_(kp)
+        m.v_cache.copy_(vp)
+        kv = PagedKVCache(m)
+        o = 0
+        for s, c in enumerate(ctx):
+            n = (int(c) + 16) // 16  # room for the step's token and one more
+            kv.add_sequence(s, perm[o:o + n].tolist(), int(c) - 1)
+            o += n
+        out.append((m, kv))
+    assert o <= nb
+    return out
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_decode_step_graph_equals_forward_layers(dt):
+    """DecodeStepGraph.run (host rows in, host outputs back, one graph replay)
+    against forward_layers on a copy of the same cache: outputs and pools
+    bit-identical, padding rows zero, lengths advanced, and a step that needs
+    a wider table recaptures."""
+    from pagedkv.graphs import DecodeStepGraph
+
+    rng = np.random.default_rng(5)
+    ctx = rng.integers(1, 300, size=21)
+    ctx[:2] = [16, 17]
+    (m1, kv1), (m2, kv2) = _decode_state(dt, ctx, 1024, 9)
+    L, R, B = 5, 24, len(ctx)
+    hqkv = torch.randn((L, R, 18, 64), dtype=torch.float32).to(dt).pin_memory()
+    hout = torch.full((L, R, 14, 64), 7.0, dtype=dt).pin_memory()
+    runner = DecodeStepGraph(kv1, hqkv, hout, 0.125, chunks=(1, 2, 2), max_blocks_per_seq=4)
+    seqs = [(s, 1) for s in range(B)]
+    for step in range(2):
+        runner.run(seqs, advance=True)
+        torch.cuda.synchronize()
+        meta = kv2.prepare_step(seqs)
+        d = hqkv.cuda()
+        ref = kv2.forward_layers(0, d[:, :B, :14], d[:, :B, 14:16], d[:, :B, 16:18], meta, 0.125)
+        torch.cuda.synchronize()
+        m1.check_errors()
+        assert torch.equal(hout[:, :B], ref.cpu()), step
+        assert not hout[:, B:].float().abs().sum()  # padding rows: no keys, zero output
+        assert torch.equal(m1.k_cache, m2.k_cache) and torch.equal(m1.v_cache, m2.v_cache)
+        assert [kv1.seq_len(s) for s in range(B)] == [kv2.seq_len(s) for s in range(B)]
+        assert [kv1.seq_len(s) for s in range(B)] == [int(c) + step for c in ctx]
+    assert runner.replays == 2 and runner.W >= 32  # 300-token contexts outgrew 4 blocks
