@@ -56,6 +56,9 @@ def parse():
                     help="migrate: blocks per copy launch (x 24 layers, K and V)")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="prefill: fp8 e4m3 pools (quantising append, tensor-core fp8 prefill)")
+    ap.add_argument("--fp8-prefill", choices=("scratch", "in-kernel"), default="scratch",
+                    help="prefill --kv-fp8: 16-bit scratch pass + tcgen05 kernel, or the tcgen05 "
+                         "kernel converting e4m3 tiles itself (no scratch)")
     ap.add_argument("--append-tokens", type=int, nargs="+", default=[8192, 65536],
                     help="cache_ops: tokens appended per reshape_and_cache launch")
     ap.add_argument("--copy-pairs", type=int, default=4096, help="cache_ops: (src, dst) block pairs")
@@ -669,8 +672,9 @@ def run_prefill(args):
     if fp8:
         # quantising append, then the tensor-core fp8 prefill: the pass that
         # writes the visible blocks into the 16-bit scratch is timed with it
-        scratch = torch.empty(ops.prefill_fp8_scratch_bytes(B, tabs.shape[1], 2, 64),
-                              dtype=torch.uint8, device=dev)
+        scratch = (torch.empty(ops.prefill_fp8_scratch_bytes(B, tabs.shape[1], 2, 64),
+                               dtype=torch.uint8, device=dev)
+                   if args.fp8_prefill == "scratch" else None)  # None: the scratch-free entry
         appends = [ops.bind_reshape_and_cache_fp8(kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l],
                                                   mgr.k_scale[l], mgr.v_scale[l], slots, err)
                    for l in range(L)]
@@ -748,13 +752,16 @@ def run_prefill(args):
         "data": "synthetic (seeded normal Q/K/V)",
         "config": {"workload": "config4: 16 seqs x 512-token chunk over 48-token shared prefix + "
                                "private prior U[0,4096], 24 layers x (append + prefill), 14q/2kv, d64",
-                   "sum_prior": int(prior.sum()), "flops_per_layer": flops, "layers": L},
-        "roofline": {"kernel": "paged_prefill_tc_kernel<half>" + (" + fp8 scratch pass" if fp8 else ""),
+                   "sum_prior": int(prior.sum()), "flops_per_layer": flops, "layers": L,
+                   **({"fp8_prefill": args.fp8_prefill} if fp8 else {})},
+        "roofline": {"kernel": "paged_prefill_tc_kernel<half>" + (
+                         (" + fp8 scratch pass" if args.fp8_prefill == "scratch"
+                          else " (fp8 tiles converted in kernel)") if fp8 else ""),
                      "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": kind,
                      "avg_launch_ms": round(ker_ms, 5)},
-        "gpu_launches": (3 if fp8 else 2) * L * args.steps,
+        "gpu_launches": (3 if fp8 and args.fp8_prefill == "scratch" else 2) * L * args.steps,
         "clocks": sampler.summary(t0, t1) if sampler else None,
     }
     print(json.dumps(line), flush=True)

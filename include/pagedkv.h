@@ -131,6 +131,32 @@ int pkv_paged_decode_append_attention_fp8_scheduled(
     const void* schedule);
 
 /*
+ * Chunked prefill over fp8 e4m3 pools on the tensor cores with no scratch:
+ * the tcgen05 prefill kernel stages each key tile's e4m3 bytes and row
+ * scales in shared memory, and two of its warps convert them into the fp16
+ * tiles its MMAs read (value x scale, rounded to fp16 twice: the scale x 2^8
+ * and the product), so no pass over the visible blocks writes a 16-bit copy
+ * to memory.  Same arguments and semantics as pkv_paged_prefill_attention_fp8
+ * (which stays the CUDA-core kernel).  Serves fp16 queries (dtype
+ * PKV_DTYPE_F16), head_dim 64, block_size 16, up to 4 KV heads, 16-byte
+ * aligned pools and scale arrays; other cases return PKV_ERR_UNSUPPORTED.
+ * For callers that cannot hold the scratch: every CTA converts the tiles it
+ * reads, where the scratch pass converts each visible block once, so at
+ * config 4's shape this entry is about a quarter slower than
+ * pkv_paged_prefill_attention_fp8_scratch.  Replaces, for fp8 pools, the
+ * gather + _attention of mini_engine/model/qwen2.py:98-128 with num_new > 1.
+ */
+int pkv_paged_prefill_attention_fp8_tc(void* out, int64_t out_row_stride, const void* q,
+                                       int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                       const float* k_scale, const float* v_scale, int num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       int max_blocks_per_seq, const int32_t* query_start_loc,
+                                       const int32_t* num_prior, int n_seqs, int n_tokens,
+                                       int max_query_len, int n_q_heads, int n_kv_heads,
+                                       int head_dim, int block_size, float scale, int dtype,
+                                       int* err_flags, pkv_stream_t stream);
+
+/*
  * Chunked prefill over fp8 e4m3 pools on the tensor cores.  Same arguments
  * and semantics as pkv_paged_prefill_attention_fp8, plus a caller-provided
  * scratch buffer (pkv_prefill_fp8_scratch_bytes(n_seqs, max_blocks_per_seq,

@@ -868,6 +868,63 @@ int pkv_paged_decode_append_attention_layers(
   return PKV_OK;
 }
 
+// the tcgen05 prefill over fp8 pools, e4m3 tiles converted inside the kernel
+static int prefill_fp8_tc(const AttnArgs& a, cudaStream_t st) {
+  CUtensorMap qm, km, vm;
+  int rc = encode_q_tensormap(&qm, a.q, a.q_stride, a.n_tokens, a.n_q_heads, a.head_dim, a.dtype);
+  if (rc != 0) return rc;
+  rc = cached_pool_map(&km, a.k_pool, a.num_blocks, a.block_size, a.n_kv_heads, a.head_dim, kPoolFp8);
+  if (rc != 0) return rc;
+  rc = cached_pool_map(&vm, a.v_pool, a.num_blocks, a.block_size, a.n_kv_heads, a.head_dim, kPoolFp8);
+  if (rc != 0) return rc;
+  return status_of(launch_prefill_fast(a, &qm, &km, &vm, st));
+}
+
+int pkv_paged_prefill_attention_fp8_tc(void* out, int64_t out_row_stride, const void* q,
+                                       int64_t q_row_stride, const void* k_pool, const void* v_pool,
+                                       const float* k_scale, const float* v_scale, int num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       int max_blocks_per_seq, const int32_t* query_start_loc,
+                                       const int32_t* num_prior, int n_seqs, int n_tokens,
+                                       int max_query_len, int n_q_heads, int n_kv_heads,
+                                       int head_dim, int block_size, float scale, int dtype,
+                                       int* err_flags, pkv_stream_t stream) {
+  if (n_seqs < 0 || n_tokens < 0 || max_query_len < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_seqs == 0 || n_tokens == 0) return PKV_OK;
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  if (!query_start_loc || !num_prior || !k_scale || !v_scale) return PKV_ERR_NULL_POINTER;
+  AttnArgs a{};
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.query_start_loc = query_start_loc;
+  a.num_prior = num_prior;
+  a.n_seqs = n_seqs;
+  a.n_tokens = n_tokens;
+  a.max_query_len = max_query_len;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.block_size = block_size;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.err = err_flags;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  if (!prefill_fp8_tc_supported(a)) return PKV_ERR_UNSUPPORTED;
+  return prefill_fp8_tc(a, static_cast<cudaStream_t>(stream));
+}
+
 size_t pkv_prefill_fp8_scratch_bytes(int n_seqs, int max_blocks_per_seq, int n_kv_heads,
                                      int head_dim) {
   if (n_seqs < 0 || max_blocks_per_seq < 0 || n_kv_heads <= 0 || head_dim <= 0) return 0;

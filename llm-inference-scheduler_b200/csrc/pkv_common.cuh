@@ -84,6 +84,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// e4m3 -> f16 on the integer pipes: the e4m3 fields moved into f16 position,
+// which is the value times 2^-8 (exact, e4m3 subnormals included: they land
+// on f16 subnormals).  The NaN encodings 0x7f / 0xff map to +-480; the
+// quantising append never stores them.  Keeps conversions off the
+// transcendental pipe, which the softmax's exponentials use.
+// bytes 1 and 3 of x -> f16x2 (byte 1 in the low half)
+__device__ __forceinline__ uint32_t e4m3_odd_h2(uint32_t x) {
+  return (x & 0x80008000u) | ((x >> 1) & 0x3f803f80u);
+}
+// bytes 0 and 2 of x -> f16x2 (byte 0 in the low half)
+__device__ __forceinline__ uint32_t e4m3_even_h2(uint32_t x) {
+  const uint32_t z = (x << 7) & 0x7f807f80u;  // sign lands on bit 14 / 30
+  return z + (z & 0x40004000u);               // ... and is carried to bit 15 / 31
+}
 // Bounded wait: gives up after ~2^31 SM cycles (about a second) and returns
 // false, so a lost transaction can never hang the GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {

@@ -173,15 +173,6 @@ template <> __device__ __forceinline__ uint32_t fp8x2_to<__nv_bfloat16>(uint32_t
 #ifndef PKV_FP8_ALU_CVT
 #define PKV_FP8_ALU_CVT 2  // bit 0: K tiles, bit 1: V tiles (K by cvt measured faster)
 #endif
-// bytes 1 and 3 of x -> f16x2 (byte 1 in the low half)
-__device__ __forceinline__ uint32_t e4m3_odd_h2(uint32_t x) {
-  return (x & 0x80008000u) | ((x >> 1) & 0x3f803f80u);
-}
-// bytes 0 and 2 of x -> f16x2 (byte 0 in the low half)
-__device__ __forceinline__ uint32_t e4m3_even_h2(uint32_t x) {
-  const uint32_t z = (x << 7) & 0x7f807f80u;  // sign lands on bit 14 / 30
-  return z + (z & 0x40004000u);               // ... and is carried to bit 15 / 31
-}
 
 template <typename T>
 __device__ __forceinline__ void fp8x16_to(const uint4& in, uint4& lo, uint4& hi) {

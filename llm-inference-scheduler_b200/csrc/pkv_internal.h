@@ -133,6 +133,7 @@ int encode_pool_tensormap(CUtensorMap* map, const void* pool, int num_blocks, in
 // Chunked prefill on tcgen05 tensor cores: fp16/bf16, head_dim 64, block 16,
 // 16-byte aligned q / out rows.
 bool prefill_fast_supported(const AttnArgs& a);
+bool prefill_fp8_tc_supported(const AttnArgs& a);
 size_t prefill_fp8_scratch_bytes(int n_seqs, int max_blocks, int n_kv_heads, int head_dim);
 cudaError_t launch_dequant_blocks(const AttnArgs& a, void* scratch, cudaStream_t stream,
                                   void** k_out, void** v_out, int32_t** table_out);

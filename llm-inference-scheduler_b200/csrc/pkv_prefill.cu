@@ -91,11 +91,23 @@ constexpr int kOffQ = 0;                               // Q_A, Q_B
 constexpr int kOffK = kOffQ + 2 * kPfTile;
 constexpr int kOffV = kOffK + kPfStages * kPfTile;
 constexpr int kOffBar = kOffV + kPfStages * kPfTile;
-constexpr int kNumBars = 1 + 2 * kPfStages + 4 * 2;
+constexpr int kNumBars = 1 + 2 * kPfStages + 4 * 2 + 2 * 2;
 constexpr int kOffSched = kOffBar + kNumBars * 8;      // tmem slot, work item, length keys
 constexpr int kSchedInts = 4 + kPfOrderMaxSeqs;
 constexpr int kPfSmemBytes = 1024 + kOffSched + kSchedInts * 4;
 static_assert(kPfSmemBytes <= 232448, "prefill ring does not fit the 227 KB of shared memory per CTA");
+// fp8 pools: a 2-stage ring of the raw e4m3 key tiles (128 keys x 64 bytes for
+// K and for V) and their rows' fp32 scales (8 blocks x 16 rows x up to
+// kPf8MaxKvHeads heads), after the 16-bit ring, 1024-byte aligned
+constexpr int kPf8Stages = 2;
+constexpr int kPf8MaxKvHeads = 4;
+constexpr int kPf8Tile = 128 * 64;                     // 8 KB of e4m3
+constexpr int kPf8Scales = 8 * 16 * kPf8MaxKvHeads * 4;  // one tile's scales, K or V
+constexpr int kPf8Stage = 2 * kPf8Tile + 2 * kPf8Scales;
+constexpr int kOffS8 = (kOffSched + kSchedInts * 4 + 1023) / 1024 * 1024;
+constexpr int kPfSmemBytesFp8 = 1024 + kOffS8 + kPf8Stages * kPf8Stage;
+static_assert(kPfSmemBytesFp8 <= 232448, "fp8 staging does not fit the 227 KB of shared memory per CTA");
+constexpr int kPfConvWarp0 = 10;  // warps 10 and 11 convert the fp8 tiles
 
 struct PrefillParams {
   void* out;
@@ -114,9 +126,13 @@ struct PrefillParams {
   int group;
   float scale_log2;
   int* err;
+  // fp8 pools: fp32 scale per (slot, KV head)
+  const float* k_scale;
+  const float* v_scale;
+  int n_kv_heads;
 };
 
-template <typename T>
+template <typename T, bool FP8>
 __global__ void __launch_bounds__(kPfThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                             const __grid_constant__ CUtensorMap kmap,
@@ -134,6 +150,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* s_empty = s_full + 2;           // [tile]: the softmax holds S_x in registers
   uint64_t* p_full = s_empty + 2;           // [tile]: P_x is in tensor memory
   uint64_t* o_done = p_full + 2;            // [tile]: O_x += P_x V has completed
+  uint64_t* s8_full = o_done + 2;           // fp8: the raw tiles and scales of a stage landed
+  uint64_t* s8_empty = s8_full + kPf8Stages;  // fp8: the converters are done with a stage
   int* sched = reinterpret_cast<int*>(base + kOffSched);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sched);
   const uint32_t sbase = smem_u32(base);
@@ -167,8 +185,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == 1 && lane == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < kPfStages; ++i) {
-      mbar_init(&kv_full[i], 1);
+      // fp8: the 16-bit tiles are written by the two converter warps
+      mbar_init(&kv_full[i], FP8 ? 2 : 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < kPf8Stages; ++i) {
+      mbar_init(&s8_full[i], 1);
+      mbar_init(&s8_empty[i], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -249,6 +272,33 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int toks[8];
 #pragma unroll
       for (int b = 0; b < 8; ++b) toks[b] = __shfl_sync(0xffffffffu, tok, b);
+      if constexpr (FP8) {
+        // raw e4m3 tiles and their rows' scales into the staging ring; the
+        // converter warps turn them into the 16-bit ring's tiles
+        const int s8 = j % kPf8Stages;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s8_empty[s8], ((j / kPf8Stages) & 1) ^ 1))) {
+          if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+          break;
+        }
+        const int nvalid = min(max(nb_needed - j * 8, 0), 8);  // blocks with keys: a prefix
+        const int sbytes = 16 * p.n_kv_heads * 4;
+        if (elect_one()) {
+          uint8_t* stg = base + kOffS8 + s8 * kPf8Stage;
+          mbar_arrive_expect_tx(&s8_full[s8], 2 * kPf8Tile + 2 * nvalid * sbytes);
+#pragma unroll
+          for (int b = 0; b < 8; ++b) {
+            tma_load_3d(stg + b * 1024, &kmap, &s8_full[s8], 0, g, toks[b]);
+            tma_load_3d(stg + kPf8Tile + b * 1024, &vmap, &s8_full[s8], 0, g, toks[b]);
+          }
+          for (int b = 0; b < nvalid; ++b) {
+            const int64_t so = static_cast<int64_t>(toks[b]) * p.n_kv_heads;  // row (block*16) x heads
+            bulk_load(stg + 2 * kPf8Tile + b * sbytes, p.k_scale + so, sbytes, &s8_full[s8]);
+            bulk_load(stg + 2 * kPf8Tile + kPf8Scales + b * sbytes, p.v_scale + so, sbytes, &s8_full[s8]);
+          }
+        }
+        __syncwarp();
+        continue;
+      }
       const int st = j % kPfStages;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / kPfStages) & 1) ^ 1))) {
         if (lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
@@ -347,6 +397,72 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (dead) break;
       if (elect_one()) tc_commit(&kv_empty[j % kPfStages]);
       __syncwarp();
+    }
+    if (dead && lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+  } else if (FP8 && warp >= kPfConvWarp0) {
+    // ======================= fp8 converters (warps 10, 11) =======================
+    // Key tile j: wait for its raw stage and for the 16-bit ring stage to be
+    // free, then each of the 64 threads converts 4 of the tile's 256 rows (128
+    // of K, 128 of V): 64 e4m3 bytes -> 64 fp16 values x the row's scale,
+    // stored with the 128-byte swizzle the MMA descriptors read (16-byte chunk
+    // c of row r at c ^ (r & 7)).  The conversion moves the e4m3 fields into
+    // f16 position on the integer pipes (the value x 2^-8, exact), widens to
+    // fp32 and multiplies by (scale x 2^8): one rounding of the product, as
+    // the 16-bit scratch pass computes it (no transcendental-pipe work: that
+    // pipe bounds the softmax).  Rows past the CTA's last visible key are
+    // written as zeros (an unused slot may hold any bytes).
+    const int u = (warp - kPfConvWarp0) * 32 + lane;
+    const int kv_max = max(kv[0], kv[1]);
+    const int hkv = p.n_kv_heads;
+    bool dead = false;
+    for (int j = 0; j < n_kv_tiles; ++j) {
+      const int s8 = j % kPf8Stages, st = j % kPfStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s8_full[s8], (j / kPf8Stages) & 1)) ||
+          !__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / kPfStages) & 1) ^ 1))) {
+        dead = true;
+        break;
+      }
+      const uint8_t* stg = base + kOffS8 + s8 * kPf8Stage;
+      for (int rr = u; rr < 2 * kPfN; rr += 64) {
+        const bool isv = rr >= kPfN;
+        const int r = rr & (kPfN - 1);
+        const uint8_t* src = stg + (isv ? kPf8Tile : 0) + r * 64;
+        uint8_t* dst = base + (isv ? kOffV : kOffK) + st * kPfTile + r * 128;
+        const int sw = r & 7;
+        if (j * kPfN + r < kv_max) {
+          const float* scl = reinterpret_cast<const float*>(stg + 2 * kPf8Tile + (isv ? kPf8Scales : 0));
+          // (e4m3 x 2^-8) x (scale x 2^8): the 2^8 factors are exact, so the
+          // fp32 product is e4m3 x scale rounded once, then once to fp16
+          const float sc2 = scl[(r >> 4) * 16 * hkv + (r & 15) * hkv + g] * 256.f;
+#pragma unroll
+          for (int c16 = 0; c16 < 4; ++c16) {
+            const uint4 w = *reinterpret_cast<const uint4*>(src + c16 * 16);
+            const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+            uint32_t o[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // even bytes (0, 2) and odd bytes (1, 3) of the word, as f16 pairs
+              const uint32_t ev = e4m3_even_h2(in[k]), od = e4m3_odd_h2(in[k]);
+              const float2 fe = __half22float2(*reinterpret_cast<const __half2*>(&ev));
+              const float2 fo = __half22float2(*reinterpret_cast<const __half2*>(&od));
+              o[2 * k] = pack2<__half>(fe.x * sc2, fo.x * sc2);      // values 4k, 4k + 1
+              o[2 * k + 1] = pack2<__half>(fe.y * sc2, fo.y * sc2);  // values 4k + 2, 4k + 3
+            }
+            *reinterpret_cast<uint4*>(dst + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + (((2 * c16 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        } else {
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + (c << 4)) = z;
+        }
+      }
+      fence_proxy_async_smem();  // the generic-proxy tile writes, before the tensor core reads them
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&kv_full[st]);
+        mbar_arrive(&s8_empty[s8]);
+      }
     }
     if (dead && lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
   }
@@ -503,9 +619,18 @@ bool prefill_fast_supported(const AttnArgs& a) {
          a.scale > 0.f && static_cast<int64_t>(a.n_tokens) + kPfPair < (int64_t{1} << 31);
 }
 
+// fp8 pools on the tensor cores with the in-kernel conversion: fp16 queries,
+// up to kPf8MaxKvHeads KV heads, scale rows bulk-copyable
+bool prefill_fp8_tc_supported(const AttnArgs& a) {
+  auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
+  return a.k_scale != nullptr && a.v_scale != nullptr && a.dtype == PKV_DTYPE_F16 &&
+         a.n_kv_heads <= kPf8MaxKvHeads && al(a.k_scale, 16) && al(a.v_scale, 16) &&
+         prefill_fast_supported(a);
+}
+
 namespace {
 std::mutex g_pf_mu;
-int g_pf_state[64][2] = {};  // 0 unchecked, 1 ready, -1 register split does not fit
+int g_pf_state[64][4] = {};  // [device][dtype x fp8]: 0 unchecked, 1 ready, -1 split does not fit
 }  // namespace
 
 cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, const CUtensorMap* kmap,
@@ -514,11 +639,16 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  auto kern = a.dtype == PKV_DTYPE_F16 ? paged_prefill_tc_kernel<__half>
-                                       : paged_prefill_tc_kernel<__nv_bfloat16>;
+  // fp8 pools (the scales given): the kernel converts the e4m3 tiles itself
+  const bool fp8 = a.k_scale != nullptr;
+  if (fp8 && !prefill_fp8_tc_supported(a)) return cudaErrorNotSupported;
+  auto kern = fp8 ? paged_prefill_tc_kernel<__half, true>
+              : a.dtype == PKV_DTYPE_F16 ? paged_prefill_tc_kernel<__half, false>
+                                         : paged_prefill_tc_kernel<__nv_bfloat16, false>;
+  const int smem = fp8 ? kPfSmemBytesFp8 : kPfSmemBytes;
   {
     std::lock_guard<std::mutex> lk(g_pf_mu);
-    const int k = a.dtype == PKV_DTYPE_F16 ? 0 : 1;
+    const int k = fp8 ? 2 : a.dtype == PKV_DTYPE_F16 ? 0 : 1;
     int state = dev < 64 ? g_pf_state[dev][k] : 0;
     if (state == 0) {
       cudaFuncAttributes fa;
@@ -526,7 +656,7 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
       if (e != cudaSuccess) return e;
       state = fa.numRegs * kPfThreads >= kPfRegSplit ? 1 : -1;
       if (state == 1) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
       }
       if (dev < 64) g_pf_state[dev][k] = state;
@@ -552,8 +682,11 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
   p.group = a.n_q_heads / a.n_kv_heads;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = a.err;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
+  p.n_kv_heads = a.n_kv_heads;
   const dim3 grid(static_cast<unsigned>(p.n_pairs * a.n_q_heads * a.n_seqs));
-  kern<<<grid, kPfThreads, kPfSmemBytes, stream>>>(*qmap, *kmap, *vmap, p);
+  kern<<<grid, kPfThreads, smem, stream>>>(*qmap, *kmap, *vmap, p);
   return cudaGetLastError();
 }
 

@@ -73,6 +73,8 @@ SIGNATURES: dict = {
                                                    _P, _I, _P, _I64, _I, _P, _I, _I, _I, _I, _I, _F,
                                                    _I, _P, _SZ, _P, _P]),
     "pkv_prefill_fp8_scratch_bytes": (_SZ, [_I, _I, _I, _I]),
+    "pkv_paged_prefill_attention_fp8_tc": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _I64, _I,
+                                                _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "pkv_paged_prefill_attention_fp8_scratch": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P,
                                                      _I64, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I,
                                                      _F, _I, _P, _SZ, _P, _P]),

@@ -252,7 +252,7 @@ class StepGraphs:
             self._step(R, P)  # library handles, kernel attributes, argument caches
         cur.wait_stream(side)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, pool=self.pool):
+        with torch.cuda.graph(g, pool=self.pool, capture_error_mode="thread_local"):
             self._step(R, P)
         self.graphs[(R, P)] = g
 
@@ -529,7 +529,9 @@ class DecodeStepGraph:
             self._step()
         cur.wait_stream(side)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # thread-local capture: other threads of the process (a process
+        # group's watchdog) may query their events while this one captures
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
             self._step()
         self.graph = g
 

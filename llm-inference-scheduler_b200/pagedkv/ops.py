@@ -531,12 +531,19 @@ def prefill_fp8_scratch_bytes(n_seqs: int, max_blocks_per_seq: int, n_kv_heads: 
 
 def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
                                 num_prior, max_query_len, scale, out=None, err=None,
-                                tensor_cores: bool = True, scratch=None) -> torch.Tensor:
-    """paged_prefill_attention over fp8 e4m3 pools.  tensor_cores=True: the
-    blocks the step sees are written as 16-bit rows (e4m3 x scale, rounded
-    once to q's dtype) into `scratch` (prefill_fp8_scratch_bytes; allocated
-    here when None) and the tcgen05 prefill runs over them; False: the
-    CUDA-core kernel dequantises on load (no scratch, no extra rounding)."""
+                                tensor_cores: bool = True, scratch=None,
+                                scratch_free: bool = False) -> torch.Tensor:
+    """paged_prefill_attention over fp8 e4m3 pools.
+
+    tensor_cores=True: the tcgen05 prefill over 16-bit rows.  By default the
+    blocks the step sees are first written as 16-bit rows (e4m3 x scale,
+    rounded once to q's dtype) into `scratch` (prefill_fp8_scratch_bytes;
+    allocated here when None).  scratch_free=True (fp16 q only): the kernel
+    converts the e4m3 tiles in shared memory itself
+    (pkv_paged_prefill_attention_fp8_tc), no scratch; slower at config 4's
+    shape (each CTA converts the tiles it reads, where the scratch pass
+    converts each visible block once).  tensor_cores=False: the CUDA-core
+    kernel dequantises on load (no scratch, no extra rounding)."""
     nb, bs, hkv, d = _check_fp8_pools(k_pool, v_pool, k_scale, v_scale)
     for t, n in ((q, "q"), (query_start_loc, "query_start_loc"), (num_prior, "num_prior")):
         _cuda(t, n)
@@ -548,6 +555,15 @@ def paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_table
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     if T == 0 or n_seqs == 0:
+        return out
+    if tensor_cores and scratch_free:
+        rc = _lib.load().pkv_paged_prefill_attention_fp8_tc(
+            out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+            block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+            query_start_loc.data_ptr(), num_prior.data_ptr(), n_seqs, T, int(max_query_len), hq, hkv,
+            d, bs, float(scale), dtype_code(q.dtype), _ptr(err), _stream(q))
+        _lib.check(rc, "pkv_paged_prefill_attention_fp8_tc")
         return out
     if tensor_cores and q.dtype in (torch.float16, torch.bfloat16):
         need = prefill_fp8_scratch_bytes(n_seqs, block_tables.shape[1], hkv, d)
@@ -731,11 +747,24 @@ def bind_paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_sc
 def bind_paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables,
                                      query_start_loc, num_prior, max_query_len, scale, out, scratch,
                                      err=None) -> BoundLaunch:
-    """The tensor-core fp8 prefill (scratch pass + tcgen05 kernel) bound to fixed tensors."""
+    """The tensor-core fp8 prefill bound to fixed tensors: scratch pass +
+    tcgen05 kernel, or with scratch=None the scratch-free entry (fp16 q)."""
     paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
-                                num_prior, max_query_len, scale, out=out, err=err, scratch=scratch)
+                                num_prior, max_query_len, scale, out=out, err=err, scratch=scratch,
+                                scratch_free=scratch is None)
     nb, bs, hkv, d = k_pool.shape
     T, hq, _ = q.shape
+    if scratch is None:
+        args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
+                k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
+                block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+                query_start_loc.data_ptr(), num_prior.data_ptr(), query_start_loc.shape[0] - 1, T,
+                int(max_query_len), hq, hkv, d, bs, float(scale), dtype_code(q.dtype), _ptr(err),
+                _stream(q))
+        return BoundLaunch(_lib.load().pkv_paged_prefill_attention_fp8_tc, args,
+                           "pkv_paged_prefill_attention_fp8_tc",
+                           (q, k_pool, v_pool, k_scale, v_scale, block_tables, query_start_loc,
+                            num_prior, out, err))
     args = (out.data_ptr(), _row_stride(out, "out"), q.data_ptr(), _row_stride(q, "q"),
             k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), nb,
             block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],

@@ -719,11 +719,12 @@ def test_decode_fp8_matches_oracle(oracle_mod, decode_impl, q_dt):
     assert np.abs(got - ref).max() <= fp8_atol(q_dt, ref)
 
 
-@pytest.mark.parametrize("q_dt", ("f16", "bf16"))
-@pytest.mark.parametrize("tensor_cores", (True, False))
-def test_prefill_fp8_matches_oracle(oracle_mod, q_dt, tensor_cores):
+@pytest.mark.parametrize("q_dt,path", [("f16", "scratch"), ("bf16", "scratch"), ("f16", "in_kernel"),
+                                         ("f16", "cuda_cores"), ("bf16", "cuda_cores")])
+def test_prefill_fp8_matches_oracle(oracle_mod, q_dt, path):
     """Chunked prefill over fp8 pools, chunks over a prior: the tensor-core
-    path (16-bit scratch pool + tcgen05 kernel) and the CUDA-core kernel."""
+    path (16-bit scratch pool + tcgen05 kernel; fp16 q also with the e4m3
+    tiles converted inside the tcgen05 kernel) and the CUDA-core kernel."""
     prior = np.array([48, 0, 300, 17, 1000], dtype=np.int64)
     chunk = np.array([64, 130, 1, 40, 300], dtype=np.int64)
     c = _fp8_case(73, prior + chunk, "f16")
@@ -734,7 +735,8 @@ def test_prefill_fp8_matches_oracle(oracle_mod, q_dt, tensor_cores):
     err = ops.new_error_flags("cuda")
     out = ops.paged_prefill_attention_fp8(dev(q, q_dt), c["kp"], c["vp"], c["ks"], c["vs"], dev(tabs),
                                           dev(qsl), dev(prior.astype(np.int32)), int(chunk.max()), 0.125,
-                                          err=err, tensor_cores=tensor_cores)
+                                          err=err, tensor_cores=path != "cuda_cores",
+                                          scratch_free=path == "in_kernel")
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     ref = oracle_mod.paged_attention_fp8(as_f32(q, q_dt), c["kp"].cpu().numpy(),
@@ -746,9 +748,10 @@ def test_prefill_fp8_matches_oracle(oracle_mod, q_dt, tensor_cores):
 
 def test_prefill_fp8_tensor_cores_config4_shape():
     """Config-4 shape over fp8 pools (16 chunks of 512 over a 48-token shared
-    prefix plus private priors): the tensor-core path against the CUDA-core
-    kernel, within the fp16 fp8 tolerance; the scratch is reused across two
-    calls with different pools (no state carried)."""
+    prefix plus private priors): the tensor-core paths (scratch pass, and
+    in-kernel conversion) against the CUDA-core kernel, within the fp16 fp8
+    tolerance; the scratch is reused across two calls with different pools
+    (no state carried)."""
     rng = np.random.default_rng(74)
     prior = 48 + rng.integers(0, 4096, size=16)
     chunk = np.full(16, 512)
@@ -768,10 +771,58 @@ def test_prefill_fp8_tensor_cores_config4_shape():
                                             err=err, scratch=scratch)
         b = ops.paged_prefill_attention_fp8(q, kp, c["vp"], c["ks"], c["vs"], tabs, qsl, pr, 512, 0.125,
                                             err=err, tensor_cores=False)
+        k = ops.paged_prefill_attention_fp8(q, kp, c["vp"], c["ks"], c["vs"], tabs, qsl, pr, 512, 0.125,
+                                            err=err, scratch_free=True)
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         ref = b.float().cpu().numpy()
         assert np.abs(a.float().cpu().numpy() - ref).max() <= 2 * fp8_atol("f16", ref)
+        assert np.abs(k.float().cpu().numpy() - ref).max() <= 2 * fp8_atol("f16", ref)
+
+
+def test_prefill_fp8_in_kernel_conversion_ignores_unused_slots(oracle_mod):
+    """The tcgen05 prefill converting e4m3 tiles itself: the slots past each
+    sequence's last key (the tail of its last block) may hold any bytes and
+    scales, here +448-magnitude bytes and an infinite scale; the converters
+    write those rows as zeros, so the output is bit-identical to the run over
+    clean pools and matches the oracle.  bf16 queries are refused by the
+    scratch-free entry point (PKV_ERR_UNSUPPORTED)."""
+    prior = np.array([5, 0, 77, 200], dtype=np.int64)
+    chunk = np.array([19, 33, 130, 3], dtype=np.int64)
+    c = _fp8_case(91, prior + chunk, "f16")
+    T = int(chunk.sum())
+    q = dev(C.to_dtype(c["rng"].standard_normal((T, 14, 64), dtype=np.float32), "f16"), "f16")
+    tabs = C.pad_tables(c["tables"])
+    qsl = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    args = (dev(tabs), dev(qsl), dev(prior.astype(np.int32)), int(chunk.max()), 0.125)
+    err = ops.new_error_flags("cuda")
+    clean = ops.paged_prefill_attention_fp8(q, c["kp"], c["vp"], c["ks"], c["vs"], *args, err=err,
+                                            scratch_free=True)
+    torch.cuda.synchronize()
+    kp, vp, ks, vs = c["kp"].clone(), c["vp"].clone(), c["ks"].clone(), c["vs"].clone()
+    for t, n in zip(c["tables"], c["ctx"]):
+        last, used = t[-1], int(n) - 16 * (len(t) - 1)
+        kp[last, used:] = 0x7E
+        vp[last, used:] = 0xFE
+        ks[last, used:] = float("inf")
+        vs[last, used:] = float("inf")
+    dirty = ops.paged_prefill_attention_fp8(q, kp, vp, ks, vs, *args, err=err, scratch_free=True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(clean, dirty)
+    ref = oracle_mod.paged_attention_fp8(host(q, "f16").astype(np.float32), c["kp"].cpu().numpy(),
+                                         c["vp"].cpu().numpy(), c["ks"].cpu().numpy(),
+                                         c["vs"].cpu().numpy(), tabs, qsl, prior.astype(np.int32))
+    assert np.abs(clean.float().cpu().numpy() - ref).max() <= fp8_atol("f16", ref)
+    qb = q.to(torch.bfloat16)
+    out = torch.empty_like(qb)
+    nb = c["kp"].shape[0]
+    rc = _lib.load().pkv_paged_prefill_attention_fp8_tc(
+        out.data_ptr(), 14 * 64, qb.data_ptr(), 14 * 64, c["kp"].data_ptr(), c["vp"].data_ptr(),
+        c["ks"].data_ptr(), c["vs"].data_ptr(), nb, args[0].data_ptr(), args[0].stride(0),
+        args[0].shape[1], args[1].data_ptr(), args[2].data_ptr(), len(chunk), T, int(chunk.max()), 14, 2,
+        64, 16, 0.125, _lib.BF16, None, torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.ERR_UNSUPPORTED
 
 
 def test_forward_layer_fp8_pools_and_cow(oracle_mod):
