@@ -1027,8 +1027,10 @@ def run_cache_ops(args):
         rcalls = [lambda l=l: ops.rope_reshape_and_cache(qkv[l], pos, cos, sin, kp[l], vp[l], slots,
                                                          q_out=qo[l], err=err) for l in range(L)]
         ms = time_calls(rcalls, max(3, args.steps // L))
-        nbytes = T * (18 * 64 * 2 + 2 * 64 * 2 * 2 + 16 + 14 * 64 * 2 + 2 * 2 * 64 * 2)
-        results.append({"kernel": "pkv::rope_reshape_and_cache_kernel<half>", "tokens": T,
+        # per token: the projection row read, rotated q written, k and v rows
+        # written, position and slot; the cos / sin tables (2 MB) once
+        nbytes = T * (18 * 64 * 2 + 14 * 64 * 2 + 2 * 2 * 64 * 2 + 16) + 2 * cos.numel() * cos.element_size()
+        results.append({"kernel": "pkv::rope_reshape_and_cache_vec_kernel<half>", "tokens": T,
                         "bytes_per_launch": nbytes, "us": round(ms * 1e3, 3),
                         "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
                         "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)})

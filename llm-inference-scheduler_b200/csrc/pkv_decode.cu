@@ -48,11 +48,15 @@
 //    epilogue writes them back in natural order).  Scales are applied
 //    outside the MMAs: K's to the token's scores, V's folded into P after
 //    the softmax sums.
-//  * Fused append (k_new != NULL): before loading the block that holds a
+//  * Fused append (k_new != NULL).  16-bit pools: the consumer warp of each
+//    KV head writes the newest token's row of its head into the staged K and
+//    V tiles of the sequence's last block (after the TMA lands, before the
+//    MMAs read it) and into the pool, so the producer's ring never waits on
+//    an append.  fp8 pools: before loading the block that holds a
 //    sequence's newest token, the producer warp writes that token's K and V
-//    rows into the pool (fp8: quantised per row with their scales, exactly
-//    as the separate fp8 append does), then fences the generic-proxy writes
-//    against its TMA read.
+//    rows into the pool, quantised per row with their scales exactly as the
+//    separate fp8 append does, then fences the generic-proxy writes against
+//    its TMA read.
 //  * Programmatic dependent launch chains append -> decode -> merge: each
 //    kernel's prologue (context scan, block-table reads) runs before
 //    griddepcontrol.wait and overlaps its predecessor; pool, q, out and
@@ -409,8 +413,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         }
         if (id < 0) {
           id = 0;  // read a valid block; never write through a bad id
-        } else if (p.k_new != nullptr && gb == prefix[s + 1] - 1) {
-          app_seq = s;
+        } else if (FP8 && p.k_new != nullptr && gb == prefix[s + 1] - 1) {
+          app_seq = s;  // 16-bit pools: the consumers append (see below)
           app_row = id * 16 + ((ctxs[s] - 1) & 15);
         }
       }
@@ -424,33 +428,21 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         waited = true;
       }
       const int n = min(32, r1 - b0);
-      // fused append: the warp writes the K and V rows of the sequence whose
-      // newest token lies in batch block kk (fp8: quantised, with their
-      // scales); fence_appends() then orders those generic-proxy writes
+      // fused append, fp8 pools: the warp writes the quantised K and V rows
+      // (with their scales) of the sequence whose newest token lies in batch
+      // block kk; fence_appends() then orders those generic-proxy writes
       // before lane 0's TMA reads
       auto append_rows = [&](int kk) {
         const int a_seq = __shfl_sync(0xffffffffu, app_seq, kk);
         const int row = __shfl_sync(0xffffffffu, app_row, kk);
-        if constexpr (FP8) {
-          fp8_store_token<T>(reinterpret_cast<const T*>(p.k_new + a_seq * p.k_new_stride_b),
-                             p.k_pool + static_cast<int64_t>(row) * (nkv * 64),
-                             const_cast<float*>(p.k_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
-                             lane);
-          fp8_store_token<T>(reinterpret_cast<const T*>(p.v_new + a_seq * p.v_new_stride_b),
-                             p.v_pool + static_cast<int64_t>(row) * (nkv * 64),
-                             const_cast<float*>(p.v_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
-                             lane);
-        } else {
-          constexpr int row_vecs = nkv * 8;  // 16-byte vectors per row
-          for (int v = lane; v < 2 * row_vecs; v += 32) {
-            const bool is_v = v >= row_vecs;
-            const int vi = is_v ? v - row_vecs : v;
-            const uint8_t* src = (is_v ? p.v_new + a_seq * p.v_new_stride_b
-                                       : p.k_new + a_seq * p.k_new_stride_b) + vi * 16;
-            uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + static_cast<int64_t>(row) * (row_vecs * 16) + vi * 16;
-            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<const int4*>(src);
-          }
-        }
+        fp8_store_token<T>(reinterpret_cast<const T*>(p.k_new + a_seq * p.k_new_stride_b),
+                           p.k_pool + static_cast<int64_t>(row) * (nkv * 64),
+                           const_cast<float*>(p.k_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                           lane);
+        fp8_store_token<T>(reinterpret_cast<const T*>(p.v_new + a_seq * p.v_new_stride_b),
+                           p.v_pool + static_cast<int64_t>(row) * (nkv * 64),
+                           const_cast<float*>(p.v_scale) + static_cast<int64_t>(row) * nkv, nkv, 64,
+                           lane);
       };
       auto fence_appends = [&]() {
         fence_proxy_async_global();
@@ -458,7 +450,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         if (lane == 0) fence_proxy_async_global();
       };
       // batch blocks that hold a sequence's newest token and are not yet written
-      uint32_t pending = __ballot_sync(0xffffffffu, app_seq >= 0);
+      uint32_t pending = FP8 ? __ballot_sync(0xffffffffu, app_seq >= 0) : 0u;
       for (int k = 0; k < n; ++k, ++i) {
         const int blk = __shfl_sync(0xffffffffu, id, k);
         if ((pending >> k) & 1u) {  // append before the block is loaded
@@ -492,19 +484,6 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
                         p.v_scale + static_cast<int64_t>(blk) * 16 * nkv, scale_bytes, &full_bar[st]);
             }
           }
-        }
-        // 16-bit pools: the ring is full from here on, so the next load waits
-        // for a consumer to free a stage; write the batch's later appends
-        // now, while the tiles in flight arrive, instead of stalling the
-        // 3-stage ring at their blocks (each is still written and fenced
-        // before its block's load).  The fp8 appends (quantisation) stay at
-        // their blocks: done early they delay the next load once a stage
-        // frees, and the 6-stage fp8 ring hides them where they are.
-        if (!FP8 && i + 1 >= kDecStages && k + 1 < n && (pending >> (k + 1)) != 0u) {
-          for (uint32_t rest = pending >> (k + 1), kk = k + 1; rest != 0u; rest >>= 1, ++kk)
-            if (rest & 1u) append_rows(static_cast<int>(kk));
-          fence_appends();
-          pending &= (2u << k) - 1u;
         }
       }
     }
@@ -727,6 +706,29 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         }
       }
     } else {
+    // Fused append, 16-bit pools: the segment that ends a sequence holds its
+    // newest token (row ctx - 1).  This warp, the only reader of its KV
+    // head's tiles, loads the head's new K and V values now (4 bytes a
+    // lane), writes them into the staged tiles of the last block once its
+    // TMA has landed (the slot's old bytes are overwritten before any
+    // ldmatrix reads them) and stores them to the pool.  The producer never
+    // waits on the append; whether its TMA read of the slot sees the old or
+    // the new bytes, the tile the MMAs read holds the new row.
+    const bool app = p.k_new != nullptr && seg_end == prefix[s + 1];
+    uint32_t kn = 0u, vn = 0u;
+    int app_id = -1;
+    if (app) {
+      kn = __ldg(reinterpret_cast<const uint32_t*>(p.k_new + s * p.k_new_stride_b + h * 128) + lane);
+      vn = __ldg(reinterpret_cast<const uint32_t*>(p.v_new + s * p.v_new_stride_b + h * 128) + lane);
+      const int gl = prefix[s + 1] - 1;  // the sequence's last block in the step's order
+      if (p.sched != nullptr) {
+        // validated by the schedule builder (a bad id is stored as -1)
+        app_id = __ldg(p.sched + sched_ids_offset(B) + static_cast<int64_t>(vcta) * p.sched_rows + (gl - r0));
+      } else {
+        app_id = __ldg(p.block_tables + static_cast<int64_t>(s) * p.bt_stride + (gl - prefix[s]));
+        if (app_id >= p.num_blocks) app_id = -1;  // flagged by the producer
+      }
+    }
     for (int jb = jb0; jb < jb_end; ++jb, ++i) {
       const int st = i % kDecStages;
       if (!dead && !mbar_wait(&full_bar[st], (i / kDecStages) & 1)) {
@@ -738,6 +740,16 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       const int valid = min(16, ctx - jb * 16);
       const uint32_t kt = smem_u32(tiles + st * stage_bytes + h * kDecTile);
       const uint32_t vt = smem_u32(tiles + st * stage_bytes + (nkv + h) * kDecTile);
+      const bool patch = app && jb == jb_end - 1;  // warp-uniform
+      if (patch) {
+        // row valid - 1 of the 128B-swizzled tiles: 16-byte chunk c of row r
+        // sits at chunk c ^ (r & 7); lane l holds bytes 4l .. 4l + 3
+        const int r = valid - 1;
+        const int off = r * 128 + (((lane >> 2) ^ (r & 7)) << 4) + (lane & 3) * 4;
+        *reinterpret_cast<uint32_t*>(tiles + st * stage_bytes + h * kDecTile + off) = kn;
+        *reinterpret_cast<uint32_t*>(tiles + st * stage_bytes + (nkv + h) * kDecTile + off) = vn;
+        __syncwarp();
+      }
       // ---- S^T = K Q^T (16 tokens x 8 heads), 4 k-steps of 16 dims
       float sc[4] = {0.f, 0.f, 0.f, 0.f};
       const int mi = lane >> 3;
@@ -791,8 +803,15 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         ldsm_x4_t(vt + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
         mma16816<T>(o[mt], a, b0, b1);
       }
+      // the patched row's generic writes before the stage's next TMA write
+      if (patch) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[st]);
+    }
+    if (app_id >= 0) {  // the new row into the pool (its slot of the last block)
+      const int64_t row = static_cast<int64_t>(app_id) * 16 + ((ctx - 1) & 15);
+      reinterpret_cast<uint32_t*>(p.k_pool + (row * nkv + h) * 128)[lane] = kn;
+      reinterpret_cast<uint32_t*>(p.v_pool + (row * nkv + h) * 128)[lane] = vn;
     }
     }
 

@@ -543,13 +543,23 @@ def test_decode_layers_abi_rejects_overlapping_pools():
 
 # ---------------------------------------------------------------- fused RoPE + append
 
+def qkv_rows(T, width, g, tdt, layout, mul=1.0):
+    """[T, width] projection rows: "packed" (row stride = width: 16-byte
+    aligned rows, the vectorised RoPE kernel) or "padded" (row stride width +
+    2 elements: rows off the 16-byte grid, the warp-per-head kernel)."""
+    pad = 2 if layout == "padded" else 0
+    big = (mul * torch.randn((T, width + pad), generator=g, device="cuda")).to(tdt)
+    return big[:, :width]
+
+
+@pytest.mark.parametrize("layout", ("packed", "padded"))
 @pytest.mark.parametrize("dt", DTS)
-def test_rope_reshape_and_cache_bit_identical_to_torch_rope(dt):
+def test_rope_reshape_and_cache_bit_identical_to_torch_rope(dt, layout):
     """pkv_rope_reshape_and_cache against the unfused path it replaces:
     Rope.rotate on q and k (separate torch multiply / add) then
     reshape_and_cache.  Rotated q and both pools must be identical bit for
     bit; a padding slot (-1) writes q only; a position outside the tables is
-    flagged and that token skipped."""
+    flagged and that token skipped.  Both kernel forms (qkv_rows)."""
     from pagedkv.model import Rope
 
     tdt = TORCH_DT[dt]
@@ -557,7 +567,7 @@ def test_rope_reshape_and_cache_bit_identical_to_torch_rope(dt):
     T, hq, hkv, d, nb = 200, 14, 2, 64, 64
     rope = Rope(d, 1e6, "cuda", tdt)
     cos, sin = rope.tables(5000)
-    qkv = torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda").to(tdt)
+    qkv = qkv_rows(T, (hq + 2 * hkv) * d, g, tdt, layout)
     pos = torch.randint(0, 5000, (T,), generator=g, device="cuda")
     slots = torch.randperm(nb * 16, generator=g, device="cuda")[:T]
     slots[7] = -1
@@ -998,12 +1008,13 @@ def test_scheduled_decode_rejects_schedule_of_another_table_width():
 
 # ---------------------------------------------------------------- fused RoPE + fp8 append
 
+@pytest.mark.parametrize("layout", ("packed", "padded"))
 @pytest.mark.parametrize("dt", DTS)
-def test_rope_reshape_and_cache_fp8_bit_identical(dt):
+def test_rope_reshape_and_cache_fp8_bit_identical(dt, layout):
     """pkv_rope_reshape_and_cache_fp8 against the unfused path: Rope.rotate in
     the model dtype, then reshape_and_cache_fp8.  Rotated q, the e4m3 bytes
     and the scales must be identical bit for bit; a padding slot (-1) writes
-    q only."""
+    q only.  Both kernel forms (qkv_rows)."""
     from pagedkv.model import Rope
 
     tdt = TORCH_DT[dt]
@@ -1011,7 +1022,7 @@ def test_rope_reshape_and_cache_fp8_bit_identical(dt):
     T, hq, hkv, d, nb = 200, 14, 2, 64, 64
     rope = Rope(d, 1e6, "cuda", tdt)
     cos, sin = rope.tables(5000)
-    qkv = (3 * torch.randn((T, (hq + 2 * hkv) * d), generator=g, device="cuda")).to(tdt)
+    qkv = qkv_rows(T, (hq + 2 * hkv) * d, g, tdt, layout, mul=3.0)
     pos = torch.randint(0, 5000, (T,), generator=g, device="cuda")
     slots = torch.randperm(nb * 16, generator=g, device="cuda")[:T]
     slots[7] = -1
