@@ -73,9 +73,10 @@ def parse():
     ap.add_argument("--strong", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50, help="e2e: steps per timing window")
     ap.add_argument("--e2e-windows", type=int, default=5, help="e2e: timing windows (median reported)")
-    ap.add_argument("--e2e-chunks", default="1,2,4,5,5,4,2,1",
-                    help="e2e: layers per chunk (comma list summing to --layers); each chunk's copies "
-                         "overlap the other chunks' compute")
+    ap.add_argument("--e2e-chunks", default="",
+                    help="e2e: layers per chunk (comma list summing to --layers; default: "
+                         "DecodeStepGraph's, one layer a chunk); each chunk's copies overlap the "
+                         "other chunks' compute")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0,
@@ -244,15 +245,38 @@ def run_reference(args):
 
 # --------------------------------------------------------------- GPU arm
 
+def gpu_local_cpus(cuda_indices) -> list:
+    """Per CUDA device: the host cores the driver reports as local to it
+    (NVML CPU affinity, matched by UUID), or None where it cannot say."""
+    out = []
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+    except Exception:  # noqa: BLE001 - no NVML: no locality information
+        return [None for _ in cuda_indices]
+    words = (os.cpu_count() or 64) // 64 + 1
+    for uid in smi_ids(cuda_indices).split(","):
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(uid)
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+            out.append([64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1])
+        except Exception:  # noqa: BLE001
+            out.append(None)
+    return out
+
+
 def pin_rank_cpus(local: int, local_world: int) -> list[int]:
-    """Pin this process to its disjoint share of the host cores (torchrun
-    ranks of one node would otherwise contend for the same cores while they
-    enqueue launches and copies).  Returns the cores now allowed."""
+    """Pin this process to host cores near its GPU, disjoint from the other
+    local ranks' (torchrun ranks of one node would otherwise contend for the
+    same cores while they enqueue launches and copies), before any pinned
+    host buffer is allocated, so those land in the GPU's NUMA node.  Returns
+    the cores now allowed."""
     from pagedkv import workloads as W
 
     cpus = sorted(os.sched_getaffinity(0))
-    mine = W.rank_cpus(cpus, local, local_world)
-    if mine and local_world > 1:
+    mine = W.local_cpu_share(cpus, gpu_local_cpus(range(local_world)), local)
+    if mine:
         os.sched_setaffinity(0, mine)
     return sorted(os.sched_getaffinity(0))
 
@@ -343,6 +367,7 @@ def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    all_cpus = sorted(os.sched_getaffinity(0))
     cpus = pin_rank_cpus(local, local_world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -421,11 +446,15 @@ def run_ours(args):
     # (PagedKVCache.prepare_step + forward_layers per chunk).
     from pagedkv.graphs import DecodeStepGraph
 
-    sizes = [int(x) for x in args.e2e_chunks.split(",")]
-    if sum(sizes) != L:
+    from pagedkv.graphs import event_chunks
+
+    sizes = [int(x) for x in args.e2e_chunks.split(",")] if args.e2e_chunks else None
+    if sizes is not None and sum(sizes) != L:
         sizes = [L]
     seqs_all = [(i, 1) for i in range(B)]
     runner = DecodeStepGraph(kv, hqkv, hout, scale, chunks=sizes, max_blocks_per_seq=int(nblk.max()))
+    # the Python-issued pipeline waits on copy events: event_chunks' sizes
+    sizes = sizes or event_chunks(L)
 
     def e2e_step():
         runner.run(seqs_all)
@@ -491,6 +520,7 @@ def run_ours(args):
     meta_bytes = 4 * (B * runner.W + 2 * B + 1) + 8 * B
     h2d = hqkv.numel() * 2 + meta_bytes
     d2h = hout.numel() * 2
+    e2e_chunks, e2e_ready = [b - a for a, b in runner.bounds], runner.gated
     del kv, dqkv, hqkv, hout, runner
 
     # ---- the same job under strong scaling (BASELINE config 3's wording:
@@ -573,24 +603,30 @@ def run_ours(args):
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4),
                 "api": "pagedkv.graphs.DecodeStepGraph.run: PagedKVCache.step_arrays into pinned staging, "
-                       "one metadata copy, one CUDA-graph replay (per-chunk H2D of q|k|v, the decode "
-                       "schedule, one pkv_paged_decode_append_attention_layers call per chunk, per-chunk D2H)",
+                       "one metadata copy, one CUDA-graph replay (per-chunk H2D of q|k|v then a ready word, "
+                       "the decode schedule, one pkv_paged_decode_append_attention_layers call per chunk "
+                       "whose kernels wait on the chunk's ready word, per-chunk D2H)",
+                "chunks": e2e_chunks,
+                "ready_words": e2e_ready,
                 "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back, max over ranks",
                 "windows_ms_per_step": [round(x, 4) for x in win_ms],
-                "copies": f"pinned host buffers; per step: metadata, then q|k|v of 24 layers H2D in "
-                          f"chunks of {sizes} layers (one copy each) on a copy stream, outputs D2H per chunk "
+                "copies": f"pinned host buffers; per step: metadata, then q|k|v of {L} layers H2D in "
+                          "the chunks above (one copy each) on a copy stream, outputs D2H per chunk "
                           "on a second copy stream, overlapped with the step's own compute; the step ends "
                           "when its outputs are on the host",
                 "eager": {"ms_per_step": round(eager_ms, 4),
                           "value": round(total_bytes / (eager_ms * 1e-3) / 1e9, 2),
                           "api": "the same pipeline issued from Python: PagedKVCache.prepare_step + "
-                                 "forward_layers per chunk (host-bound)"},
-                "host_cpus_per_rank": len(cpus)},
+                                 "forward_layers per chunk (host-bound), chunks waiting on copy events",
+                          "chunks": sizes},
+                "host_cpus_per_rank": len(cpus),
+                "host_cpus_near_gpu": "NVML CPU affinity of the rank's GPU" if cpus != all_cpus else None},
         "strong": strong,
         "gpu_launches": (2 * L + 1) * args.steps,  # per timed step: schedule + (decode, merge) x 24
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:
+        os.sched_setaffinity(0, all_cpus)  # the CPU baseline runs on every core the job may use
         gbs, cores, sample, _, _ = cpu_sample(args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": cores,
                                 "kind": "port", "sample": sample}

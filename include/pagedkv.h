@@ -134,8 +134,8 @@ int pkv_paged_decode_append_attention_fp8_scheduled(
  * Chunked prefill over fp8 e4m3 pools on the tensor cores with no scratch:
  * the tcgen05 prefill kernel stages each key tile's e4m3 bytes and row
  * scales in shared memory, and two of its warps convert them into the fp16
- * tiles its MMAs read (value x scale, rounded to fp16 twice: the scale x 2^8
- * and the product), so no pass over the visible blocks writes a 16-bit copy
+ * tiles its MMAs read (value x scale as an fp32 product rounded once to
+ * fp16, as the scratch pass rounds it), so no pass over the visible blocks writes a 16-bit copy
  * to memory.  Same arguments and semantics as pkv_paged_prefill_attention_fp8
  * (which stays the CUDA-core kernel).  Serves fp16 queries (dtype
  * PKV_DTYPE_F16), head_dim 64, block_size 16, up to 4 KV heads, 16-byte
@@ -247,6 +247,16 @@ int pkv_paged_decode_append_attention_scheduled(
  * (a schedule built for the step serves them all; NULL: none).  Arguments
  * are checked for the first and the last layer before anything launches; on
  * a launch error the call returns it and the later layers are not issued.
+ * input_ready: NULL, or a 4-byte aligned device word.  Every layer's decode
+ * kernel waits until the word is nonzero before it reads q, k_new or v_new;
+ * the wait is bounded (about a second): on a timeout it sets
+ * PKV_FLAG_PIPELINE_TIMEOUT and the call's outputs are unspecified.  It is for inputs that a copy on
+ * another stream brings in: the copy stream sets the word after the data
+ * (a 4-byte copy from a host word holding 1, the word cleared before the
+ * data copy), and the call needs no event wait on that stream.  Such a
+ * wait between two launches of the chain would end their programmatic
+ * overlap (about 5 us per chain break on B200).  Only the tensor-core
+ * decode kernel serves it: other shapes return PKV_ERR_UNSUPPORTED.
  */
 int pkv_paged_decode_append_attention_layers(
     int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
@@ -256,7 +266,7 @@ int pkv_paged_decode_append_attention_layers(
     int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
     int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
     void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
-    const void* schedule);
+    const void* schedule, const int32_t* input_ready);
 
 /*
  * KV block migration between GPUs (one process per GPU).  Replaces the

@@ -545,7 +545,8 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
                                                   int block_size, float scale, int dtype,
                                                   void* workspace, size_t workspace_bytes,
                                                   int* err_flags, pkv_stream_t stream,
-                                                  const void* schedule) {
+                                                  const void* schedule,
+                                                  const int* input_ready = nullptr) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -553,6 +554,7 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
                       block_size, dtype);
   if (rc != PKV_OK) return rc;
   if (!context_lens || !k_new || !v_new) return PKV_ERR_NULL_POINTER;
+  if (input_ready && (reinterpret_cast<uintptr_t>(input_ready) & 3) != 0) return PKV_ERR_MISALIGNED;
   const int64_t kv_row = static_cast<int64_t>(n_kv_heads) * head_dim;
   if (k_new_row_stride < kv_row || v_new_row_stride < kv_row) return PKV_ERR_BAD_SHAPE;
   AttnArgs a{};
@@ -582,8 +584,11 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
   a.v_new = v_new;
   a.k_new_stride = k_new_row_stride;
   a.v_new_stride = v_new_row_stride;
+  a.input_ready = input_ready;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a)) {
+  const bool fast = g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a);
+  if (input_ready && !fast) return PKV_ERR_UNSUPPORTED;  // only the tensor-core kernel waits
+  if (fast) {
     if (!workspace) return PKV_ERR_NULL_POINTER;
     if (workspace_bytes < decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
       return PKV_ERR_WORKSPACE_TOO_SMALL;
@@ -815,7 +820,7 @@ int pkv_paged_decode_append_attention_layers(
     int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
     int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
     void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
-    const void* schedule) {
+    const void* schedule, const int32_t* input_ready) {
   if (n_layers < 0 || n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_layers == 0 || n_seqs == 0) return PKV_OK;
   if (!out || !q || !k_new || !v_new || !k_pools || !v_pools) return PKV_ERR_NULL_POINTER;
@@ -844,7 +849,7 @@ int pkv_paged_decode_append_attention_layers(
         o, out_row_stride, ql, q_row_stride, kn, vn, k_new_row_stride, v_new_row_stride, kp, vp,
         num_blocks, block_tables, block_table_stride, max_blocks_per_seq, context_lens, n_seqs,
         n_q_heads, n_kv_heads, head_dim, block_size, scale, dtype, workspace, workspace_bytes,
-        err_flags, stream, schedule);
+        err_flags, stream, schedule, input_ready);
   };
   // the shared arguments and the last layer's pointers are checked before
   // the first launch, so a bad call issues nothing

@@ -108,6 +108,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
   return true;
 }
+// Bounded wait for a device word that another agent (a copy engine) sets
+// nonzero: acquire loads at GPU scope, a short sleep between them; gives up
+// after ~2^31 SM cycles (about a second) and returns false.
+__device__ __forceinline__ bool wait_word_nonzero(const int* w) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(w) : "memory");
+  if (v != 0) return true;
+  const long long t0 = clock64();
+  do {
+    if (clock64() - t0 > (1ll << 31)) return false;
+    __nanosleep(256);
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(w) : "memory");
+  } while (v == 0);
+  return true;
+}
 
 // ----------------------------------------------------------------------------
 // TMA: 3-D tiled tensor load global -> shared, completion on an mbarrier

@@ -134,6 +134,8 @@ struct DecodeParams {
   // lengths and each CTA's block ids in rows of sched_rows
   const int32_t* sched;
   int sched_rows;
+  // nonzero once q / k_new / v_new are in memory (NULL: they already are)
+  const int* input_ready;
 };
 
 // Decode schedule (int32): kSchedHdr header words {n_seqs, total blocks,
@@ -499,6 +501,14 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
   //                   16-dim tile, B = P^T from C via movmatrix.trans,
   //                   C holds dims {16mt+g, 16mt+g+8} x heads {2t, 2t+1}.
   pdl_wait();
+  if (p.input_ready != nullptr) {
+    // inputs that a copy on another stream brings in: one lane waits for the
+    // word the copy engine sets after them, then the warp reads them
+    int ok = 1;
+    if (lane == 0) ok = wait_word_nonzero(p.input_ready);
+    if (!__shfl_sync(0xffffffffu, ok, 0) && lane == 0) raise_flag(p.err, PKV_FLAG_PIPELINE_TIMEOUT);
+    __syncwarp();
+  }
   const int h = pwarp;
   const int g = lane >> 2, t = lane & 3;
   // fp8 conversion on the integer pipes (fp16) or by cvt (bf16)
@@ -1267,6 +1277,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.v_scale = a.v_scale;
   p.sched = static_cast<const int32_t*>(a.schedule);
   p.sched_rows = a.schedule != nullptr ? sched_rows_for(a.n_seqs, a.max_blocks, grid) : 0;
+  p.input_ready = a.input_ready;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid / pipes_for(nkv));

@@ -71,6 +71,9 @@ struct AttnArgs {
   const float* v_scale = nullptr;
   // decode: the step's schedule built by pkv_decode_schedule (NULL = none)
   const void* schedule = nullptr;
+  // decode (tensor-core path): a device word the kernel waits on, bounded,
+  // until it is nonzero before reading q / k_new / v_new (NULL = none)
+  const int* input_ready = nullptr;
 };
 cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,
                                          int64_t v_stride, void* k_pool, void* v_pool,

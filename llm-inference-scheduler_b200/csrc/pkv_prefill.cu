@@ -206,6 +206,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched with programmatic serialization: the set-up above (work item,
+  // barriers, tensor memory; it reads only the step's metadata, which no
+  // preceding kernel of the chain writes) overlaps the kernel before this
+  // one.  Q, the pools (the append before this kernel writes them) and out
+  // are touched only after the wait.  The trigger lets the next kernel
+  // launch once every CTA of this grid has started.
+  if (tid == 0) pdl_trigger();
+  pdl_wait();
   const uint32_t tbase = *tmem_slot;
   const int s = sched[1], qp = sched[2], h = sched[3];
 
@@ -685,9 +693,17 @@ cudaError_t launch_prefill_fast(const AttnArgs& a, const CUtensorMap* qmap, cons
   p.k_scale = a.k_scale;
   p.v_scale = a.v_scale;
   p.n_kv_heads = a.n_kv_heads;
-  const dim3 grid(static_cast<unsigned>(p.n_pairs * a.n_q_heads * a.n_seqs));
-  kern<<<grid, kPfThreads, smem, stream>>>(*qmap, *kmap, *vmap, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.n_pairs * a.n_q_heads * a.n_seqs));
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, *qmap, *kmap, *vmap, p);
 }
 
 }  // namespace pkv

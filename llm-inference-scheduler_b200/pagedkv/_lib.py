@@ -87,7 +87,7 @@ SIGNATURES: dict = {
     "pkv_paged_decode_append_attention_layers": (_I, [_I, _P, _I64, _I64, _P, _I64, _I64, _P, _P,
                                                       _I64, _I64, _I64, _P, _P, _I64, _I, _P, _I64,
                                                       _I, _P, _I, _I, _I, _I, _I, _F, _I, _P, _SZ,
-                                                      _P, _P, _P]),
+                                                      _P, _P, _P, _P]),
 }
 
 

@@ -576,14 +576,18 @@ class PagedKVCache:
 
     def forward_layers(self, first_layer: int, q: torch.Tensor, k_new: torch.Tensor,
                        v_new: torch.Tensor, meta: StepMetadata, scale: float,
-                       out: torch.Tensor | None = None, advance: bool = True) -> torch.Tensor:
+                       out: torch.Tensor | None = None, advance: bool = True,
+                       input_ready: torch.Tensor | None = None) -> torch.Tensor:
         """forward_layer for the n consecutive layers first_layer ..
         first_layer + n - 1 at once, with layer-major inputs: q [n, T, Hq, D],
         k_new / v_new [n, T, Hkv, D] -> out [n, T, Hq, D].  A decode-only step
         over 16-bit pools is one C call for the whole run
         (pkv_paged_decode_append_attention_layers: the fused append + decode
         and the merge of every layer); other steps run forward_layer layer by
-        layer.  The results are those of forward_layer either way."""
+        layer.  The results are those of forward_layer either way.
+        input_ready (one-call form only): a one-element int32 device tensor
+        that the kernels wait on, bounded, until a copy on another stream has
+        set it nonzero after q / k_new / v_new."""
         mgr = self.mgr
         n = q.shape[0]
         last = first_layer + n
@@ -600,10 +604,13 @@ class PagedKVCache:
                 plan = meta.layers_plan = ops.DecodeAppendLayersPlan(
                     meta.block_tables, meta.context_lens, scale, ws, mgr.err,
                     schedule=self._step_schedule(meta, q[0]))
-            plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out)
+            plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out,
+                 input_ready=input_ready)
             if advance and last == mgr.num_layers:
                 self._advance(meta)
             return out
+        if input_ready is not None:
+            raise ValueError("pagedkv: input_ready serves decode-only steps over 16-bit pools")
         for i in range(n):
             self.forward_layer(first_layer + i, q[i], k_new[i], v_new[i], meta, scale, out=out[i],
                                advance=advance)

@@ -60,7 +60,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 from .block_manager import PagedKVCache, StepMetadata
 from .model import PagedQwen2Model, SequenceForwardInfo
 
@@ -405,12 +405,20 @@ class DecodeStepGraph:
     pinned staging buffer, padded to R rows), copies it with one H2D copy and
     launches one graph holding:
     * the decode schedule build;
-    * per chunk of layers, on a copy stream, the H2D copy of the chunk's rows;
-    * per chunk, once its rows have landed, one
-      pkv_paged_decode_append_attention_layers call (the fused append + decode
-      and the merge of each of its layers);
+    * per chunk of layers, on a copy stream, the H2D copy of the chunk's rows,
+      then a 4-byte copy that sets the chunk's ready word (cleared at the
+      step's start);
+    * per chunk, one pkv_paged_decode_append_attention_layers call (the fused
+      append + decode and the merge of each of its layers) whose kernels wait,
+      bounded, for the chunk's ready word before reading its rows.  An event
+      wait on the copy stream there would end the programmatic overlap
+      between the chunk's first launch and the one before it (about 5 us a
+      chunk); the ready word keeps the whole step one launch chain;
     * per chunk, on a second copy stream, the D2H copy of the chunk's outputs.
-    Small first and last chunks shorten the pipeline's fill and drain.
+    By default a chunk is one layer: the pipeline's fill is one layer's copy
+    in and its drain one layer's copy out.  Where the tensor-core decode does
+    not serve the shapes (the ready word is then refused), the chunks wait on
+    copy events instead, in event_chunks' sizes unless chunks were given.
 
     A step of B <= R sequences (one new token each, host rows 0 .. B-1) pads
     rows B .. R-1: context length 0, slot -1, so they read and write no KV
@@ -439,7 +447,8 @@ class DecodeStepGraph:
         if not (host_qkv.is_pinned() and host_out.is_pinned() and host_qkv.is_contiguous()
                 and host_out.is_contiguous()):
             raise ValueError("pagedkv: host_qkv / host_out must be contiguous pinned host tensors")
-        chunks = tuple(chunks or _default_chunks(L))
+        self._chunks_given = chunks is not None
+        chunks = tuple(chunks or [1] * L)  # ready words: a chunk boundary costs nothing
         if sum(chunks) != L or min(chunks) <= 0:
             raise ValueError(f"pagedkv: chunks {chunks} must be positive and sum to {L}")
         self.kv, self.scale = kv_cache, float(scale)
@@ -454,6 +463,10 @@ class DecodeStepGraph:
         self.dev_out = torch.empty((L, R, hq, D), dtype=mgr.dtype, device=dev)
         self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         self.workspace = kv_cache.decode_workspace(R, hq, D)
+        # per chunk: nonzero once its rows are on the device (set by the copy stream)
+        self.ready = torch.zeros(len(self.bounds), dtype=torch.int32, device=dev)
+        self._one = torch.ones(1, dtype=torch.int32).pin_memory()
+        self.gated = True
         self._alloc()
 
     def _layout(self) -> dict:
@@ -489,28 +502,35 @@ class DecodeStepGraph:
         hkv, q = mgr.num_kv_heads, self.dev_qkv
         # the input copies first: they depend on nothing in the step and run
         # beside the schedule build
+        if self.gated:
+            self.ready.zero_()
         self.h2d.wait_stream(cur)
         ev_in = [torch.cuda.Event() for _ in self.bounds]
         with torch.cuda.stream(self.h2d):
-            for (a, b), ev in zip(self.bounds, ev_in):
+            for c, ((a, b), ev) in enumerate(zip(self.bounds, ev_in)):
                 q[a:b].copy_(self.host_qkv[a:b], non_blocking=True)
-                ev.record(self.h2d)
+                if self.gated:
+                    self.ready[c:c + 1].copy_(self._one, non_blocking=True)
+                else:
+                    ev.record(self.h2d)
         meta.decode_schedule = ops.build_decode_schedule(
             self.schedule, meta.block_tables, meta.context_lens, mgr.num_blocks, self.hq,
             mgr.num_kv_heads, mgr.head_dim, mgr.dtype, err=mgr.err)
         meta.layers_plan = ops.DecodeAppendLayersPlan(meta.block_tables, meta.context_lens, self.scale,
                                                       self.workspace, mgr.err,
                                                       schedule=meta.decode_schedule)
-        for (a, b), ev in zip(self.bounds, ev_in):
-            cur.wait_event(ev)
+        for c, ((a, b), ev) in enumerate(zip(self.bounds, ev_in)):
+            if not self.gated:
+                cur.wait_event(ev)
             kv.forward_layers(a, q[a:b, :, :self.hq], q[a:b, :, self.hq:self.hq + hkv],
                               q[a:b, :, self.hq + hkv:], meta, self.scale, out=self.dev_out[a:b],
-                              advance=False)
+                              advance=False, input_ready=self.ready[c:c + 1] if self.gated else None)
             done = torch.cuda.Event()
             done.record(cur)
             self.d2h.wait_event(done)
             with torch.cuda.stream(self.d2h):
                 self.host_out[a:b].copy_(self.dev_out[a:b], non_blocking=True)
+        cur.wait_stream(self.h2d)
         cur.wait_stream(self.d2h)
 
     def capture(self) -> None:
@@ -525,8 +545,19 @@ class DecodeStepGraph:
         cur = torch.cuda.current_stream(mgr.device)
         side = torch.cuda.Stream(mgr.device)
         side.wait_stream(cur)
-        with torch.cuda.stream(side):
-            self._step()
+        try:
+            with torch.cuda.stream(side):
+                self._step()
+        except _lib.PagedKVError as e:
+            if not self.gated or e.status != _lib.ERR_UNSUPPORTED:
+                raise
+            torch.cuda.synchronize(mgr.device)
+            self.gated = False  # shapes outside the tensor-core decode: event waits
+            if not self._chunks_given:
+                ch = event_chunks(self.L)
+                self.bounds = [(sum(ch[:i]), sum(ch[:i + 1])) for i in range(len(ch))]
+            with torch.cuda.stream(side):
+                self._step()
         cur.wait_stream(side)
         g = torch.cuda.CUDAGraph()
         # thread-local capture: other threads of the process (a process
@@ -575,13 +606,16 @@ class DecodeStepGraph:
                 kv._len[s_id] = p + 1
 
 
-def _default_chunks(n_layers: int) -> list[int]:
-    """Chunks of layers for the copy pipeline (24 layers: 1, 2, 4, 5, 5, 4, 2,
-    1).  Small first and last chunks shorten the fill (first copy in) and the
-    drain (last copy out).  Every chunk boundary costs the first decode of the
-    chunk its overlap with the kernel before it (it waits on a copy event), so
-    finer chunks that would track the host-to-device rate more closely (1, 1,
-    2, 3, 4, 5, 5, 2, 1) measured slower: 0.826 against 0.810 ms per step."""
+def event_chunks(n_layers: int) -> list[int]:
+    """Chunks of layers for a copy pipeline whose chunks wait on copy events
+    (24 layers: 1, 2, 4, 5, 5, 4, 2, 1).  Small first and last chunks shorten
+    the fill (first copy in) and the drain (last copy out).  Every chunk
+    boundary costs the first decode of the chunk its overlap with the kernel
+    before it (it waits on a copy event), so finer chunks that would track the
+    host-to-device rate more closely (1, 1, 2, 3, 4, 5, 5, 2, 1) measured
+    slower: 0.826 against 0.810 ms per step.  With ready words (no event
+    waits) a boundary costs nothing and DecodeStepGraph takes one layer per
+    chunk."""
     head, tail = [1, 2, 4], [4, 2, 1]
     mid = n_layers - sum(head) - sum(tail)
     if mid < 0:

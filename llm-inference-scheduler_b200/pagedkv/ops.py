@@ -654,7 +654,10 @@ class DecodeAppendLayersPlan:
             raise ValueError(f"pagedkv: `{name}` must be [layers, rows, heads, head_dim]")
         return t.stride(0)
 
-    def __call__(self, q, k_new, v_new, k_pools, v_pools, out) -> torch.Tensor:
+    def __call__(self, q, k_new, v_new, k_pools, v_pools, out, input_ready=None) -> torch.Tensor:
+        """input_ready: None, or a one-element int32 device tensor that the
+        kernels wait on (bounded) until it is nonzero before reading q,
+        k_new and v_new (set by a copy on another stream after them)."""
         n = q.shape[0]
         if k_new.shape[0] != n or v_new.shape[0] != n or out.shape[0] != n or \
                 k_pools.shape[0] != n or v_pools.shape[0] != n:
@@ -679,12 +682,17 @@ class DecodeAppendLayersPlan:
                           q_rs, kn, vn, self._layer_stride(k_new, "k_new"), kn_rs, vn_rs, kp, vp,
                           k_pools.stride(0) * k_pools.element_size(), nb, bt, bt_s, mb, cl, B, hq,
                           hkv, d, bs, sc, dt, wsp, wsb, errp, st,
-                          None if self.schedule is None else self.schedule.data_ptr()]
+                          None if self.schedule is None else self.schedule.data_ptr(), None]
             self._key = key
         a = self._args
         a[0], a[1], a[4], a[7], a[8], a[12], a[13] = (n, out.data_ptr(), q.data_ptr(), k_new.data_ptr(),
                                                       v_new.data_ptr(), k_pools.data_ptr(),
                                                       v_pools.data_ptr())
+        if input_ready is not None:
+            _cuda(input_ready, "input_ready")
+            if input_ready.dtype != torch.int32 or input_ready.numel() != 1:
+                raise ValueError("pagedkv: input_ready must be one int32 element on the device")
+        a[-1] = None if input_ready is None else input_ready.data_ptr()
         rc = self._fn(*a)
         if rc:
             _lib.check(rc, "pkv_paged_decode_append_attention_layers")

@@ -140,6 +140,23 @@ def rank_cpus(cpus, local_rank: int, local_world: int) -> list[int]:
     return cpus[start:start + base + (1 if local_rank < extra else 0)]
 
 
+def local_cpu_share(allowed, gpu_cpus, local_rank: int) -> list[int]:
+    """This rank's host cores, near its GPU: the allowed cores that the driver
+    reports as local to the rank's GPU (gpu_cpus[r]: the cores of local rank
+    r's GPU, or None), split disjointly (rank_cpus) among the local ranks
+    whose GPUs report the same allowed set.  Pinned host buffers that the
+    rank allocates afterwards then sit in its GPU's NUMA node.  A rank whose
+    GPU reports no allowed core gets its rank_cpus share of all allowed
+    cores."""
+    allowed = sorted(set(int(c) for c in allowed))
+    local = [sorted(set(s or ()) & set(allowed)) for s in gpu_cpus]
+    mine = local[local_rank]
+    if not mine:
+        return rank_cpus(allowed, local_rank, len(gpu_cpus))
+    peers = [r for r, s in enumerate(local) if s == mine]
+    return rank_cpus(mine, peers.index(local_rank), len(peers))
+
+
 def config4_layout(seed: int = 4, n_seqs: int = 16, chunk: int = 512, prior_hi: int = 4096,
                    shared: int = 48):
     """Config 4: n_seqs chunks of `chunk` queries over a `shared`-token radix

@@ -535,10 +535,73 @@ def test_decode_layers_abi_rejects_overlapping_pools():
             L, out.data_ptr(), q.stride(0), 14 * 64, q.data_ptr(), q.stride(0), 14 * 64,
             kn.data_ptr(), kn.data_ptr(), kn.stride(0), 128, 128, kc.data_ptr(), vc.data_ptr(), stride,
             nb, tabs.data_ptr(), 1, 1, ctx.data_ptr(), B, 14, 2, 64, 16, 0.125, _lib.F16,
-            ws.data_ptr(), ws.numel(), None, torch.cuda.current_stream().cuda_stream, None)
+            ws.data_ptr(), ws.numel(), None, torch.cuda.current_stream().cuda_stream, None, None)
         assert rc == want, (stride, rc)
     torch.cuda.synchronize()
     assert bool((out == 7.0).all()) and not kc.any()
+
+
+def test_decode_layers_input_ready_word():
+    """forward_layers with input_ready (the word a copy stream sets after the
+    inputs; the kernels wait for it before reading them):
+    * a set word: outputs and pools bit-identical to the call without it;
+    * a word that nothing sets: the bounded wait runs out (about a second)
+      and the call flags PKV_FLAG_PIPELINE_TIMEOUT (its outputs are then
+      unspecified); the next call on the same context is clean and exact;
+    * shapes outside the tensor-core decode (fp32) refuse it before launching."""
+    from pagedkv import _lib
+
+    rng = np.random.default_rng(47)
+    L, nb = 2, 512
+    ctx = rng.integers(1, 600, size=21)
+    pk = rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32)
+    pv = rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32)
+    qkv = rng.standard_normal((L, len(ctx), 18, 64), dtype=np.float32)
+
+    def setup(tdt):
+        m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=tdt)
+        m.k_cache.copy_(torch.from_numpy(pk).to(tdt))
+        m.v_cache.copy_(torch.from_numpy(pv).to(tdt))
+        kv = PagedKVCache(m)
+        o = 0
+        for s, c in enumerate(ctx):
+            n = (int(c) + 15) // 16
+            kv.add_sequence(s, list(range(o, o + n)), int(c) - 1)
+            o += n
+        x = torch.from_numpy(qkv).to(tdt).cuda()
+        meta = kv.prepare_step([(s, 1) for s in range(len(ctx))])
+        return m, kv, x, meta
+
+    def call(kv, x, meta, ready=None, layers=L):
+        return kv.forward_layers(0, x[:layers, :, :14], x[:layers, :, 14:16], x[:layers, :, 16:18],
+                                 meta, 0.125, advance=False, input_ready=ready)
+
+    m1, kv1, x1, meta1 = setup(torch.float16)
+    m2, kv2, x2, meta2 = setup(torch.float16)
+    set_word = torch.ones(1, dtype=torch.int32, device="cuda")
+    o1 = call(kv1, x1, meta1, set_word)
+    o2 = call(kv2, x2, meta2)
+    torch.cuda.synchronize()
+    m1.check_errors()
+    assert torch.equal(o1, o2)
+    assert torch.equal(m1.k_cache, m2.k_cache) and torch.equal(m1.v_cache, m2.v_cache)
+    # a word nothing sets: one layer, so one bounded wait
+    never = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o3 = call(kv1, x1, meta1, never, layers=1)
+    torch.cuda.synchronize()
+    flags = int(m1.err.item())
+    assert flags & _lib.FLAG_PIPELINE_TIMEOUT, flags
+    assert o3.shape == o2[:1].shape
+    m1.err.zero_()
+    o4 = call(kv1, x1, meta1)
+    torch.cuda.synchronize()
+    m1.check_errors()
+    assert torch.equal(o4, o2)
+    # fp32: the CUDA-core decode serves it, which does not wait on a word
+    m5, kv5, x5, meta5 = setup(torch.float32)
+    with pytest.raises(_lib.PagedKVError) as e:
+        call(kv5, x5, meta5, set_word)
+    assert e.value.status == _lib.ERR_UNSUPPORTED
 
 
 # ---------------------------------------------------------------- fused RoPE + append

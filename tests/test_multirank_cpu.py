@@ -103,3 +103,30 @@ def test_rank_cpu_shares_are_disjoint_and_cover_the_node(n_cpus, world):
             assert s == list(range(s[0], s[0] + len(s)))
     else:
         assert all(len(s) == 1 for s in shares)
+
+
+def test_local_cpu_share_keeps_ranks_near_their_gpu():
+    """Two NUMA nodes of 16 cores, four GPUs each: every rank's cores are on
+    its GPU's node, the ranks of a node split it disjointly; a GPU reporting
+    no allowed core falls back to a share of all allowed cores; a
+    restricted affinity is respected."""
+    import sys
+
+    sys.path.insert(0, PKG_ROOT)
+    from pagedkv import workloads as W
+
+    node0, node1 = list(range(0, 16)), list(range(16, 32))
+    gpu_cpus = [node0] * 4 + [node1] * 4
+    allowed = list(range(32))
+    shares = [W.local_cpu_share(allowed, gpu_cpus, r) for r in range(8)]
+    for r, s in enumerate(shares):
+        assert s and set(s) <= set(gpu_cpus[r])
+    assert sorted(c for s in shares[:4] for c in s) == node0
+    assert sorted(c for s in shares[4:] for c in s) == node1
+    # one GPU, whole node
+    assert W.local_cpu_share(allowed, [node1], 0) == node1
+    # the driver reports nothing (or nothing allowed): plain share of the allowed cores
+    assert W.local_cpu_share(allowed, [None, None], 1) == W.rank_cpus(allowed, 1, 2)
+    assert W.local_cpu_share(list(range(8)), [node1], 0) == list(range(8))
+    # affinity restricted to part of a node
+    assert W.local_cpu_share(list(range(4, 12)), [node0, node0], 0) == [4, 5, 6, 7]
