@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--batch", type=int, default=256, help="sequences per GPU (weak) or in total (--strong)")
     ap.add_argument("--strong", action="store_true")
+    ap.add_argument("--per-layer-calls", action="store_true",
+                    help="decode: one call per layer (decode + merge each) instead of one "
+                         "multi-layer call whose layers chain")
     ap.add_argument("--e2e-steps", type=int, default=50, help="e2e: steps per timing window")
     ap.add_argument("--e2e-windows", type=int, default=5, help="e2e: timing windows (median reported)")
     ap.add_argument("--e2e-chunks", default="",
@@ -287,7 +290,8 @@ class DecodeRun:
     step's q / new K / new V per layer, and the bound launches of one step
     (schedule build, then one fused append + decode call per layer)."""
 
-    def __init__(self, batch: int, strong: bool, rank: int, world: int, L: int, dev):
+    def __init__(self, batch: int, strong: bool, rank: int, world: int, L: int, dev,
+                 per_layer_calls: bool = False):
         import numpy as np
         import torch
 
@@ -313,28 +317,38 @@ class DecodeRun:
         self.out = torch.empty_like(self.q)
         self.tabs = torch.from_numpy(self.tabs_np).to(dev)
         self.ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
-        self.ws = ops.new_decode_workspace(B, 14, 64, dev)
         self.err = ops.new_error_flags(dev)
         self.sched = ops.new_decode_schedule(B, self.tabs.shape[1], dev)
         self.build_sched = ops.bind_decode_schedule(self.sched, self.tabs, self.ctx_d, nb, 14, 2, 64, dt,
                                                     err=self.err)
-        self.decodes = [ops.bind_paged_decode_append_attention(
-            self.q[l], self.kn[l], self.vn[l], mgr.k_pool[l], mgr.v_pool[l], self.tabs, self.ctx_d,
-            self.scale, self.ws, self.out[l], self.err, schedule=self.sched) for l in range(L)]
+        if per_layer_calls:
+            # one pkv_paged_decode_append_attention_scheduled call per layer
+            self.ws = ops.new_decode_workspace(B, 14, 64, dev)
+            self.decodes = [ops.bind_paged_decode_append_attention(
+                self.q[l], self.kn[l], self.vn[l], mgr.k_pool[l], mgr.v_pool[l], self.tabs, self.ctx_d,
+                self.scale, self.ws, self.out[l], self.err, schedule=self.sched) for l in range(L)]
+        else:
+            # one pkv_paged_decode_append_attention_layers call for all layers,
+            # a split-K set per layer: the layers' decode kernels chain and one
+            # merge launch follows them
+            self.ws = ops.new_decode_workspace(B, 14, 64, dev, layers=L)
+            plan = ops.DecodeAppendLayersPlan(self.tabs, self.ctx_d, self.scale, self.ws, self.err,
+                                              schedule=self.sched)
+            self.decodes = [lambda: plan(self.q, self.kn, self.vn, mgr.k_cache, mgr.v_cache, self.out)]
         self.dec_bytes = W.decode_bytes(ctx)
         self.app_bytes = W.append_bytes(B)
         self.step_bytes = L * (self.dec_bytes + self.app_bytes)
 
     def step(self):
-        """One decode step: the schedule, then one call per layer (the decode
-        kernel appends the step's token itself, then its merge)."""
+        """One decode step: the schedule, then the layers' fused append +
+        decode and their merge (one multi-layer call, or one call per layer)."""
         self.build_sched()
         for f in self.decodes:
             f()
 
     def calls(self):
-        """The step's 24 calls without the schedule build (it stays valid:
-        the lengths and tables do not change)."""
+        """The step's calls without the schedule build (it stays valid: the
+        lengths and tables do not change)."""
         for f in self.decodes:
             f()
 
@@ -381,7 +395,7 @@ def run_ours(args):
             dist.barrier(device_ids=[local])
 
     L = args.layers
-    R = DecodeRun(args.batch, args.strong, rank, world, L, dev)
+    R = DecodeRun(args.batch, args.strong, rank, world, L, dev, per_layer_calls=args.per_layer_calls)
     B, ctx, nblk, mgr, scale, dt = R.B, R.ctx, R.nblk, R.mgr, R.scale, R.dt
 
     for _ in range(args.warmup):
@@ -530,7 +544,7 @@ def run_ours(args):
         if world == 1:
             strong = {"same_as_weak": True}
         else:
-            S = DecodeRun(args.batch, True, rank, world, L, dev)
+            S = DecodeRun(args.batch, True, rank, world, L, dev, per_layer_calls=args.per_layer_calls)
             for _ in range(args.warmup):
                 S.step()
             torch.cuda.synchronize()
@@ -596,9 +610,12 @@ def run_ours(args):
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic_from_profiles(), "bytes_per_launch": call_bytes,
                      "avg_launch_ms": round(dec_ms0, 5),
-                     "timing": "rank 0; CUDA events around --steps rounds of the 24 fused append+decode "
-                               "calls back to back (the step without its schedule build), / (steps x 24); "
-                               "a call is the decode kernel plus its split-K merge"},
+                     "timing": ("rank 0; CUDA events around --steps rounds of the 24 fused append+decode "
+                                "calls back to back (the step without its schedule build), / (steps x 24); "
+                                "a call is the decode kernel plus its split-K merge") if args.per_layer_calls
+                               else ("rank 0; CUDA events around --steps rounds of the step's multi-layer call "
+                                     "(24 chained decode kernels, then one merge launch for all layers; the "
+                                     "step without its schedule build), / (steps x 24)")},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4),
@@ -622,7 +639,9 @@ def run_ours(args):
                 "host_cpus_per_rank": len(cpus),
                 "host_cpus_near_gpu": "NVML CPU affinity of the rank's GPU" if cpus != all_cpus else None},
         "strong": strong,
-        "gpu_launches": (2 * L + 1) * args.steps,  # per timed step: schedule + (decode, merge) x 24
+        # per timed step: the schedule, then (decode, merge) per layer, or the
+        # chained decodes and one merge launch
+        "gpu_launches": ((2 * L + 1) if args.per_layer_calls else (L + 2)) * args.steps,
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:

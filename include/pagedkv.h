@@ -243,8 +243,16 @@ int pkv_paged_decode_append_attention_scheduled(
  *   k_new, v_new : layer l at + l * new_layer_stride elements;
  *   k_pools, v_pools : layer l's pool at + l * pool_layer_stride_bytes bytes
  *                  (the [num_layers][num_blocks][block_size][Hkv][D] caches).
- * Tables, lengths, scale, workspace and schedule are shared by the layers
- * (a schedule built for the step serves them all; NULL: none).  Arguments
+ * Tables, lengths, scale and schedule are shared by the layers (a schedule
+ * built for the step serves them all; NULL: none).  Workspace: with
+ * workspace_bytes >= n_layers x pkv_decode_workspace_bytes (one split-K set
+ * per layer, layer l's at l x that size), the layers chain on the
+ * tensor-core path: each later layer's decode kernel starts on the SMs the
+ * previous layer's tail frees (it waits for its predecessor only at its
+ * end; nothing it reads is written by the layers before it), and one merge
+ * launch after the last decode covers every layer.  With a single set, every
+ * layer's decode is followed by its own merge.  The results are the same
+ * bits either way.  Arguments
  * are checked for the first and the last layer before anything launches; on
  * a launch error the call returns it and the later layers are not issued.
  * input_ready: NULL, or a 4-byte aligned device word.  Every layer's decode

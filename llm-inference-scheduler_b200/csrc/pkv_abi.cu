@@ -546,7 +546,8 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
                                                   void* workspace, size_t workspace_bytes,
                                                   int* err_flags, pkv_stream_t stream,
                                                   const void* schedule,
-                                                  const int* input_ready = nullptr) {
+                                                  const int* input_ready = nullptr,
+                                                  const LayerChain* chain = nullptr) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -585,9 +586,11 @@ static int pkv_paged_decode_append_attention_impl(void* out, int64_t out_row_str
   a.k_new_stride = k_new_row_stride;
   a.v_new_stride = v_new_row_stride;
   a.input_ready = input_ready;
+  a.chain = chain;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fast = g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a);
-  if (input_ready && !fast) return PKV_ERR_UNSUPPORTED;  // only the tensor-core kernel waits
+  // only the tensor-core kernel waits on a word or chains layers
+  if ((input_ready || chain) && !fast) return PKV_ERR_UNSUPPORTED;
   if (fast) {
     if (!workspace) return PKV_ERR_NULL_POINTER;
     if (workspace_bytes < decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
@@ -866,6 +869,31 @@ int pkv_paged_decode_append_attention_layers(
                   block_size, dtype);
   if (rc != PKV_OK) return rc;
   if (!context_lens) return PKV_ERR_NULL_POINTER;
+  // A workspace of one split-K set per layer chains the layers: the decode
+  // kernels run back to back, each later one waiting for its predecessor only
+  // at its end (so it starts on the SMs the previous layer's tail frees), and
+  // one merge launch covers every layer at the end.  Otherwise each layer's
+  // decode is followed by its own merge.
+  const size_t ws1 = decode_workspace_bytes(n_seqs, n_q_heads, head_dim);
+  if (n_layers > 1 && workspace && ws1 > 0 && workspace_bytes / static_cast<size_t>(n_layers) >= ws1) {
+    LayerChain ch{0, 0, n_layers, out, out_layer_stride, workspace, static_cast<int64_t>(ws1)};
+    for (int l = 0; l < n_layers; ++l) {
+      ch.defer_wait = l > 0;
+      ch.merge = l == n_layers - 1;
+      void* o = const_cast<void*>(at(out, l * out_layer_stride * es));
+      void* wsl = static_cast<uint8_t*>(workspace) + static_cast<size_t>(l) * ws1;
+      rc = pkv_paged_decode_append_attention_impl(
+          o, out_row_stride, at(q, l * q_layer_stride * es), q_row_stride,
+          at(k_new, l * new_layer_stride * es), at(v_new, l * new_layer_stride * es), k_new_row_stride,
+          v_new_row_stride, const_cast<void*>(at(k_pools, l * pool_layer_stride_bytes)),
+          const_cast<void*>(at(v_pools, l * pool_layer_stride_bytes)), num_blocks, block_tables,
+          block_table_stride, max_blocks_per_seq, context_lens, n_seqs, n_q_heads, n_kv_heads,
+          head_dim, block_size, scale, dtype, wsl, ws1, err_flags, stream, schedule, input_ready, &ch);
+      if (rc == PKV_ERR_UNSUPPORTED && l == 0 && !input_ready) break;  // not the tensor-core path
+      if (rc != PKV_OK) return rc;
+      if (l == n_layers - 1) return PKV_OK;
+    }
+  }
   for (int l = 0; l < n_layers; ++l) {
     rc = layer_call(l);
     if (rc != PKV_OK) return rc;

@@ -136,6 +136,16 @@ struct DecodeParams {
   int sched_rows;
   // nonzero once q / k_new / v_new are in memory (NULL: they already are)
   const int* input_ready;
+  // 1: nothing this launch reads is written by the kernels just before it
+  // (a later layer of one multi-layer call, with its own workspace): skip
+  // griddepcontrol.wait before the main loop and wait at the end instead, so
+  // the grid starts on SMs the previous layer's tail frees and still
+  // completes after it
+  int defer_wait;
+  // merge over layers (blockIdx.y): out advances by out_layer_stride
+  // elements, the partials by ws_layer_stride bytes per layer
+  int64_t out_layer_stride;
+  int64_t ws_layer_stride;
 };
 
 // Decode schedule (int32): kSchedHdr header words {n_seqs, total blocks,
@@ -343,6 +353,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       // a schedule built for another batch or grid: do nothing
       if (tid == 0 && vcta == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
       if (tid == 0) pdl_trigger();
+      if (p.defer_wait) pdl_wait();
       return;
     }
     __syncthreads();
@@ -378,7 +389,10 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
     fence_barrier_init();
   }
   __syncthreads();
-  if (!active) return;
+  if (!active) {
+    if (p.defer_wait) pdl_wait();
+    return;
+  }
 
   const int r0 = vcta * per;
   const int r1 = min(r0 + per, total);
@@ -426,7 +440,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
           prefetch_l2(p.k_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
           prefetch_l2(p.v_pool + static_cast<int64_t>(id) * (nkv * tile_bytes), nkv * tile_bytes);
         }
-        pdl_wait();  // the pool may still be written by the preceding kernel
+        if (!p.defer_wait) pdl_wait();  // the pool may still be written by the preceding kernel
         waited = true;
       }
       const int n = min(32, r1 - b0);
@@ -489,6 +503,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         }
       }
     }
+    if (p.defer_wait) pdl_wait();  // complete only after the kernel before this one
     return;
   }
 
@@ -500,7 +515,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
   //   O^T += V^T P^T: A = V^T (16 dims x 16 tokens, ldmatrix.trans) per
   //                   16-dim tile, B = P^T from C via movmatrix.trans,
   //                   C holds dims {16mt+g, 16mt+g+8} x heads {2t, 2t+1}.
-  pdl_wait();
+  if (!p.defer_wait) pdl_wait();
   if (p.input_ready != nullptr) {
     // inputs that a copy on another stream brings in: one lane waits for the
     // word the copy engine sets after them, then the warp reads them
@@ -906,6 +921,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
       for (int kk = 0; kk < 4; ++kk) { qa[kk][0] = qn[kk][0]; qa[kk][1] = qn[kk][1]; }
     }
   }
+  if (p.defer_wait) pdl_wait();  // complete only after the kernel before this one
 }
 
 // Schedule builder: what every layer's decode launch of a step would
@@ -1014,7 +1030,13 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
   // the decode grid's tail frees, measured 2% slower)
   if (tid == 0) pdl_trigger();
   const int Hq = p.n_q_heads;
-  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(s) * p.out_stride;
+  // layer blockIdx.y of a multi-layer call (0: a single layer)
+  const int64_t layer = blockIdx.y;
+  T* orow = static_cast<T*>(p.out) + layer * p.out_layer_stride + static_cast<int64_t>(s) * p.out_stride;
+  const float* part_o = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(p.part_o) +
+                                                       layer * p.ws_layer_stride);
+  const float* part_ml = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(p.part_ml) +
+                                                        layer * p.ws_layer_stride);
   if (nb_s == 0) {
     for (int i = tid; i < Hq * 64; i += kMergeThreads) orow[i] = Elem<T>::from_f(0.f);
     return;
@@ -1034,7 +1056,7 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
     for (int idx = tid; idx < n * Hq; idx += kMergeThreads) {
       const int k = idx / Hq, hh = idx - k * Hq;
       const int64_t sl = partial_slot(c0 + k, per, blk_lo);
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + sl * p.ml_stride + hh * 2));
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + sl * p.ml_stride + hh * 2));
       s_m[k][hh] = ml.x;
       s_l[k][hh] = ml.y;
     }
@@ -1067,7 +1089,7 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
           for (int k = 0; k < 8; ++k) {
             if (k0 + k < n) {
               const int64_t sl = partial_slot(c0 + k0 + k, per, blk_lo);
-              o[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + sl * Hq * 64) + j);
+              o[k] = __ldcg(reinterpret_cast<const float4*>(part_o + sl * Hq * 64) + j);
             }
           }
 #pragma unroll
@@ -1278,6 +1300,9 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.sched = static_cast<const int32_t*>(a.schedule);
   p.sched_rows = a.schedule != nullptr ? sched_rows_for(a.n_seqs, a.max_blocks, grid) : 0;
   p.input_ready = a.input_ready;
+  p.defer_wait = a.chain != nullptr ? a.chain->defer_wait : 0;
+  p.out_layer_stride = 0;
+  p.ws_layer_stride = 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid / pipes_for(nkv));
@@ -1296,9 +1321,19 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
     sched_table_set(a.schedule, true);
   }
 
+  if (a.chain != nullptr && !a.chain->merge) return cudaSuccess;  // a later launch merges
+  if (a.chain != nullptr) {  // the merge of every layer of the call
+    const LayerChain& ch = *a.chain;
+    uint8_t* ws0 = static_cast<uint8_t*>(ch.ws0);
+    p.out = ch.out0;
+    p.part_o = reinterpret_cast<float*>(ws0);
+    p.part_ml = reinterpret_cast<float*>(ws0 + parts_o);
+    p.out_layer_stride = ch.out_layer_stride;
+    p.ws_layer_stride = ch.ws_layer_stride;
+  }
   cudaLaunchConfig_t mcfg = cfg;
   mcfg.numAttrs = 1;
-  mcfg.gridDim = dim3(a.n_seqs);
+  mcfg.gridDim = dim3(a.n_seqs, a.chain != nullptr ? a.chain->n_layers : 1);
   mcfg.blockDim = dim3(kMergeThreads);
   mcfg.dynamicSmemBytes = 0;
   if (a.dtype == PKV_DTYPE_F16)

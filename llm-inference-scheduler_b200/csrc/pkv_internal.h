@@ -74,6 +74,23 @@ struct AttnArgs {
   // decode (tensor-core path): a device word the kernel waits on, bounded,
   // until it is nonzero before reading q / k_new / v_new (NULL = none)
   const int* input_ready = nullptr;
+  // decode: one layer of a multi-layer call with a workspace per layer (NULL:
+  // a single-layer call, its merge launched behind it)
+  const struct LayerChain* chain = nullptr;
+};
+
+// Layers of one multi-layer decode call, each with its own split-K
+// workspace: the decode kernels of layers after the first wait for their
+// predecessor only at their end (defer_wait), and one merge launch after the
+// last layer's decode covers every layer.
+struct LayerChain {
+  int defer_wait;            // this layer's decode kernel
+  int merge;                 // launch the merge of all n_layers after this decode
+  int n_layers;
+  void* out0;                // layer 0's output rows
+  int64_t out_layer_stride;  // elements between layers' outputs
+  void* ws0;                 // layer 0's workspace
+  int64_t ws_layer_stride;   // bytes between layers' workspaces
 };
 cudaError_t launch_reshape_and_cache_fp8(const void* k, const void* v, int64_t k_stride,
                                          int64_t v_stride, void* k_pool, void* v_pool,

@@ -525,8 +525,11 @@ class PagedKVCache:
             self._fp8_scratch = torch.empty(need, dtype=torch.uint8, device=self.mgr.device)
         return self._fp8_scratch
 
-    def decode_workspace(self, n_seqs: int, n_q_heads: int, head_dim: int) -> torch.Tensor:
-        need = ops.decode_workspace_bytes(n_seqs, n_q_heads, head_dim)
+    def decode_workspace(self, n_seqs: int, n_q_heads: int, head_dim: int,
+                         layers: int = 1) -> torch.Tensor:
+        """The cache's split-K scratch (grown on demand); layers > 1: one set
+        per layer, so a multi-layer decode call chains its layers."""
+        need = ops.decode_workspace_bytes(n_seqs, n_q_heads, head_dim) * max(1, layers)
         if self._workspace is None or self._workspace.numel() < need:
             self._workspace = torch.empty(need, dtype=torch.uint8, device=self.mgr.device)
         return self._workspace
@@ -600,7 +603,7 @@ class PagedKVCache:
         if not mgr.fp8 and 0 < nd == meta.n_tokens:
             plan = meta.layers_plan
             if plan is None or plan.scale != scale:
-                ws = self.decode_workspace(nd, q.shape[2], q.shape[3])
+                ws = self.decode_workspace(nd, q.shape[2], q.shape[3], layers=mgr.num_layers)
                 plan = meta.layers_plan = ops.DecodeAppendLayersPlan(
                     meta.block_tables, meta.context_lens, scale, ws, mgr.err,
                     schedule=self._step_schedule(meta, q[0]))

@@ -462,7 +462,8 @@ class DecodeStepGraph:
         self.dev_qkv = torch.empty((L, R, width, D), dtype=mgr.dtype, device=dev)
         self.dev_out = torch.empty((L, R, hq, D), dtype=mgr.dtype, device=dev)
         self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        self.workspace = kv_cache.decode_workspace(R, hq, D)
+        # one split-K set per layer of the largest chunk: a chunk's layers chain
+        self.workspace = kv_cache.decode_workspace(R, hq, D, layers=max(chunks))
         # per chunk: nonzero once its rows are on the device (set by the copy stream)
         self.ready = torch.zeros(len(self.bounds), dtype=torch.int32, device=dev)
         self._one = torch.ones(1, dtype=torch.int32).pin_memory()

@@ -164,10 +164,13 @@ def decode_workspace_bytes(n_seqs: int, n_q_heads: int, head_dim: int) -> int:
     return int(_lib.load().pkv_decode_workspace_bytes(n_seqs, n_q_heads, head_dim))
 
 
-def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device) -> torch.Tensor:
-    """Split-K scratch of paged_decode_attention (any initial contents)."""
-    return torch.empty(decode_workspace_bytes(n_seqs, n_q_heads, head_dim), dtype=torch.uint8,
-                       device=device)
+def new_decode_workspace(n_seqs: int, n_q_heads: int, head_dim: int, device,
+                         layers: int = 1) -> torch.Tensor:
+    """Split-K scratch of paged_decode_attention (any initial contents).
+    layers > 1: one set per layer, for a multi-layer call
+    (pkv_paged_decode_append_attention_layers) to chain its layers."""
+    return torch.empty(decode_workspace_bytes(n_seqs, n_q_heads, head_dim) * max(1, layers),
+                       dtype=torch.uint8, device=device)
 
 
 def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor,
