@@ -535,6 +535,7 @@ def run_ours(args):
     h2d = hqkv.numel() * 2 + meta_bytes
     d2h = hout.numel() * 2
     e2e_chunks, e2e_ready = [b - a for a, b in runner.bounds], runner.gated
+    e2e_copies = [b - a for a, b in runner.copy_bounds]
     del kv, dqkv, hqkv, hout, runner
 
     # ---- the same job under strong scaling (BASELINE config 3's wording:
@@ -624,6 +625,7 @@ def run_ours(args):
                        "the decode schedule, one pkv_paged_decode_append_attention_layers call per chunk "
                        "whose kernels wait on the chunk's ready word, per-chunk D2H)",
                 "chunks": e2e_chunks,
+                "input_copies_layers": e2e_copies,
                 "ready_words": e2e_ready,
                 "timing": f"median of {n_win} windows of {args.e2e_steps} steps back to back, max over ranks",
                 "windows_ms_per_step": [round(x, 4) for x in win_ms],

@@ -255,15 +255,16 @@ int pkv_paged_decode_append_attention_scheduled(
  * bits either way.  Arguments
  * are checked for the first and the last layer before anything launches; on
  * a launch error the call returns it and the later layers are not issued.
- * input_ready: NULL, or a 4-byte aligned device word.  Every layer's decode
- * kernel waits until the word is nonzero before it reads q, k_new or v_new;
- * the wait is bounded (about a second): on a timeout it sets
- * PKV_FLAG_PIPELINE_TIMEOUT and the call's outputs are unspecified.  It is for inputs that a copy on
- * another stream brings in: the copy stream sets the word after the data
- * (a 4-byte copy from a host word holding 1, the word cleared before the
- * data copy), and the call needs no event wait on that stream.  Such a
- * wait between two launches of the chain would end their programmatic
- * overlap (about 5 us per chain break on B200).  Only the tensor-core
+ * input_ready: NULL, or n_layers 4-byte aligned device words.  Layer l's
+ * decode kernel waits until input_ready[l] is nonzero before it reads layer
+ * l's q, k_new or v_new; the wait is bounded (about a second): on a timeout
+ * it sets PKV_FLAG_PIPELINE_TIMEOUT and the call's outputs are unspecified.
+ * It is for inputs that a copy on another stream brings in: the copy stream
+ * sets a layer's word after that layer's rows (a 4-byte copy from a host
+ * word holding 1, the words cleared before the data copies), and the call
+ * needs no event wait on that stream.  Such a wait between two launches of
+ * the chain would end their programmatic overlap (about 5 us per chain
+ * break on B200).  Only the tensor-core
  * decode kernel serves it: other shapes return PKV_ERR_UNSUPPORTED.
  */
 int pkv_paged_decode_append_attention_layers(

@@ -852,7 +852,7 @@ int pkv_paged_decode_append_attention_layers(
         o, out_row_stride, ql, q_row_stride, kn, vn, k_new_row_stride, v_new_row_stride, kp, vp,
         num_blocks, block_tables, block_table_stride, max_blocks_per_seq, context_lens, n_seqs,
         n_q_heads, n_kv_heads, head_dim, block_size, scale, dtype, workspace, workspace_bytes,
-        err_flags, stream, schedule, input_ready);
+        err_flags, stream, schedule, input_ready ? input_ready + l : nullptr);
   };
   // the shared arguments and the last layer's pointers are checked before
   // the first launch, so a bad call issues nothing
@@ -888,7 +888,8 @@ int pkv_paged_decode_append_attention_layers(
           v_new_row_stride, const_cast<void*>(at(k_pools, l * pool_layer_stride_bytes)),
           const_cast<void*>(at(v_pools, l * pool_layer_stride_bytes)), num_blocks, block_tables,
           block_table_stride, max_blocks_per_seq, context_lens, n_seqs, n_q_heads, n_kv_heads,
-          head_dim, block_size, scale, dtype, wsl, ws1, err_flags, stream, schedule, input_ready, &ch);
+          head_dim, block_size, scale, dtype, wsl, ws1, err_flags, stream, schedule,
+          input_ready ? input_ready + l : nullptr, &ch);
       if (rc == PKV_ERR_UNSUPPORTED && l == 0 && !input_ready) break;  // not the tensor-core path
       if (rc != PKV_OK) return rc;
       if (l == n_layers - 1) return PKV_OK;

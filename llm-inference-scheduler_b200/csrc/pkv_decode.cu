@@ -142,6 +142,11 @@ struct DecodeParams {
   // the grid starts on SMs the previous layer's tail frees and still
   // completes after it
   int defer_wait;
+  // 1 (the first layer of such a call): let the next kernel launch only
+  // after this one's griddepcontrol.wait, so the call's later layers start
+  // after everything before the call (a previous call's merge, which reads
+  // the workspace sets they write) has completed
+  int late_trigger;
   // merge over layers (blockIdx.y): out advances by out_layer_stride
   // elements, the partials by ws_layer_stride bytes per layer
   int64_t out_layer_stride;
@@ -352,8 +357,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         __ldg(p.sched + 5) != p.max_blocks) {
       // a schedule built for another batch or grid: do nothing
       if (tid == 0 && vcta == 0) raise_flag(p.err, PKV_FLAG_BAD_SCHEDULE);
+      if (p.defer_wait || p.late_trigger) pdl_wait();
       if (tid == 0) pdl_trigger();
-      if (p.defer_wait) pdl_wait();
       return;
     }
     __syncthreads();
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
 
   // the merge kernel behind this one may be scheduled now: it waits for this
   // grid's completion before it reads anything this grid writes
-  if (tid == 0) pdl_trigger();
+  if (tid == 0 && !p.late_trigger) pdl_trigger();
 
   if (tid == 0) {
     for (int i = 0; i < PIPES * 2 * kDecStages; ++i)
@@ -390,7 +395,8 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
   }
   __syncthreads();
   if (!active) {
-    if (p.defer_wait) pdl_wait();
+    if (p.defer_wait || p.late_trigger) pdl_wait();
+    if (p.late_trigger && tid == 0) pdl_trigger();
     return;
   }
 
@@ -516,6 +522,7 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
   //                   16-dim tile, B = P^T from C via movmatrix.trans,
   //                   C holds dims {16mt+g, 16mt+g+8} x heads {2t, 2t+1}.
   if (!p.defer_wait) pdl_wait();
+  if (p.late_trigger && tid == 0) pdl_trigger();  // thread 0 is a consumer lane of pipeline 0
   if (p.input_ready != nullptr) {
     // inputs that a copy on another stream brings in: one lane waits for the
     // word the copy engine sets after them, then the warp reads them
@@ -1301,6 +1308,7 @@ cudaError_t launch_decode_fast(const AttnArgs& a, const CUtensorMap* kmap, const
   p.sched_rows = a.schedule != nullptr ? sched_rows_for(a.n_seqs, a.max_blocks, grid) : 0;
   p.input_ready = a.input_ready;
   p.defer_wait = a.chain != nullptr ? a.chain->defer_wait : 0;
+  p.late_trigger = a.chain != nullptr && !a.chain->defer_wait;
   p.out_layer_stride = 0;
   p.ws_layer_stride = 0;
 

@@ -588,9 +588,9 @@ class PagedKVCache:
         (pkv_paged_decode_append_attention_layers: the fused append + decode
         and the merge of every layer); other steps run forward_layer layer by
         layer.  The results are those of forward_layer either way.
-        input_ready (one-call form only): a one-element int32 device tensor
-        that the kernels wait on, bounded, until a copy on another stream has
-        set it nonzero after q / k_new / v_new."""
+        input_ready (one-call form only): an int32 device tensor of one word
+        per layer; layer l's kernels wait, bounded, until a copy on another
+        stream has set word l nonzero after that layer's q / k_new / v_new."""
         mgr = self.mgr
         n = q.shape[0]
         last = first_layer + n

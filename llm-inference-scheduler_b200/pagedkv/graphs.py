@@ -405,20 +405,23 @@ class DecodeStepGraph:
     pinned staging buffer, padded to R rows), copies it with one H2D copy and
     launches one graph holding:
     * the decode schedule build;
-    * per chunk of layers, on a copy stream, the H2D copy of the chunk's rows,
-      then a 4-byte copy that sets the chunk's ready word (cleared at the
-      step's start);
-    * per chunk, one pkv_paged_decode_append_attention_layers call (the fused
-      append + decode and the merge of each of its layers) whose kernels wait,
-      bounded, for the chunk's ready word before reading its rows.  An event
-      wait on the copy stream there would end the programmatic overlap
-      between the chunk's first launch and the one before it (about 5 us a
-      chunk); the ready word keeps the whole step one launch chain;
-    * per chunk, on a second copy stream, the D2H copy of the chunk's outputs.
-    By default a chunk is one layer: the pipeline's fill is one layer's copy
-    in and its drain one layer's copy out.  Where the tensor-core decode does
-    not serve the shapes (the ready word is then refused), the chunks wait on
-    copy events instead, in event_chunks' sizes unless chunks were given.
+    * on a copy stream, the H2D copies of the rows (copy_chunks: one layer,
+      then three, then four at a time), each followed by one copy that sets
+      its layers' ready words (cleared at the step's start);
+    * per chunk of layers, one pkv_paged_decode_append_attention_layers call
+      with a split-K set per layer: the layers' decode kernels chain (each
+      later one starts on the SMs the previous one's tail frees) and one merge
+      launch follows them.  Each layer's kernels wait, bounded, for its ready
+      word before reading its rows.  An event wait on the copy stream would
+      instead end the programmatic overlap between two launches (about 5 us
+      each); the ready words keep the step one launch chain;
+    * per chunk, on a second copy stream, the D2H copy of the chunk's outputs
+      once its merge is done.
+    The pipeline's fill is one layer's copy in; the drain is the last chunk's
+    copy out, so the default chunks taper at the end (ready_chunks).  Where
+    the tensor-core decode does not serve the shapes (the ready words are
+    then refused), chunks wait on copy events instead, in event_chunks'
+    sizes unless chunks were given.
 
     A step of B <= R sequences (one new token each, host rows 0 .. B-1) pads
     rows B .. R-1: context length 0, slot -1, so they read and write no KV
@@ -448,7 +451,7 @@ class DecodeStepGraph:
                 and host_out.is_contiguous()):
             raise ValueError("pagedkv: host_qkv / host_out must be contiguous pinned host tensors")
         self._chunks_given = chunks is not None
-        chunks = tuple(chunks or [1] * L)  # ready words: a chunk boundary costs nothing
+        chunks = tuple(chunks or ready_chunks(L))
         if sum(chunks) != L or min(chunks) <= 0:
             raise ValueError(f"pagedkv: chunks {chunks} must be positive and sum to {L}")
         self.kv, self.scale = kv_cache, float(scale)
@@ -464,9 +467,14 @@ class DecodeStepGraph:
         self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         # one split-K set per layer of the largest chunk: a chunk's layers chain
         self.workspace = kv_cache.decode_workspace(R, hq, D, layers=max(chunks))
-        # per chunk: nonzero once its rows are on the device (set by the copy stream)
-        self.ready = torch.zeros(len(self.bounds), dtype=torch.int32, device=dev)
-        self._one = torch.ones(1, dtype=torch.int32).pin_memory()
+        # per layer: nonzero once its rows are on the device (set by the copy stream)
+        self.ready = torch.zeros(L, dtype=torch.int32, device=dev)
+        self._ones = torch.ones(L, dtype=torch.int32).pin_memory()
+        # the input copies (each followed by one copy of its layers' ready
+        # words): one layer first, so compute starts after one layer's copy,
+        # then larger copies (every copy costs the copy engine a fixed time)
+        cc = copy_chunks(L)
+        self.copy_bounds = [(sum(cc[:i]), sum(cc[:i + 1])) for i in range(len(cc))]
         self.gated = True
         self._alloc()
 
@@ -508,11 +516,13 @@ class DecodeStepGraph:
         self.h2d.wait_stream(cur)
         ev_in = [torch.cuda.Event() for _ in self.bounds]
         with torch.cuda.stream(self.h2d):
-            for c, ((a, b), ev) in enumerate(zip(self.bounds, ev_in)):
-                q[a:b].copy_(self.host_qkv[a:b], non_blocking=True)
-                if self.gated:
-                    self.ready[c:c + 1].copy_(self._one, non_blocking=True)
-                else:
+            if self.gated:  # each copy followed by its layers' ready words
+                for a, b in self.copy_bounds:
+                    q[a:b].copy_(self.host_qkv[a:b], non_blocking=True)
+                    self.ready[a:b].copy_(self._ones[: b - a], non_blocking=True)
+            else:
+                for (a, b), ev in zip(self.bounds, ev_in):
+                    q[a:b].copy_(self.host_qkv[a:b], non_blocking=True)
                     ev.record(self.h2d)
         meta.decode_schedule = ops.build_decode_schedule(
             self.schedule, meta.block_tables, meta.context_lens, mgr.num_blocks, self.hq,
@@ -525,7 +535,7 @@ class DecodeStepGraph:
                 cur.wait_event(ev)
             kv.forward_layers(a, q[a:b, :, :self.hq], q[a:b, :, self.hq:self.hq + hkv],
                               q[a:b, :, self.hq + hkv:], meta, self.scale, out=self.dev_out[a:b],
-                              advance=False, input_ready=self.ready[c:c + 1] if self.gated else None)
+                              advance=False, input_ready=self.ready[a:b] if self.gated else None)
             done = torch.cuda.Event()
             done.record(cur)
             self.d2h.wait_event(done)
@@ -605,6 +615,39 @@ class DecodeStepGraph:
         if advance:
             for s_id, p in zip(a["seq_ids"], a["num_prior"]):
                 kv._len[s_id] = p + 1
+
+
+def copy_chunks(n_layers: int) -> list[int]:
+    """Layers per input copy of DecodeStepGraph (24: 1, 3, 4, 4, 4, 4, 4):
+    the first compute waits for one layer's copy only, and the copy engine
+    stays ahead of the compute (a layer's copy takes about 11 us at 54 GB/s,
+    its decode 26 us) with few copies (each costs a fixed few us)."""
+    out, left = [], n_layers
+    for size in (1, 3):
+        if left > 0:
+            out.append(min(size, left))
+            left -= out[-1]
+    while left > 0:
+        out.append(min(4, left))
+        left -= out[-1]
+    return out
+
+
+def ready_chunks(n_layers: int) -> list[int]:
+    """Chunks of layers for DecodeStepGraph with ready words (24 layers: 4,
+    4, 4, 4, 4, 2, 1, 1).  Within a chunk the layers' decode kernels chain;
+    each chunk ends with one merge launch, which the next chunk's first
+    decode waits for, and the last chunk's outputs are the pipeline's drain:
+    chunks of four, tapering to one at the end."""
+    tail = [2, 1, 1]
+    body = n_layers - sum(tail)
+    if body < 0:
+        return [1] * n_layers
+    out = []
+    while body > 0:
+        out.append(min(4, body))
+        body -= out[-1]
+    return out + tail
 
 
 def event_chunks(n_layers: int) -> list[int]:

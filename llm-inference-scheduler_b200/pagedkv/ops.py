@@ -658,9 +658,10 @@ class DecodeAppendLayersPlan:
         return t.stride(0)
 
     def __call__(self, q, k_new, v_new, k_pools, v_pools, out, input_ready=None) -> torch.Tensor:
-        """input_ready: None, or a one-element int32 device tensor that the
-        kernels wait on (bounded) until it is nonzero before reading q,
-        k_new and v_new (set by a copy on another stream after them)."""
+        """input_ready: None, or an int32 device tensor of one word per layer:
+        layer l's kernels wait (bounded) until input_ready[l] is nonzero
+        before reading its q, k_new and v_new (set by a copy on another
+        stream after that layer's rows)."""
         n = q.shape[0]
         if k_new.shape[0] != n or v_new.shape[0] != n or out.shape[0] != n or \
                 k_pools.shape[0] != n or v_pools.shape[0] != n:
@@ -693,8 +694,8 @@ class DecodeAppendLayersPlan:
                                                       v_pools.data_ptr())
         if input_ready is not None:
             _cuda(input_ready, "input_ready")
-            if input_ready.dtype != torch.int32 or input_ready.numel() != 1:
-                raise ValueError("pagedkv: input_ready must be one int32 element on the device")
+            if input_ready.dtype != torch.int32 or input_ready.numel() != n or not input_ready.is_contiguous():
+                raise ValueError("pagedkv: input_ready must hold one contiguous int32 word per layer")
         a[-1] = None if input_ready is None else input_ready.data_ptr()
         rc = self._fn(*a)
         if rc:

@@ -578,7 +578,7 @@ def test_decode_layers_input_ready_word():
 
     m1, kv1, x1, meta1 = setup(torch.float16)
     m2, kv2, x2, meta2 = setup(torch.float16)
-    set_word = torch.ones(1, dtype=torch.int32, device="cuda")
+    set_word = torch.ones(L, dtype=torch.int32, device="cuda")  # one word per layer
     o1 = call(kv1, x1, meta1, set_word)
     o2 = call(kv2, x2, meta2)
     torch.cuda.synchronize()
@@ -587,7 +587,7 @@ def test_decode_layers_input_ready_word():
     assert torch.equal(m1.k_cache, m2.k_cache) and torch.equal(m1.v_cache, m2.v_cache)
     # a word nothing sets: one layer, so one bounded wait
     never = torch.zeros(1, dtype=torch.int32, device="cuda")
-    o3 = call(kv1, x1, meta1, never, layers=1)
+    o3 = call(kv1, x1, meta1, never, layers=1)  # layer 0's word
     torch.cuda.synchronize()
     flags = int(m1.err.item())
     assert flags & _lib.FLAG_PIPELINE_TIMEOUT, flags
