@@ -964,15 +964,23 @@ def run_decode_fp8(args):
     out = torch.empty_like(q)
     tabs = torch.from_numpy(tabs_np).to(dev)
     ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
-    ws = ops.new_decode_workspace(B, 14, 64, dev)
-    # per step: the schedule, then one call per layer in which the decode
-    # kernel quantises the step's new token into the fp8 pools itself
+    # per step: the schedule, then the layers' decodes, in which the decode
+    # kernel quantises the step's new token into the fp8 pools itself: one
+    # multi-layer call whose layers chain (a split-K set per layer), or with
+    # --per-layer-calls one call (decode + merge) per layer
     sched = ops.new_decode_schedule(B, tabs.shape[1], dev)
     launches = [ops.bind_decode_schedule(sched, tabs, ctx_d, nb, 14, 2, 64, dt, fp8=True, err=err)]
-    for l in range(L):
-        launches.append(ops.bind_paged_decode_append_attention_fp8(
-            q[l], kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], mgr.k_scale[l], mgr.v_scale[l], tabs,
-            ctx_d, scale, ws, out[l], err, schedule=sched))
+    if args.per_layer_calls:
+        ws = ops.new_decode_workspace(B, 14, 64, dev)
+        for l in range(L):
+            launches.append(ops.bind_paged_decode_append_attention_fp8(
+                q[l], kn[l], vn[l], mgr.k_pool[l], mgr.v_pool[l], mgr.k_scale[l], mgr.v_scale[l], tabs,
+                ctx_d, scale, ws, out[l], err, schedule=sched))
+    else:
+        ws = ops.new_decode_workspace(B, 14, 64, dev, layers=L)
+        plan = ops.DecodeAppendFp8LayersPlan(tabs, ctx_d, scale, ws, err, schedule=sched)
+        launches.append(lambda: plan(q, kn, vn, mgr.k_cache, mgr.v_cache, mgr.k_scale_cache,
+                                     mgr.v_scale_cache, out))
     tot = int(ctx.sum())
     dec_bytes = (tot * 2 * 64 * 2 + tot * 2 * 2 * 4 + B * 14 * 64 * 2 * 2 + int(nblk.sum()) * 4 + B * 4)
     app_bytes = B * (2 * 2 * 64 * 2 + 2 * 2 * 64 + 2 * 2 * 4 + 8)
@@ -1012,7 +1020,10 @@ def run_decode_fp8(args):
                    "bytes_per_token": 2 * 64 * 2 + 2 * 2 * 4},
         "decode_tok_s": round(B / (ms * 1e-3), 1),
         "hbm_frac_step": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak": peak, "peak_kind": kind,
-        "gpu_launches": (2 * L + 1) * args.steps,  # schedule + (decode with fused append, merge) per layer
+        # schedule + (decode with fused append, merge) per layer, or the
+        # chained decodes and one merge launch
+        "gpu_launches": ((2 * L + 1) if args.per_layer_calls else (L + 2)) * args.steps,
+        "calls": "one call per layer" if args.per_layer_calls else "one multi-layer call, layers chained",
         "clocks": sampler.summary(t0, t1),
     }
     print(json.dumps(line), flush=True)

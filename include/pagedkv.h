@@ -131,6 +131,30 @@ int pkv_paged_decode_append_attention_fp8_scheduled(
     const void* schedule);
 
 /*
+ * pkv_paged_decode_append_attention_layers for fp8 e4m3 pools: for layer
+ * l = 0 .. n_layers-1 exactly pkv_paged_decode_append_attention_fp8(_scheduled)
+ * with the per-layer pointers advanced by their layer strides, the scale
+ * arrays by scale_layer_stride floats ([num_layers][num_blocks][block_size]
+ * [Hkv] scales).  A workspace of n_layers x pkv_decode_workspace_bytes
+ * chains the layers on the tensor-core path as in the 16-bit call (each later
+ * decode starts on the SMs the previous one's tail frees, one merge launch for
+ * every layer); with a single set each layer's decode has its own merge.
+ * dtype: the q / out / new-row type (PKV_DTYPE_F16 or PKV_DTYPE_BF16).
+ * Replaces, for fp8 pools, the per-layer loop of Qwen2Model.forward
+ * (mini_engine/model/qwen2.py:159-166) over append_and_fetch + _attention.
+ */
+int pkv_paged_decode_append_attention_fp8_layers(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, float* k_scales, float* v_scales,
+    int64_t scale_layer_stride, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule);
+
+/*
  * Chunked prefill over fp8 e4m3 pools on the tensor cores with no scratch:
  * the tcgen05 prefill kernel stages each key tile's e4m3 bytes and row
  * scales in shared memory, and two of its warps convert them into the fp16

@@ -621,7 +621,7 @@ static int pkv_paged_decode_append_attention_fp8_impl(
     int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
     int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
     void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
-    const void* schedule) {
+    const void* schedule, const LayerChain* chain = nullptr) {
   if (n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_seqs == 0) return PKV_OK;
   int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pool, v_pool, num_blocks, block_tables,
@@ -660,9 +660,11 @@ static int pkv_paged_decode_append_attention_fp8_impl(
   a.v_new = v_new;
   a.k_new_stride = k_new_row_stride;
   a.v_new_stride = v_new_row_stride;
+  a.chain = chain;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (g_decode_impl.load() == PKV_DECODE_AUTO && decode_fast_supported(a))
     return decode_dispatch(a, workspace, workspace_bytes, st);
+  if (chain) return PKV_ERR_UNSUPPORTED;  // only the tensor-core kernel chains layers
   // separate quantising append (slot from the block table) + CUDA-core attention
   cudaError_t e = launch_append_at_context_end_fp8(
       k_new, v_new, k_new_row_stride, v_new_row_stride, k_pool, v_pool, k_scale, v_scale,
@@ -897,6 +899,76 @@ int pkv_paged_decode_append_attention_layers(
   }
   for (int l = 0; l < n_layers; ++l) {
     rc = layer_call(l);
+    if (rc != PKV_OK) return rc;
+  }
+  return PKV_OK;
+}
+
+int pkv_paged_decode_append_attention_fp8_layers(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, float* k_scales, float* v_scales,
+    int64_t scale_layer_stride, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule) {
+  if (n_layers < 0 || n_seqs < 0) return PKV_ERR_BAD_SHAPE;
+  if (n_layers == 0 || n_seqs == 0) return PKV_OK;
+  if (!out || !q || !k_new || !v_new || !k_pools || !v_pools || !k_scales || !v_scales || !context_lens)
+    return PKV_ERR_NULL_POINTER;
+  if (schedule && (reinterpret_cast<uintptr_t>(schedule) & 15) != 0) return PKV_ERR_MISALIGNED;
+  if (dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16) return PKV_ERR_BAD_DTYPE;
+  const int64_t es = esize_of(dtype);
+  const int64_t pool_bytes = static_cast<int64_t>(num_blocks) * block_size * n_kv_heads * head_dim;
+  const int64_t scale_count = static_cast<int64_t>(num_blocks) * block_size * n_kv_heads;
+  if (n_layers > 1 && (pool_layer_stride_bytes < pool_bytes || scale_layer_stride < scale_count ||
+                       out_layer_stride <= 0 || q_layer_stride <= 0 || new_layer_stride <= 0))
+    return PKV_ERR_BAD_SHAPE;
+  if ((pool_layer_stride_bytes & 15) != 0 || (scale_layer_stride & 3) != 0) return PKV_ERR_MISALIGNED;
+  auto at = [](const void* base, int64_t off_bytes) {
+    return static_cast<const void*>(static_cast<const uint8_t*>(base) + off_bytes);
+  };
+  // layer l's call; `chain`: the call's layers chain (a split-K set per layer)
+  auto layer_call = [&](int l, const LayerChain* chain, void* ws, size_t wsb) -> int {
+    return pkv_paged_decode_append_attention_fp8_impl(
+        const_cast<void*>(at(out, l * out_layer_stride * es)), out_row_stride,
+        at(q, l * q_layer_stride * es), q_row_stride, at(k_new, l * new_layer_stride * es),
+        at(v_new, l * new_layer_stride * es), k_new_row_stride, v_new_row_stride,
+        const_cast<void*>(at(k_pools, l * pool_layer_stride_bytes)),
+        const_cast<void*>(at(v_pools, l * pool_layer_stride_bytes)), k_scales + l * scale_layer_stride,
+        v_scales + l * scale_layer_stride, num_blocks, block_tables, block_table_stride,
+        max_blocks_per_seq, context_lens, n_seqs, n_q_heads, n_kv_heads, head_dim, block_size, scale,
+        dtype, ws, wsb, err_flags, stream, schedule, chain);
+  };
+  // the first and the last layer's pointers are checked before anything launches
+  int rc = check_attn(out, out_row_stride, q, q_row_stride, k_pools, v_pools, num_blocks, block_tables,
+                      block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim,
+                      block_size, dtype);
+  if (rc != PKV_OK) return rc;
+  const int last = n_layers - 1;
+  rc = check_attn(at(out, last * out_layer_stride * es), out_row_stride, at(q, last * q_layer_stride * es),
+                  q_row_stride, at(k_pools, last * pool_layer_stride_bytes),
+                  at(v_pools, last * pool_layer_stride_bytes), num_blocks, block_tables,
+                  block_table_stride, max_blocks_per_seq, n_q_heads, n_kv_heads, head_dim, block_size,
+                  dtype);
+  if (rc != PKV_OK) return rc;
+  // a split-K set per layer chains the layers, as in the 16-bit call
+  const size_t ws1 = decode_workspace_bytes(n_seqs, n_q_heads, head_dim);
+  if (n_layers > 1 && workspace && ws1 > 0 && workspace_bytes / static_cast<size_t>(n_layers) >= ws1) {
+    LayerChain ch{0, 0, n_layers, out, out_layer_stride, workspace, static_cast<int64_t>(ws1)};
+    for (int l = 0; l < n_layers; ++l) {
+      ch.defer_wait = l > 0;
+      ch.merge = l == last;
+      rc = layer_call(l, &ch, static_cast<uint8_t*>(workspace) + static_cast<size_t>(l) * ws1, ws1);
+      if (rc == PKV_ERR_UNSUPPORTED && l == 0) break;  // not the tensor-core path
+      if (rc != PKV_OK) return rc;
+      if (l == last) return PKV_OK;
+    }
+  }
+  for (int l = 0; l < n_layers; ++l) {
+    rc = layer_call(l, nullptr, workspace, workspace_bytes);
     if (rc != PKV_OK) return rc;
   }
   return PKV_OK;

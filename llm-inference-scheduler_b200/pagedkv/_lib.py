@@ -84,6 +84,10 @@ SIGNATURES: dict = {
     "pkv_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "pkv_ipc_close": (_I, [_P]),
     "pkv_copy_blocks_peer": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I, _P, _I, _I64, _P, _P]),
+    "pkv_paged_decode_append_attention_fp8_layers": (_I, [_I, _P, _I64, _I64, _P, _I64, _I64, _P, _P,
+                                                          _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64,
+                                                          _I, _P, _I64, _I, _P, _I, _I, _I, _I, _I,
+                                                          _F, _I, _P, _SZ, _P, _P, _P]),
     "pkv_paged_decode_append_attention_layers": (_I, [_I, _P, _I64, _I64, _P, _I64, _I64, _P, _P,
                                                       _I64, _I64, _I64, _P, _P, _I64, _I, _P, _I64,
                                                       _I, _P, _I, _I, _I, _I, _I, _F, _I, _P, _SZ,

@@ -584,10 +584,10 @@ class PagedKVCache:
         """forward_layer for the n consecutive layers first_layer ..
         first_layer + n - 1 at once, with layer-major inputs: q [n, T, Hq, D],
         k_new / v_new [n, T, Hkv, D] -> out [n, T, Hq, D].  A decode-only step
-        over 16-bit pools is one C call for the whole run
-        (pkv_paged_decode_append_attention_layers: the fused append + decode
-        and the merge of every layer); other steps run forward_layer layer by
-        layer.  The results are those of forward_layer either way.
+        is one C call for the whole run (pkv_paged_decode_append_attention_layers,
+        or _fp8_layers over fp8 pools: the fused append + decode of every
+        layer, chained, then one merge launch); other steps run forward_layer
+        layer by layer.  The results are those of forward_layer either way.
         input_ready (one-call form only): an int32 device tensor of one word
         per layer; layer l's kernels wait, bounded, until a copy on another
         stream has set word l nonzero after that layer's q / k_new / v_new."""
@@ -600,15 +600,21 @@ class PagedKVCache:
         if mgr._pending:
             mgr.flush_copies()
         nd = meta.n_decode
-        if not mgr.fp8 and 0 < nd == meta.n_tokens:
+        if 0 < nd == meta.n_tokens:
             plan = meta.layers_plan
-            if plan is None or plan.scale != scale:
+            kind = ops.DecodeAppendFp8LayersPlan if mgr.fp8 else ops.DecodeAppendLayersPlan
+            if plan is None or plan.scale != scale or not isinstance(plan, kind):
                 ws = self.decode_workspace(nd, q.shape[2], q.shape[3], layers=mgr.num_layers)
-                plan = meta.layers_plan = ops.DecodeAppendLayersPlan(
-                    meta.block_tables, meta.context_lens, scale, ws, mgr.err,
-                    schedule=self._step_schedule(meta, q[0]))
-            plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out,
-                 input_ready=input_ready)
+                plan = meta.layers_plan = kind(meta.block_tables, meta.context_lens, scale, ws, mgr.err,
+                                               schedule=self._step_schedule(meta, q[0]))
+            if mgr.fp8:
+                if input_ready is not None:
+                    raise ValueError("pagedkv: input_ready serves 16-bit pools")
+                plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last],
+                     mgr.k_scale_cache[first_layer:last], mgr.v_scale_cache[first_layer:last], out)
+            else:
+                plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out,
+                     input_ready=input_ready)
             if advance and last == mgr.num_layers:
                 self._advance(meta)
             return out

@@ -756,6 +756,60 @@ def bind_paged_decode_append_attention_fp8(q, k_new, v_new, k_pool, v_pool, k_sc
                         workspace, out, err, schedule))
 
 
+class DecodeAppendFp8LayersPlan:
+    """pkv_paged_decode_append_attention_fp8_layers for runs of consecutive
+    layers of one decode-only step over fp8 pools: q / out [n, B, Hq, D] and
+    k_new / v_new [n, B, Hkv, D] in the 16-bit model dtype, the uint8 pools
+    [n, NB, bs, Hkv, D] and fp32 scales [n, NB, bs, Hkv] of the step's
+    contiguous caches.  A workspace of one split-K set per layer chains the
+    run's layers.  Validated arguments are reused, with the run's pointers and
+    length swapped in."""
+
+    def __init__(self, block_tables, context_lens, scale, workspace, err=None, schedule=None):
+        self._static = (block_tables, context_lens, scale, workspace, err)
+        self.scale = scale
+        self.schedule = schedule
+        self._key = None
+        self._args: list = []
+        self._fn = _lib.load().pkv_paged_decode_append_attention_fp8_layers
+
+    def __call__(self, q, k_new, v_new, k_pools, v_pools, k_scales, v_scales, out) -> torch.Tensor:
+        n = q.shape[0]
+        if any(t.shape[0] != n for t in (k_new, v_new, out, k_pools, v_pools, k_scales, v_scales)):
+            raise ValueError("pagedkv: the inputs, pools, scales and out must cover the same layers")
+        if n == 0:
+            return out
+        key = (q.dtype, q.shape[1:], q.stride(), k_new.shape[1:], k_new.stride(), v_new.stride(),
+               k_pools.shape[1:], k_pools.stride(), v_pools.stride(), k_scales.stride(),
+               v_scales.stride(), out.shape[1:], out.stride(), q.get_device(), _raw_stream(q))
+        if key != self._key:
+            if k_new.stride(0) != v_new.stride(0) or k_scales.stride() != v_scales.stride():
+                raise ValueError("pagedkv: k_new / v_new and the two scale arrays must be equally strided")
+            if k_pools.stride() != v_pools.stride() or not k_pools[0].is_contiguous():
+                raise ValueError("pagedkv: the K and V pools must be equally strided, layers dense")
+            tables, ctx, scale, ws, err = self._static
+            # the per-layer checks of the single-layer call, on layer 0
+            args, _ = _decode_append_fp8_args(q[0], k_new[0], v_new[0], k_pools[0], v_pools[0],
+                                              k_scales[0], v_scales[0], tables, ctx, scale, ws, out[0], err)
+            (o, o_rs, qp, q_rs, kn, vn, kn_rs, vn_rs, kp, vp, ksp, vsp, nb, bt, bt_s, mb, cl, B, hq, hkv, d,
+             bs, sc, dt, wsp, wsb, errp, st) = args
+            self._args = [n, o, DecodeAppendLayersPlan._layer_stride(out, "out"), o_rs, qp,
+                          DecodeAppendLayersPlan._layer_stride(q, "q"), q_rs, kn, vn,
+                          DecodeAppendLayersPlan._layer_stride(k_new, "k_new"), kn_rs, vn_rs, kp, vp,
+                          k_pools.stride(0) * k_pools.element_size(), ksp, vsp, k_scales.stride(0), nb, bt,
+                          bt_s, mb, cl, B, hq, hkv, d, bs, sc, dt, wsp, wsb, errp, st,
+                          None if self.schedule is None else self.schedule.data_ptr()]
+            self._key = key
+        a = self._args
+        a[0], a[1], a[4], a[7], a[8], a[12], a[13], a[15], a[16] = (
+            n, out.data_ptr(), q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_pools.data_ptr(),
+            v_pools.data_ptr(), k_scales.data_ptr(), v_scales.data_ptr())
+        rc = self._fn(*a)
+        if rc:
+            _lib.check(rc, "pkv_paged_decode_append_attention_fp8_layers")
+        return out
+
+
 def bind_paged_prefill_attention_fp8(q, k_pool, v_pool, k_scale, v_scale, block_tables,
                                      query_start_loc, num_prior, max_query_len, scale, out, scratch,
                                      err=None) -> BoundLaunch:

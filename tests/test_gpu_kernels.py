@@ -1108,6 +1108,52 @@ def test_rope_reshape_and_cache_fp8_bit_identical(dt, layout):
         assert torch.equal(a, b)
 
 
+def test_forward_layers_fp8_equals_forward_layer_fp8():
+    """PagedKVCache.forward_layers over fp8 pools (one
+    pkv_paged_decode_append_attention_fp8_layers call per run of layers, the
+    layers chained on a split-K set each) against forward_layer layer by
+    layer on a copy of the same pools: outputs, e4m3 bytes and scales
+    bit-identical.  Two consecutive runs share the workspace."""
+    rng = np.random.default_rng(48)
+    L, nb = 5, 768
+    ctx = rng.integers(1, 600, size=29)
+    ctx[:3] = [1, 16, 17]
+    managers = []
+    for _ in range(2):
+        m = BlockManager(nb, 16, L, 2, 64, device="cuda", dtype=torch.float8_e4m3fn)
+        kv = PagedKVCache(m)
+        o = 0
+        for s_, c in enumerate(ctx):
+            n = (int(c) + 15) // 16
+            kv.add_sequence(s_, list(range(o, o + n)), int(c) - 1)
+            o += n
+        managers.append((m, kv))
+    (m1, kv1), (m2, kv2) = managers
+    g = torch.Generator(device="cuda").manual_seed(48)
+    fill = torch.randn((nb * 16, 2, 64), generator=g, device="cuda").half()
+    slots = torch.arange(nb * 16, device="cuda", dtype=torch.int64)
+    for layer in range(L):  # identical quantised pools in both caches
+        for m in (m1, m2):
+            ops.reshape_and_cache_fp8(fill, fill * 0.5, m.k_pool[layer], m.v_pool[layer], m.k_scale[layer],
+                                      m.v_scale[layer], slots, m.err)
+    B = len(ctx)
+    x = torch.randn((L, B, 18, 64), generator=g, device="cuda").half()
+    meta1 = kv1.prepare_step([(s_, 1) for s_ in range(B)])
+    meta2 = kv2.prepare_step([(s_, 1) for s_ in range(B)])
+    out1 = torch.empty((L, B, 14, 64), dtype=torch.float16, device="cuda")
+    for a, b in ((0, 2), (2, 5)):
+        kv1.forward_layers(a, x[a:b, :, :14], x[a:b, :, 14:16], x[a:b, :, 16:18], meta1, 0.125,
+                           out=out1[a:b])
+    out2 = torch.stack([kv2.forward_layer(layer, x[layer, :, :14], x[layer, :, 14:16], x[layer, :, 16:18],
+                                          meta2, 0.125) for layer in range(L)])
+    torch.cuda.synchronize()
+    m1.check_errors()
+    m2.check_errors()
+    assert torch.equal(out1, out2)
+    assert torch.equal(m1.k_cache, m2.k_cache) and torch.equal(m1.v_cache, m2.v_cache)
+    assert torch.equal(m1.k_scale_cache, m2.k_scale_cache) and torch.equal(m1.v_scale_cache, m2.v_scale_cache)
+
+
 def test_forward_layer_qkv_fp8_equals_forward_layer_fp8():
     """Over fp8 pools, forward_layer_qkv (fused RoPE + quantising append, then
     the fp8 decode and prefill) equals rotating in torch and calling
