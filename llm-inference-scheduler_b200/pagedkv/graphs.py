@@ -451,7 +451,10 @@ class DecodeStepGraph:
                 and host_out.is_contiguous()):
             raise ValueError("pagedkv: host_qkv / host_out must be contiguous pinned host tensors")
         self._chunks_given = chunks is not None
-        chunks = tuple(chunks or ready_chunks(L))
+        # sized by bytes: chunks of about 1.8 MB of outputs (4 layers at
+        # config 3), input copies of about 2.4 MB (4 layers)
+        esz = host_qkv.element_size()
+        chunks = tuple(chunks or ready_chunks(L, pieces_for(L, R * hq * D * esz, 1_800_000)))
         if sum(chunks) != L or min(chunks) <= 0:
             raise ValueError(f"pagedkv: chunks {chunks} must be positive and sum to {L}")
         self.kv, self.scale = kv_cache, float(scale)
@@ -473,7 +476,7 @@ class DecodeStepGraph:
         # the input copies (each followed by one copy of its layers' ready
         # words): one layer first, so compute starts after one layer's copy,
         # then larger copies (every copy costs the copy engine a fixed time)
-        cc = copy_chunks(L)
+        cc = copy_chunks(L, pieces_for(L, R * width * D * esz, 2_400_000))
         self.copy_bounds = [(sum(cc[:i]), sum(cc[:i + 1])) for i in range(len(cc))]
         self.gated = True
         self._alloc()
@@ -617,37 +620,43 @@ class DecodeStepGraph:
                 kv._len[s_id] = p + 1
 
 
-def copy_chunks(n_layers: int) -> list[int]:
-    """Layers per input copy of DecodeStepGraph (24: 1, 3, 4, 4, 4, 4, 4):
-    the first compute waits for one layer's copy only, and the copy engine
-    stays ahead of the compute (a layer's copy takes about 11 us at 54 GB/s,
-    its decode 26 us) with few copies (each costs a fixed few us)."""
+def copy_chunks(n_layers: int, per_copy: int = 4) -> list[int]:
+    """Layers per input copy of DecodeStepGraph (24 layers, per_copy 4: 1, 3,
+    4, 4, 4, 4, 4): the first compute waits for one layer's copy only, and
+    the copy engine stays ahead of the compute (at config 3 a layer's copy
+    takes about 11 us at 54 GB/s, its decode 26 us) with few copies (each
+    costs a fixed few us, so small layers go in larger pieces)."""
     out, left = [], n_layers
-    for size in (1, 3):
-        if left > 0:
+    for size in (1, per_copy - 1):
+        if left > 0 and size > 0:
             out.append(min(size, left))
             left -= out[-1]
     while left > 0:
-        out.append(min(4, left))
+        out.append(min(per_copy, left))
         left -= out[-1]
     return out
 
 
-def ready_chunks(n_layers: int) -> list[int]:
-    """Chunks of layers for DecodeStepGraph with ready words (24 layers: 4,
-    4, 4, 4, 4, 2, 1, 1).  Within a chunk the layers' decode kernels chain;
-    each chunk ends with one merge launch, which the next chunk's first
-    decode waits for, and the last chunk's outputs are the pipeline's drain:
-    chunks of four, tapering to one at the end."""
+def ready_chunks(n_layers: int, per_chunk: int = 4) -> list[int]:
+    """Chunks of layers for DecodeStepGraph with ready words (24 layers,
+    per_chunk 4: 4, 4, 4, 4, 4, 2, 1, 1).  Within a chunk the layers' decode
+    kernels chain; each chunk ends with one merge launch, which the next
+    chunk's first decode waits for, and the last chunk's outputs are the
+    pipeline's drain: chunks of per_chunk layers, tapering to one at the end."""
     tail = [2, 1, 1]
     body = n_layers - sum(tail)
     if body < 0:
         return [1] * n_layers
     out = []
     while body > 0:
-        out.append(min(4, body))
+        out.append(min(per_chunk, body))
         body -= out[-1]
     return out + tail
+
+
+def pieces_for(n_layers: int, layer_bytes: int, target_bytes: int) -> int:
+    """Layers per copy piece: about target_bytes of copy each, 1 .. n_layers."""
+    return max(1, min(n_layers, round(target_bytes / max(1, layer_bytes))))
 
 
 def event_chunks(n_layers: int) -> list[int]:

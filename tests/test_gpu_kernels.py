@@ -604,6 +604,47 @@ def test_decode_layers_input_ready_word():
     assert e.value.status == _lib.ERR_UNSUPPORTED
 
 
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_decode_layers_chained_equals_per_layer_merges(dt):
+    """pkv_paged_decode_append_attention_layers with one split-K set per
+    layer (the layers' decodes chained, one merge launch for all) against the
+    same call with a single set (each layer's decode followed by its merge),
+    on copies of the same pools, twice in a row: outputs and pools
+    bit-identical, and equal to the single-layer entry point."""
+    rng = np.random.default_rng(49)
+    L, nb, tdt = 4, 1024, TORCH_DT[dt]
+    ctx = rng.integers(1, 900, size=41)
+    ctx[:2] = [1, 16]
+    tabs_np = C.pad_tables([list(x) for x in np.split(rng.permutation(nb)[:int(((ctx + 15) // 16).sum())],
+                                                     np.cumsum((ctx + 15) // 16)[:-1])])
+    B = len(ctx)
+    pools = [dev(C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt), dt)
+             for _ in range(2)]
+    x = dev(C.to_dtype(rng.standard_normal((L, B, 18, 64), dtype=np.float32), dt), dt)
+    tabs, ctx_d = dev(tabs_np), dev(ctx.astype(np.int32))
+    err = ops.new_error_flags("cuda")
+    outs, caches = [], []
+    for layers_ws in (L, 1):
+        kc, vc = pools[0].clone(), pools[1].clone()
+        ws = ops.new_decode_workspace(B, 14, 64, "cuda", layers=layers_ws)
+        plan = ops.DecodeAppendLayersPlan(tabs, ctx_d, 0.125, ws, err)
+        out = torch.empty((L, B, 14, 64), dtype=tdt, device="cuda")
+        for _ in range(2):
+            plan(x[:, :, :14], x[:, :, 14:16], x[:, :, 16:18], kc, vc, out)
+        outs.append(out)
+        caches.append((kc, vc))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+    kc, vc = pools[0].clone(), pools[1].clone()
+    for layer in range(L):
+        for _ in range(2):
+            single = ops.paged_decode_append_attention(x[layer, :, :14], x[layer, :, 14:16], x[layer, :, 16:18],
+                                                       kc[layer], vc[layer], tabs, ctx_d, 0.125, err=err)
+        assert torch.equal(single, outs[0][layer])
+
+
 # ---------------------------------------------------------------- fused RoPE + append
 
 def qkv_rows(T, width, g, tdt, layout, mul=1.0):
