@@ -22,9 +22,12 @@
 //    key tile of 128 keys (8 blocks), the K and V blocks into a 4-stage ring;
 //    blocks past the visible keys are fetched from an out-of-range coordinate
 //    and arrive as zeros.
-//  * warp 9 (MMA): allocates all 512 TMEM columns (S_A, S_B: 128 fp32 each;
-//    O_A, O_B: 64 fp32 each; P_A, P_B: 64 columns of fp16/bf16 pairs each)
-//    and one elected lane issues tcgen05.mma kind::f16 (M=128):
+//  * warps 9 and 10 (MMA; fp8: warp 9 alone): warp 9 allocates all 512 TMEM
+//    columns (S_A, S_B: 128 fp32 each; O_A, O_B: 64 fp32 each; P_A, P_B: 64
+//    columns of fp16/bf16 pairs each).  Warp 9 issues tile A's MMAs and warp
+//    10 tile B's, so neither tile's next S or PV waits on the other tile's
+//    softmax (2% over one issuer for both); one elected lane of each issues
+//    tcgen05.mma kind::f16 (M=128):
 //    S_x = Q_x K_j^T (N=128, K=64, both K-major, from shared memory) and
 //    O_x += P_x V_j (N=64, K=128; A = P_x from tensor memory, B = V the
 //    MN-major shared operand), committing to mbarriers.  S_x of key tile j+1
@@ -187,7 +190,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int i = 0; i < kPfStages; ++i) {
       // fp8: the 16-bit tiles are written by the two converter warps
       mbar_init(&kv_full[i], FP8 ? 2 : 1);
-      mbar_init(&kv_empty[i], 1);
+      // 16-bit: both MMA warps (one per query tile) release each stage
+      mbar_init(&kv_empty[i], FP8 ? 1 : 2);
     }
     for (int i = 0; i < kPf8Stages; ++i) {
       mbar_init(&s8_full[i], 1);
@@ -324,8 +328,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       __syncwarp();
     }
-  } else if (warp == kPfMmaWarp) {
-    // ======================= MMA issuer =======================
+  } else if (warp == kPfMmaWarp || (!FP8 && warp == kPfMmaWarp + 1)) {
+    // ======================= MMA issuers =======================
     // The whole warp runs the loop, so descriptors and tensor-memory
     // addresses are warp-uniform values; one elected lane (the same lane every
     // time) issues every tcgen05.mma and tcgen05.commit (a commit tracks the
@@ -370,11 +374,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       __syncwarp();
     };
+    // 16-bit: warp 9 issues tile A's MMAs and warp 10 tile B's, so neither
+    // tile's next S or PV waits on the other tile's softmax; fp8 (warps 10
+    // and 11 convert): warp 9 issues both.  Each warp waits for every key
+    // tile and releases every stage, including tiles its query tile does not
+    // reach, so a release always follows that stage's load.
+    const int xs = FP8 ? -1 : warp - kPfMmaWarp;  // the query tile this warp serves (-1: both)
+    auto serves = [&](int x) { return xs < 0 || x == xs; };
     bool dead = !wait_all(q_full, 0);
     if (!dead && !wait_all(&kv_full[0], 0)) dead = true;
     if (!dead) {
-      if (nt[0] > 0) issue_qk(0, 0);
-      if (nt[1] > 0) issue_qk(1, 0);
+      if (serves(0) && nt[0] > 0) issue_qk(0, 0);
+      if (serves(1) && nt[1] > 0) issue_qk(1, 0);
     }
     for (int j = 0; j < n_kv_tiles && !dead; ++j) {
       // S of key tile j+1 once the softmax has read S of tile j
@@ -384,7 +395,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
-        if (j + 1 >= nt[x]) continue;
+        if (!serves(x) || j + 1 >= nt[x]) continue;
         if (!wait_all(&s_empty[x], j & 1)) {
           dead = true;
           break;
@@ -395,7 +406,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // O_x += P_x V_j once the softmax has written P_x
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
-        if (j >= nt[x]) continue;
+        if (!serves(x) || j >= nt[x]) continue;
         if (!wait_all(&p_full[x], j & 1)) {
           dead = true;
           break;
