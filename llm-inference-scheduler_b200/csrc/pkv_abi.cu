@@ -1084,7 +1084,9 @@ int pkv_paged_prefill_attention_fp8_scratch(
   AttnArgs t = a;  // the tensor-core prefill over the 16-bit scratch pool
   t.k_scale = t.v_scale = nullptr;
   t.k_pool = t.v_pool = scratch;  // alignment stand-ins until the pass sets them
-  if (g_decode_impl.load() != PKV_DECODE_AUTO || !prefill_fast_supported(t))
+  // the pass reads the e4m3 pools 16 bytes at a time
+  const bool pools16 = ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool)) & 15) == 0;
+  if (g_decode_impl.load() != PKV_DECODE_AUTO || !prefill_fast_supported(t) || !pools16)
     return status_of(launch_generic_attention(a, st));
   void *kq = nullptr, *vq = nullptr;
   int32_t* tab = nullptr;
