@@ -67,6 +67,9 @@ extern "C" {
 #define PKV_IPC_HANDLE_BYTES 64
 
 /* decode-attention kernel choice (pkv_set_decode_impl) */
+/* flags of pkv_paged_decode_append_attention_layers_flags */
+#define PKV_LAYERS_DEFER_FIRST 1
+
 #define PKV_DECODE_AUTO 0
 #define PKV_DECODE_GENERIC 1
 
@@ -300,6 +303,34 @@ int pkv_paged_decode_append_attention_layers(
     int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
     void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
     const void* schedule, const int32_t* input_ready);
+
+/*
+ * pkv_paged_decode_append_attention_layers with flags (0: the same call).
+ * PKV_LAYERS_DEFER_FIRST: the call's first decode kernel also starts before
+ * the launch before it completes and waits for it only at its end, as the
+ * call's later layers do, so two calls over consecutive runs of layers form
+ * one chain: the next run's first layer starts while the previous run's
+ * merge is still running, instead of after it.  With the flag the caller
+ * promises that no work enqueued before the call and possibly still running
+ * writes anything the call reads (the q / k_new / v_new rows, the pools,
+ * tables, lengths, schedule) or reads or writes anything it writes (out, the
+ * pools' appended slots, the workspace): in particular the previous run used
+ * other split-K sets, which is why a step's runs take slices of one
+ * workspace of a set per layer of the step.  Inputs still arriving from a
+ * copy stream are covered by input_ready.  The flag needs the chained form
+ * (a split-K set per layer of the call, a single layer included); otherwise
+ * it is ignored and the call runs as without it.  Other flag bits return
+ * PKV_ERR_UNSUPPORTED.
+ */
+int pkv_paged_decode_append_attention_layers_flags(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule, const int32_t* input_ready, int flags);
 
 /*
  * KV block migration between GPUs (one process per GPU).  Replaces the

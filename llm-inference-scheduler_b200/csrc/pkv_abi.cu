@@ -826,6 +826,25 @@ int pkv_paged_decode_append_attention_layers(
     int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
     void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
     const void* schedule, const int32_t* input_ready) {
+  return pkv_paged_decode_append_attention_layers_flags(
+      n_layers, out, out_layer_stride, out_row_stride, q, q_layer_stride, q_row_stride, k_new, v_new,
+      new_layer_stride, k_new_row_stride, v_new_row_stride, k_pools, v_pools, pool_layer_stride_bytes,
+      num_blocks, block_tables, block_table_stride, max_blocks_per_seq, context_lens, n_seqs,
+      n_q_heads, n_kv_heads, head_dim, block_size, scale, dtype, workspace, workspace_bytes,
+      err_flags, stream, schedule, input_ready, 0);
+}
+
+int pkv_paged_decode_append_attention_layers_flags(
+    int n_layers, void* out, int64_t out_layer_stride, int64_t out_row_stride, const void* q,
+    int64_t q_layer_stride, int64_t q_row_stride, const void* k_new, const void* v_new,
+    int64_t new_layer_stride, int64_t k_new_row_stride, int64_t v_new_row_stride, void* k_pools,
+    void* v_pools, int64_t pool_layer_stride_bytes, int num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, int max_blocks_per_seq, const int32_t* context_lens, int n_seqs,
+    int n_q_heads, int n_kv_heads, int head_dim, int block_size, float scale, int dtype,
+    void* workspace, size_t workspace_bytes, int* err_flags, pkv_stream_t stream,
+    const void* schedule, const int32_t* input_ready, int flags) {
+  if ((flags & ~PKV_LAYERS_DEFER_FIRST) != 0) return PKV_ERR_UNSUPPORTED;
+  const bool defer_first = (flags & PKV_LAYERS_DEFER_FIRST) != 0;
   if (n_layers < 0 || n_seqs < 0) return PKV_ERR_BAD_SHAPE;
   if (n_layers == 0 || n_seqs == 0) return PKV_OK;
   if (!out || !q || !k_new || !v_new || !k_pools || !v_pools) return PKV_ERR_NULL_POINTER;
@@ -876,11 +895,15 @@ int pkv_paged_decode_append_attention_layers(
   // at its end (so it starts on the SMs the previous layer's tail frees), and
   // one merge launch covers every layer at the end.  Otherwise each layer's
   // decode is followed by its own merge.
+  // PKV_LAYERS_DEFER_FIRST: the first layer's decode defers its wait too
+  // (the caller's promise that nothing still running before the call touches
+  // what the call reads or writes), also for a single layer.
   const size_t ws1 = decode_workspace_bytes(n_seqs, n_q_heads, head_dim);
-  if (n_layers > 1 && workspace && ws1 > 0 && workspace_bytes / static_cast<size_t>(n_layers) >= ws1) {
+  if ((n_layers > 1 || defer_first) && workspace && ws1 > 0 &&
+      workspace_bytes / static_cast<size_t>(n_layers) >= ws1) {
     LayerChain ch{0, 0, n_layers, out, out_layer_stride, workspace, static_cast<int64_t>(ws1)};
     for (int l = 0; l < n_layers; ++l) {
-      ch.defer_wait = l > 0;
+      ch.defer_wait = l > 0 || defer_first;
       ch.merge = l == n_layers - 1;
       void* o = const_cast<void*>(at(out, l * out_layer_stride * es));
       void* wsl = static_cast<uint8_t*>(workspace) + static_cast<size_t>(l) * ws1;

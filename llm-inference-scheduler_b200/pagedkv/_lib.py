@@ -41,6 +41,9 @@ FLAG_BAD_SCHEDULE = 64
 DECODE_AUTO = 0
 DECODE_GENERIC = 1
 
+# flags of pkv_paged_decode_append_attention_layers_flags
+LAYERS_DEFER_FIRST = 1
+
 # every symbol include/pagedkv.h declares, with (restype, argtypes)
 _P, _I, _I64, _F, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 SIGNATURES: dict = {
@@ -92,6 +95,10 @@ SIGNATURES: dict = {
                                                       _I64, _I64, _I64, _P, _P, _I64, _I, _P, _I64,
                                                       _I, _P, _I, _I, _I, _I, _I, _F, _I, _P, _SZ,
                                                       _P, _P, _P, _P]),
+    "pkv_paged_decode_append_attention_layers_flags": (_I, [_I, _P, _I64, _I64, _P, _I64, _I64, _P,
+                                                            _P, _I64, _I64, _I64, _P, _P, _I64, _I, _P,
+                                                            _I64, _I, _P, _I, _I, _I, _I, _I, _F, _I,
+                                                            _P, _SZ, _P, _P, _P, _P, _I]),
 }
 
 

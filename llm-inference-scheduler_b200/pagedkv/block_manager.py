@@ -580,7 +580,8 @@ class PagedKVCache:
     def forward_layers(self, first_layer: int, q: torch.Tensor, k_new: torch.Tensor,
                        v_new: torch.Tensor, meta: StepMetadata, scale: float,
                        out: torch.Tensor | None = None, advance: bool = True,
-                       input_ready: torch.Tensor | None = None) -> torch.Tensor:
+                       input_ready: torch.Tensor | None = None,
+                       defer_first: bool = False) -> torch.Tensor:
         """forward_layer for the n consecutive layers first_layer ..
         first_layer + n - 1 at once, with layer-major inputs: q [n, T, Hq, D],
         k_new / v_new [n, T, Hkv, D] -> out [n, T, Hq, D].  A decode-only step
@@ -590,7 +591,11 @@ class PagedKVCache:
         layer by layer.  The results are those of forward_layer either way.
         input_ready (one-call form only): an int32 device tensor of one word
         per layer; layer l's kernels wait, bounded, until a copy on another
-        stream has set word l nonzero after that layer's q / k_new / v_new."""
+        stream has set word l nonzero after that layer's q / k_new / v_new.
+        defer_first (one-call form over 16-bit pools): the run's first decode
+        kernel continues the launch chain of the run enqueued just before it,
+        whose layers used other split-K sets (meta.layers_plan must hold this
+        run's own workspace slice)."""
         mgr = self.mgr
         n = q.shape[0]
         last = first_layer + n
@@ -600,6 +605,9 @@ class PagedKVCache:
         if mgr._pending:
             mgr.flush_copies()
         nd = meta.n_decode
+        if defer_first and (meta.layers_plan is None or mgr.fp8):
+            raise ValueError("pagedkv: defer_first needs meta.layers_plan over this run's own "
+                             "split-K sets (16-bit pools)")
         if 0 < nd == meta.n_tokens:
             plan = meta.layers_plan
             kind = ops.DecodeAppendFp8LayersPlan if mgr.fp8 else ops.DecodeAppendLayersPlan
@@ -614,7 +622,7 @@ class PagedKVCache:
                      mgr.k_scale_cache[first_layer:last], mgr.v_scale_cache[first_layer:last], out)
             else:
                 plan(q, k_new, v_new, mgr.k_cache[first_layer:last], mgr.v_cache[first_layer:last], out,
-                     input_ready=input_ready)
+                     input_ready=input_ready, defer_first=defer_first)
             if advance and last == mgr.num_layers:
                 self._advance(meta)
             return out

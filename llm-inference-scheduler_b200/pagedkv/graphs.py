@@ -411,7 +411,9 @@ class DecodeStepGraph:
     * per chunk of layers, one pkv_paged_decode_append_attention_layers call
       with a split-K set per layer: the layers' decode kernels chain (each
       later one starts on the SMs the previous one's tail frees) and one merge
-      launch follows them.  Each layer's kernels wait, bounded, for its ready
+      launch follows them.  Every layer of the step has its own set, so a
+      chunk's first decode continues the chain too (PKV_LAYERS_DEFER_FIRST):
+      it starts beside the previous chunk's merge instead of after it.  Each layer's kernels wait, bounded, for its ready
       word before reading its rows.  An event wait on the copy stream would
       instead end the programmatic overlap between two launches (about 5 us
       each); the ready words keep the step one launch chain;
@@ -468,8 +470,11 @@ class DecodeStepGraph:
         self.dev_qkv = torch.empty((L, R, width, D), dtype=mgr.dtype, device=dev)
         self.dev_out = torch.empty((L, R, hq, D), dtype=mgr.dtype, device=dev)
         self.h2d, self.d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        # one split-K set per layer of the largest chunk: a chunk's layers chain
-        self.workspace = kv_cache.decode_workspace(R, hq, D, layers=max(chunks))
+        # one split-K set per layer of the step: a chunk's layers chain, and a
+        # chunk's first layer continues the chain of the chunk before it
+        # (PKV_LAYERS_DEFER_FIRST), whose merge may still read its own sets
+        self.ws1 = ops.decode_workspace_bytes(R, hq, D)
+        self.workspace = kv_cache.decode_workspace(R, hq, D, layers=L)
         # per layer: nonzero once its rows are on the device (set by the copy stream)
         self.ready = torch.zeros(L, dtype=torch.int32, device=dev)
         self._ones = torch.ones(L, dtype=torch.int32).pin_memory()
@@ -530,15 +535,17 @@ class DecodeStepGraph:
         meta.decode_schedule = ops.build_decode_schedule(
             self.schedule, meta.block_tables, meta.context_lens, mgr.num_blocks, self.hq,
             mgr.num_kv_heads, mgr.head_dim, mgr.dtype, err=mgr.err)
-        meta.layers_plan = ops.DecodeAppendLayersPlan(meta.block_tables, meta.context_lens, self.scale,
-                                                      self.workspace, mgr.err,
-                                                      schedule=meta.decode_schedule)
         for c, ((a, b), ev) in enumerate(zip(self.bounds, ev_in)):
             if not self.gated:
                 cur.wait_event(ev)
+            # chunk c's layers use split-K sets a .. b-1 of the step's workspace
+            meta.layers_plan = ops.DecodeAppendLayersPlan(
+                meta.block_tables, meta.context_lens, self.scale,
+                self.workspace[a * self.ws1: b * self.ws1], mgr.err, schedule=meta.decode_schedule)
             kv.forward_layers(a, q[a:b, :, :self.hq], q[a:b, :, self.hq:self.hq + hkv],
                               q[a:b, :, self.hq + hkv:], meta, self.scale, out=self.dev_out[a:b],
-                              advance=False, input_ready=self.ready[a:b] if self.gated else None)
+                              advance=False, input_ready=self.ready[a:b] if self.gated else None,
+                              defer_first=self.gated and c > 0)
             done = torch.cuda.Event()
             done.record(cur)
             self.d2h.wait_event(done)

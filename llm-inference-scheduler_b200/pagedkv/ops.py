@@ -649,7 +649,7 @@ class DecodeAppendLayersPlan:
         self.schedule = schedule
         self._key = None
         self._args: list = []
-        self._fn = _lib.load().pkv_paged_decode_append_attention_layers
+        self._fn = _lib.load().pkv_paged_decode_append_attention_layers_flags
 
     @staticmethod
     def _layer_stride(t: torch.Tensor, name: str) -> int:
@@ -657,11 +657,15 @@ class DecodeAppendLayersPlan:
             raise ValueError(f"pagedkv: `{name}` must be [layers, rows, heads, head_dim]")
         return t.stride(0)
 
-    def __call__(self, q, k_new, v_new, k_pools, v_pools, out, input_ready=None) -> torch.Tensor:
+    def __call__(self, q, k_new, v_new, k_pools, v_pools, out, input_ready=None,
+                 defer_first: bool = False) -> torch.Tensor:
         """input_ready: None, or an int32 device tensor of one word per layer:
         layer l's kernels wait (bounded) until input_ready[l] is nonzero
         before reading its q, k_new and v_new (set by a copy on another
-        stream after that layer's rows)."""
+        stream after that layer's rows).  defer_first: PKV_LAYERS_DEFER_FIRST
+        (the run continues the chain of a run just enqueued over other layers
+        and other split-K sets; nothing still running touches this run's
+        data)."""
         n = q.shape[0]
         if k_new.shape[0] != n or v_new.shape[0] != n or out.shape[0] != n or \
                 k_pools.shape[0] != n or v_pools.shape[0] != n:
@@ -686,7 +690,7 @@ class DecodeAppendLayersPlan:
                           q_rs, kn, vn, self._layer_stride(k_new, "k_new"), kn_rs, vn_rs, kp, vp,
                           k_pools.stride(0) * k_pools.element_size(), nb, bt, bt_s, mb, cl, B, hq,
                           hkv, d, bs, sc, dt, wsp, wsb, errp, st,
-                          None if self.schedule is None else self.schedule.data_ptr(), None]
+                          None if self.schedule is None else self.schedule.data_ptr(), None, 0]
             self._key = key
         a = self._args
         a[0], a[1], a[4], a[7], a[8], a[12], a[13] = (n, out.data_ptr(), q.data_ptr(), k_new.data_ptr(),
@@ -696,7 +700,8 @@ class DecodeAppendLayersPlan:
             _cuda(input_ready, "input_ready")
             if input_ready.dtype != torch.int32 or input_ready.numel() != n or not input_ready.is_contiguous():
                 raise ValueError("pagedkv: input_ready must hold one contiguous int32 word per layer")
-        a[-1] = None if input_ready is None else input_ready.data_ptr()
+        a[-2] = None if input_ready is None else input_ready.data_ptr()
+        a[-1] = _lib.LAYERS_DEFER_FIRST if defer_first else 0
         rc = self._fn(*a)
         if rc:
             _lib.check(rc, "pkv_paged_decode_append_attention_layers")

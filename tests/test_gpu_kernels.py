@@ -645,6 +645,50 @@ def test_decode_layers_chained_equals_per_layer_merges(dt):
         assert torch.equal(single, outs[0][layer])
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_decode_layers_defer_first_runs_equal_one_chain(dt):
+    """Consecutive runs of layers as one launch chain: runs of 3, 1, 2 and 1
+    layers, each after the first with PKV_LAYERS_DEFER_FIRST over its own
+    slice of a workspace of one split-K set per layer, twice in a row, against
+    one call over all layers on copies of the same pools: outputs and pools
+    bit-identical.  An unknown flag bit is refused before any launch."""
+    rng = np.random.default_rng(53)
+    L, nb, tdt = 7, 1024, TORCH_DT[dt]
+    ctx = rng.integers(1, 700, size=37)
+    ctx[:3] = [1, 16, 17]
+    tabs_np = C.pad_tables([list(x) for x in np.split(rng.permutation(nb)[:int(((ctx + 15) // 16).sum())],
+                                                     np.cumsum((ctx + 15) // 16)[:-1])])
+    B = len(ctx)
+    pools = [dev(C.to_dtype(rng.standard_normal((L, nb, 16, 2, 64), dtype=np.float32), dt), dt)
+             for _ in range(2)]
+    x = dev(C.to_dtype(rng.standard_normal((L, B, 18, 64), dtype=np.float32), dt), dt)
+    tabs, ctx_d = dev(tabs_np), dev(ctx.astype(np.int32))
+    err = ops.new_error_flags("cuda")
+    ws1 = ops.decode_workspace_bytes(B, 14, 64)
+    ws = ops.new_decode_workspace(B, 14, 64, "cuda", layers=L)
+    ref_ws = ops.new_decode_workspace(B, 14, 64, "cuda", layers=L)
+    ref_k, ref_v = pools[0].clone(), pools[1].clone()
+    ref = torch.empty((L, B, 14, 64), dtype=tdt, device="cuda")
+    one = ops.DecodeAppendLayersPlan(tabs, ctx_d, 0.125, ref_ws, err)
+    kc, vc = pools[0].clone(), pools[1].clone()
+    out = torch.empty_like(ref)
+    runs = [(0, 3), (3, 4), (4, 6), (6, 7)]
+    plans = [ops.DecodeAppendLayersPlan(tabs, ctx_d, 0.125, ws[a * ws1: b * ws1], err) for a, b in runs]
+    for _ in range(2):
+        one(x[:, :, :14], x[:, :, 14:16], x[:, :, 16:18], ref_k, ref_v, ref)
+        for i, ((a, b), plan) in enumerate(zip(runs, plans)):
+            plan(x[a:b, :, :14], x[a:b, :, 14:16], x[a:b, :, 16:18], kc[a:b], vc[a:b], out[a:b],
+                 defer_first=i > 0)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out, ref)
+    assert torch.equal(kc, ref_k) and torch.equal(vc, ref_v)
+    a = list(plans[1]._args)
+    a[-1] = 2  # not a defined flag
+    assert _lib.load().pkv_paged_decode_append_attention_layers_flags(*a) == _lib.ERR_UNSUPPORTED
+
+
 # ---------------------------------------------------------------- fused RoPE + append
 
 def qkv_rows(T, width, g, tdt, layout, mul=1.0):
