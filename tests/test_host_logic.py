@@ -411,3 +411,20 @@ def test_step_arrays_track_table_changes():
         np.testing.assert_array_equal(a["slots"], slots)
         for s, n in seqs:  # advance, as the last layer of forward_layer does
             kv._len[s] += n
+
+
+def test_decode_step_graph_chunk_sizes():
+    """DecodeStepGraph's default compute chunks: they cover every layer once,
+    end in chunks of 1, 1, 2, 4 ... layers (each chunk's copy out overlaps the
+    compute of the chunks after it), and the front chunk holds at most twice
+    the layers after it; 24 layers (config 3) give 16, 4, 2, 1, 1."""
+    from pagedkv.graphs import ready_chunks
+
+    assert ready_chunks(24) == [16, 4, 2, 1, 1]
+    for n in range(1, 100):
+        ch = ready_chunks(n)
+        assert sum(ch) == n and min(ch) >= 1
+        assert ch[-1] == 1
+        for i, c in enumerate(ch[1:], 1):
+            assert c <= max(1, sum(ch[i + 1:]))  # the tail doubles at most
+        assert ch[0] <= 2 * max(1, sum(ch[1:]))
