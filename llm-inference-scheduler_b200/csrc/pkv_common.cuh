@@ -413,6 +413,22 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   const float p = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
+// exp2_poly3 of two values with the paired fp32 instructions of sm_100
+// (__fadd2_rn / __ffma2_rn round each lane as __fadd_rn / fmaf do, so each
+// lane's result equals exp2_poly3 bit for bit) at half the issue slots
+__device__ __forceinline__ float2 exp2_poly3x2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 big = make_float2(12582912.f, 12582912.f), nbig = make_float2(-12582912.f, -12582912.f);
+  const float2 t = __fadd2_rn(x, big);
+  const float2 n = __fadd2_rn(t, nbig);
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+  p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+  p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
 
 // ---- fp8 e4m3 KV: one scale per (token, KV head) row, absmax / 448
 constexpr float kFp8Max = 448.f;  // largest finite e4m3 value

@@ -81,9 +81,12 @@ constexpr int kPfMmaWarp = 9;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfOrderMaxSeqs = 64;
 #ifndef PKV_PF_POLY_EVERY
-#define PKV_PF_POLY_EVERY 8
+#define PKV_PF_POLY_EVERY 3
 #endif
-// one key pair in kPfPolyEvery takes the FMA-pipe exp2 (0: all on the MUFU)
+// one key pair in kPfPolyEvery takes the FMA-pipe exp2 (0: all on the MUFU);
+// with the paired fp32 instructions a pair's polynomial costs about a dozen
+// issue slots, and one pair in three measured best (1/2: 610, 1/3: 624,
+// 1/4: 622, 1/5: 611, 1/8: 598 TFLOP/s over the config-4 step)
 constexpr int kPfPolyEvery = PKV_PF_POLY_EVERY;
 
 // tensor-memory columns: S_A, S_B (fp32), O_A, O_B (fp32), P_A, P_B (fp16/bf16 pairs)
@@ -547,20 +550,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
       // P in two halves of 64 keys: the first half covers the wait for the
       // PV of tile j-1 (which last read P_x and last wrote O_x)
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // key pairs through the paired fp32 instructions of sm_100 (one
+      // issue slot per pair for the scale-and-shift and for the row sum)
+      float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 sl2v = make_float2(sl2, sl2), nmv = make_float2(nm, nm);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int c2 = half * 32 + i, c = 2 * c2;
-          const float x0 = fmaf(__uint_as_float(sr[c >> 5][c & 31]), sl2, nm);
-          const float x1 = fmaf(__uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31]), sl2, nm);
+          const float2 xs = __ffma2_rn(make_float2(__uint_as_float(sr[c >> 5][c & 31]),
+                                                   __uint_as_float(sr[(c + 1) >> 5][(c + 1) & 31])),
+                                       sl2v, nmv);
           const bool poly = kPfPolyEvery > 0 && (c2 % (kPfPolyEvery > 0 ? kPfPolyEvery : 1)) == kPfPolyEvery - 1;
-          const float p0 = poly ? exp2_poly3(x0) : ex2_approx(x0);
-          const float p1 = poly ? exp2_poly3(x1) : ex2_approx(x1);
-          ls[i & 3] += p0 + p1;
-          pk[i] = pack2<T>(p0, p1);
+          const float2 pp = poly ? exp2_poly3x2(xs) : make_float2(ex2_approx(xs.x), ex2_approx(xs.y));
+          ls[i & 1] = __fadd2_rn(ls[i & 1], pp);
+          pk[i] = pack2<T>(pp.x, pp.y);
         }
         if (half == 0) {
           if (j >= 1 && !dead && !mbar_wait(&o_done[x], (j - 1) & 1)) dead = true;
@@ -581,7 +587,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // row r of P: 64 columns of packed (even key, odd key) pairs
         tmem_st32(t_p + half * 32, pk);
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l += (ls[0].x + ls[1].x) + (ls[0].y + ls[1].y);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
