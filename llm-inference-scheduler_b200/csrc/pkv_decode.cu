@@ -684,21 +684,26 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
         float sa_[4], sb_[4];
         qk(fa, sa_);
         qk(fb, sb_);
-        // ---- online softmax per head over the 32 tokens (exp2 domain)
-        float xa0 = sa_[0] * (sl2 * fa.ks0), xa1 = sa_[1] * (sl2 * fa.ks0);  // block a, token g
-        float xa2 = sa_[2] * (sl2 * fa.ks1), xa3 = sa_[3] * (sl2 * fa.ks1);  // block a, token g + 8
-        float xb0 = sb_[0] * (sl2 * fb.ks0), xb1 = sb_[1] * (sl2 * fb.ks0);
-        float xb2 = sb_[2] * (sl2 * fb.ks1), xb3 = sb_[3] * (sl2 * fb.ks1);
+        // ---- online softmax per head over the 32 tokens (exp2 domain).  A
+        // lane's two heads (2t, 2t + 1) of one token are a pair for the
+        // paired fp32 instructions of sm_100 (each lane rounded as the scalar
+        // instruction rounds it)
+        const float ka0 = sl2 * fa.ks0, ka1 = sl2 * fa.ks1, kb0 = sl2 * fb.ks0, kb1 = sl2 * fb.ks1;
+        float2 xa01 = __fmul2_rn(make_float2(sa_[0], sa_[1]), make_float2(ka0, ka0));  // block a, token g
+        float2 xa23 = __fmul2_rn(make_float2(sa_[2], sa_[3]), make_float2(ka1, ka1));  // block a, token g + 8
+        float2 xb01 = __fmul2_rn(make_float2(sb_[0], sb_[1]), make_float2(kb0, kb0));
+        float2 xb23 = __fmul2_rn(make_float2(sb_[2], sb_[3]), make_float2(kb1, kb1));
+        const float2 ninf = make_float2(-INFINITY, -INFINITY);
         if (fa.valid < 16) {
-          if (g >= fa.valid) xa0 = xa1 = -INFINITY;
-          if (g + 8 >= fa.valid) xa2 = xa3 = -INFINITY;
+          if (g >= fa.valid) xa01 = ninf;
+          if (g + 8 >= fa.valid) xa23 = ninf;
         }
         if (fb.valid < 16) {
-          if (g >= fb.valid) xb0 = xb1 = -INFINITY;
-          if (g + 8 >= fb.valid) xb2 = xb3 = -INFINITY;
+          if (g >= fb.valid) xb01 = ninf;
+          if (g + 8 >= fb.valid) xb23 = ninf;
         }
-        float ma = fmaxf(fmaxf(xa0, xa2), fmaxf(xb0, xb2));
-        float mb = fmaxf(fmaxf(xa1, xa3), fmaxf(xb1, xb3));
+        float ma = fmaxf(fmaxf(xa01.x, xa23.x), fmaxf(xb01.x, xb23.x));
+        float mb = fmaxf(fmaxf(xa01.y, xa23.y), fmaxf(xb01.y, xb23.y));
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) {
           ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, off));
@@ -717,17 +722,26 @@ __global__ void __launch_bounds__(32 * (NKV + 1) * PIPES, PIPES > 1 ? 1 : PKV_DE
           m0 = mna;
           m1 = mnb;
         }
-        const float pa0 = ex2_approx(xa0 - m0), pa2 = ex2_approx(xa2 - m0);
-        const float pa1 = ex2_approx(xa1 - m1), pa3 = ex2_approx(xa3 - m1);
-        const float pb0 = ex2_approx(xb0 - m0), pb2 = ex2_approx(xb2 - m0);
-        const float pb1 = ex2_approx(xb1 - m1), pb3 = ex2_approx(xb3 - m1);
-        l0 += (pa0 + pa2) + (pb0 + pb2);
-        l1 += (pa1 + pa3) + (pb1 + pb3);
+        const float2 nm = make_float2(-m0, -m1);
+        const float2 da01 = __fadd2_rn(xa01, nm), da23 = __fadd2_rn(xa23, nm);
+        const float2 db01 = __fadd2_rn(xb01, nm), db23 = __fadd2_rn(xb23, nm);
+        const float2 pa01 = make_float2(ex2_approx(da01.x), ex2_approx(da01.y));
+        const float2 pa23 = make_float2(ex2_approx(da23.x), ex2_approx(da23.y));
+        const float2 pb01 = make_float2(ex2_approx(db01.x), ex2_approx(db01.y));
+        const float2 pb23 = make_float2(ex2_approx(db23.x), ex2_approx(db23.y));
+        // l += (pa(g) + pa(g + 8)) + (pb(g) + pb(g + 8)), per head
+        const float2 ls = __fadd2_rn(__fadd2_rn(pa01, pa23), __fadd2_rn(pb01, pb23));
+        l0 += ls.x;
+        l1 += ls.y;
         // P^T fragments with V's per-token scale folded in (l sums the unscaled P)
-        const uint32_t ba0 = movmatrix_t(pack2<T>(pa0 * fa.vs0, pa1 * fa.vs0));  // tokens 0-7
-        const uint32_t ba1 = movmatrix_t(pack2<T>(pa2 * fa.vs1, pa3 * fa.vs1));  // tokens 8-15
-        const uint32_t bb0 = movmatrix_t(pack2<T>(pb0 * fb.vs0, pb1 * fb.vs0));
-        const uint32_t bb1 = movmatrix_t(pack2<T>(pb2 * fb.vs1, pb3 * fb.vs1));
+        const float2 qa01 = __fmul2_rn(pa01, make_float2(fa.vs0, fa.vs0));
+        const float2 qa23 = __fmul2_rn(pa23, make_float2(fa.vs1, fa.vs1));
+        const float2 qb01 = __fmul2_rn(pb01, make_float2(fb.vs0, fb.vs0));
+        const float2 qb23 = __fmul2_rn(pb23, make_float2(fb.vs1, fb.vs1));
+        const uint32_t ba0 = movmatrix_t(pack2<T>(qa01.x, qa01.y));  // tokens 0-7
+        const uint32_t ba1 = movmatrix_t(pack2<T>(qa23.x, qa23.y));  // tokens 8-15
+        const uint32_t bb0 = movmatrix_t(pack2<T>(qb01.x, qb01.y));
+        const uint32_t bb1 = movmatrix_t(pack2<T>(qb23.x, qb23.y));
 #pragma unroll
         for (int mt = 0; mt < 4; ++mt) {
           uint32_t aa[4], ab[4];
