@@ -344,6 +344,64 @@ def test_prefill_equal_lengths_and_many_sequences(oracle_mod, dt):
     assert max_abs_diff(out, ref, dt) <= PRODUCT_ATOL[dt]
 
 
+def prefill_fp64(c, scale=0.125):
+    """Causal attention of a prefill case in float64 from its stored (16-bit)
+    inputs: scores and probabilities unrounded.  A yardstick for cases whose
+    scores are too large for the reference's rounding points (the oracle
+    rounds Q.K^T to the KV dtype, an ulp of several percent of P there)."""
+    dt = c["dt"]
+    f64 = lambda a: C.to_float32(a, dt).astype(np.float64)  # noqa: E731
+    kp, vp, q, kn, vn = f64(c["k_pool"]), f64(c["v_pool"]), f64(c["q"]), f64(c["k_new"]), f64(c["v_new"])
+    out = np.zeros_like(q)
+    g = C.HQ // C.HKV
+    for s in range(len(c["chunk"])):
+        P, a, b = int(c["prior"][s]), int(c["qsl"][s]), int(c["qsl"][s + 1])
+        pos = np.arange(P)
+        blocks = np.asarray(c["tables"][s], dtype=np.int64)[pos // C.BS]
+        K = np.concatenate([kp[blocks, pos % C.BS], kn[a:b]])  # [P + n, HKV, D]
+        V = np.concatenate([vp[blocks, pos % C.BS], vn[a:b]])
+        visible = np.arange(P + b - a)[None, :] <= (P + np.arange(b - a))[:, None]
+        for h in range(C.HQ):
+            sc = np.where(visible, q[a:b, h] @ K[:, h // g].T * scale, -np.inf)
+            w = np.exp(sc - sc.max(axis=1, keepdims=True))
+            out[a:b, h] = (w / w.sum(axis=1, keepdims=True)) @ V[:, h // g]
+    return out
+
+
+@pytest.mark.parametrize("dt", ("f16", "bf16"))
+def test_prefill_running_max_jumps(dt):
+    """Scores that grow along the keys: K rows of a sequence's blocks 8-23
+    scaled by 4 and from block 24 on by 16 (the new rows too, by the block
+    they land in), so rows' maxima jump by far more than the rescale slack
+    (2^8) in later key tiles.  The tensor-core kernel runs a tile's
+    exponentials against the running max and redoes the tile when a row's
+    max moved; the redone tiles and the O rescales with them, against float64
+    attention of the same inputs.  Tolerance: the output's rounding plus P
+    rounded to the pool dtype (relative 2^-11 for fp16, 2^-8 for bf16) over
+    |V| < 5."""
+    c = C.make_prefill_case(31, [300, 200, 129], [700, 300, 0], 32, 256, dt)
+    factor = lambda j: 16.0 if j >= 24 else 4.0 if j >= 8 else 1.0  # noqa: E731
+    scale_of = {}
+    for s, tab in enumerate(c["tables"]):
+        for j, b in enumerate(tab):
+            if j >= 2:  # the shared prefix blocks stay as they are
+                scale_of[b] = factor(j)
+    kp = C.to_float32(c["k_pool"], dt).copy()
+    for b, f in scale_of.items():
+        kp[b] *= f  # powers of two: exact in every dtype
+    c["k_pool"] = C.to_dtype(kp, dt)
+    kn = C.to_float32(c["k_new"], dt).copy()
+    for s in range(len(c["chunk"])):
+        for i in range(int(c["chunk"][s])):
+            kn[c["qsl"][s] + i] *= factor((int(c["prior"][s]) + i) // 16)
+    c["k_new"] = C.to_dtype(kn, dt)
+    out, err = run_prefill_gpu(c)
+    assert err == 0
+    ref = prefill_fp64(c)
+    tol = {"f16": 4e-3, "bf16": 3.2e-2}[dt]
+    assert float(np.max(np.abs(as_f32(out, dt).astype(np.float64) - ref))) <= tol
+
+
 def test_prefill_config4_full(oracle_mod, decode_impl):
     c = C.make_c4_case()
     out, err = run_prefill_gpu(c)
